@@ -1,0 +1,439 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 decode-attention hot path (one JSON line on rank 0).
+
+Metric: decode-attention achieved HBM GB/s (% of peak) and
+seq-steps/s at 1/2/4/8 B200.  Default workload = BASELINE config 4, the one
+the metric's "at 1/2/4/8 B200" is quoted on: long-context split-KV
+flash-decoding, batch 4, context 131072, 14 Q / 2 KV heads, head_dim 64,
+bf16 KV ~ N(0,1); the KV sequence is sharded evenly over the N GPUs and the
+per-shard softmax partials are all-gathered over NCCL and merged.  A step
+is one decode step of all 24 Qwen2-0.5B layers: per layer RoPE on q/k, the
+owner's cache-write of the new row, split-KV attention and the merge.
+
+  value       whole-job algorithmic bytes / step time, inputs resident in HBM
+  e2e         the same through the C ABI with pinned HOST buffers, every
+              step's host->device inputs and device->host outputs included
+  roofline    dominant kernel (decode attention), bytes per launch over its
+              CUDA-event launch time, vs the measured HBM copy bandwidth
+  cpu_baseline  the reference's own CPU code (oracle/_ref, compiled from
+              tmac_gguf.cpp:990-1016 / :1090-1128) on a bounded sample
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W]
+                       [--impl tg|reference] [--workload longctx|batched|cfg2|cfg1]
+For N > 1 launch with torch.distributed.run (one rank per GPU).
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import datetime
+import importlib.util
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "tmac_gguf.cpp_b200")
+
+N_HEAD, N_KV, HD = 14, 2, 64
+QD, KD = N_HEAD * HD, N_KV * HD
+
+WORKLOADS = {
+    # BASELINE config 4
+    "longctx": dict(B=4, ctx=131072, layers=24, dtype="bf16", split=True,
+                    desc="config4: long-context split-KV decode, B=4, ctx=131072, bf16 KV, "
+                         "KV sharded over the GPUs, NCCL all-gather merge"),
+    # BASELINE config 3
+    "batched": dict(B=256, ctx=4096, layers=24, dtype="bf16", split=False,
+                    desc="config3: batched decode, B=256 per GPU, ctx=4096, bf16 KV, "
+                         "24 layers with independent seeds, sequences partitioned per GPU"),
+    # BASELINE config 2
+    "cfg2": dict(B=64, ctx=256, layers=24, dtype="f32", split=False, ragged=True,
+                 desc="config2: batched decode, B=64, ctx~U[1,256], fp32 KV, 24 layers"),
+    # BASELINE config 1
+    "cfg1": dict(B=1, ctx=256, layers=24, dtype="f32", split=False,
+                 desc="config1: single sequence, pos=255, fp32 KV, 24 layers"),
+}
+
+
+def load_package():
+    name = "tmac_gguf_cpp_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(
+        name, os.path.join(PKG_DIR, "__init__.py"), submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def load_oracle():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # noqa: E402
+    return oracle
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def positions(wl, seed=1234):
+    """Global position of each sequence's current token (past_len)."""
+    if wl.get("ragged"):
+        rng = np.random.default_rng(seed)
+        return rng.integers(0, wl["ctx"], size=wl["B"]).astype(np.int32)
+    return np.full(wl["B"], wl["ctx"] - 1, dtype=np.int32)
+
+
+def algo_bytes_step(wl, pos):
+    """Algorithmic HBM bytes of one decode step over all layers and
+    sequences (whole job): K and V rows read once, the new row written,
+    q read and the output written (fp32)."""
+    s_kv = 2 if wl["dtype"] == "bf16" else 4
+    n = pos.astype(np.int64) + 1
+    per_layer = int(np.sum(n * 2 * KD * s_kv + 2 * KD * s_kv + 2 * QD * 4))
+    return per_layer * wl["layers"]
+
+
+def kernel_bytes_launch(wl, pos, shard_start, shard_len, split):
+    """Algorithmic bytes of one decode-attention launch on one rank."""
+    s_kv = 2 if wl["dtype"] == "bf16" else 4
+    n_loc = np.clip(pos.astype(np.int64) + 1 - shard_start, 0, shard_len)
+    out_b = N_HEAD * (HD + 2) * 4 if split else QD * 4
+    return int(np.sum(n_loc * 2 * KD * s_kv) + len(pos) * (QD * 4 + out_b))
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,"
+              "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self, t0, t1):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = []
+        for r in csv.reader(io.StringIO(out)):
+            if len(r) < 10:
+                continue
+            try:
+                ts = datetime.datetime.strptime(r[0].strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                idx = int(r[1])
+                sm = float(r[2])
+                smax = float(r[3])
+            except ValueError:
+                continue
+            if idx not in self.gpus:
+                continue
+            rows.append((ts, sm, smax, [x.strip() for x in r[6:10]]))
+        if not rows:
+            return None
+        inside = [x for x in rows if t0 - 0.05 <= x[0] <= t1 + 0.05] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for x in inside for i, v in enumerate(x[3])
+                          if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(x[1] for x in inside),
+                "sm_max_mhz": max(x[2] for x in inside),
+                "reasons": reasons, "samples": len(inside)}
+
+
+# ---------------------------------------------------------------- CPU legs
+
+def cpu_units(O, wl, n_units, seed=7):
+    """n_units independent (sequence, layer) units for the reference CPU
+    code: fp32 caches holding bf16-rounded N(0,1) values (the reference
+    only has fp32 caches), at the workload's positions.  At most 32 distinct
+    cache arrays are allocated; further units reuse them."""
+    pos = positions(wl)
+    n_distinct = min(n_units, 32)
+    caches = []
+    for u in range(n_distinct):
+        p = int(pos[u % len(pos)])
+        gen = O.normal_bf16 if wl["dtype"] == "bf16" else O.normal
+        k = gen(O.derive_seed(seed, u, 0, 4), (p + 1) * KD).reshape(p + 1, KD)
+        v = gen(O.derive_seed(seed, u, 0, 5), (p + 1) * KD).reshape(p + 1, KD)
+        caches.append((k, v, p))
+    ks = [caches[u % n_distinct][0] for u in range(n_units)]
+    vs = [caches[u % n_distinct][1] for u in range(n_units)]
+    ps = np.array([caches[u % n_distinct][2] for u in range(n_units)], np.int32)
+    q = np.stack([O.normal(O.derive_seed(seed, u, 0, 1), QD) for u in range(n_units)])
+    return q, ks, vs, ps
+
+
+def unit_bytes(wl, ps):
+    s_kv = 2 if wl["dtype"] == "bf16" else 4
+    return int(np.sum((ps.astype(np.int64) + 1) * 2 * KD * s_kv + 2 * QD * 4))
+
+
+def time_reference_cpu(O, wl, n_units, n_threads, reps=1):
+    q, ks, vs, ps = cpu_units(O, wl, n_units)
+    best = None
+    for _ in range(reps):
+        t = time.perf_counter()
+        O.ref_attention_units_mt(q, ks, vs, ps, n_threads)
+        dt = time.perf_counter() - t
+        best = dt if best is None else min(best, dt)
+    return unit_bytes(wl, ps) / best / 1e9, best, int(np.sum(ps + 1))
+
+
+def run_reference_arm(args, wl, rank, world):
+    """--impl reference: the reference's CPU implementation of the path,
+    all host threads, bounded sample per step (rank 0 only)."""
+    if rank != 0:
+        return
+    O = load_oracle()
+    kind = "reference" if O.ref_available() else "port"
+    if kind == "port":
+        run = lambda q, ks, vs, ps, nt: O.attention_units_mt(q, ks, vs, ps, nt)
+    else:
+        run = lambda q, ks, vs, ps, nt: O.ref_attention_units_mt(q, ks, vs, ps, nt)
+    threads = os.cpu_count() or 1
+    total_units = wl["B"] * wl["layers"]
+    # whole layers of the batch, enough units to keep every thread busy
+    n_units = min(total_units, max(wl["B"], (threads // wl["B"]) * wl["B"]))
+    q, ks, vs, ps = cpu_units(O, wl, n_units)
+    for _ in range(args.warmup):
+        run(q, ks, vs, ps, threads)
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        run(q, ks, vs, ps, threads)
+    dt = time.perf_counter() - t
+    gbs = unit_bytes(wl, ps) * args.steps / dt / 1e9
+    sample = (f"{n_units} of the {total_units} (sequence, layer) units of one step per "
+              f"timed step ({n_units // wl['B']} layer(s) x {wl['B']} sequences), fp32 "
+              f"caches of the workload's values, {threads} threads")
+    line = {
+        "metric": "decode-attn achieved HBM GB/s (algorithmic bytes / time)",
+        "value": gbs, "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong" if wl["split"] else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (splitmix64 + Box-Muller N(0,1))",
+        "config": {"workload": wl["desc"], "cpu_sample": sample},
+        "seq_steps_per_s": n_units / wl["layers"] * args.steps / dt,
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="tg", choices=["tg", "reference"])
+    ap.add_argument("--workload", default="longctx", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference_arm(args, wl, rank, world)
+    if args.warmup < 3:
+        args.warmup = 3
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    tg = load_package()
+    be = tg.CudaBackend(local)
+    split = wl["split"] and world > 1
+    if split:
+        uid = [tg.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        be.comm_init(uid[0], rank, world, timeout_ms=120000)
+
+    B, L = wl["B"], wl["layers"]
+    pos = positions(wl)
+    if wl["split"]:
+        shard_start, shard_len = tg.shard_range(wl["ctx"], world, rank)
+        gctx = wl["ctx"]
+    else:
+        shard_start, shard_len, gctx = 0, wl["ctx"], wl["ctx"]
+    dtype = tg.DTYPE_BF16 if wl["dtype"] == "bf16" else tg.DTYPE_F32
+    kv = tg.KVCache(be, L, B, max(shard_len, 1), dtype=dtype, shard_start=shard_start,
+                    global_ctx=gctx)
+    kv.fill_normal(0x5EED0000 + 7919 * rank)
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1000 + (0 if wl["split"] else rank))
+    q = torch.randn(L, B, QD, device="cuda", generator=g)
+    kn = torch.randn(L, B, KD, device="cuda", generator=g)
+    vn = torch.randn(L, B, KD, device="cuda", generator=g)
+    out = torch.zeros(L, B, QD, device="cuda")
+    pos_d = torch.from_numpy(pos).cuda()
+    stream = torch.cuda.ExternalStream(be.stream())
+
+    def step(qs, ks, vs, ps, os_):
+        for l in range(L):
+            if split:
+                kv.decode_layer_splitkv(l, qs[l], ks[l], vs[l], ps, os_[l])
+            else:
+                kv.decode_layer(l, qs[l], ks[l], vs[l], ps, os_[l])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timed region -----------------------------------
+    for _ in range(args.warmup):
+        step(q, kn, vn, pos_d, out)
+    be.synchronize()
+    sampler = ClockSampler(set(range(world))) if local == 0 else None
+    time.sleep(0.3 if sampler else 0)
+    barrier()
+    launches0 = be.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step(q, kn, vn, pos_d, out)
+    e1.record(stream)
+    be.synchronize()
+    t_wall1 = time.time()
+    launches = be.launch_count() - launches0
+    barrier()
+    ms_total = max_over_ranks(e0.elapsed_time(e1))
+    clocks = sampler.stop(t_wall0, t_wall1) if sampler else None
+    ms_step = ms_total / args.steps
+    bytes_step = algo_bytes_step(wl, pos) * (1 if wl["split"] else world)
+    seqs_step = B * (1 if wl["split"] else world)
+    value = bytes_step / (ms_step * 1e-3) / 1e9
+
+    # ---- roofline: decode-kernel launches timed with CUDA events -----------
+    be.profile_enable(True)
+    for _ in range(max(3, min(args.steps, 50))):
+        step(q, kn, vn, pos_d, out)
+    kms, kn_launch = be.profile_read()
+    be.profile_enable(False)
+    k_bytes = kernel_bytes_launch(wl, pos, shard_start, shard_len, split)
+    k_avg_ms = kms / max(kn_launch, 1)
+    hbm_peak, peak_kind = peaks()
+    achieved = k_bytes / (k_avg_ms * 1e-3) / 1e9
+    achieved_min = max_over_ranks(-achieved)  # slowest rank's kernel
+    achieved = -achieved_min if world > 1 else achieved
+
+    # ---- end to end through the C ABI with pinned host buffers ---------------
+    qh = torch.randn(L, B, QD).pin_memory()
+    kh = torch.randn(L, B, KD).pin_memory()
+    vh = torch.randn(L, B, KD).pin_memory()
+    oh = torch.zeros(L, B, QD).pin_memory()
+    ph = torch.from_numpy(pos.copy()).pin_memory()
+
+    def e2e_step():
+        be.metal_batch_begin()
+        step(qh, kh, vh, ph, oh)
+        be.metal_batch_end()
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    e2e_steps = max(3, args.steps // 2)
+    t = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_s = max_over_ranks(time.perf_counter() - t)
+    e2e_value = bytes_step * e2e_steps / e2e_s / 1e9
+    h2d = L * B * (QD + 2 * KD) * 4 + L * B * 4
+    d2h = L * B * (2 * QD + KD) * 4
+
+    # ---- CPU baseline (rank 0, one GPU only) -------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        O = load_oracle()
+        if O.ref_available():
+            n_units = 2 if wl["ctx"] > 8192 else 24
+            gbs, dt, npos = time_reference_cpu(O, wl, n_units, 1)
+            cpu = {"value": gbs, "unit": "GB/s", "cores": 1, "kind": "reference",
+                   "sample": f"{n_units} (sequence, layer) units at the workload's positions "
+                             f"({npos} cache rows, {dt:.2f} s), reference code single-threaded "
+                             "as it runs; fp32 caches of bf16-rounded values, bytes counted as "
+                             "the workload's"}
+
+    if rank == 0:
+        line = {
+            "metric": "decode-attn achieved HBM GB/s (algorithmic bytes / time)",
+            "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong" if wl["split"] else "weak", "vs_baseline": None,
+            "dtype": wl["dtype"], "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": wl["desc"], "batch": B, "context": wl["ctx"],
+                       "layers_per_step": L, "n_head": N_HEAD, "n_kv_head": N_KV,
+                       "head_dim": HD, "parallelism": f"split-kv x{world}" if wl["split"]
+                       else f"sequence-partitioned x{world}",
+                       "l2": "inputs larger than L2: %.0f MB of KV per GPU per step"
+                             % (algo_bytes_step(wl, pos) / max(world if wl["split"] else 1, 1) / 1e6)},
+            "seq_steps_per_s": seqs_step / (ms_step * 1e-3),
+            "hbm_frac_of_measured": value / (hbm_peak * world),
+            "gpu_launches": launches,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak,
+                         "unit": "GB/s", "frac": achieved / hbm_peak,
+                         "peak_kind": peak_kind, "kernel": "decode_mma_kernel"
+                         if kv.uses_tensor_cores() else "decode_generic_kernel",
+                         "bytes_per_launch": k_bytes, "launch_ms": k_avg_ms,
+                         "traffic": None},
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    kv.destroy()
+    if split:
+        be.comm_destroy()
+    be.shutdown()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,248 @@
+/*
+ * tg_cuda_backend.h -- C ABI of the B200 (sm_100a) decode-attention backend.
+ *
+ * Drop-in for the attention hot path of tmac_gguf.cpp: the reference's
+ * forward loop (tmac_gguf.cpp:1490-1496, :1562-1568) drives RoPE, the KV
+ * cache-write and GQA decode attention through metal_backend::{rope_op,
+ * elem_op, attention_op, metal_batch_begin, metal_batch_end}; each of those
+ * has an entry point here with the same argument order and meaning.  On top
+ * of that surface the library adds what the reference does not have:
+ * device-resident KV caches, batched variable-length decode, bf16 caches
+ * and split-KV decode across GPUs.
+ *
+ * Conventions
+ *  - Every function returns an int status: TG_OK (0) or a TG_ERR_* code;
+ *    tg_last_error() gives a message for the calling thread.  (The reference
+ *    dispatch helpers return void and report nothing.)
+ *  - A tg_context binds one CUDA device and one stream.  It is not
+ *    thread-safe: use one context per host thread.
+ *  - Pointers may be CUDA device (or managed) pointers, used in place, or
+ *    host pointers, which the library stages through device memory.  For
+ *    the reference-compatible ops (tg_rope_op, tg_elem_op, tg_attention_op)
+ *    host arrays get persistent device mirrors, like the reference's buffer
+ *    wrapper cache (metal_backend.hpp:44-65); results in host arrays are
+ *    valid after tg_batch_end (or on return when no batch is open), exactly
+ *    when Metal results are valid after metal_batch_end.
+ *  - Shapes: head_dim even and <= 128, n_head a multiple of n_kv_head,
+ *    n_head*head_dim <= 4096.  The tensor-core path serves bf16 caches with
+ *    head_dim 64, n_kv_head in {1,2,4} and n_head/n_kv_head <= 8 (Qwen2-0.5B:
+ *    14 / 2 / 64); other shapes run on the CUDA-core kernel.
+ */
+#ifndef TG_CUDA_BACKEND_H
+#define TG_CUDA_BACKEND_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TG_API __attribute__((visibility("default")))
+#else
+#define TG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+#define TG_OK 0
+#define TG_ERR_INVALID_ARG 1   /* bad shape, null pointer, out-of-range pos */
+#define TG_ERR_CUDA 2          /* a CUDA runtime call failed */
+#define TG_ERR_NO_DEVICE 3
+#define TG_ERR_OUT_OF_MEMORY 4
+#define TG_ERR_UNSUPPORTED 5   /* e.g. elem_op op 1 (SiLU*up): not this path */
+#define TG_ERR_DEVICE 6        /* a kernel reported an error (bad position,
+                                  a bounded wait expired) */
+#define TG_ERR_COMM 7          /* NCCL unavailable or failed */
+#define TG_ERR_STATE 8         /* call order (batch_end without begin, ...) */
+
+/* KV cache element types */
+#define TG_DTYPE_F32 0
+#define TG_DTYPE_BF16 1
+
+/* tg_register_host flags */
+#define TG_REGION_MIRROR 0        /* host copy is authoritative */
+#define TG_REGION_DEVICE_OWNED 1  /* device copy is authoritative */
+
+typedef struct tg_context tg_context;
+typedef struct tg_kv_cache tg_kv_cache;
+
+TG_API const char* tg_status_string(int status);
+/* Message of the last failing call on this thread ("" if none). */
+TG_API const char* tg_last_error(void);
+/* Library version string. */
+TG_API const char* tg_version(void);
+
+/* ------------------------------------------------------ context / batches */
+
+/* metal_backend::init (metal_backend.hpp:519, metal_backend.cpp:21-89).
+ * Binds `device`, creates a stream and the device error word. */
+TG_API int tg_init(int device, tg_context** out_ctx);
+/* metal_backend::shutdown (metal_backend.hpp:520).  Synchronises, frees
+ * everything the context owns. */
+TG_API int tg_shutdown(tg_context* ctx);
+/* Use an existing cudaStream_t (e.g. a framework's stream) for all work. */
+TG_API int tg_set_stream(tg_context* ctx, void* cuda_stream);
+TG_API int tg_get_stream(tg_context* ctx, void** cuda_stream);
+/* Number of SMs of the bound device. */
+TG_API int tg_device_sms(tg_context* ctx, int* out_sms);
+
+/* metal_batch_begin (metal_backend.hpp:114-122): subsequent ops are queued
+ * on the context stream and host-array results are deferred. */
+TG_API int tg_batch_begin(tg_context* ctx);
+/* metal_batch_end (metal_backend.hpp:176-191): copies back host arrays the
+ * batch wrote, waits for the stream and reports device errors. */
+TG_API int tg_batch_end(tg_context* ctx);
+/* Wait for the stream and report device errors (no batch semantics). */
+TG_API int tg_synchronize(tg_context* ctx);
+
+/* Device mirror of a host array, the explicit form of wrap_buffer
+ * (metal_backend.hpp:52-65).  TG_REGION_DEVICE_OWNED marks arrays only GPU
+ * ops write, such as the reference's g_k_cache / g_v_cache
+ * (tmac_gguf.cpp:200-201) in the fused path: they are uploaded once here
+ * and never copied automatically again. */
+TG_API int tg_register_host(tg_context* ctx, void* host_ptr, size_t bytes, int flags);
+TG_API int tg_unregister_host(tg_context* ctx, void* host_ptr);
+/* Copy [host_ptr, host_ptr+bytes) of a registered array device -> host
+ * (or host -> device with to_device = 1). */
+TG_API int tg_region_sync(tg_context* ctx, void* host_ptr, size_t bytes, int to_device);
+
+/* ------------------------------------------- reference-compatible ops */
+
+/* rope_op (metal_backend.hpp:381-396; kernel_rope.metal:5-22; CPU
+ * apply_rope tmac_gguf.cpp:990-1016): rotate adjacent pairs of n_heads
+ * heads of `data` in place at position pos.  Results are bit-identical to
+ * the reference CPU code (host-libm cos/sin table, one rounding per
+ * product and sum). */
+TG_API int tg_rope_op(tg_context* ctx, float* data, int n_heads, int head_dim,
+               int pos, float base);
+
+/* elem_op (metal_backend.hpp:354-379; kernel_elem.metal:6-21) for op 0
+ * (data += aux) and op 2 (data = aux, the cache-write of
+ * tmac_gguf.cpp:1492-1493).  op 1 (SiLU x up, FFN) is not on this path and
+ * returns TG_ERR_UNSUPPORTED. */
+TG_API int tg_elem_op(tg_context* ctx, int op, float* data, const float* aux, int dim);
+
+/* attention_op (metal_backend.hpp:413-453; kernels kernel_flash_attn.metal /
+ * kernel_attn.metal; CPU tmac_gguf.cpp:1093-1128): one query token, n_head
+ * query heads over n_kv_head KV heads, fp32 K/V caches laid out
+ * [pos][n_kv_head*head_dim] from the layer base, attending rows
+ * 0..past_len.  output[h*head_dim + d]. */
+TG_API int tg_attention_op(tg_context* ctx, const float* Q, const float* K_cache,
+                    const float* V_cache, float* output, int n_head,
+                    int n_kv_head, int head_dim, int past_len);
+
+/* ------------------------------------------------- device KV caches */
+
+/* A device-resident cache replacing the static g_k_cache / g_v_cache
+ * (tmac_gguf.cpp:200-201), for n_seqs sequences: K and V are each laid out
+ * [n_layers][n_seqs][max_ctx][n_kv_head*head_dim] of `dtype`.  The cache
+ * holds global positions [shard_start, shard_start + max_ctx) (shard_start
+ * 0 for a whole cache; > 0 for one GPU's shard in split-KV decode).
+ * Zero-initialised. */
+typedef struct tg_kv_desc {
+  int n_layers, n_seqs, max_ctx, n_head, n_kv_head, head_dim, dtype;
+  int shard_start;
+  int global_ctx;  /* positions over all shards; 0 means shard_start+max_ctx.
+                      RoPE accepts positions 0..global_ctx-1. */
+  float rope_base; /* RoPE base for this model (1e6 for Qwen2) */
+} tg_kv_desc;
+
+TG_API int tg_kv_create(tg_context* ctx, const tg_kv_desc* desc, tg_kv_cache** out);
+/* Destroy before tg_shutdown of its context; tg_shutdown frees caches that
+ * are still alive, after which their handles must not be used. */
+TG_API int tg_kv_destroy(tg_kv_cache* kv);
+/* reset_cache (tmac_gguf.cpp:1430-1434): zero both caches. */
+TG_API int tg_kv_reset(tg_kv_cache* kv);
+/* Device pointers to layer `layer` of K and V ([n_seqs][max_ctx][row]). */
+TG_API int tg_kv_layer_ptrs(tg_kv_cache* kv, int layer, void** k, void** v);
+/* Fill K and V with synthetic N(0,1) values rounded to the cache type. */
+TG_API int tg_kv_fill_normal(tg_kv_cache* kv, uint64_t seed);
+/* Write n_rows fp32 rows (host or device) at local rows row0.. of one
+ * sequence/layer, converted to the cache type (RNE for bf16). */
+TG_API int tg_kv_write_rows(tg_kv_cache* kv, int layer, int seq, int row0,
+                     int n_rows, const float* k_rows, const float* v_rows);
+/* Read n_rows raw rows (cache type) into host or device memory. */
+TG_API int tg_kv_read_rows(tg_kv_cache* kv, int layer, int seq, int row0,
+                    int n_rows, void* k_out, void* v_out);
+
+/* ------------------------------------------------- batched decode */
+
+/* RoPE + cache-write for n_seqs sequences (tmac_gguf.cpp:1087-1091; the
+ * rope_op x2 + elem_op(2) x2 of :1490-1493 fused into one launch).
+ * q [n_seqs][n_head*head_dim] and k_new [n_seqs][n_kv*head_dim] are rotated
+ * in place; the rotated k row and v_new are written at each sequence's
+ * position pos[s] (global) when this cache holds it. */
+TG_API int tg_rope_cache_write(tg_context* ctx, tg_kv_cache* kv, int layer,
+                        int n_seqs, float* q, float* k_new,
+                        const float* v_new, const int32_t* pos);
+
+/* Decode attention for n_seqs sequences of one layer: sequence s attends
+ * rows 0..past_len[s] of its cache (tmac_gguf.cpp:1093-1128 per sequence).
+ * q: [n_seqs][n_head*head_dim] (rotated), out: same shape. */
+TG_API int tg_attention_batched(tg_context* ctx, tg_kv_cache* kv, int layer,
+                         int n_seqs, const float* q, const int32_t* past_len,
+                         float* out);
+
+/* The whole per-layer decode step: tg_rope_cache_write then
+ * tg_attention_batched with past_len = pos. */
+TG_API int tg_decode_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs,
+                    float* q, float* k_new, const float* v_new,
+                    const int32_t* pos, float* out);
+
+/* ------------------------------------------------- split-KV across GPUs */
+
+/* NCCL unique id (128 bytes) for tg_comm_init; call on one rank and share
+ * it out of band. */
+TG_API int tg_comm_unique_id(void* id_out, size_t id_bytes);
+/* Join a world of `world` ranks (one per GPU).  timeout_ms bounds the
+ * initialisation and every later collective wait on this context. */
+TG_API int tg_comm_init(tg_context* ctx, const void* id, int rank, int world,
+                 int timeout_ms);
+TG_API int tg_comm_destroy(tg_context* ctx);
+
+/* Split-KV (flash-decoding) step across the world: each rank holds a shard
+ * of every sequence's positions (its kv cache's [shard_start,
+ * shard_start+max_ctx)), computes the softmax partials of its shard, the
+ * ranks all-gather them over NCCL and every rank merges the same result
+ * into out.  Inputs and outputs are replicated on all ranks. */
+TG_API int tg_attention_splitkv(tg_context* ctx, tg_kv_cache* shard, int layer,
+                         int n_seqs, const float* q, const int32_t* past_len,
+                         float* out);
+
+/* The two halves of tg_attention_splitkv, for callers that move the
+ * partials themselves.  tg_attention_records writes, per sequence, the
+ * softmax record of this cache's shard: records[s] = { o[n_head][head_dim]
+ * (un-normalised), m[n_head] (running max, log2 units), l[n_head] } --
+ * n_head*(head_dim+2) floats.  tg_merge_records combines n_parts such
+ * record arrays, laid out [n_parts][n_seqs][record], into out. */
+TG_API int tg_attention_records(tg_context* ctx, tg_kv_cache* shard, int layer,
+                                int n_seqs, const float* q,
+                                const int32_t* past_len, float* records);
+TG_API int tg_merge_records(tg_context* ctx, int n_parts, int n_seqs,
+                            int n_head, int head_dim, const float* records,
+                            float* out);
+
+/* RoPE + owner cache-write + split-KV attention, one layer. */
+TG_API int tg_decode_layer_splitkv(tg_context* ctx, tg_kv_cache* shard, int layer,
+                            int n_seqs, float* q, float* k_new,
+                            const float* v_new, const int32_t* pos,
+                            float* out);
+
+/* ------------------------------------------------- introspection */
+
+/* Kernel launches this context has issued since creation (all kinds). */
+TG_API int tg_launch_count(tg_context* ctx, long long* out);
+/* CUDA-event timing of every decode-attention kernel launch on the context
+ * stream (events recorded just before and after each launch).  Enabling
+ * resets the record; tg_profile_read waits for the stream and returns the
+ * summed kernel time and the number of timed launches since the last read. */
+TG_API int tg_profile_enable(tg_context* ctx, int on);
+TG_API int tg_profile_read(tg_context* ctx, double* total_ms, long long* launches);
+/* 1 if the next batched decode on `kv` uses the tensor-core kernel. */
+TG_API int tg_kv_uses_tensor_cores(tg_kv_cache* kv, int* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TG_CUDA_BACKEND_H */

@@ -1,0 +1,1350 @@
+// tg_backend.cu -- host side of the C ABI declared in include/tg_cuda_backend.h.
+//
+// Replaces the dispatch layer of the reference's Metal backend for the
+// attention hot path (metal_backend.hpp:114-191 batches, :354-453 elem /
+// rope / attention ops, metal_backend.cpp:21-89 init).  One tg_context per
+// device and host thread: a CUDA stream, a device error word, scratch for
+// split-KV partial records, RoPE cos/sin tables built with the host libm,
+// device mirrors of host arrays for the reference-compatible ops, and an
+// optional NCCL communicator (loaded with dlopen) for split-KV decode.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/tg_cuda_backend.h"
+#include "tg_kernels.h"
+#include "tg_shared.h"
+
+#define TG_VERSION "tmac_gguf.cpp_b200 0.1.0"
+
+namespace {
+
+thread_local std::string t_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_err = buf;
+  return code;
+}
+
+#define TG_CUDA(call)                                                        \
+  do {                                                                       \
+    cudaError_t e_ = (call);                                                 \
+    if (e_ != cudaSuccess)                                                   \
+      return fail(e_ == cudaErrorMemoryAllocation ? TG_ERR_OUT_OF_MEMORY     \
+                                                  : TG_ERR_CUDA,             \
+                  "%s failed: %s", #call, cudaGetErrorString(e_));           \
+  } while (0)
+
+#define TG_TRY(expr)          \
+  do {                        \
+    int rc_ = (expr);         \
+    if (rc_ != TG_OK) return rc_; \
+  } while (0)
+
+// ------------------------------------------------------------ NCCL (dlopen)
+
+struct NcclApi {
+  void* lib = nullptr;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int,
+                                     ncclConfig_t*) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t,
+                            ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+
+NcclApi& nccl() {
+  static NcclApi api;
+  static bool tried = false;
+  if (tried) return api;
+  tried = true;
+  // Reuse the NCCL a host framework already loaded (same soname), else the
+  // system one.
+  const char* names[] = {"libnccl.so.2", "libnccl.so"};
+  for (const char* n : names) {
+    api.lib = dlopen(n, RTLD_NOW | RTLD_GLOBAL);
+    if (api.lib) break;
+  }
+  if (!api.lib) return api;
+  auto sym = [&](const char* s) { return dlsym(api.lib, s); };
+  api.GetUniqueId = (decltype(api.GetUniqueId))sym("ncclGetUniqueId");
+  api.CommInitRankConfig = (decltype(api.CommInitRankConfig))sym("ncclCommInitRankConfig");
+  api.AllGather = (decltype(api.AllGather))sym("ncclAllGather");
+  api.CommDestroy = (decltype(api.CommDestroy))sym("ncclCommDestroy");
+  api.CommAbort = (decltype(api.CommAbort))sym("ncclCommAbort");
+  api.CommGetAsyncError = (decltype(api.CommGetAsyncError))sym("ncclCommGetAsyncError");
+  api.GetErrorString = (decltype(api.GetErrorString))sym("ncclGetErrorString");
+  api.ok = api.GetUniqueId && api.CommInitRankConfig && api.AllGather &&
+           api.CommDestroy && api.CommAbort && api.CommGetAsyncError &&
+           api.GetErrorString;
+  return api;
+}
+
+// ------------------------------------------------------------ TMA encode
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+}  // namespace
+
+// ================================================================ context
+
+struct RopeTable {
+  uint32_t base_bits = 0;
+  int head_dim = 0;
+  int len = 0;
+  float* d = nullptr;  // [len][head_dim/2][cos, sin]
+};
+
+struct Region {
+  char* host = nullptr;
+  size_t bytes = 0;
+  char* dev = nullptr;
+  int flags = TG_REGION_MIRROR;
+  bool fresh = false;   // device copy current for this batch
+  size_t dirty_lo = 0, dirty_hi = 0;  // byte range written by device ops
+};
+
+struct PendingCopy {
+  void* host;
+  const void* dev;
+  size_t bytes;
+};
+
+struct tg_context {
+  int device = 0;
+  int num_sms = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  int* d_err = nullptr;
+
+  float* part = nullptr;     size_t part_cap = 0;    // floats
+  int* sched = nullptr;      size_t sched_cap = 0;   // ints
+  float* records = nullptr;  size_t rec_cap = 0;     // floats
+  float* recv = nullptr;     size_t recv_cap = 0;    // floats
+
+  char* arena = nullptr;     size_t arena_cap = 0, arena_off = 0;
+  std::vector<PendingCopy> pending;  // device -> host copies of staged outputs
+  std::vector<void*> graveyard;      // device buffers freed at the next sync
+
+  std::vector<RopeTable> tables;
+  std::map<uintptr_t, Region> regions;
+  bool in_batch = false;
+  long long launches = 0;
+
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1;
+  int timeout_ms = 60000;
+
+  std::vector<tg_kv_cache*> caches;  // freed by tg_shutdown if still alive
+
+  // Optional CUDA-event timing of each decode-attention kernel launch.
+  bool prof_on = false;
+  std::vector<cudaEvent_t> prof_ev;  // start/stop pairs
+  size_t prof_used = 0;              // events recorded since the last read
+};
+
+struct tg_kv_cache {
+  tg_context* ctx = nullptr;
+  tg_kv_desc d{};
+  size_t row_elems = 0, esize = 0, layer_elems = 0;
+  void* k = nullptr;
+  void* v = nullptr;
+  bool tmap_ok = false;
+  alignas(64) CUtensorMap tmk;
+  alignas(64) CUtensorMap tmv;
+  int global_ctx = 0;
+};
+
+namespace {
+
+int set_device(tg_context* ctx) {
+  if (!ctx) return fail(TG_ERR_INVALID_ARG, "null context");
+  TG_CUDA(cudaSetDevice(ctx->device));
+  return TG_OK;
+}
+
+// Device-accessible without staging (device or managed memory).
+bool is_device_ptr(const void* p) {
+  if (!p) return false;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+void free_graveyard(tg_context* ctx) {
+  for (void* p : ctx->graveyard) cudaFree(p);
+  ctx->graveyard.clear();
+}
+
+template <typename T>
+int ensure_buf(tg_context* ctx, T** buf, size_t* cap, size_t need) {
+  if (need <= *cap) return TG_OK;
+  size_t n = need < 1024 ? 1024 : need;
+  n = n + n / 4;
+  T* nb = nullptr;
+  TG_CUDA(cudaMalloc(&nb, n * sizeof(T)));
+  if (*buf) ctx->graveyard.push_back(*buf);
+  *buf = nb;
+  *cap = n;
+  return TG_OK;
+}
+
+// Reads and clears the device error word (stream must be idle).
+int check_device_error(tg_context* ctx) {
+  int h = 0;
+  TG_CUDA(cudaMemcpy(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (h != 0) {
+    TG_CUDA(cudaMemset(ctx->d_err, 0, sizeof(int)));
+    const char* what = h == tg::kDevErrBadPos      ? "position outside the cache / RoPE table"
+                       : h == tg::kDevErrWaitFull  ? "bounded wait for a K/V tile expired"
+                       : h == tg::kDevErrWaitEmpty ? "bounded wait for a free stage expired"
+                                                   : "device error";
+    return fail(TG_ERR_DEVICE, "kernel reported 0x%x: %s", h, what);
+  }
+  return TG_OK;
+}
+
+// Waits for the stream; with a communicator, polls NCCL's async error and
+// aborts the communicator once the timeout passes.
+int wait_stream(tg_context* ctx) {
+  if (!ctx->comm) {
+    TG_CUDA(cudaStreamSynchronize(ctx->stream));
+    return TG_OK;
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t q = cudaStreamQuery(ctx->stream);
+    if (q == cudaSuccess) return TG_OK;
+    if (q != cudaErrorNotReady)
+      return fail(TG_ERR_CUDA, "stream failed: %s", cudaGetErrorString(q));
+    ncclResult_t ae = ncclSuccess;
+    nccl().CommGetAsyncError(ctx->comm, &ae);
+    const double ms = std::chrono::duration<double, std::milli>(
+                          std::chrono::steady_clock::now() - t0)
+                          .count();
+    if ((ae != ncclSuccess && ae != ncclInProgress) || ms > ctx->timeout_ms) {
+      nccl().CommAbort(ctx->comm);
+      ctx->comm = nullptr;
+      ctx->world = 1;
+      return fail(TG_ERR_COMM, "collective did not complete (%s, %.0f ms); communicator aborted",
+                  ae != ncclSuccess ? nccl().GetErrorString(ae) : "timeout", ms);
+    }
+  }
+}
+
+// ------------------------------------------------ staging for host pointers
+
+int arena_alloc(tg_context* ctx, size_t bytes, void** out) {
+  bytes = (bytes + 255) & ~size_t(255);
+  if (ctx->arena_off + bytes > ctx->arena_cap) {
+    size_t n = ctx->arena_cap * 2;
+    if (n < bytes * 2) n = bytes * 2;
+    if (n < (size_t(1) << 20)) n = size_t(1) << 20;
+    char* na = nullptr;
+    TG_CUDA(cudaMalloc(&na, n));
+    if (ctx->arena) ctx->graveyard.push_back(ctx->arena);
+    ctx->arena = na;
+    ctx->arena_cap = n;
+    ctx->arena_off = 0;
+  }
+  *out = ctx->arena + ctx->arena_off;
+  ctx->arena_off += bytes;
+  return TG_OK;
+}
+
+int stage_in(tg_context* ctx, const void* p, size_t bytes, const void** dev) {
+  if (!p || bytes == 0 || is_device_ptr(p)) {
+    *dev = p;
+    return TG_OK;
+  }
+  void* d = nullptr;
+  TG_TRY(arena_alloc(ctx, bytes, &d));
+  TG_CUDA(cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  *dev = d;
+  return TG_OK;
+}
+
+// Output (copy_in = false) or in/out (copy_in = true) buffer.
+int stage_out(tg_context* ctx, void* p, size_t bytes, bool copy_in, void** dev) {
+  if (!p || bytes == 0 || is_device_ptr(p)) {
+    *dev = p;
+    return TG_OK;
+  }
+  void* d = nullptr;
+  TG_TRY(arena_alloc(ctx, bytes, &d));
+  if (copy_in) TG_CUDA(cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  ctx->pending.push_back({p, d, bytes});
+  *dev = d;
+  return TG_OK;
+}
+
+// Issues the device->host copies of staged outputs; outside a batch also
+// waits and recycles the staging arena.
+int finish_call(tg_context* ctx) {
+  for (const PendingCopy& c : ctx->pending)
+    TG_CUDA(cudaMemcpyAsync(c.host, c.dev, c.bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  ctx->pending.clear();
+  if (ctx->in_batch) return TG_OK;
+  TG_TRY(wait_stream(ctx));
+  ctx->arena_off = 0;
+  free_graveyard(ctx);
+  return check_device_error(ctx);
+}
+
+// ------------------------------------------------ host-array mirrors
+
+Region* find_region(tg_context* ctx, const char* p, size_t bytes) {
+  auto it = ctx->regions.upper_bound(reinterpret_cast<uintptr_t>(p));
+  if (it == ctx->regions.begin()) return nullptr;
+  --it;
+  Region& r = it->second;
+  if (r.host <= p && p + bytes <= r.host + r.bytes) return &r;
+  return nullptr;
+}
+
+int make_fresh(tg_context* ctx, Region& r) {
+  if (r.fresh || (r.flags & TG_REGION_DEVICE_OWNED) || r.dirty_hi > r.dirty_lo)
+    return TG_OK;
+  TG_CUDA(cudaMemcpyAsync(r.dev, r.host, r.bytes, cudaMemcpyHostToDevice, ctx->stream));
+  r.fresh = true;
+  return TG_OK;
+}
+
+// Creates a mirror for [p, p+bytes), absorbing any mirrors it overlaps: the
+// new device copy starts as the host contents, then every absorbed mirror
+// whose device copy is newer (written or device-owned) is copied over it.
+int create_region(tg_context* ctx, char* p, size_t bytes, int flags, Region** out) {
+  char* lo = p;
+  char* hi = p + bytes;
+  std::vector<uintptr_t> absorbed;
+  for (auto& kv : ctx->regions) {
+    Region& r = kv.second;
+    if (r.host < hi && p < r.host + r.bytes) {
+      absorbed.push_back(kv.first);
+      if (r.host < lo) lo = r.host;
+      if (r.host + r.bytes > hi) hi = r.host + r.bytes;
+      flags |= r.flags;
+    }
+  }
+  Region nr;
+  nr.host = lo;
+  nr.bytes = (size_t)(hi - lo);
+  nr.flags = flags;
+  TG_CUDA(cudaMalloc(&nr.dev, nr.bytes));
+  TG_CUDA(cudaMemcpyAsync(nr.dev, nr.host, nr.bytes, cudaMemcpyHostToDevice, ctx->stream));
+  nr.fresh = true;
+  for (uintptr_t key : absorbed) {
+    Region& r = ctx->regions[key];
+    const bool dev_newer = (r.flags & TG_REGION_DEVICE_OWNED) || r.dirty_hi > r.dirty_lo;
+    if (dev_newer)
+      TG_CUDA(cudaMemcpyAsync(nr.dev + (r.host - nr.host), r.dev, r.bytes,
+                              cudaMemcpyDeviceToDevice, ctx->stream));
+    if (r.dirty_hi > r.dirty_lo) {
+      const size_t a = (size_t)(r.host - nr.host) + r.dirty_lo;
+      const size_t b = (size_t)(r.host - nr.host) + r.dirty_hi;
+      if (nr.dirty_hi <= nr.dirty_lo) {
+        nr.dirty_lo = a;
+        nr.dirty_hi = b;
+      } else {
+        if (a < nr.dirty_lo) nr.dirty_lo = a;
+        if (b > nr.dirty_hi) nr.dirty_hi = b;
+      }
+    }
+    ctx->graveyard.push_back(r.dev);
+    ctx->regions.erase(key);
+  }
+  auto res = ctx->regions.emplace(reinterpret_cast<uintptr_t>(nr.host), nr);
+  *out = &res.first->second;
+  return TG_OK;
+}
+
+// Creates the mirror of a host range if none covers it yet.  Compat ops
+// call this for every argument before resolving any, so that a merge of
+// overlapping mirrors cannot move an address that was already handed out.
+int ensure_region(tg_context* ctx, const void* p, size_t bytes) {
+  if (!p) return fail(TG_ERR_INVALID_ARG, "null pointer argument");
+  if (is_device_ptr(p)) return TG_OK;
+  char* hp = const_cast<char*>(static_cast<const char*>(p));
+  if (find_region(ctx, hp, bytes)) return TG_OK;
+  Region* r = nullptr;
+  return create_region(ctx, hp, bytes, TG_REGION_MIRROR, &r);
+}
+
+// Device address for a compat-op argument.  write: the op writes the range.
+int resolve(tg_context* ctx, const void* p, size_t bytes, bool write, char** dev) {
+  if (!p) return fail(TG_ERR_INVALID_ARG, "null pointer argument");
+  if (is_device_ptr(p)) {
+    *dev = const_cast<char*>(static_cast<const char*>(p));
+    return TG_OK;
+  }
+  char* hp = const_cast<char*>(static_cast<const char*>(p));
+  Region* r = find_region(ctx, hp, bytes);
+  if (!r) TG_TRY(create_region(ctx, hp, bytes, TG_REGION_MIRROR, &r));
+  TG_TRY(make_fresh(ctx, *r));
+  const size_t off = (size_t)(hp - r->host);
+  if (write && !(r->flags & TG_REGION_DEVICE_OWNED)) {
+    if (r->dirty_hi <= r->dirty_lo) {
+      r->dirty_lo = off;
+      r->dirty_hi = off + bytes;
+    } else {
+      if (off < r->dirty_lo) r->dirty_lo = off;
+      if (off + bytes > r->dirty_hi) r->dirty_hi = off + bytes;
+    }
+  }
+  *dev = r->dev + off;
+  return TG_OK;
+}
+
+// metal_batch_end analogue for mirrors: copy back written ranges.
+int flush_regions(tg_context* ctx) {
+  for (auto& kv : ctx->regions) {
+    Region& r = kv.second;
+    if (r.dirty_hi > r.dirty_lo)
+      TG_CUDA(cudaMemcpyAsync(r.host + r.dirty_lo, r.dev + r.dirty_lo, r.dirty_hi - r.dirty_lo,
+                              cudaMemcpyDeviceToHost, ctx->stream));
+  }
+  TG_TRY(wait_stream(ctx));
+  for (auto& kv : ctx->regions) {
+    kv.second.dirty_lo = kv.second.dirty_hi = 0;
+    kv.second.fresh = false;
+  }
+  ctx->arena_off = 0;
+  free_graveyard(ctx);
+  return check_device_error(ctx);
+}
+
+// ------------------------------------------------ RoPE tables
+
+// cos/sin for positions [0, len) exactly as apply_rope computes them
+// (tmac_gguf.cpp:993-996): theta = 1/powf(base, (float)d/head_dim),
+// freq = pos*theta, cosf/sinf -- evaluated here with the host libm so the
+// device rotation reproduces the reference bit for bit.
+int get_table(tg_context* ctx, float base, int head_dim, int need_len, RopeTable** out) {
+  uint32_t bits;
+  std::memcpy(&bits, &base, 4);
+  RopeTable* t = nullptr;
+  for (RopeTable& x : ctx->tables)
+    if (x.base_bits == bits && x.head_dim == head_dim) t = &x;
+  if (t && t->len >= need_len) {
+    *out = t;
+    return TG_OK;
+  }
+  int len = 4096;
+  while (len < need_len) len *= 2;
+  const int half = head_dim / 2;
+  std::vector<float> theta(half);
+  for (int j = 0; j < half; ++j) theta[j] = 1.0f / powf(base, (float)(2 * j) / head_dim);
+  std::vector<float> h((size_t)len * head_dim);
+  for (int pos = 0; pos < len; ++pos) {
+    float* row = h.data() + (size_t)pos * head_dim;
+    for (int j = 0; j < half; ++j) {
+      const float freq = pos * theta[j];
+      row[2 * j] = cosf(freq);
+      row[2 * j + 1] = sinf(freq);
+    }
+  }
+  float* d = nullptr;
+  TG_CUDA(cudaMalloc(&d, h.size() * sizeof(float)));
+  TG_CUDA(cudaMemcpy(d, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice));
+  if (!t) {
+    ctx->tables.push_back(RopeTable());
+    t = &ctx->tables.back();
+    t->base_bits = bits;
+    t->head_dim = head_dim;
+  } else {
+    ctx->graveyard.push_back(t->d);
+  }
+  t->len = len;
+  t->d = d;
+  *out = t;
+  return TG_OK;
+}
+
+int check_shape(int n_head, int n_kv, int hd) {
+  if (n_head <= 0 || n_kv <= 0 || hd <= 0 || hd % 2 || hd > 128 || n_head % n_kv)
+    return fail(TG_ERR_INVALID_ARG, "unsupported shape n_head=%d n_kv_head=%d head_dim=%d", n_head,
+                n_kv, hd);
+  if (n_head * hd > 4096 || n_kv * hd > 1024 || (n_kv * hd) % 8)
+    return fail(TG_ERR_INVALID_ARG, "shape too large n_head=%d n_kv_head=%d head_dim=%d", n_head,
+                n_kv, hd);
+  return TG_OK;
+}
+
+bool mma_eligible(const tg_kv_cache* kv) {
+  return kv->tmap_ok && kv->d.dtype == TG_DTYPE_BF16 && kv->d.head_dim == 64 &&
+         (kv->d.n_kv_head == 1 || kv->d.n_kv_head == 2 || kv->d.n_kv_head == 4) &&
+         kv->d.n_head / kv->d.n_kv_head <= 8;
+}
+
+int generic_grid(tg_context* ctx, int dtype, size_t smem) {
+  int per_sm = tg::decode_generic_blocks_per_sm(dtype, smem);
+  if (per_sm > 4) per_sm = 4;
+  return ctx->num_sms * per_sm;
+}
+
+// Core decode launch on device pointers.  mode 0 writes `out`; mode 1
+// writes per-sequence records to ctx->records.
+int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const float* q,
+               const int* past_dev, int past_scalar, float* out, int mode) {
+  const tg_kv_desc& d = kv->d;
+  const int rf = tg::record_floats(d.n_head, d.head_dim);
+  tg::DecodeParams p{};
+  p.q = q;
+  p.out = out;
+  p.past_len = past_dev;
+  p.past_len_scalar = past_scalar;
+  p.k = static_cast<const char*>(kv->k) + (size_t)layer * kv->layer_elems * kv->esize;
+  p.v = static_cast<const char*>(kv->v) + (size_t)layer * kv->layer_elems * kv->esize;
+  p.row0 = (long long)layer * d.n_seqs * d.max_ctx;
+  p.B = B;
+  p.n_head = d.n_head;
+  p.n_kv = d.n_kv_head;
+  p.head_dim = d.head_dim;
+  p.group = d.n_head / d.n_kv_head;
+  p.max_ctx = d.max_ctx;
+  p.shard_start = d.shard_start;
+  p.scale_log2 = kLog2e / sqrtf((float)d.head_dim);
+  p.mode = mode;
+  p.err = ctx->d_err;
+
+  const bool mma = mma_eligible(kv);
+  int grid;
+  size_t smem;
+  if (mma) {
+    smem = tg::decode_mma_smem(d.n_kv_head, B);
+    grid = ctx->num_sms;
+  } else {
+    smem = tg::decode_generic_smem(B, d.n_head, d.n_kv_head, d.head_dim);
+    grid = generic_grid(ctx, d.dtype, smem);
+  }
+  if (smem > 227 * 1024)
+    return fail(TG_ERR_INVALID_ARG, "batch of %d sequences exceeds the shared-memory schedule", B);
+  TG_TRY(ensure_buf(ctx, &ctx->part, &ctx->part_cap, (size_t)2 * grid * rf));
+  TG_TRY(ensure_buf(ctx, &ctx->sched, &ctx->sched_cap, (size_t)B + 1));
+  if (mode == 1) TG_TRY(ensure_buf(ctx, &ctx->records, &ctx->rec_cap, (size_t)B * rf));
+  p.part = ctx->part;
+  p.sched = ctx->sched;
+  p.records = ctx->records;
+
+  cudaEvent_t ev_stop = nullptr;
+  if (ctx->prof_on) {
+    while (ctx->prof_ev.size() < ctx->prof_used + 2) {
+      cudaEvent_t ev;
+      TG_CUDA(cudaEventCreate(&ev));
+      ctx->prof_ev.push_back(ev);
+    }
+    TG_CUDA(cudaEventRecord(ctx->prof_ev[ctx->prof_used], ctx->stream));
+    ev_stop = ctx->prof_ev[ctx->prof_used + 1];
+    ctx->prof_used += 2;
+  }
+  cudaError_t e = mma ? tg::launch_decode_mma(kv->tmk, kv->tmv, p, grid, ctx->stream)
+                      : tg::launch_decode_generic(p, d.dtype, grid, ctx->stream);
+  if (e != cudaSuccess) return fail(TG_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
+  ctx->launches++;
+  if (ev_stop) TG_CUDA(cudaEventRecord(ev_stop, ctx->stream));
+
+  tg::MergeParams m{};
+  m.part = ctx->part;
+  m.sched = ctx->sched;
+  m.out = out;
+  m.records = ctx->records;
+  m.B = B;
+  m.n_head = d.n_head;
+  m.head_dim = d.head_dim;
+  m.G = grid;
+  m.mode = mode;
+  e = tg::launch_merge(m, ctx->stream);
+  if (e != cudaSuccess) return fail(TG_ERR_CUDA, "merge launch: %s", cudaGetErrorString(e));
+  ctx->launches++;
+  return TG_OK;
+}
+
+int run_rope(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, float* q, float* k,
+             const float* v, const int* pos_dev) {
+  const tg_kv_desc& d = kv->d;
+  RopeTable* t = nullptr;
+  TG_TRY(get_table(ctx, d.rope_base, d.head_dim, kv->global_ctx, &t));
+  tg::RopeParams rp{};
+  rp.q = q;
+  rp.k = k;
+  rp.v = v;
+  rp.pos = pos_dev;
+  rp.cs = t->d;
+  rp.table_len = kv->global_ctx;
+  rp.k_cache = static_cast<char*>(kv->k) + (size_t)layer * kv->layer_elems * kv->esize;
+  rp.v_cache = static_cast<char*>(kv->v) + (size_t)layer * kv->layer_elems * kv->esize;
+  rp.B = B;
+  rp.n_head = d.n_head;
+  rp.n_kv = d.n_kv_head;
+  rp.head_dim = d.head_dim;
+  rp.max_ctx = d.max_ctx;
+  rp.shard_start = d.shard_start;
+  rp.dtype = d.dtype;
+  rp.err = ctx->d_err;
+  cudaError_t e = tg::launch_rope(rp, ctx->stream);
+  if (e != cudaSuccess) return fail(TG_ERR_CUDA, "rope launch: %s", cudaGetErrorString(e));
+  ctx->launches++;
+  return TG_OK;
+}
+
+int check_kv_call(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs) {
+  if (!ctx || !kv) return fail(TG_ERR_INVALID_ARG, "null context or cache");
+  if (kv->ctx != ctx) return fail(TG_ERR_INVALID_ARG, "cache belongs to another context");
+  if (layer < 0 || layer >= kv->d.n_layers)
+    return fail(TG_ERR_INVALID_ARG, "layer %d outside [0, %d)", layer, kv->d.n_layers);
+  if (n_seqs < 0 || n_seqs > kv->d.n_seqs)
+    return fail(TG_ERR_INVALID_ARG, "n_seqs %d outside [0, %d]", n_seqs, kv->d.n_seqs);
+  return set_device(ctx);
+}
+
+// Host position arrays are validated here; device ones by the kernels.
+int check_host_pos(const int32_t* pos, int n, int limit, const char* what) {
+  if (!pos || is_device_ptr(pos)) return TG_OK;
+  for (int i = 0; i < n; ++i)
+    if (pos[i] < 0 || pos[i] >= limit)
+      return fail(TG_ERR_INVALID_ARG, "%s[%d] = %d outside [0, %d)", what, i, pos[i], limit);
+  return TG_OK;
+}
+
+}  // namespace
+
+// ================================================================ C ABI
+
+extern "C" {
+
+const char* tg_status_string(int s) {
+  switch (s) {
+    case TG_OK: return "ok";
+    case TG_ERR_INVALID_ARG: return "invalid argument";
+    case TG_ERR_CUDA: return "CUDA error";
+    case TG_ERR_NO_DEVICE: return "no CUDA device";
+    case TG_ERR_OUT_OF_MEMORY: return "out of device memory";
+    case TG_ERR_UNSUPPORTED: return "unsupported";
+    case TG_ERR_DEVICE: return "device-side error";
+    case TG_ERR_COMM: return "communicator error";
+    case TG_ERR_STATE: return "invalid call order";
+    default: return "unknown status";
+  }
+}
+
+const char* tg_last_error(void) { return t_err.c_str(); }
+const char* tg_version(void) { return TG_VERSION; }
+
+int tg_init(int device, tg_context** out) {
+  if (!out) return fail(TG_ERR_INVALID_ARG, "null output pointer");
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return fail(TG_ERR_NO_DEVICE, "no CUDA device available");
+  }
+  if (device < 0 || device >= n)
+    return fail(TG_ERR_INVALID_ARG, "device %d outside [0, %d)", device, n);
+  TG_CUDA(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  TG_CUDA(cudaGetDeviceProperties(&prop, device));
+  if (prop.major < 10)
+    return fail(TG_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", device,
+                prop.major, prop.minor);
+  tg_context* c = new tg_context();
+  c->device = device;
+  c->num_sms = prop.multiProcessorCount;
+  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&c->d_err, sizeof(int)) != cudaSuccess ||
+      cudaMemset(c->d_err, 0, sizeof(int)) != cudaSuccess) {
+    cudaError_t e = cudaGetLastError();
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+    return fail(TG_ERR_CUDA, "context setup failed: %s", cudaGetErrorString(e));
+  }
+  c->own_stream = true;
+  *out = c;
+  return TG_OK;
+}
+
+int tg_shutdown(tg_context* ctx) {
+  if (!ctx) return TG_OK;
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  if (ctx->comm) {
+    nccl().CommDestroy(ctx->comm);
+    ctx->comm = nullptr;
+  }
+  free_graveyard(ctx);
+  for (tg_kv_cache* kv : ctx->caches) {
+    cudaFree(kv->k);
+    cudaFree(kv->v);
+    delete kv;
+  }
+  ctx->caches.clear();
+  for (auto& kv : ctx->regions) cudaFree(kv.second.dev);
+  for (RopeTable& t : ctx->tables) cudaFree(t.d);
+  for (cudaEvent_t ev : ctx->prof_ev) cudaEventDestroy(ev);
+  cudaFree(ctx->part);
+  cudaFree(ctx->sched);
+  cudaFree(ctx->records);
+  cudaFree(ctx->recv);
+  cudaFree(ctx->arena);
+  cudaFree(ctx->d_err);
+  if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+  return TG_OK;
+}
+
+int tg_set_stream(tg_context* ctx, void* stream) {
+  TG_TRY(set_device(ctx));
+  TG_CUDA(cudaStreamSynchronize(ctx->stream));
+  if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
+  ctx->stream = static_cast<cudaStream_t>(stream);
+  ctx->own_stream = false;
+  return TG_OK;
+}
+
+int tg_get_stream(tg_context* ctx, void** stream) {
+  if (!ctx || !stream) return fail(TG_ERR_INVALID_ARG, "null argument");
+  *stream = ctx->stream;
+  return TG_OK;
+}
+
+int tg_device_sms(tg_context* ctx, int* out) {
+  if (!ctx || !out) return fail(TG_ERR_INVALID_ARG, "null argument");
+  *out = ctx->num_sms;
+  return TG_OK;
+}
+
+int tg_batch_begin(tg_context* ctx) {
+  TG_TRY(set_device(ctx));
+  if (ctx->in_batch) return fail(TG_ERR_STATE, "batch already open");
+  ctx->in_batch = true;
+  return TG_OK;
+}
+
+int tg_batch_end(tg_context* ctx) {
+  TG_TRY(set_device(ctx));
+  if (!ctx->in_batch) return fail(TG_ERR_STATE, "tg_batch_end without tg_batch_begin");
+  ctx->in_batch = false;
+  for (const PendingCopy& c : ctx->pending)
+    TG_CUDA(cudaMemcpyAsync(c.host, c.dev, c.bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  ctx->pending.clear();
+  return flush_regions(ctx);
+}
+
+int tg_synchronize(tg_context* ctx) {
+  TG_TRY(set_device(ctx));
+  TG_TRY(wait_stream(ctx));
+  if (!ctx->in_batch) {
+    ctx->arena_off = 0;
+    free_graveyard(ctx);
+  }
+  return check_device_error(ctx);
+}
+
+int tg_register_host(tg_context* ctx, void* host_ptr, size_t bytes, int flags) {
+  TG_TRY(set_device(ctx));
+  if (!host_ptr || bytes == 0) return fail(TG_ERR_INVALID_ARG, "empty host range");
+  if (is_device_ptr(host_ptr)) return fail(TG_ERR_INVALID_ARG, "pointer is device memory");
+  Region* r = nullptr;
+  TG_TRY(create_region(ctx, static_cast<char*>(host_ptr), bytes, flags, &r));
+  if (!ctx->in_batch) return flush_regions(ctx);
+  return TG_OK;
+}
+
+int tg_unregister_host(tg_context* ctx, void* host_ptr) {
+  TG_TRY(set_device(ctx));
+  auto it = ctx->regions.find(reinterpret_cast<uintptr_t>(host_ptr));
+  if (it == ctx->regions.end()) return fail(TG_ERR_INVALID_ARG, "pointer is not a region start");
+  if (ctx->in_batch) return fail(TG_ERR_STATE, "cannot unregister inside a batch");
+  TG_CUDA(cudaStreamSynchronize(ctx->stream));
+  cudaFree(it->second.dev);
+  ctx->regions.erase(it);
+  return TG_OK;
+}
+
+int tg_region_sync(tg_context* ctx, void* host_ptr, size_t bytes, int to_device) {
+  TG_TRY(set_device(ctx));
+  Region* r = find_region(ctx, static_cast<char*>(host_ptr), bytes);
+  if (!r) return fail(TG_ERR_INVALID_ARG, "range is not inside a registered region");
+  const size_t off = (size_t)(static_cast<char*>(host_ptr) - r->host);
+  if (to_device)
+    TG_CUDA(cudaMemcpyAsync(r->dev + off, host_ptr, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  else
+    TG_CUDA(cudaMemcpyAsync(host_ptr, r->dev + off, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  if (ctx->in_batch) return TG_OK;
+  TG_TRY(wait_stream(ctx));
+  return TG_OK;
+}
+
+// ------------------------------------------------ reference-compatible ops
+
+int tg_rope_op(tg_context* ctx, float* data, int n_heads, int head_dim, int pos, float base) {
+  TG_TRY(set_device(ctx));
+  if (!data || n_heads <= 0 || head_dim <= 0 || head_dim % 2 || pos < 0)
+    return fail(TG_ERR_INVALID_ARG, "rope_op: bad arguments (n_heads=%d head_dim=%d pos=%d)",
+                n_heads, head_dim, pos);
+  char* d = nullptr;
+  TG_TRY(resolve(ctx, data, (size_t)n_heads * head_dim * 4, true, &d));
+  RopeTable* t = nullptr;
+  TG_TRY(get_table(ctx, base, head_dim, pos + 1, &t));
+  tg::RopeParams rp{};
+  rp.q = reinterpret_cast<float*>(d);
+  rp.pos_scalar = pos;
+  rp.cs = t->d;
+  rp.table_len = t->len;
+  rp.B = 1;
+  rp.n_head = n_heads;
+  rp.n_kv = 1;
+  rp.head_dim = head_dim;
+  rp.err = ctx->d_err;
+  cudaError_t e = tg::launch_rope(rp, ctx->stream);
+  if (e != cudaSuccess) return fail(TG_ERR_CUDA, "rope launch: %s", cudaGetErrorString(e));
+  ctx->launches++;
+  if (ctx->in_batch) return TG_OK;
+  return flush_regions(ctx);
+}
+
+int tg_elem_op(tg_context* ctx, int op, float* data, const float* aux, int dim) {
+  TG_TRY(set_device(ctx));
+  if (op == 1)
+    return fail(TG_ERR_UNSUPPORTED, "elem_op op 1 (SiLU x up) belongs to the FFN, not this path");
+  if (op != 0 && op != 2) return fail(TG_ERR_INVALID_ARG, "elem_op: unknown op %d", op);
+  if (!data || !aux || dim < 0) return fail(TG_ERR_INVALID_ARG, "elem_op: bad arguments");
+  if (dim == 0) return TG_OK;
+  char *dd = nullptr, *da = nullptr;
+  TG_TRY(ensure_region(ctx, aux, (size_t)dim * 4));
+  TG_TRY(ensure_region(ctx, data, (size_t)dim * 4));
+  TG_TRY(resolve(ctx, aux, (size_t)dim * 4, false, &da));
+  TG_TRY(resolve(ctx, data, (size_t)dim * 4, true, &dd));
+  cudaError_t e = tg::launch_elem(op, reinterpret_cast<float*>(dd),
+                                  reinterpret_cast<const float*>(da), dim, ctx->stream);
+  if (e != cudaSuccess) return fail(TG_ERR_CUDA, "elem launch: %s", cudaGetErrorString(e));
+  ctx->launches++;
+  if (ctx->in_batch) return TG_OK;
+  return flush_regions(ctx);
+}
+
+int tg_attention_op(tg_context* ctx, const float* Q, const float* K_cache, const float* V_cache,
+                    float* output, int n_head, int n_kv_head, int head_dim, int past_len) {
+  TG_TRY(set_device(ctx));
+  TG_TRY(check_shape(n_head, n_kv_head, head_dim));
+  if (past_len < 0) return fail(TG_ERR_INVALID_ARG, "attention_op: past_len %d < 0", past_len);
+  const size_t qbytes = (size_t)n_head * head_dim * 4;
+  const size_t cbytes = (size_t)(past_len + 1) * n_kv_head * head_dim * 4;
+  char *dq = nullptr, *dk = nullptr, *dv = nullptr, *dout = nullptr;
+  TG_TRY(ensure_region(ctx, Q, qbytes));
+  TG_TRY(ensure_region(ctx, K_cache, cbytes));
+  TG_TRY(ensure_region(ctx, V_cache, cbytes));
+  TG_TRY(ensure_region(ctx, output, qbytes));
+  TG_TRY(resolve(ctx, Q, qbytes, false, &dq));
+  TG_TRY(resolve(ctx, K_cache, cbytes, false, &dk));
+  TG_TRY(resolve(ctx, V_cache, cbytes, false, &dv));
+  TG_TRY(resolve(ctx, output, qbytes, true, &dout));
+  // A one-sequence, one-layer view of the caller's fp32 cache.
+  tg_kv_cache view;
+  view.ctx = ctx;
+  view.d.n_layers = 1;
+  view.d.n_seqs = 1;
+  view.d.max_ctx = past_len + 1;
+  view.d.n_head = n_head;
+  view.d.n_kv_head = n_kv_head;
+  view.d.head_dim = head_dim;
+  view.d.dtype = TG_DTYPE_F32;
+  view.row_elems = (size_t)n_kv_head * head_dim;
+  view.esize = 4;
+  view.layer_elems = view.row_elems * (past_len + 1);
+  view.k = dk;
+  view.v = dv;
+  view.global_ctx = past_len + 1;
+  TG_TRY(run_decode(ctx, &view, 0, 1, reinterpret_cast<const float*>(dq), nullptr, past_len,
+                    reinterpret_cast<float*>(dout), 0));
+  if (ctx->in_batch) return TG_OK;
+  return flush_regions(ctx);
+}
+
+// ------------------------------------------------ KV caches
+
+int tg_kv_create(tg_context* ctx, const tg_kv_desc* desc, tg_kv_cache** out) {
+  TG_TRY(set_device(ctx));
+  if (!desc || !out) return fail(TG_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  const tg_kv_desc& d = *desc;
+  TG_TRY(check_shape(d.n_head, d.n_kv_head, d.head_dim));
+  if (d.n_layers <= 0 || d.n_seqs <= 0 || d.max_ctx <= 0 || d.shard_start < 0)
+    return fail(TG_ERR_INVALID_ARG, "kv_create: bad sizes");
+  if (d.dtype != TG_DTYPE_F32 && d.dtype != TG_DTYPE_BF16)
+    return fail(TG_ERR_INVALID_ARG, "kv_create: dtype %d", d.dtype);
+  const long long rows = (long long)d.n_layers * d.n_seqs * d.max_ctx;
+  if (rows >= (1LL << 31)) return fail(TG_ERR_INVALID_ARG, "kv_create: %lld rows is too many", rows);
+  if (!(d.rope_base > 0.f)) return fail(TG_ERR_INVALID_ARG, "kv_create: rope_base must be > 0");
+  tg_kv_cache* kv = new tg_kv_cache();
+  kv->ctx = ctx;
+  kv->d = d;
+  kv->row_elems = (size_t)d.n_kv_head * d.head_dim;
+  kv->esize = d.dtype == TG_DTYPE_F32 ? 4 : 2;
+  kv->layer_elems = kv->row_elems * (size_t)d.n_seqs * d.max_ctx;
+  kv->global_ctx = d.global_ctx > 0 ? d.global_ctx : d.shard_start + d.max_ctx;
+  if (kv->global_ctx < d.shard_start + d.max_ctx) kv->global_ctx = d.shard_start + d.max_ctx;
+  const size_t bytes = kv->layer_elems * d.n_layers * kv->esize;
+  if (cudaMalloc(&kv->k, bytes) != cudaSuccess || cudaMalloc(&kv->v, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(kv->k);
+    cudaFree(kv->v);
+    delete kv;
+    return fail(TG_ERR_OUT_OF_MEMORY, "kv_create: %zu bytes per cache", bytes);
+  }
+  cudaMemsetAsync(kv->k, 0, bytes, ctx->stream);
+  cudaMemsetAsync(kv->v, 0, bytes, ctx->stream);
+  if (d.dtype == TG_DTYPE_BF16 && d.head_dim == 64) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (enc) {
+      cuuint64_t gdim[2] = {(cuuint64_t)kv->row_elems, (cuuint64_t)rows};
+      cuuint64_t gstride[1] = {(cuuint64_t)(kv->row_elems * 2)};
+      cuuint32_t box[2] = {64, 64};
+      cuuint32_t estr[2] = {1, 1};
+      CUresult r1 = enc(&kv->tmk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv->k, gdim, gstride, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      CUresult r2 = enc(&kv->tmv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv->v, gdim, gstride, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      kv->tmap_ok = (r1 == CUDA_SUCCESS && r2 == CUDA_SUCCESS);
+    }
+  }
+  RopeTable* t = nullptr;
+  int rc = get_table(ctx, d.rope_base, d.head_dim, kv->global_ctx, &t);
+  if (rc != TG_OK) {
+    cudaFree(kv->k);
+    cudaFree(kv->v);
+    delete kv;
+    return rc;
+  }
+  if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) {
+    cudaError_t e = cudaGetLastError();
+    return fail(TG_ERR_CUDA, "kv_create: %s", cudaGetErrorString(e));
+  }
+  ctx->caches.push_back(kv);
+  *out = kv;
+  return TG_OK;
+}
+
+int tg_kv_destroy(tg_kv_cache* kv) {
+  if (!kv) return TG_OK;
+  cudaSetDevice(kv->ctx->device);
+  cudaStreamSynchronize(kv->ctx->stream);
+  auto& cs = kv->ctx->caches;
+  for (size_t i = 0; i < cs.size(); ++i)
+    if (cs[i] == kv) {
+      cs.erase(cs.begin() + i);
+      break;
+    }
+  cudaFree(kv->k);
+  cudaFree(kv->v);
+  delete kv;
+  return TG_OK;
+}
+
+int tg_kv_reset(tg_kv_cache* kv) {
+  if (!kv) return fail(TG_ERR_INVALID_ARG, "null cache");
+  TG_TRY(set_device(kv->ctx));
+  const size_t bytes = kv->layer_elems * kv->d.n_layers * kv->esize;
+  TG_CUDA(cudaMemsetAsync(kv->k, 0, bytes, kv->ctx->stream));
+  TG_CUDA(cudaMemsetAsync(kv->v, 0, bytes, kv->ctx->stream));
+  if (kv->ctx->in_batch) return TG_OK;
+  return tg_synchronize(kv->ctx);
+}
+
+int tg_kv_layer_ptrs(tg_kv_cache* kv, int layer, void** k, void** v) {
+  if (!kv || layer < 0 || layer >= kv->d.n_layers)
+    return fail(TG_ERR_INVALID_ARG, "bad cache or layer");
+  const size_t off = (size_t)layer * kv->layer_elems * kv->esize;
+  if (k) *k = static_cast<char*>(kv->k) + off;
+  if (v) *v = static_cast<char*>(kv->v) + off;
+  return TG_OK;
+}
+
+int tg_kv_fill_normal(tg_kv_cache* kv, uint64_t seed) {
+  if (!kv) return fail(TG_ERR_INVALID_ARG, "null cache");
+  tg_context* ctx = kv->ctx;
+  TG_TRY(set_device(ctx));
+  const size_t n = kv->layer_elems * kv->d.n_layers;
+  cudaError_t e = tg::launch_fill_normal(kv->k, n, kv->d.dtype, seed, ctx->num_sms, ctx->stream);
+  if (e == cudaSuccess)
+    e = tg::launch_fill_normal(kv->v, n, kv->d.dtype, seed ^ 0x5bd1e995ULL, ctx->num_sms,
+                               ctx->stream);
+  if (e != cudaSuccess) return fail(TG_ERR_CUDA, "fill launch: %s", cudaGetErrorString(e));
+  ctx->launches += 2;
+  if (ctx->in_batch) return TG_OK;
+  return tg_synchronize(ctx);
+}
+
+int tg_kv_write_rows(tg_kv_cache* kv, int layer, int seq, int row0, int n_rows,
+                     const float* k_rows, const float* v_rows) {
+  if (!kv) return fail(TG_ERR_INVALID_ARG, "null cache");
+  tg_context* ctx = kv->ctx;
+  TG_TRY(check_kv_call(ctx, kv, layer, kv->d.n_seqs));
+  if (seq < 0 || seq >= kv->d.n_seqs || row0 < 0 || n_rows < 0 || row0 + n_rows > kv->d.max_ctx)
+    return fail(TG_ERR_INVALID_ARG, "kv_write_rows: rows [%d, %d) of seq %d out of range", row0,
+                row0 + n_rows, seq);
+  if (n_rows == 0) return TG_OK;
+  const size_t n = (size_t)n_rows * kv->row_elems;
+  const size_t off = ((size_t)layer * kv->layer_elems +
+                      ((size_t)seq * kv->d.max_ctx + row0) * kv->row_elems) * kv->esize;
+  const void* src[2] = {k_rows, v_rows};
+  void* dst[2] = {static_cast<char*>(kv->k) + off, static_cast<char*>(kv->v) + off};
+  for (int i = 0; i < 2; ++i) {
+    if (!src[i]) continue;
+    const void* ds = nullptr;
+    TG_TRY(stage_in(ctx, src[i], n * 4, &ds));
+    cudaError_t e = tg::launch_convert_rows(dst[i], static_cast<const float*>(ds), n,
+                                            kv->d.dtype, ctx->num_sms, ctx->stream);
+    if (e != cudaSuccess) return fail(TG_ERR_CUDA, "convert launch: %s", cudaGetErrorString(e));
+    ctx->launches++;
+  }
+  return finish_call(ctx);
+}
+
+int tg_kv_read_rows(tg_kv_cache* kv, int layer, int seq, int row0, int n_rows, void* k_out,
+                    void* v_out) {
+  if (!kv) return fail(TG_ERR_INVALID_ARG, "null cache");
+  tg_context* ctx = kv->ctx;
+  TG_TRY(check_kv_call(ctx, kv, layer, kv->d.n_seqs));
+  if (seq < 0 || seq >= kv->d.n_seqs || row0 < 0 || n_rows < 0 || row0 + n_rows > kv->d.max_ctx)
+    return fail(TG_ERR_INVALID_ARG, "kv_read_rows: rows out of range");
+  const size_t bytes = (size_t)n_rows * kv->row_elems * kv->esize;
+  const size_t off = ((size_t)layer * kv->layer_elems +
+                      ((size_t)seq * kv->d.max_ctx + row0) * kv->row_elems) * kv->esize;
+  if (k_out)
+    TG_CUDA(cudaMemcpyAsync(k_out, static_cast<char*>(kv->k) + off, bytes, cudaMemcpyDefault,
+                            ctx->stream));
+  if (v_out)
+    TG_CUDA(cudaMemcpyAsync(v_out, static_cast<char*>(kv->v) + off, bytes, cudaMemcpyDefault,
+                            ctx->stream));
+  if (ctx->in_batch) return TG_OK;
+  return tg_synchronize(ctx);
+}
+
+// ------------------------------------------------ batched decode
+
+int tg_rope_cache_write(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, float* q,
+                        float* k_new, const float* v_new, const int32_t* pos) {
+  TG_TRY(check_kv_call(ctx, kv, layer, n_seqs));
+  if (!pos) return fail(TG_ERR_INVALID_ARG, "null pos");
+  if (n_seqs == 0) return TG_OK;
+  TG_TRY(check_host_pos(pos, n_seqs, kv->global_ctx, "pos"));
+  const tg_kv_desc& d = kv->d;
+  void *dq = nullptr, *dk = nullptr;
+  const void *dv = nullptr, *dp = nullptr;
+  TG_TRY(stage_out(ctx, q, (size_t)n_seqs * d.n_head * d.head_dim * 4, true, &dq));
+  TG_TRY(stage_out(ctx, k_new, (size_t)n_seqs * kv->row_elems * 4, true, &dk));
+  TG_TRY(stage_in(ctx, v_new, (size_t)n_seqs * kv->row_elems * 4, &dv));
+  TG_TRY(stage_in(ctx, pos, (size_t)n_seqs * 4, &dp));
+  TG_TRY(run_rope(ctx, kv, layer, n_seqs, static_cast<float*>(dq), static_cast<float*>(dk),
+                  static_cast<const float*>(dv), static_cast<const int*>(dp)));
+  return finish_call(ctx);
+}
+
+int tg_attention_batched(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, const float* q,
+                         const int32_t* past_len, float* out) {
+  TG_TRY(check_kv_call(ctx, kv, layer, n_seqs));
+  if (!q || !past_len || !out) return fail(TG_ERR_INVALID_ARG, "null argument");
+  if (n_seqs == 0) return TG_OK;
+  TG_TRY(check_host_pos(past_len, n_seqs, kv->d.shard_start + kv->d.max_ctx, "past_len"));
+  const size_t qb = (size_t)n_seqs * kv->d.n_head * kv->d.head_dim * 4;
+  const void *dq = nullptr, *dp = nullptr;
+  void* dout = nullptr;
+  TG_TRY(stage_in(ctx, q, qb, &dq));
+  TG_TRY(stage_in(ctx, past_len, (size_t)n_seqs * 4, &dp));
+  TG_TRY(stage_out(ctx, out, qb, false, &dout));
+  TG_TRY(run_decode(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
+                    static_cast<const int*>(dp), 0, static_cast<float*>(dout), 0));
+  return finish_call(ctx);
+}
+
+int tg_decode_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, float* q,
+                    float* k_new, const float* v_new, const int32_t* pos, float* out) {
+  TG_TRY(check_kv_call(ctx, kv, layer, n_seqs));
+  if (!q || !k_new || !v_new || !pos || !out) return fail(TG_ERR_INVALID_ARG, "null argument");
+  if (n_seqs == 0) return TG_OK;
+  TG_TRY(check_host_pos(pos, n_seqs, kv->d.shard_start + kv->d.max_ctx, "pos"));
+  const tg_kv_desc& d = kv->d;
+  const size_t qb = (size_t)n_seqs * d.n_head * d.head_dim * 4;
+  const size_t kb = (size_t)n_seqs * kv->row_elems * 4;
+  void *dq = nullptr, *dk = nullptr, *dout = nullptr;
+  const void *dv = nullptr, *dp = nullptr;
+  TG_TRY(stage_out(ctx, q, qb, true, &dq));
+  TG_TRY(stage_out(ctx, k_new, kb, true, &dk));
+  TG_TRY(stage_in(ctx, v_new, kb, &dv));
+  TG_TRY(stage_in(ctx, pos, (size_t)n_seqs * 4, &dp));
+  TG_TRY(stage_out(ctx, out, qb, false, &dout));
+  TG_TRY(run_rope(ctx, kv, layer, n_seqs, static_cast<float*>(dq), static_cast<float*>(dk),
+                  static_cast<const float*>(dv), static_cast<const int*>(dp)));
+  TG_TRY(run_decode(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
+                    static_cast<const int*>(dp), 0, static_cast<float*>(dout), 0));
+  return finish_call(ctx);
+}
+
+// ------------------------------------------------ split-KV
+
+int tg_comm_unique_id(void* id_out, size_t id_bytes) {
+  if (!id_out || id_bytes < sizeof(ncclUniqueId))
+    return fail(TG_ERR_INVALID_ARG, "id buffer must hold %zu bytes", sizeof(ncclUniqueId));
+  if (!nccl().ok) return fail(TG_ERR_COMM, "NCCL library not found");
+  ncclUniqueId id;
+  ncclResult_t r = nccl().GetUniqueId(&id);
+  if (r != ncclSuccess) return fail(TG_ERR_COMM, "ncclGetUniqueId: %s", nccl().GetErrorString(r));
+  std::memcpy(id_out, &id, sizeof(id));
+  return TG_OK;
+}
+
+int tg_comm_init(tg_context* ctx, const void* id, int rank, int world, int timeout_ms) {
+  TG_TRY(set_device(ctx));
+  if (!id || world < 1 || rank < 0 || rank >= world)
+    return fail(TG_ERR_INVALID_ARG, "comm_init: rank %d world %d", rank, world);
+  if (ctx->comm) return fail(TG_ERR_STATE, "communicator already initialised");
+  if (!nccl().ok) return fail(TG_ERR_COMM, "NCCL library not found");
+  ncclUniqueId uid;
+  std::memcpy(&uid, id, sizeof(uid));
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;  // initialisation is polled with a deadline below
+  ncclComm_t comm = nullptr;
+  ncclResult_t r = nccl().CommInitRankConfig(&comm, world, uid, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress)
+    return fail(TG_ERR_COMM, "ncclCommInitRankConfig: %s", nccl().GetErrorString(r));
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t ae = ncclInProgress;
+    nccl().CommGetAsyncError(comm, &ae);
+    if (ae == ncclSuccess) break;
+    const double ms = std::chrono::duration<double, std::milli>(
+                          std::chrono::steady_clock::now() - t0)
+                          .count();
+    if (ae != ncclInProgress || ms > timeout_ms) {
+      nccl().CommAbort(comm);
+      return fail(TG_ERR_COMM, "communicator init failed (%s after %.0f ms)",
+                  ae == ncclInProgress ? "timeout" : nccl().GetErrorString(ae), ms);
+    }
+  }
+  ctx->comm = comm;
+  ctx->rank = rank;
+  ctx->world = world;
+  ctx->timeout_ms = timeout_ms > 0 ? timeout_ms : 60000;
+  return TG_OK;
+}
+
+int tg_comm_destroy(tg_context* ctx) {
+  TG_TRY(set_device(ctx));
+  if (!ctx->comm) return TG_OK;
+  cudaStreamSynchronize(ctx->stream);
+  nccl().CommDestroy(ctx->comm);
+  ctx->comm = nullptr;
+  ctx->world = 1;
+  ctx->rank = 0;
+  return TG_OK;
+}
+
+namespace {
+int splitkv_core(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, const float* dq,
+                 const int* dp, float* dout) {
+  const tg_kv_desc& d = kv->d;
+  const int rf = tg::record_floats(d.n_head, d.head_dim);
+  TG_TRY(run_decode(ctx, kv, layer, n_seqs, dq, dp, 0, nullptr, 1));
+  const size_t count = (size_t)n_seqs * rf;
+  TG_TRY(ensure_buf(ctx, &ctx->recv, &ctx->recv_cap, count * ctx->world));
+  if (ctx->world > 1) {
+    ncclResult_t r = nccl().AllGather(ctx->records, ctx->recv, count, ncclFloat32, ctx->comm,
+                                      ctx->stream);
+    if (r == ncclInProgress) {
+      const auto t0 = std::chrono::steady_clock::now();
+      do {
+        nccl().CommGetAsyncError(ctx->comm, &r);
+        const double ms = std::chrono::duration<double, std::milli>(
+                              std::chrono::steady_clock::now() - t0)
+                              .count();
+        if (r == ncclInProgress && ms > ctx->timeout_ms) break;
+      } while (r == ncclInProgress);
+    }
+    if (r != ncclSuccess) {
+      nccl().CommAbort(ctx->comm);
+      ctx->comm = nullptr;
+      ctx->world = 1;
+      return fail(TG_ERR_COMM, "ncclAllGather: %s; communicator aborted",
+                  r == ncclInProgress ? "timeout" : nccl().GetErrorString(r));
+    }
+  } else {
+    TG_CUDA(cudaMemcpyAsync(ctx->recv, ctx->records, count * 4, cudaMemcpyDeviceToDevice,
+                            ctx->stream));
+  }
+  tg::GatherMergeParams g{};
+  g.records = ctx->recv;
+  g.out = dout;
+  g.world = ctx->world;
+  g.B = n_seqs;
+  g.n_head = d.n_head;
+  g.head_dim = d.head_dim;
+  cudaError_t e = tg::launch_gather_merge(g, ctx->stream);
+  if (e != cudaSuccess) return fail(TG_ERR_CUDA, "gather merge: %s", cudaGetErrorString(e));
+  ctx->launches++;
+  return TG_OK;
+}
+}  // namespace
+
+int tg_attention_splitkv(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs,
+                         const float* q, const int32_t* past_len, float* out) {
+  TG_TRY(check_kv_call(ctx, kv, layer, n_seqs));
+  if (!q || !past_len || !out) return fail(TG_ERR_INVALID_ARG, "null argument");
+  if (n_seqs == 0) return TG_OK;
+  TG_TRY(check_host_pos(past_len, n_seqs, kv->global_ctx, "past_len"));
+  const size_t qb = (size_t)n_seqs * kv->d.n_head * kv->d.head_dim * 4;
+  const void *dq = nullptr, *dp = nullptr;
+  void* dout = nullptr;
+  TG_TRY(stage_in(ctx, q, qb, &dq));
+  TG_TRY(stage_in(ctx, past_len, (size_t)n_seqs * 4, &dp));
+  TG_TRY(stage_out(ctx, out, qb, false, &dout));
+  TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
+                      static_cast<const int*>(dp), static_cast<float*>(dout)));
+  return finish_call(ctx);
+}
+
+int tg_attention_records(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs,
+                         const float* q, const int32_t* past_len, float* records) {
+  TG_TRY(check_kv_call(ctx, kv, layer, n_seqs));
+  if (!q || !past_len || !records) return fail(TG_ERR_INVALID_ARG, "null argument");
+  if (n_seqs == 0) return TG_OK;
+  TG_TRY(check_host_pos(past_len, n_seqs, kv->global_ctx, "past_len"));
+  const int rf = tg::record_floats(kv->d.n_head, kv->d.head_dim);
+  const size_t qb = (size_t)n_seqs * kv->d.n_head * kv->d.head_dim * 4;
+  const void *dq = nullptr, *dp = nullptr;
+  void* drec = nullptr;
+  TG_TRY(stage_in(ctx, q, qb, &dq));
+  TG_TRY(stage_in(ctx, past_len, (size_t)n_seqs * 4, &dp));
+  TG_TRY(stage_out(ctx, records, (size_t)n_seqs * rf * 4, false, &drec));
+  TG_TRY(run_decode(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
+                    static_cast<const int*>(dp), 0, nullptr, 1));
+  TG_CUDA(cudaMemcpyAsync(drec, ctx->records, (size_t)n_seqs * rf * 4, cudaMemcpyDeviceToDevice,
+                          ctx->stream));
+  return finish_call(ctx);
+}
+
+int tg_merge_records(tg_context* ctx, int n_parts, int n_seqs, int n_head, int head_dim,
+                     const float* records, float* out) {
+  TG_TRY(set_device(ctx));
+  if (n_parts <= 0 || n_seqs < 0 || !records || !out)
+    return fail(TG_ERR_INVALID_ARG, "merge_records: bad arguments");
+  TG_TRY(check_shape(n_head, 1, head_dim));
+  if (n_seqs == 0) return TG_OK;
+  const int rf = tg::record_floats(n_head, head_dim);
+  const void* drec = nullptr;
+  void* dout = nullptr;
+  TG_TRY(stage_in(ctx, records, (size_t)n_parts * n_seqs * rf * 4, &drec));
+  TG_TRY(stage_out(ctx, out, (size_t)n_seqs * n_head * head_dim * 4, false, &dout));
+  tg::GatherMergeParams g{};
+  g.records = static_cast<const float*>(drec);
+  g.out = static_cast<float*>(dout);
+  g.world = n_parts;
+  g.B = n_seqs;
+  g.n_head = n_head;
+  g.head_dim = head_dim;
+  cudaError_t e = tg::launch_gather_merge(g, ctx->stream);
+  if (e != cudaSuccess) return fail(TG_ERR_CUDA, "gather merge: %s", cudaGetErrorString(e));
+  ctx->launches++;
+  return finish_call(ctx);
+}
+
+int tg_decode_layer_splitkv(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, float* q,
+                            float* k_new, const float* v_new, const int32_t* pos, float* out) {
+  TG_TRY(check_kv_call(ctx, kv, layer, n_seqs));
+  if (!q || !k_new || !v_new || !pos || !out) return fail(TG_ERR_INVALID_ARG, "null argument");
+  if (n_seqs == 0) return TG_OK;
+  TG_TRY(check_host_pos(pos, n_seqs, kv->global_ctx, "pos"));
+  const tg_kv_desc& d = kv->d;
+  const size_t qb = (size_t)n_seqs * d.n_head * d.head_dim * 4;
+  const size_t kb = (size_t)n_seqs * kv->row_elems * 4;
+  void *dq = nullptr, *dk = nullptr, *dout = nullptr;
+  const void *dv = nullptr, *dp = nullptr;
+  TG_TRY(stage_out(ctx, q, qb, true, &dq));
+  TG_TRY(stage_out(ctx, k_new, kb, true, &dk));
+  TG_TRY(stage_in(ctx, v_new, kb, &dv));
+  TG_TRY(stage_in(ctx, pos, (size_t)n_seqs * 4, &dp));
+  TG_TRY(stage_out(ctx, out, qb, false, &dout));
+  TG_TRY(run_rope(ctx, kv, layer, n_seqs, static_cast<float*>(dq), static_cast<float*>(dk),
+                  static_cast<const float*>(dv), static_cast<const int*>(dp)));
+  TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
+                      static_cast<const int*>(dp), static_cast<float*>(dout)));
+  return finish_call(ctx);
+}
+
+// ------------------------------------------------ introspection
+
+int tg_launch_count(tg_context* ctx, long long* out) {
+  if (!ctx || !out) return fail(TG_ERR_INVALID_ARG, "null argument");
+  *out = ctx->launches;
+  return TG_OK;
+}
+
+int tg_profile_enable(tg_context* ctx, int on) {
+  TG_TRY(set_device(ctx));
+  ctx->prof_on = on != 0;
+  ctx->prof_used = 0;
+  return TG_OK;
+}
+
+int tg_profile_read(tg_context* ctx, double* total_ms, long long* launches) {
+  TG_TRY(set_device(ctx));
+  if (!total_ms || !launches) return fail(TG_ERR_INVALID_ARG, "null argument");
+  TG_CUDA(cudaStreamSynchronize(ctx->stream));
+  double sum = 0.0;
+  for (size_t i = 0; i + 1 < ctx->prof_used; i += 2) {
+    float ms = 0.f;
+    TG_CUDA(cudaEventElapsedTime(&ms, ctx->prof_ev[i], ctx->prof_ev[i + 1]));
+    sum += ms;
+  }
+  *total_ms = sum;
+  *launches = (long long)(ctx->prof_used / 2);
+  ctx->prof_used = 0;
+  return TG_OK;
+}
+
+int tg_kv_uses_tensor_cores(tg_kv_cache* kv, int* out) {
+  if (!kv || !out) return fail(TG_ERR_INVALID_ARG, "null argument");
+  *out = mma_eligible(kv) ? 1 : 0;
+  return TG_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,835 @@
+// tg_kernels.cu -- CUDA kernels of the decode-attention hot path (sm_100a).
+//
+//   rope_cache_write_kernel   RoPE on q and k + K/V cache-write, one CTA per
+//                             sequence (tmac_gguf.cpp:990-1016, :1090-1091;
+//                             kernel_rope.metal, kernel_elem.metal op 2).
+//   decode_mma_kernel<NKV>    split-KV GQA decode attention over a bf16
+//                             cache: TMA-staged K/V tiles, warp-level bf16
+//                             tensor-core products with hi/lo operand
+//                             splitting, online softmax with warp shuffles
+//                             (tmac_gguf.cpp:1093-1128, kernel_attn.metal).
+//   decode_generic_kernel<T>  the same contract on CUDA cores for fp32 (and
+//                             any shape the tensor-core kernel does not take).
+//   merge_kernel              combines the partial records of sequences that
+//                             were split across CTAs.
+//   gather_merge_kernel       combines per-GPU records after the all-gather.
+//   elem_kernel, fill_normal_kernel  elem_op ops 0/2 and synthetic inputs.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "tg_device.cuh"
+#include "tg_kernels.h"
+#include "tg_shared.h"
+
+namespace tg {
+
+// ===================================================================== RoPE
+
+__global__ void __launch_bounds__(128) rope_cache_write_kernel(const RopeParams p) {
+  const int s = blockIdx.x;
+  const int pos = p.pos ? p.pos[s] : p.pos_scalar;
+  if (pos < 0 || pos >= p.table_len) {
+    if (threadIdx.x == 0) record_error(p.err, kDevErrBadPos);
+    return;
+  }
+  const int hd = p.head_dim, half = hd >> 1;
+  const float* cs = p.cs + (size_t)pos * hd;  // [half][cos, sin]
+
+  if (p.q) {
+    float* q = p.q + (size_t)s * p.n_head * hd;
+    for (int i = threadIdx.x; i < p.n_head * half; i += blockDim.x) {
+      const int h = i / half, j = i - h * half;
+      const int idx = h * hd + 2 * j;
+      const float x0 = q[idx], x1 = q[idx + 1];
+      const float c = cs[2 * j], sn = cs[2 * j + 1];
+      // x0*c - x1*s and x0*s + x1*c, each product and sum rounded once.
+      q[idx] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+      q[idx + 1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    }
+  }
+
+  const int kdim = p.n_kv * hd;
+  const int local = pos - p.shard_start;
+  const bool write = p.k_cache && local >= 0 && local < p.max_ctx;
+  const size_t row = ((size_t)s * p.max_ctx + (write ? local : 0)) * kdim;
+
+  if (p.k) {
+    float* k = p.k + (size_t)s * kdim;
+    for (int i = threadIdx.x; i < p.n_kv * half; i += blockDim.x) {
+      const int h = i / half, j = i - h * half;
+      const int idx = h * hd + 2 * j;
+      const float x0 = k[idx], x1 = k[idx + 1];
+      const float c = cs[2 * j], sn = cs[2 * j + 1];
+      const float r0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+      const float r1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+      k[idx] = r0;
+      k[idx + 1] = r1;
+      if (write) {
+        if (p.dtype == 0) {
+          float* kc = static_cast<float*>(p.k_cache) + row;
+          kc[idx] = r0;
+          kc[idx + 1] = r1;
+        } else {
+          __nv_bfloat16* kc = static_cast<__nv_bfloat16*>(p.k_cache) + row;
+          kc[idx] = __float2bfloat16_rn(r0);
+          kc[idx + 1] = __float2bfloat16_rn(r1);
+        }
+      }
+    }
+  }
+  if (write && p.v) {
+    const float* v = p.v + (size_t)s * kdim;
+    for (int i = threadIdx.x; i < kdim; i += blockDim.x) {
+      if (p.dtype == 0)
+        static_cast<float*>(p.v_cache)[row + i] = v[i];
+      else
+        static_cast<__nv_bfloat16*>(p.v_cache)[row + i] = __float2bfloat16_rn(v[i]);
+    }
+  }
+}
+
+// ============================================================ tile schedule
+
+// Builds prefix[0..B] (tiles per sequence, exclusive scan) in shared memory
+// with all threads of the block; warp_tot is 32 ints of scratch.  Invalid
+// positions are recorded and contribute no tiles.
+__device__ void build_tile_prefix(const DecodeParams& p, int tile, int* prefix,
+                                  int* warp_tot) {
+  const int NT = blockDim.x, t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int chunk = (p.B + NT - 1) / NT;
+  const int b0 = min(t * chunk, p.B), b1 = min(b0 + chunk, p.B);
+  const int pos_limit = p.shard_start + p.max_ctx;
+  int sum = 0;
+  for (int s = b0; s < b1; ++s) {
+    const int pl = past_of(p, s);
+    int tiles = 0;
+    if (pl < 0 || (p.mode == 0 && pl >= pos_limit)) {
+      record_error(p.err, kDevErrBadPos);
+    } else {
+      const int n = local_rows(pl, p.shard_start, p.max_ctx);
+      tiles = (n + tile - 1) / tile;
+    }
+    prefix[s + 1] = tiles;
+    sum += tiles;
+  }
+  int incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) warp_tot[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    const int nw = (NT + 31) >> 5;
+    const int v = lane < nw ? warp_tot[lane] : 0;
+    int inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += u;
+    }
+    if (lane < nw) warp_tot[lane] = inc - v;
+  }
+  __syncthreads();
+  int run = warp_tot[w] + incl - sum;
+  if (t == 0) prefix[0] = 0;
+  for (int s = b0; s < b1; ++s) {
+    run += prefix[s + 1];
+    prefix[s + 1] = run;
+  }
+  __syncthreads();
+}
+
+// Where a finished segment's state goes.
+struct SegDest {
+  float* ptr;     // record base or output row base
+  bool normalise; // write O / L (mode 0, complete sequence)
+};
+
+__device__ __forceinline__ SegDest segment_dest(const DecodeParams& p, int s,
+                                                long long seg_lo,
+                                                long long seg_hi,
+                                                long long t_lo,
+                                                const int* prefix, int cta) {
+  const int rf = record_floats(p.n_head, p.head_dim);
+  const bool complete = seg_lo == prefix[s] && seg_hi == prefix[s + 1];
+  SegDest d;
+  if (complete) {
+    if (p.mode == 0) {
+      d.ptr = p.out + (size_t)s * p.n_head * p.head_dim;
+      d.normalise = true;
+    } else {
+      d.ptr = p.records + (size_t)s * rf;
+      d.normalise = false;
+    }
+  } else {
+    const int slot = 2 * cta + (seg_lo == t_lo ? 0 : 1);
+    d.ptr = p.part + (size_t)slot * rf;
+    d.normalise = false;
+  }
+  return d;
+}
+
+// ========================================================= tensor-core path
+
+template <int NKV>
+struct MmaCfg {
+  static constexpr int TILE = 64;                 // cache rows per stage
+  static constexpr int STAGES = 4;
+  static constexpr int CWARPS = 2 * NKV;          // consumer warps
+  static constexpr int THREADS = 32 * (CWARPS + 1);
+  static constexpr int BOX = TILE * 128;          // one KV head's rows: 64 bf16
+  static constexpr int STAGE_BYTES = 2 * NKV * BOX;
+  static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+  static constexpr int MRG_FLOATS = 8 * 64 + 16;  // o[8][64], m[8], l[8]
+  static constexpr int OFF_MRG = OFF_BAR + 2 * STAGES * 8;
+  static constexpr int OFF_WTOT = OFF_MRG + CWARPS * MRG_FLOATS * 4;
+  static constexpr int OFF_PREFIX = OFF_WTOT + 32 * 4;
+  static constexpr size_t smem_bytes(int B) {
+    return 1024 + OFF_PREFIX + (size_t)(B + 1) * 4;
+  }
+};
+
+__device__ __forceinline__ void consumer_bar_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+// One CTA: a producer warp streams K/V tiles of its flat tile range into a
+// STAGES-deep shared-memory ring with TMA; consumer warp w handles KV head
+// g = w/2 and rows [32*(w%2), 32*(w%2)+32) of every tile.  Each consumer
+// warp keeps an online-softmax state for the (up to 8) query heads of its KV
+// head: rows 0-7 of the m16 tile carry the bf16 "hi" part of q (or of the
+// probabilities), rows 8-15 the bf16 "lo" remainder, so one m16n8k16 product
+// yields hi + lo in the same thread and the products keep ~17 mantissa bits.
+template <int NKV>
+__global__ void __launch_bounds__(MmaCfg<NKV>::THREADS, 1)
+    decode_mma_kernel(const __grid_constant__ CUtensorMap tmk,
+                      const __grid_constant__ CUtensorMap tmv,
+                      const DecodeParams p) {
+  using Cfg = MmaCfg<NKV>;
+  constexpr int TILE = Cfg::TILE, STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  float* mrg = reinterpret_cast<float*>(smem + Cfg::OFF_MRG);
+  int* warp_tot = reinterpret_cast<int*>(smem + Cfg::OFF_WTOT);
+  int* prefix = reinterpret_cast<int*>(smem + Cfg::OFF_PREFIX);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  build_tile_prefix(p, TILE, prefix, warp_tot);
+  const long long T = prefix[p.B];
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i <= p.B; i += blockDim.x) p.sched[i] = prefix[i];
+  const int G = gridDim.x, cta = blockIdx.x;
+  const long long t_lo = cta_tile_lo(cta, G, T), t_hi = cta_tile_lo(cta + 1, G, T);
+  if (t_lo >= t_hi) return;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], Cfg::CWARPS);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == Cfg::CWARPS) {
+    // ------------------------------------------------------------ producer
+    if (lane != 0) return;
+    tma_prefetch_desc(&tmk);
+    tma_prefetch_desc(&tmv);
+    int s = 0;
+    long long i = 0;
+    bool ok = true;
+    for (long long t = t_lo; t < t_hi; ++t, ++i) {
+      while (prefix[s + 1] <= t) ++s;
+      const int j = (int)(t - prefix[s]);
+      const int st = (int)(i % STAGES);
+      const uint32_t ph = (uint32_t)((i / STAGES) & 1);
+      if (!mbar_wait(&empty[st], ph ^ 1u, p.err, kDevErrWaitEmpty)) {
+        ok = false;
+        break;
+      }
+      uint8_t* stage = smem + st * Cfg::STAGE_BYTES;
+      mbar_arrive_expect_tx(&full[st], Cfg::STAGE_BYTES);
+      const int y = (int)(p.row0 + (long long)s * p.max_ctx + (long long)j * TILE);
+#pragma unroll
+      for (int g = 0; g < NKV; ++g) {
+        tma_load_2d(stage + g * Cfg::BOX, &tmk, &full[st], 64 * g, y);
+        tma_load_2d(stage + (NKV + g) * Cfg::BOX, &tmv, &full[st], 64 * g, y);
+      }
+    }
+    // Drain: every issued load must land before the CTA may exit.
+    const long long issued = i;
+    for (long long k = issued - STAGES; k < issued; ++k) {
+      if (k < 0) continue;
+      const int st = (int)(k % STAGES);
+      mbar_wait(&full[st], (uint32_t)((k / STAGES) & 1), p.err, kDevErrWaitFull);
+    }
+    (void)ok;
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int g = warp >> 1, hf = warp & 1;
+  const int r = lane >> 2, qd = lane & 3;  // mma row (query head) / quad lane
+  const bool row_ok = r < p.group;
+  const float sl2 = p.scale_log2;
+  float* my_mrg = mrg + warp * Cfg::MRG_FLOATS;
+
+  uint32_t qa[4][4];                 // q A-fragments, 4 k-steps of 16 dims
+  float o[8][4];                     // O accumulators, 8 chunks of 8 dims
+  float m_run = kNegBig, l_run = 0.f;
+  bool failed = false;
+
+  int s = 0;
+  long long i = 0;
+  long long seg_lo = t_lo;
+  for (long long t = t_lo; t < t_hi; ++t, ++i) {
+    const bool new_seg = (t == seg_lo) || (t == prefix[s + 1]);
+    while (prefix[s + 1] <= t) ++s;
+    if (new_seg) {
+      seg_lo = t;
+      // Load this warp's query heads and split them into bf16 hi + lo.
+      const float* qh = p.q + ((size_t)s * p.n_head + (size_t)g * p.group + (row_ok ? r : 0)) * 64;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          float2 v = make_float2(0.f, 0.f);
+          if (row_ok) v = *reinterpret_cast<const float2*>(qh + 16 * kk + 8 * half + 2 * qd);
+          float h0, l0, h1, l1;
+          split_bf16(v.x, h0, l0);
+          split_bf16(v.y, h1, l1);
+          qa[kk][2 * half] = pack_bf16x2(h0, h1);
+          qa[kk][2 * half + 1] = pack_bf16x2(l0, l1);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) o[c][0] = o[c][1] = o[c][2] = o[c][3] = 0.f;
+      m_run = kNegBig;
+      l_run = 0.f;
+    }
+    const int j = (int)(t - prefix[s]);
+    const int n_loc = local_rows(past_of(p, s), p.shard_start, p.max_ctx);
+    const int tile_valid = min(TILE, n_loc - j * TILE);
+    const int my_valid = max(0, min(32, tile_valid - 32 * hf));
+
+    const int st = (int)(i % STAGES);
+    const uint32_t ph = (uint32_t)((i / STAGES) & 1);
+    if (!failed && !mbar_wait(&full[st], ph, p.err, kDevErrWaitFull)) failed = true;
+
+    if (!failed && my_valid > 0) {
+      uint8_t* kbox = smem + st * Cfg::STAGE_BYTES + g * Cfg::BOX;
+      uint8_t* vbox = smem + st * Cfg::STAGE_BYTES + (NKV + g) * Cfg::BOX;
+      const int rb = 32 * hf;  // first row of this warp in the tile
+      if (my_valid < 32) {
+        // Rows past the attended window may hold anything; zero their V so
+        // that 0-weighted rows add exactly zero.
+        for (int e = lane; e < (32 - my_valid) * 8; e += 32) {
+          const int row = rb + my_valid + (e >> 3);
+          reinterpret_cast<uint4*>(vbox + row * 128)[e & 7] = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
+      const uint32_t kb = smem_u32(kbox), vb = smem_u32(vbox);
+
+      // S = q . K^T for 32 rows: 4 n-tiles of 8 rows.
+      float sc[4][2];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const int row = rb + 8 * nt + (lane & 7);
+#pragma unroll
+        for (int kq = 0; kq < 2; ++kq) {
+          const int chunk = 4 * kq + (lane >> 3);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(kb + row * 128 + ((chunk ^ (row & 7)) << 4), b0, b1, b2, b3);
+          mma_bf16_16816(acc, qa[2 * kq], b0, b1);
+          mma_bf16_16816(acc, qa[2 * kq + 1], b2, b3);
+        }
+        const int c0 = 8 * nt + 2 * qd;
+        sc[nt][0] = (c0 < my_valid) ? (acc[0] + acc[2]) * sl2 : -INFINITY;
+        sc[nt][1] = (c0 + 1 < my_valid) ? (acc[1] + acc[3]) * sl2 : -INFINITY;
+      }
+      // Online softmax over the 32 rows (per query head = per quad).
+      float mx = fmaxf(fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1])),
+                       fmaxf(fmaxf(sc[2][0], sc[2][1]), fmaxf(sc[3][0], sc[3][1])));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_run, mx);
+      const float alpha = ex2(m_run - m_new);
+      m_run = m_new;
+      float pr[4][2];
+      float lsum = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        pr[nt][0] = ex2(sc[nt][0] - m_new);
+        pr[nt][1] = ex2(sc[nt][1] - m_new);
+        lsum += pr[nt][0] + pr[nt][1];
+      }
+      l_run = l_run * alpha + lsum;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        o[c][0] *= alpha; o[c][1] *= alpha; o[c][2] *= alpha; o[c][3] *= alpha;
+      }
+      // O += P . V, two k-steps of 16 rows.
+#pragma unroll
+      for (int kp = 0; kp < 2; ++kp) {
+        uint32_t pa[4];
+        float h0, l0, h1, l1;
+        split_bf16(pr[2 * kp][0], h0, l0);
+        split_bf16(pr[2 * kp][1], h1, l1);
+        pa[0] = pack_bf16x2(h0, h1);
+        pa[1] = pack_bf16x2(l0, l1);
+        split_bf16(pr[2 * kp + 1][0], h0, l0);
+        split_bf16(pr[2 * kp + 1][1], h1, l1);
+        pa[2] = pack_bf16x2(h0, h1);
+        pa[3] = pack_bf16x2(l0, l1);
+        const int row = rb + 16 * kp + ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+        for (int cp = 0; cp < 4; ++cp) {
+          const int chunk = 2 * cp + (lane >> 4);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4_trans(vb + row * 128 + ((chunk ^ (row & 7)) << 4), b0, b1, b2, b3);
+          mma_bf16_16816(o[2 * cp], pa, b0, b1);
+          mma_bf16_16816(o[2 * cp + 1], pa, b2, b3);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+
+    // Segment end: merge the two warps of each KV head and write out.
+    const bool seg_end = (t + 1 == t_hi) || (t + 1 == prefix[s + 1]);
+    if (seg_end) {
+      float l_tot = l_run;
+      l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 1);
+      l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 2);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const int d = 8 * c + 2 * qd;
+        my_mrg[r * 64 + d] = o[c][0] + o[c][2];
+        my_mrg[r * 64 + d + 1] = o[c][1] + o[c][3];
+      }
+      if (qd == 0) {
+        my_mrg[512 + r] = m_run;
+        my_mrg[520 + r] = l_tot;
+      }
+      consumer_bar_sync(32 * Cfg::CWARPS);
+      if (hf == 0 && row_ok) {
+        const float* other = my_mrg + Cfg::MRG_FLOATS;
+        const float m0 = my_mrg[512 + r], m1 = other[512 + r];
+        const float M = fmaxf(m0, m1);
+        const float w0 = ex2(m0 - M), w1 = ex2(m1 - M);
+        const float L = my_mrg[520 + r] * w0 + other[520 + r] * w1;
+        const SegDest dst = segment_dest(p, s, seg_lo, t + 1, t_lo, prefix, cta);
+        const int h = g * p.group + r;
+        const float inv = dst.normalise ? 1.f / L : 1.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int d = 8 * c + 2 * qd;
+          float2 v;
+          v.x = (my_mrg[r * 64 + d] * w0 + other[r * 64 + d] * w1) * inv;
+          v.y = (my_mrg[r * 64 + d + 1] * w0 + other[r * 64 + d + 1] * w1) * inv;
+          *reinterpret_cast<float2*>(dst.ptr + h * 64 + d) = v;
+        }
+        if (!dst.normalise && qd == 0) {
+          dst.ptr[p.n_head * 64 + h] = M;
+          dst.ptr[p.n_head * 64 + p.n_head + h] = L;
+        }
+      }
+      consumer_bar_sync(32 * Cfg::CWARPS);
+    }
+  }
+}
+
+// ============================================================ CUDA-core path
+
+constexpr int GEN_TILE = 32;
+constexpr int GEN_THREADS = 128;
+constexpr int GEN_MAX_OUT = 32;  // outputs per thread: n_head*head_dim <= 4096
+
+struct GenLayout {
+  int q_off, k_off, v_off, p_off, ml_off, wt_off, pre_off, total;
+  int row_pad;
+};
+
+__host__ __device__ inline GenLayout gen_layout(int B, int n_head, int n_kv,
+                                                int hd) {
+  GenLayout L;
+  const int kdim = n_kv * hd;
+  L.row_pad = kdim + 1;
+  int off = 0;
+  L.q_off = off;  off += n_head * hd;
+  L.k_off = off;  off += GEN_TILE * L.row_pad;
+  L.v_off = off;  off += GEN_TILE * L.row_pad;
+  L.p_off = off;  off += n_head * GEN_TILE;
+  L.ml_off = off; off += 3 * n_head;  // m, l, alpha
+  L.wt_off = off; off += 32;
+  L.pre_off = off; off += B + 1;
+  L.total = off * 4;
+  return L;
+}
+
+size_t decode_generic_smem(int B, int n_head, int n_kv, int hd) {
+  return (size_t)gen_layout(B, n_head, n_kv, hd).total;
+}
+
+template <typename Elem>
+__global__ void __launch_bounds__(GEN_THREADS) decode_generic_kernel(const DecodeParams p) {
+  extern __shared__ float gsm[];
+  const GenLayout Ly = gen_layout(p.B, p.n_head, p.n_kv, p.head_dim);
+  float* q_s = gsm + Ly.q_off;
+  float* k_s = gsm + Ly.k_off;
+  float* v_s = gsm + Ly.v_off;
+  float* p_s = gsm + Ly.p_off;
+  float* m_s = gsm + Ly.ml_off;
+  float* l_s = m_s + p.n_head;
+  float* a_s = l_s + p.n_head;
+  int* warp_tot = reinterpret_cast<int*>(gsm + Ly.wt_off);
+  int* prefix = reinterpret_cast<int*>(gsm + Ly.pre_off);
+
+  build_tile_prefix(p, GEN_TILE, prefix, warp_tot);
+  const long long T = prefix[p.B];
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i <= p.B; i += blockDim.x) p.sched[i] = prefix[i];
+  const int G = gridDim.x, cta = blockIdx.x;
+  const long long t_lo = cta_tile_lo(cta, G, T), t_hi = cta_tile_lo(cta + 1, G, T);
+  if (t_lo >= t_hi) return;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int hd = p.head_dim, kdim = p.n_kv * hd, qdim = p.n_head * hd;
+  const int rp = Ly.row_pad;
+  const Elem* kbase = static_cast<const Elem*>(p.k);
+  const Elem* vbase = static_cast<const Elem*>(p.v);
+
+  float acc[GEN_MAX_OUT];
+  int s = 0;
+  long long seg_lo = t_lo;
+  for (long long t = t_lo; t < t_hi; ++t) {
+    const bool new_seg = (t == seg_lo) || (t == prefix[s + 1]);
+    while (prefix[s + 1] <= t) ++s;
+    if (new_seg) {
+      seg_lo = t;
+      for (int i = tid; i < qdim; i += GEN_THREADS) q_s[i] = p.q[(size_t)s * qdim + i];
+      for (int h = tid; h < p.n_head; h += GEN_THREADS) {
+        m_s[h] = -INFINITY;
+        l_s[h] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < GEN_MAX_OUT; ++i) acc[i] = 0.f;
+    }
+    const int j = (int)(t - prefix[s]);
+    const int n_loc = local_rows(past_of(p, s), p.shard_start, p.max_ctx);
+    const int nv = min(GEN_TILE, n_loc - j * GEN_TILE);
+    const size_t row0 = (size_t)s * p.max_ctx + (size_t)j * GEN_TILE;
+    // Stage the valid rows of K and V as fp32 with a padded row stride.
+    for (int e = tid; e < nv * kdim; e += GEN_THREADS) {
+      const int rr = e / kdim, cc = e - rr * kdim;
+      k_s[rr * rp + cc] = to_f32(kbase[(row0 + rr) * kdim + cc]);
+      v_s[rr * rp + cc] = to_f32(vbase[(row0 + rr) * kdim + cc]);
+    }
+    __syncthreads();
+    // Scores and the online-softmax update: warp w owns heads w, w+4, ...
+    for (int h = warp; h < p.n_head; h += GEN_THREADS / 32) {
+      const int kv = h / p.group;
+      float sc = -INFINITY;
+      if (lane < nv) {
+        const float* qh = q_s + h * hd;
+        const float* kr = k_s + lane * rp + kv * hd;
+        float a = 0.f;
+        for (int d = 0; d < hd; ++d) a = fmaf(qh[d], kr[d], a);
+        sc = a * p.scale_log2;
+      }
+      const float mx = warp_max(sc);
+      const float m_old = m_s[h];
+      const float m_new = fmaxf(m_old, mx);
+      const float e = ex2(sc - m_new);
+      const float alpha = ex2(m_old - m_new);
+      const float sum = warp_sum(e);
+      p_s[h * GEN_TILE + lane] = e;
+      __syncwarp();
+      if (lane == 0) {
+        a_s[h] = alpha;
+        l_s[h] = l_s[h] * alpha + sum;
+        m_s[h] = m_new;
+      }
+    }
+    __syncthreads();
+    // O = O*alpha + P.V for this thread's outputs.
+#pragma unroll
+    for (int i = 0; i < GEN_MAX_OUT; ++i) {
+      const int idx = tid + i * GEN_THREADS;
+      if (idx < qdim) {
+        const int h = idx / hd, d = idx - h * hd;
+        const int col = (h / p.group) * hd + d;
+        float a = acc[i] * a_s[h];
+        const float* ph = p_s + h * GEN_TILE;
+        for (int r2 = 0; r2 < nv; ++r2) a = fmaf(ph[r2], v_s[r2 * rp + col], a);
+        acc[i] = a;
+      }
+    }
+    const bool seg_end = (t + 1 == t_hi) || (t + 1 == prefix[s + 1]);
+    if (seg_end) {
+      const SegDest dst = segment_dest(p, s, seg_lo, t + 1, t_lo, prefix, cta);
+#pragma unroll
+      for (int i = 0; i < GEN_MAX_OUT; ++i) {
+        const int idx = tid + i * GEN_THREADS;
+        if (idx < qdim) {
+          const int h = idx / hd;
+          dst.ptr[idx] = dst.normalise ? acc[i] / l_s[h] : acc[i];
+        }
+      }
+      if (!dst.normalise)
+        for (int h = tid; h < p.n_head; h += GEN_THREADS) {
+          dst.ptr[qdim + h] = m_s[h];
+          dst.ptr[qdim + p.n_head + h] = l_s[h];
+        }
+    }
+    __syncthreads();
+  }
+}
+
+// ================================================================== merges
+
+__global__ void __launch_bounds__(128) merge_kernel(const MergeParams p) {
+  const int s = blockIdx.x;
+  const int t0 = p.sched[s], t1 = p.sched[s + 1];
+  const long long T = p.sched[p.B];
+  const int hd = p.head_dim, qdim = p.n_head * hd;
+  const int rf = record_floats(p.n_head, hd);
+  if (t1 == t0) {
+    if (p.mode == 1) {
+      float* rec = p.records + (size_t)s * rf;
+      for (int i = threadIdx.x; i < rf; i += blockDim.x)
+        rec[i] = (i >= qdim && i < qdim + p.n_head) ? kNegBig : 0.f;
+    }
+    return;
+  }
+  const int c1 = cta_of_tile(t0, p.G, T), c2 = cta_of_tile(t1 - 1, p.G, T);
+  if (c1 == c2) return;
+  const int first_slot = 2 * c1 + (cta_tile_lo(c1, p.G, T) == t0 ? 0 : 1);
+  const int n_parts = 1 + (c2 - c1);
+  for (int idx = threadIdx.x; idx < qdim; idx += blockDim.x) {
+    const int h = idx / hd;
+    float M = kNegBig;
+    for (int k = 0; k < n_parts; ++k) {
+      const int slot = k == 0 ? first_slot : 2 * (c1 + k);
+      M = fmaxf(M, p.part[(size_t)slot * rf + qdim + h]);
+    }
+    float O = 0.f, L = 0.f;
+    for (int k = 0; k < n_parts; ++k) {
+      const int slot = k == 0 ? first_slot : 2 * (c1 + k);
+      const float* rec = p.part + (size_t)slot * rf;
+      const float w = ex2(rec[qdim + h] - M);
+      O = fmaf(rec[idx], w, O);
+      L = fmaf(rec[qdim + p.n_head + h], w, L);
+    }
+    if (p.mode == 0) {
+      p.out[(size_t)s * qdim + idx] = O / L;
+    } else {
+      float* rec = p.records + (size_t)s * rf;
+      rec[idx] = O;
+      if (idx - h * hd == 0) {
+        rec[qdim + h] = M;
+        rec[qdim + p.n_head + h] = L;
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(128) gather_merge_kernel(const GatherMergeParams p) {
+  const int s = blockIdx.x;
+  const int hd = p.head_dim, qdim = p.n_head * hd;
+  const int rf = record_floats(p.n_head, hd);
+  for (int idx = threadIdx.x; idx < qdim; idx += blockDim.x) {
+    const int h = idx / hd;
+    float M = kNegBig;
+    for (int r = 0; r < p.world; ++r)
+      M = fmaxf(M, p.records[((size_t)r * p.B + s) * rf + qdim + h]);
+    float O = 0.f, L = 0.f;
+    for (int r = 0; r < p.world; ++r) {
+      const float* rec = p.records + ((size_t)r * p.B + s) * rf;
+      const float w = ex2(rec[qdim + h] - M);
+      O = fmaf(rec[idx], w, O);
+      L = fmaf(rec[qdim + p.n_head + h], w, L);
+    }
+    p.out[(size_t)s * qdim + idx] = O / L;
+  }
+}
+
+// ============================================================ elementwise
+
+// elem_op (kernel_elem.metal:6-21): op 0 data += aux, op 2 data = aux.
+__global__ void elem_kernel(int op, float* data, const float* aux, int dim) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= dim) return;
+  if (op == 0)
+    data[i] = __fadd_rn(data[i], aux[i]);
+  else
+    data[i] = aux[i];
+}
+
+// Synthetic N(0,1) values: the splitmix64 + Box-Muller stream of the oracle
+// (draw k is splitmix64 of seed + (k+1)*gamma), evaluated with the device's
+// double-precision libm and rounded to the cache type.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+
+__global__ void fill_normal_kernel(void* out, size_t n, int dtype, uint64_t seed) {
+  const uint64_t gamma = 0x9E3779B97F4A7C15ULL;
+  const size_t pairs = (n + 1) / 2;
+  for (size_t k = blockIdx.x * (size_t)blockDim.x + threadIdx.x; k < pairs;
+       k += (size_t)gridDim.x * blockDim.x) {
+    const uint64_t a = mix64(seed + (2 * k + 1) * gamma);
+    const uint64_t b = mix64(seed + (2 * k + 2) * gamma);
+    const double u1 = ((double)(a >> 11) + 1.0) * (1.0 / 9007199254740992.0);
+    const double u2 = (double)(b >> 11) * (1.0 / 9007199254740992.0);
+    const double rr = sqrt(-2.0 * log(u1));
+    const double ang = 6.283185307179586476925286766559 * u2;
+    const float z0 = (float)(rr * cos(ang)), z1 = (float)(rr * sin(ang));
+    const size_t i0 = 2 * k;
+    if (dtype == 0) {
+      float* o = static_cast<float*>(out);
+      o[i0] = z0;
+      if (i0 + 1 < n) o[i0 + 1] = z1;
+    } else {
+      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+      o[i0] = __float2bfloat16_rn(z0);
+      if (i0 + 1 < n) o[i0 + 1] = __float2bfloat16_rn(z1);
+    }
+  }
+}
+
+// f32 -> cache type (RNE for bf16), used to upload rows.
+__global__ void convert_rows_kernel(void* dst, const float* src, size_t n, int dtype) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    if (dtype == 0)
+      static_cast<float*>(dst)[i] = src[i];
+    else
+      static_cast<__nv_bfloat16*>(dst)[i] = __float2bfloat16_rn(src[i]);
+  }
+}
+
+// ================================================================ launchers
+
+cudaError_t launch_rope(const RopeParams& p, cudaStream_t st) {
+  if (p.B <= 0) return cudaSuccess;
+  rope_cache_write_kernel<<<p.B, 128, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <int NKV>
+static cudaError_t launch_mma_nkv(const CUtensorMap& tk, const CUtensorMap& tv,
+                                  const DecodeParams& p, int grid,
+                                  cudaStream_t st) {
+  const size_t smem = MmaCfg<NKV>::smem_bytes(p.B);
+  auto kfn = decode_mma_kernel<NKV>;
+  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  kfn<<<grid, MmaCfg<NKV>::THREADS, smem, st>>>(tk, tv, p);
+  return cudaGetLastError();
+}
+
+size_t decode_mma_smem(int nkv, int B) {
+  switch (nkv) {
+    case 1: return MmaCfg<1>::smem_bytes(B);
+    case 2: return MmaCfg<2>::smem_bytes(B);
+    case 4: return MmaCfg<4>::smem_bytes(B);
+    default: return 0;
+  }
+}
+
+cudaError_t launch_decode_mma(const CUtensorMap& tk, const CUtensorMap& tv,
+                              const DecodeParams& p, int grid, cudaStream_t st) {
+  switch (p.n_kv) {
+    case 1: return launch_mma_nkv<1>(tk, tv, p, grid, st);
+    case 2: return launch_mma_nkv<2>(tk, tv, p, grid, st);
+    case 4: return launch_mma_nkv<4>(tk, tv, p, grid, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_decode_generic(const DecodeParams& p, int dtype, int grid,
+                                  cudaStream_t st) {
+  const size_t smem = decode_generic_smem(p.B, p.n_head, p.n_kv, p.head_dim);
+  cudaError_t e;
+  if (dtype == 0) {
+    e = cudaFuncSetAttribute(decode_generic_kernel<float>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    decode_generic_kernel<float><<<grid, GEN_THREADS, smem, st>>>(p);
+  } else {
+    e = cudaFuncSetAttribute(decode_generic_kernel<__nv_bfloat16>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    decode_generic_kernel<__nv_bfloat16><<<grid, GEN_THREADS, smem, st>>>(p);
+  }
+  return cudaGetLastError();
+}
+
+int decode_generic_blocks_per_sm(int dtype, size_t smem) {
+  int n = 0;
+  if (dtype == 0) {
+    cudaFuncSetAttribute(decode_generic_kernel<float>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_generic_kernel<float>,
+                                                  GEN_THREADS, smem);
+  } else {
+    cudaFuncSetAttribute(decode_generic_kernel<__nv_bfloat16>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_generic_kernel<__nv_bfloat16>,
+                                                  GEN_THREADS, smem);
+  }
+  cudaGetLastError();
+  return n < 1 ? 1 : n;
+}
+
+cudaError_t launch_merge(const MergeParams& p, cudaStream_t st) {
+  if (p.B <= 0) return cudaSuccess;
+  merge_kernel<<<p.B, 128, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_merge(const GatherMergeParams& p, cudaStream_t st) {
+  if (p.B <= 0) return cudaSuccess;
+  gather_merge_kernel<<<p.B, 128, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_elem(int op, float* data, const float* aux, int dim,
+                        cudaStream_t st) {
+  if (dim <= 0) return cudaSuccess;
+  elem_kernel<<<(dim + 255) / 256, 256, 0, st>>>(op, data, aux, dim);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fill_normal(void* out, size_t n, int dtype, uint64_t seed,
+                               int num_sms, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  fill_normal_kernel<<<num_sms * 8, 256, 0, st>>>(out, n, dtype, seed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_convert_rows(void* dst, const float* src, size_t n, int dtype,
+                                int num_sms, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  convert_rows_kernel<<<num_sms * 4, 256, 0, st>>>(dst, src, n, dtype);
+  return cudaGetLastError();
+}
+
+int mma_threads(int nkv) { return 32 * (2 * nkv + 1); }
+
+}  // namespace tg

@@ -1,0 +1,39 @@
+// tg_kernels.h -- host-side launchers of the kernels in tg_kernels.cu.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "tg_shared.h"
+
+namespace tg {
+
+cudaError_t launch_rope(const RopeParams& p, cudaStream_t st);
+
+// Tensor-core split-KV decode over a bf16 cache with head_dim 64, n_kv in
+// {1, 2, 4} and at most 8 query heads per KV head.  tk / tv are 2-D TMA
+// maps of the whole cache ({n_kv*64, rows}, box {64, 64}, 128B swizzle).
+cudaError_t launch_decode_mma(const CUtensorMap& tk, const CUtensorMap& tv,
+                              const DecodeParams& p, int grid, cudaStream_t st);
+size_t decode_mma_smem(int nkv, int B);
+int mma_threads(int nkv);
+
+// CUDA-core decode (fp32 or bf16 cache, any head_dim / group the limits in
+// tg_backend.cu allow).
+cudaError_t launch_decode_generic(const DecodeParams& p, int dtype, int grid,
+                                  cudaStream_t st);
+size_t decode_generic_smem(int B, int n_head, int n_kv, int hd);
+int decode_generic_blocks_per_sm(int dtype, size_t smem);
+
+cudaError_t launch_merge(const MergeParams& p, cudaStream_t st);
+cudaError_t launch_gather_merge(const GatherMergeParams& p, cudaStream_t st);
+cudaError_t launch_elem(int op, float* data, const float* aux, int dim,
+                        cudaStream_t st);
+cudaError_t launch_fill_normal(void* out, size_t n, int dtype, uint64_t seed,
+                               int num_sms, cudaStream_t st);
+cudaError_t launch_convert_rows(void* dst, const float* src, size_t n,
+                                int dtype, int num_sms, cudaStream_t st);
+
+}  // namespace tg

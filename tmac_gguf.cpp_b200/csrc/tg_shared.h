@@ -1,0 +1,117 @@
+// tg_shared.h -- structures and index arithmetic shared by host and device
+// code of the decode-attention path.
+//
+// Work decomposition ("flat tile space").  For one layer, sequence s
+// attends over n_local(s) cache rows of this shard; they form
+// ceil(n_local(s) / TILE) tiles.  The tiles of all sequences are laid end
+// to end (tile_prefix[s] .. tile_prefix[s+1]) and CTA c of a G-CTA grid
+// takes the contiguous range [c*T/G, (c+1)*T/G), T = tile_prefix[B].  A
+// CTA's range therefore covers at most two partial sequences (its first and
+// its last segment); every sequence in between is complete.  A complete
+// segment is finished by its CTA; a partial one leaves a partial softmax
+// record in slot 2c (first segment) or 2c+1 (last segment), and the merge
+// kernel combines the records of each split sequence.
+#pragma once
+
+#include <stdint.h>
+
+#ifdef __CUDACC__
+#define TG_HD __host__ __device__ __forceinline__
+#else
+#define TG_HD inline
+#endif
+
+namespace tg {
+
+// Device error word values (first error wins).
+enum DeviceError : int {
+  kDevErrNone = 0,
+  kDevErrWaitFull = 0x101,   // consumer timed out waiting for a TMA tile
+  kDevErrWaitEmpty = 0x102,  // producer timed out waiting for a free stage
+  kDevErrBadPos = 0x103,     // position outside the RoPE table / cache
+  kDevErrTooManySeqs = 0x104,
+};
+
+constexpr float kNegBig = -1.0e30f;  // finite "minus infinity" for m
+
+// Softmax record of one sequence (or one segment of it), all heads:
+//   o[n_head][head_dim]  un-normalised sum of 2^(s*log2e - m) * V
+//   m[n_head]            running max in log2 units (score * log2(e))
+//   l[n_head]            sum of 2^(s*log2e - m)
+TG_HD int record_floats(int n_head, int head_dim) {
+  return n_head * (head_dim + 2);
+}
+
+// CTA that owns flat tile t (G CTAs, T tiles): the largest c with
+// floor(c*T/G) <= t.
+TG_HD int cta_of_tile(long long t, int G, long long T) {
+  return (int)(((t + 1) * (long long)G - 1) / T);
+}
+
+TG_HD long long cta_tile_lo(int c, int G, long long T) {
+  return (long long)c * T / G;
+}
+
+// Number of cache rows of this shard that sequence s attends over, given
+// the global position of its current token (n_pos = past_len + 1 rows in
+// total, the shard holds global rows [shard_start, shard_start + max_ctx)).
+TG_HD int local_rows(int past_len, int shard_start, int max_ctx) {
+  long long n = (long long)past_len + 1 - shard_start;
+  if (n < 0) n = 0;
+  if (n > max_ctx) n = max_ctx;
+  return (int)n;
+}
+
+struct DecodeParams {
+  const float* q;        // [B][n_head*head_dim], already rotated
+  float* out;            // [B][n_head*head_dim] normalised output (mode 0)
+  float* records;        // [B][record_floats] per-sequence records (mode 1)
+  const int* past_len;   // [B] global position of each sequence's token
+  const void* k;         // layer cache base, [B][max_ctx][n_kv*head_dim]
+  const void* v;
+  float* part;           // [2*G][record_floats] partial records
+  int* sched;            // [B+1] tile prefix written by CTA 0
+  int* err;              // device error word
+  long long row0;        // TMA row of (this layer, sequence 0, row 0)
+  int B, n_head, n_kv, head_dim, group;
+  int max_ctx, shard_start;
+  float scale_log2;      // log2(e) / sqrt(head_dim)
+  int mode;              // 0: normalised output, 1: records (split-KV)
+  int past_len_scalar;   // used for every sequence when past_len == null
+};
+
+TG_HD int past_of(const DecodeParams& p, int s) {
+  return p.past_len ? p.past_len[s] : p.past_len_scalar;
+}
+
+struct MergeParams {
+  const float* part;     // partial records of the decode launch
+  const int* sched;      // [B+1] tile prefix of that launch
+  float* out;            // mode 0
+  float* records;        // mode 1
+  int B, n_head, head_dim, G, mode;
+};
+
+// Final merge of per-rank records after the all-gather (split-KV).
+struct GatherMergeParams {
+  const float* records;  // [world][B][record_floats]
+  float* out;            // [B][n_head*head_dim]
+  int world, B, n_head, head_dim;
+};
+
+struct RopeParams {
+  float* q;              // [B][n_head*head_dim], rotated in place (or null)
+  float* k;              // [B][n_kv*head_dim], rotated in place (or null)
+  const float* v;        // [B][n_kv*head_dim] (or null)
+  const int* pos;        // [B] global positions (device) or null
+  int pos_scalar;        // used when pos == null
+  const float* cs;       // RoPE table [table_len][head_dim/2][2] = cos, sin
+  int table_len;
+  void* k_cache;         // layer cache base (null: no cache-write)
+  void* v_cache;
+  int B, n_head, n_kv, head_dim;
+  int max_ctx, shard_start, dtype;  // dtype: 0 f32, 1 bf16
+  int* err;
+};
+
+}  // namespace tg
