@@ -258,8 +258,12 @@ def main():
     ap.add_argument("--impl", default="tg", choices=["tg", "reference"])
     ap.add_argument("--workload", default="longctx", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the layers per step (small profiling cases)")
     args = ap.parse_args()
-    wl = WORKLOADS[args.workload]
+    wl = dict(WORKLOADS[args.workload])
+    if args.layers > 0:
+        wl["layers"] = args.layers
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -324,8 +328,15 @@ def main():
         return float(t.item())
 
     # ---- device-resident timed region -----------------------------------
+    # One decode step (all layers) is captured into a CUDA graph after a
+    # first direct run has sized the scratch buffers; the graph is replayed.
+    step(q, kn, vn, pos_d, out)
+    be.synchronize()
+    be.graph_begin()
+    step(q, kn, vn, pos_d, out)
+    graph = be.graph_end()
     for _ in range(args.warmup):
-        step(q, kn, vn, pos_d, out)
+        graph.launch()
     be.synchronize()
     sampler = ClockSampler(set(range(world))) if local == 0 else None
     time.sleep(0.3 if sampler else 0)
@@ -335,7 +346,7 @@ def main():
     t_wall0 = time.time()
     e0.record(stream)
     for _ in range(args.steps):
-        step(q, kn, vn, pos_d, out)
+        graph.launch()
     e1.record(stream)
     be.synchronize()
     t_wall1 = time.time()
@@ -349,11 +360,20 @@ def main():
     value = bytes_step / (ms_step * 1e-3) / 1e9
 
     # ---- roofline: decode-kernel launches timed with CUDA events -----------
+    # A second graph of the same step carries event records around every
+    # decode-attention launch; each replay re-records them on the stream.
     be.profile_enable(True)
-    for _ in range(max(3, min(args.steps, 50))):
-        step(q, kn, vn, pos_d, out)
-    kms, kn_launch = be.profile_read()
+    be.graph_begin()
+    step(q, kn, vn, pos_d, out)
+    gprof = be.graph_end()
     be.profile_enable(False)
+    kms, kn_launch = 0.0, 0
+    for _ in range(max(3, min(args.steps, 50))):
+        gprof.launch()
+        ms_i, n_i = be.profile_read()
+        kms += ms_i
+        kn_launch += n_i
+    gprof.destroy()
     k_bytes = kernel_bytes_launch(wl, pos, shard_start, shard_len, split)
     k_avg_ms = kms / max(kn_launch, 1)
     hbm_peak, peak_kind = peaks()
@@ -426,6 +446,7 @@ def main():
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    graph.destroy()
     kv.destroy()
     if split:
         be.comm_destroy()

@@ -17,7 +17,11 @@
  *  - A tg_context binds one CUDA device and one stream.  It is not
  *    thread-safe: use one context per host thread.
  *  - Pointers may be CUDA device (or managed) pointers, used in place, or
- *    host pointers, which the library stages through device memory.  For
+ *    host pointers, which the library stages through device memory.  A call
+ *    that reads or writes host memory returns when its host outputs are
+ *    valid (or, inside a batch, at tg_batch_end); a call on device pointers
+ *    only is stream-ordered and asynchronous, and errors that kernels
+ *    detect surface at the next tg_synchronize or tg_batch_end.  For
  *    the reference-compatible ops (tg_rope_op, tg_elem_op, tg_attention_op)
  *    host arrays get persistent device mirrors, like the reference's buffer
  *    wrapper cache (metal_backend.hpp:44-65); results in host arrays are
@@ -66,6 +70,7 @@ extern "C" {
 
 typedef struct tg_context tg_context;
 typedef struct tg_kv_cache tg_kv_cache;
+typedef struct tg_graph tg_graph;
 
 TG_API const char* tg_status_string(int status);
 /* Message of the last failing call on this thread ("" if none). */
@@ -95,6 +100,18 @@ TG_API int tg_batch_begin(tg_context* ctx);
 TG_API int tg_batch_end(tg_context* ctx);
 /* Wait for the stream and report device errors (no batch semantics). */
 TG_API int tg_synchronize(tg_context* ctx);
+
+/* CUDA-graph capture of a sequence of calls on device pointers -- the
+ * B200 counterpart of encoding a whole forward pass into one Metal command
+ * buffer (tmac_gguf.cpp:1468-1515).  Between tg_graph_begin and
+ * tg_graph_end, calls are recorded instead of run; host pointers are
+ * rejected and scratch must already be sized (run the same calls once
+ * before capturing).  NCCL collectives of split-KV calls are captured too.
+ * A graph replays its recorded kernels on the context stream. */
+TG_API int tg_graph_begin(tg_context* ctx);
+TG_API int tg_graph_end(tg_context* ctx, tg_graph** out);
+TG_API int tg_graph_launch(tg_context* ctx, tg_graph* g);
+TG_API int tg_graph_destroy(tg_graph* g);
 
 /* Device mirror of a host array, the explicit form of wrap_buffer
  * (metal_backend.hpp:52-65).  TG_REGION_DEVICE_OWNED marks arrays only GPU
@@ -234,9 +251,11 @@ TG_API int tg_decode_layer_splitkv(tg_context* ctx, tg_kv_cache* shard, int laye
 /* Kernel launches this context has issued since creation (all kinds). */
 TG_API int tg_launch_count(tg_context* ctx, long long* out);
 /* CUDA-event timing of every decode-attention kernel launch on the context
- * stream (events recorded just before and after each launch).  Enabling
- * resets the record; tg_profile_read waits for the stream and returns the
- * summed kernel time and the number of timed launches since the last read. */
+ * stream (events recorded just before and after each launch, also into a
+ * graph being captured, so that replays re-record them).  Enabling resets
+ * the record; tg_profile_read waits for the stream and returns the summed
+ * time of the recorded launches (for a graph: of its latest replay) and
+ * their number. */
 TG_API int tg_profile_enable(tg_context* ctx, int on);
 TG_API int tg_profile_read(tg_context* ctx, double* total_ms, long long* launches);
 /* 1 if the next batched decode on `kv` uses the tensor-core kernel. */

@@ -26,9 +26,11 @@ def maxabs(a, b):
 
 
 def run_batch(tg, backend, cases, positions, bf16, seed=11, max_ctx=None,
-              layer=0, n_layers=1):
+              layer=0, n_layers=1, stream0=False):
     """Fill a cache with each sequence's rows 0..pos-1, run one decode step
-    through tg_decode_layer and return (gpu outputs, oracle results, kv)."""
+    through tg_decode_layer and return (gpu outputs, oracle results, kv).
+    Sequence i draws its inputs from stream i (stream 0 for all when
+    stream0, as the golden fixtures do)."""
     B = len(positions)
     max_ctx = max_ctx or (max(positions) + 1)
     kv = tg.KVCache(backend, n_layers, B, max_ctx,
@@ -38,11 +40,12 @@ def run_batch(tg, backend, cases, positions, bf16, seed=11, max_ctx=None,
     V = np.zeros((B, cases.KD), np.float32)
     refs = []
     for i, pos in enumerate(positions):
-        q, k_new, v_new, kc, vc = cases.decode_inputs(seed, pos, bf16, seq=i, layer=layer)
+        sq = 0 if stream0 else i
+        q, k_new, v_new, kc, vc = cases.decode_inputs(seed, pos, bf16, seq=sq, layer=layer)
         if pos > 0:
             kv.write_rows(layer, i, 0, kc[:pos], vc[:pos])
         Q[i], K[i], V[i] = q, k_new, v_new
-        refs.append(cases.oracle_decode(seed, pos, bf16, seq=i, layer=layer))
+        refs.append(cases.oracle_decode(seed, pos, bf16, seq=sq, layer=layer))
     out = np.zeros((B, cases.QD), np.float32)
     kv.decode_layer(layer, Q, K, V, np.array(positions, np.int32), out)
     return Q, K, out, refs, kv
@@ -219,7 +222,8 @@ def test_decode_golden_through_gpu(tg, backend, golden, cases):
     seed = int(golden["seed"])
     for tag, bf16, tol in (("f32", False, F32_TOL), ("bf16", True, BF16_TOL)):
         positions = [int(p) for p in golden[f"dec_{tag}_pos"]]
-        Q, K, out, _, _ = run_batch(tg, backend, cases, positions, bf16, seed=seed)
+        Q, K, out, _, _ = run_batch(tg, backend, cases, positions, bf16, seed=seed,
+                                    stream0=True)
         for i in range(len(positions)):
             assert np.array_equal(bits(Q[i]), bits(golden[f"dec_{tag}_q"][i]))
             assert np.array_equal(bits(K[i]), bits(golden[f"dec_{tag}_k"][i]))
@@ -337,6 +341,60 @@ def test_long_context_131072_sampled_and_properties(tg, backend, O, cases):
         kv.attention(0, Q, np.array([pos], np.int32), out)
         outs.append(out[0].copy())
     assert maxabs(outs[2], outs[0] + outs[1]) <= 1e-4
+
+
+# ------------------------------------------------------ CUDA graphs
+
+def test_graph_capture_replays_decode_step(tg, backend, cases):
+    """Two layers of a decode step captured once and replayed give the same
+    results as direct calls; host pointers are refused while capturing."""
+    import torch
+    positions = [40, 700, 3]
+    B = len(positions)
+    kv = tg.KVCache(backend, 2, B, 1024, dtype=tg.DTYPE_BF16)
+    kv.fill_normal(99)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    q0 = torch.randn(2, B, 896, device="cuda", generator=g)
+    k0 = torch.randn(2, B, 128, device="cuda", generator=g)
+    v0 = torch.randn(2, B, 128, device="cuda", generator=g)
+    pos = torch.tensor(positions, dtype=torch.int32, device="cuda")
+
+    def run(q, k, out):
+        for l in range(2):
+            kv.decode_layer(l, q[l], k[l], v0[l], pos, out[l])
+
+    qa, ka, oa = q0.clone(), k0.clone(), torch.zeros(2, B, 896, device="cuda")
+    run(qa, ka, oa)                      # direct (also sizes the scratch)
+    backend.synchronize()
+    qb, kb, ob = q0.clone(), k0.clone(), torch.zeros(2, B, 896, device="cuda")
+    n0 = backend.launch_count()
+    backend.graph_begin()
+    run(qb, kb, ob)
+    with pytest.raises(tg.TGError) as e:  # host memory inside a capture
+        kv.attention(0, np.zeros((B, 896), np.float32), np.array(positions, np.int32),
+                     np.zeros((B, 896), np.float32))
+    assert e.value.status == tg.TG_ERR_STATE
+    graph = backend.graph_end()
+    assert backend.launch_count() == n0  # recorded, not run
+    graph.launch()
+    backend.synchronize()
+    assert backend.launch_count() > n0
+    assert torch.equal(qa, qb) and torch.equal(ka, kb)
+    assert torch.equal(oa, ob)
+    graph.destroy()
+    # kernel timing events captured into a graph are re-recorded per replay
+    backend.profile_enable(True)
+    backend.graph_begin()
+    run(qb, kb, ob)
+    gp = backend.graph_end()
+    backend.profile_enable(False)
+    for _ in range(2):
+        gp.launch()
+        ms, n = backend.profile_read()
+        assert n == 2 and ms > 0
+    gp.destroy()
+    kv.destroy()
 
 
 # ------------------------------------------------------ errors and hygiene

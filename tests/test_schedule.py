@@ -57,12 +57,13 @@ def _replay(sched, tiles, G):
     prefix = np.concatenate([[0], np.cumsum(tiles)]).astype(np.int64)
     T = int(prefix[-1])
     B = len(tiles)
+    G = min(G, T)  # the kernels' effective grid
     written = {s: [] for s in range(B)}
     complete = set()
     owner = np.full(T, -1)
     for c in range(G):
         lo, hi = sched.cta_tile_lo(c, G, T), sched.cta_tile_lo(c + 1, G, T)
-        assert lo <= hi
+        assert lo < hi  # no empty CTA in the effective grid
         owner[lo:hi] = c
         t = lo
         while t < hi:
@@ -112,6 +113,18 @@ def test_slots_agree_between_decode_and_merge(sched, seed):
             assert sorted(written[s]) == sorted(derived[s])
     all_slots = [x for v in written.values() for x in v]
     assert len(all_slots) == len(set(all_slots))
+
+
+@pytest.mark.parametrize("tiles,G", [([3], 592), ([2], 592), ([1, 5, 2], 148),
+                                     ([0, 4, 0, 9], 296), ([33], 32), ([7, 1], 8)])
+def test_more_ctas_than_tiles(sched, tiles, G):
+    """Short sequences on a large grid: every CTA of the effective grid owns
+    tiles, so a split sequence's slots are all written."""
+    tiles = np.array(tiles)
+    written, derived, complete = _replay(sched, tiles, G)
+    for s in range(len(tiles)):
+        if tiles[s] and s not in complete:
+            assert sorted(written[s]) == sorted(derived[s])
 
 
 def test_long_context_split_counts(sched):

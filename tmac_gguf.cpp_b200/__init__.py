@@ -115,6 +115,10 @@ _SIGS = {
                                        _vp]),
     "tg_merge_records": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_int,
                                    _vp, _vp]),
+    "tg_graph_begin": (C.c_int, [_vp]),
+    "tg_graph_end": (C.c_int, [_vp, C.POINTER(_vp)]),
+    "tg_graph_launch": (C.c_int, [_vp, _vp]),
+    "tg_graph_destroy": (C.c_int, [_vp]),
     "tg_launch_count": (C.c_int, [_vp, C.POINTER(C.c_longlong)]),
     "tg_profile_enable": (C.c_int, [_vp, C.c_int]),
     "tg_profile_read": (C.c_int, [_vp, C.POINTER(C.c_double),
@@ -242,6 +246,15 @@ class CudaBackend:
     def synchronize(self) -> None:
         _check(lib().tg_synchronize(self._h))
 
+    # -- CUDA graphs ----------------------------------------------------------
+    def graph_begin(self) -> None:
+        _check(lib().tg_graph_begin(self._h))
+
+    def graph_end(self) -> "Graph":
+        g = C.c_void_p()
+        _check(lib().tg_graph_end(self._h, C.byref(g)))
+        return Graph(self, g)
+
     def launch_count(self) -> int:
         n = C.c_longlong()
         _check(lib().tg_launch_count(self._h, C.byref(n)))
@@ -299,6 +312,29 @@ class CudaBackend:
         """Combine [n_parts][n_seqs][n_head*(head_dim+2)] softmax records."""
         _check(lib().tg_merge_records(self._h, n_parts, n_seqs, n_head,
                                       head_dim, _ptr(records), _ptr(out)))
+
+
+class Graph:
+    """A captured sequence of device-pointer calls (tg_graph_*)."""
+
+    def __init__(self, backend: CudaBackend, handle: C.c_void_p):
+        self.backend = backend
+        self._h = handle
+
+    def launch(self) -> None:
+        _check(lib().tg_graph_launch(self.backend.handle, self._h))
+
+    def destroy(self) -> None:
+        if self._h and self.backend.handle:
+            _check(lib().tg_graph_destroy(self._h))
+        self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            if getattr(self, "_h", None) and self.backend.handle:
+                lib().tg_graph_destroy(self._h)
+        except Exception:
+            pass
 
 
 class KVCache:

@@ -135,7 +135,8 @@ struct Region {
   size_t bytes = 0;
   char* dev = nullptr;
   int flags = TG_REGION_MIRROR;
-  bool fresh = false;   // device copy current for this batch
+  bool transient = true;  // created by an op: lives until the batch ends
+  bool fresh = false;     // device copy current for this batch
   size_t dirty_lo = 0, dirty_hi = 0;  // byte range written by device ops
 };
 
@@ -164,7 +165,10 @@ struct tg_context {
   std::vector<RopeTable> tables;
   std::map<uintptr_t, Region> regions;
   bool in_batch = false;
+  bool capturing = false;    // a CUDA graph capture is open on the stream
+  bool call_staged = false;  // the current call moved host data
   long long launches = 0;
+  long long capture_launches0 = 0;
 
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
@@ -176,6 +180,13 @@ struct tg_context {
   bool prof_on = false;
   std::vector<cudaEvent_t> prof_ev;  // start/stop pairs
   size_t prof_used = 0;              // events recorded since the last read
+};
+
+struct tg_graph {
+  tg_context* ctx = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  long long kernels = 0;  // kernel launches recorded into the graph
 };
 
 struct tg_kv_cache {
@@ -217,6 +228,9 @@ void free_graveyard(tg_context* ctx) {
 template <typename T>
 int ensure_buf(tg_context* ctx, T** buf, size_t* cap, size_t need) {
   if (need <= *cap) return TG_OK;
+  if (ctx->capturing)
+    return fail(TG_ERR_STATE,
+                "scratch must be sized before graph capture: run the same call once first");
   size_t n = need < 1024 ? 1024 : need;
   n = n + n / 4;
   T* nb = nullptr;
@@ -295,6 +309,9 @@ int stage_in(tg_context* ctx, const void* p, size_t bytes, const void** dev) {
     *dev = p;
     return TG_OK;
   }
+  if (ctx->capturing)
+    return fail(TG_ERR_STATE, "host pointers cannot be used inside a graph capture");
+  ctx->call_staged = true;
   void* d = nullptr;
   TG_TRY(arena_alloc(ctx, bytes, &d));
   TG_CUDA(cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, ctx->stream));
@@ -308,6 +325,9 @@ int stage_out(tg_context* ctx, void* p, size_t bytes, bool copy_in, void** dev) 
     *dev = p;
     return TG_OK;
   }
+  if (ctx->capturing)
+    return fail(TG_ERR_STATE, "host pointers cannot be used inside a graph capture");
+  ctx->call_staged = true;
   void* d = nullptr;
   TG_TRY(arena_alloc(ctx, bytes, &d));
   if (copy_in) TG_CUDA(cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, ctx->stream));
@@ -316,13 +336,18 @@ int stage_out(tg_context* ctx, void* p, size_t bytes, bool copy_in, void** dev) 
   return TG_OK;
 }
 
-// Issues the device->host copies of staged outputs; outside a batch also
-// waits and recycles the staging arena.
+// Issues the device->host copies of staged outputs.  A call that moved host
+// data waits for the stream (outside a batch) so that its host outputs are
+// valid on return; a call on device pointers only stays asynchronous, like
+// any stream-ordered CUDA work, and device-side errors surface at the next
+// tg_synchronize / tg_batch_end.
 int finish_call(tg_context* ctx) {
+  const bool staged = ctx->call_staged;
+  ctx->call_staged = false;
   for (const PendingCopy& c : ctx->pending)
     TG_CUDA(cudaMemcpyAsync(c.host, c.dev, c.bytes, cudaMemcpyDeviceToHost, ctx->stream));
   ctx->pending.clear();
-  if (ctx->in_batch) return TG_OK;
+  if (ctx->in_batch || !staged) return TG_OK;
   TG_TRY(wait_stream(ctx));
   ctx->arena_off = 0;
   free_graveyard(ctx);
@@ -351,13 +376,22 @@ int make_fresh(tg_context* ctx, Region& r) {
 // Creates a mirror for [p, p+bytes), absorbing any mirrors it overlaps: the
 // new device copy starts as the host contents, then every absorbed mirror
 // whose device copy is newer (written or device-owned) is copied over it.
-int create_region(tg_context* ctx, char* p, size_t bytes, int flags, Region** out) {
+// Transient mirrors (made by ops for unregistered host arrays) live in the
+// staging arena until the batch ends; registered ones own their memory.
+int create_region(tg_context* ctx, char* p, size_t bytes, int flags, bool transient,
+                  Region** out) {
+  if (ctx->capturing)
+    return fail(TG_ERR_STATE, "host arrays cannot be used inside a graph capture");
   char* lo = p;
   char* hi = p + bytes;
   std::vector<uintptr_t> absorbed;
   for (auto& kv : ctx->regions) {
     Region& r = kv.second;
     if (r.host < hi && p < r.host + r.bytes) {
+      if (transient && !r.transient)
+        return fail(TG_ERR_INVALID_ARG,
+                    "host range [%p, +%zu) straddles the registered array at %p (+%zu)",
+                    (void*)p, bytes, (void*)r.host, r.bytes);
       absorbed.push_back(kv.first);
       if (r.host < lo) lo = r.host;
       if (r.host + r.bytes > hi) hi = r.host + r.bytes;
@@ -368,7 +402,14 @@ int create_region(tg_context* ctx, char* p, size_t bytes, int flags, Region** ou
   nr.host = lo;
   nr.bytes = (size_t)(hi - lo);
   nr.flags = flags;
-  TG_CUDA(cudaMalloc(&nr.dev, nr.bytes));
+  nr.transient = transient;
+  if (transient) {
+    void* d = nullptr;
+    TG_TRY(arena_alloc(ctx, nr.bytes, &d));
+    nr.dev = static_cast<char*>(d);
+  } else {
+    TG_CUDA(cudaMalloc(&nr.dev, nr.bytes));
+  }
   TG_CUDA(cudaMemcpyAsync(nr.dev, nr.host, nr.bytes, cudaMemcpyHostToDevice, ctx->stream));
   nr.fresh = true;
   for (uintptr_t key : absorbed) {
@@ -388,7 +429,7 @@ int create_region(tg_context* ctx, char* p, size_t bytes, int flags, Region** ou
         if (b > nr.dirty_hi) nr.dirty_hi = b;
       }
     }
-    ctx->graveyard.push_back(r.dev);
+    if (!r.transient) ctx->graveyard.push_back(r.dev);
     ctx->regions.erase(key);
   }
   auto res = ctx->regions.emplace(reinterpret_cast<uintptr_t>(nr.host), nr);
@@ -405,7 +446,7 @@ int ensure_region(tg_context* ctx, const void* p, size_t bytes) {
   char* hp = const_cast<char*>(static_cast<const char*>(p));
   if (find_region(ctx, hp, bytes)) return TG_OK;
   Region* r = nullptr;
-  return create_region(ctx, hp, bytes, TG_REGION_MIRROR, &r);
+  return create_region(ctx, hp, bytes, TG_REGION_MIRROR, true, &r);
 }
 
 // Device address for a compat-op argument.  write: the op writes the range.
@@ -417,7 +458,8 @@ int resolve(tg_context* ctx, const void* p, size_t bytes, bool write, char** dev
   }
   char* hp = const_cast<char*>(static_cast<const char*>(p));
   Region* r = find_region(ctx, hp, bytes);
-  if (!r) TG_TRY(create_region(ctx, hp, bytes, TG_REGION_MIRROR, &r));
+  if (!r) TG_TRY(create_region(ctx, hp, bytes, TG_REGION_MIRROR, true, &r));
+  ctx->call_staged = true;
   TG_TRY(make_fresh(ctx, *r));
   const size_t off = (size_t)(hp - r->host);
   if (write && !(r->flags & TG_REGION_DEVICE_OWNED)) {
@@ -442,13 +484,27 @@ int flush_regions(tg_context* ctx) {
                               cudaMemcpyDeviceToHost, ctx->stream));
   }
   TG_TRY(wait_stream(ctx));
-  for (auto& kv : ctx->regions) {
-    kv.second.dirty_lo = kv.second.dirty_hi = 0;
-    kv.second.fresh = false;
+  for (auto it = ctx->regions.begin(); it != ctx->regions.end();) {
+    if (it->second.transient) {
+      it = ctx->regions.erase(it);
+    } else {
+      it->second.dirty_lo = it->second.dirty_hi = 0;
+      it->second.fresh = false;
+      ++it;
+    }
   }
   ctx->arena_off = 0;
+  ctx->call_staged = false;
   free_graveyard(ctx);
   return check_device_error(ctx);
+}
+
+// End of a compat op: outside a batch, host arrays are written back and the
+// stream is waited on; an op on device pointers only stays asynchronous.
+int finish_compat(tg_context* ctx) {
+  if (ctx->in_batch) return TG_OK;
+  if (!ctx->call_staged) return TG_OK;
+  return flush_regions(ctx);
 }
 
 // ------------------------------------------------ RoPE tables
@@ -467,6 +523,9 @@ int get_table(tg_context* ctx, float base, int head_dim, int need_len, RopeTable
     *out = t;
     return TG_OK;
   }
+  if (ctx->capturing)
+    return fail(TG_ERR_STATE, "RoPE table for position %d must exist before graph capture",
+                need_len - 1);
   int len = 4096;
   while (len < need_len) len *= 2;
   const int half = head_dim / 2;
@@ -571,7 +630,9 @@ int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const f
       TG_CUDA(cudaEventCreate(&ev));
       ctx->prof_ev.push_back(ev);
     }
-    TG_CUDA(cudaEventRecord(ctx->prof_ev[ctx->prof_used], ctx->stream));
+    // Inside a capture, an external record becomes an event node of the graph.
+    TG_CUDA(cudaEventRecordWithFlags(ctx->prof_ev[ctx->prof_used], ctx->stream,
+                                     ctx->capturing ? cudaEventRecordExternal : 0));
     ev_stop = ctx->prof_ev[ctx->prof_used + 1];
     ctx->prof_used += 2;
   }
@@ -579,7 +640,9 @@ int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const f
                       : tg::launch_decode_generic(p, d.dtype, grid, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
   ctx->launches++;
-  if (ev_stop) TG_CUDA(cudaEventRecord(ev_stop, ctx->stream));
+  if (ev_stop)
+    TG_CUDA(cudaEventRecordWithFlags(ev_stop, ctx->stream,
+                                     ctx->capturing ? cudaEventRecordExternal : 0));
 
   tg::MergeParams m{};
   m.part = ctx->part;
@@ -753,6 +816,7 @@ int tg_device_sms(tg_context* ctx, int* out) {
 int tg_batch_begin(tg_context* ctx) {
   TG_TRY(set_device(ctx));
   if (ctx->in_batch) return fail(TG_ERR_STATE, "batch already open");
+  if (ctx->capturing) return fail(TG_ERR_STATE, "graph capture open");
   ctx->in_batch = true;
   return TG_OK;
 }
@@ -769,6 +833,7 @@ int tg_batch_end(tg_context* ctx) {
 
 int tg_synchronize(tg_context* ctx) {
   TG_TRY(set_device(ctx));
+  if (ctx->capturing) return fail(TG_ERR_STATE, "graph capture open");
   TG_TRY(wait_stream(ctx));
   if (!ctx->in_batch) {
     ctx->arena_off = 0;
@@ -777,12 +842,62 @@ int tg_synchronize(tg_context* ctx) {
   return check_device_error(ctx);
 }
 
+int tg_graph_begin(tg_context* ctx) {
+  TG_TRY(set_device(ctx));
+  if (ctx->in_batch || ctx->capturing) return fail(TG_ERR_STATE, "batch or capture already open");
+  TG_CUDA(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+  ctx->capturing = true;
+  ctx->capture_launches0 = ctx->launches;
+  return TG_OK;
+}
+
+int tg_graph_end(tg_context* ctx, tg_graph** out) {
+  TG_TRY(set_device(ctx));
+  if (!ctx->capturing) return fail(TG_ERR_STATE, "tg_graph_end without tg_graph_begin");
+  if (!out) return fail(TG_ERR_INVALID_ARG, "null output pointer");
+  ctx->capturing = false;
+  cudaGraph_t g = nullptr;
+  TG_CUDA(cudaStreamEndCapture(ctx->stream, &g));
+  cudaGraphExec_t ex = nullptr;
+  cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+  if (e != cudaSuccess) {
+    cudaGraphDestroy(g);
+    return fail(TG_ERR_CUDA, "cudaGraphInstantiate: %s", cudaGetErrorString(e));
+  }
+  tg_graph* tgg = new tg_graph();
+  tgg->ctx = ctx;
+  tgg->graph = g;
+  tgg->exec = ex;
+  tgg->kernels = ctx->launches - ctx->capture_launches0;
+  ctx->launches = ctx->capture_launches0;  // recorded, not run
+  *out = tgg;
+  return TG_OK;
+}
+
+int tg_graph_launch(tg_context* ctx, tg_graph* g) {
+  TG_TRY(set_device(ctx));
+  if (!g || g->ctx != ctx) return fail(TG_ERR_INVALID_ARG, "graph of another context");
+  TG_CUDA(cudaGraphLaunch(g->exec, ctx->stream));
+  ctx->launches += g->kernels;
+  return TG_OK;
+}
+
+int tg_graph_destroy(tg_graph* g) {
+  if (!g) return TG_OK;
+  cudaSetDevice(g->ctx->device);
+  cudaStreamSynchronize(g->ctx->stream);
+  cudaGraphExecDestroy(g->exec);
+  cudaGraphDestroy(g->graph);
+  delete g;
+  return TG_OK;
+}
+
 int tg_register_host(tg_context* ctx, void* host_ptr, size_t bytes, int flags) {
   TG_TRY(set_device(ctx));
   if (!host_ptr || bytes == 0) return fail(TG_ERR_INVALID_ARG, "empty host range");
   if (is_device_ptr(host_ptr)) return fail(TG_ERR_INVALID_ARG, "pointer is device memory");
   Region* r = nullptr;
-  TG_TRY(create_region(ctx, static_cast<char*>(host_ptr), bytes, flags, &r));
+  TG_TRY(create_region(ctx, static_cast<char*>(host_ptr), bytes, flags, false, &r));
   if (!ctx->in_batch) return flush_regions(ctx);
   return TG_OK;
 }
@@ -790,7 +905,8 @@ int tg_register_host(tg_context* ctx, void* host_ptr, size_t bytes, int flags) {
 int tg_unregister_host(tg_context* ctx, void* host_ptr) {
   TG_TRY(set_device(ctx));
   auto it = ctx->regions.find(reinterpret_cast<uintptr_t>(host_ptr));
-  if (it == ctx->regions.end()) return fail(TG_ERR_INVALID_ARG, "pointer is not a region start");
+  if (it == ctx->regions.end() || it->second.transient)
+    return fail(TG_ERR_INVALID_ARG, "pointer is not the start of a registered array");
   if (ctx->in_batch) return fail(TG_ERR_STATE, "cannot unregister inside a batch");
   TG_CUDA(cudaStreamSynchronize(ctx->stream));
   cudaFree(it->second.dev);
@@ -836,8 +952,7 @@ int tg_rope_op(tg_context* ctx, float* data, int n_heads, int head_dim, int pos,
   cudaError_t e = tg::launch_rope(rp, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "rope launch: %s", cudaGetErrorString(e));
   ctx->launches++;
-  if (ctx->in_batch) return TG_OK;
-  return flush_regions(ctx);
+  return finish_compat(ctx);
 }
 
 int tg_elem_op(tg_context* ctx, int op, float* data, const float* aux, int dim) {
@@ -856,8 +971,7 @@ int tg_elem_op(tg_context* ctx, int op, float* data, const float* aux, int dim) 
                                   reinterpret_cast<const float*>(da), dim, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "elem launch: %s", cudaGetErrorString(e));
   ctx->launches++;
-  if (ctx->in_batch) return TG_OK;
-  return flush_regions(ctx);
+  return finish_compat(ctx);
 }
 
 int tg_attention_op(tg_context* ctx, const float* Q, const float* K_cache, const float* V_cache,
@@ -894,8 +1008,7 @@ int tg_attention_op(tg_context* ctx, const float* Q, const float* K_cache, const
   view.global_ctx = past_len + 1;
   TG_TRY(run_decode(ctx, &view, 0, 1, reinterpret_cast<const float*>(dq), nullptr, past_len,
                     reinterpret_cast<float*>(dout), 0));
-  if (ctx->in_batch) return TG_OK;
-  return flush_regions(ctx);
+  return finish_compat(ctx);
 }
 
 // ------------------------------------------------ KV caches
@@ -1321,7 +1434,7 @@ int tg_launch_count(tg_context* ctx, long long* out) {
 int tg_profile_enable(tg_context* ctx, int on) {
   TG_TRY(set_device(ctx));
   ctx->prof_on = on != 0;
-  ctx->prof_used = 0;
+  if (on) ctx->prof_used = 0;  // disabling keeps the record (a graph may replay it)
   return TG_OK;
 }
 
@@ -1337,7 +1450,6 @@ int tg_profile_read(tg_context* ctx, double* total_ms, long long* launches) {
   }
   *total_ms = sum;
   *launches = (long long)(ctx->prof_used / 2);
-  ctx->prof_used = 0;
   return TG_OK;
 }
 

@@ -28,6 +28,17 @@ __device__ __forceinline__ void record_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// ---------------------------------------------------------------- PDL
+
+// Programmatic dependent launch: allow the next kernel on the stream to be
+// launched now / wait until the previous kernel's memory is visible.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

@@ -19,6 +19,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "tg_device.cuh"
 #include "tg_kernels.h"
 #include "tg_shared.h"
@@ -28,6 +30,8 @@ namespace tg {
 // ===================================================================== RoPE
 
 __global__ void __launch_bounds__(128) rope_cache_write_kernel(const RopeParams p) {
+  griddep_launch_dependents();
+  griddep_wait();
   const int s = blockIdx.x;
   const int pos = p.pos ? p.pos[s] : p.pos_scalar;
   if (pos < 0 || pos >= p.table_len) {
@@ -222,13 +226,16 @@ __global__ void __launch_bounds__(MmaCfg<NKV>::THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+  griddep_launch_dependents();
+  griddep_wait();
   build_tile_prefix(p, TILE, prefix, warp_tot);
   const long long T = prefix[p.B];
   if (blockIdx.x == 0)
     for (int i = threadIdx.x; i <= p.B; i += blockDim.x) p.sched[i] = prefix[i];
-  const int G = gridDim.x, cta = blockIdx.x;
+  // Effective grid: never more CTAs than tiles, so no CTA range is empty.
+  const int G = (int)min((long long)gridDim.x, T), cta = blockIdx.x;
+  if (cta >= G) return;
   const long long t_lo = cta_tile_lo(cta, G, T), t_hi = cta_tile_lo(cta + 1, G, T);
-  if (t_lo >= t_hi) return;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -497,13 +504,16 @@ __global__ void __launch_bounds__(GEN_THREADS) decode_generic_kernel(const Decod
   int* warp_tot = reinterpret_cast<int*>(gsm + Ly.wt_off);
   int* prefix = reinterpret_cast<int*>(gsm + Ly.pre_off);
 
+  griddep_launch_dependents();
+  griddep_wait();
   build_tile_prefix(p, GEN_TILE, prefix, warp_tot);
   const long long T = prefix[p.B];
   if (blockIdx.x == 0)
     for (int i = threadIdx.x; i <= p.B; i += blockDim.x) p.sched[i] = prefix[i];
-  const int G = gridDim.x, cta = blockIdx.x;
+  // Effective grid: never more CTAs than tiles, so no CTA range is empty.
+  const int G = (int)min((long long)gridDim.x, T), cta = blockIdx.x;
+  if (cta >= G) return;
   const long long t_lo = cta_tile_lo(cta, G, T), t_hi = cta_tile_lo(cta + 1, G, T);
-  if (t_lo >= t_hi) return;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hd = p.head_dim, kdim = p.n_kv * hd, qdim = p.n_head * hd;
@@ -600,8 +610,15 @@ __global__ void __launch_bounds__(GEN_THREADS) decode_generic_kernel(const Decod
 
 // ================================================================== merges
 
+// One CTA per (sequence, head); thread d owns output dimension d.  The
+// partial records of a split sequence are folded with a single-pass online
+// combine; slot values are loaded in batches of 8 so the loads overlap.
+constexpr int MERGE_BATCH = 8;
+
 __global__ void __launch_bounds__(128) merge_kernel(const MergeParams p) {
-  const int s = blockIdx.x;
+  griddep_launch_dependents();
+  griddep_wait();
+  const int s = blockIdx.x / p.n_head, h = blockIdx.x - s * p.n_head;
   const int t0 = p.sched[s], t1 = p.sched[s + 1];
   const long long T = p.sched[p.B];
   const int hd = p.head_dim, qdim = p.n_head * hd;
@@ -609,36 +626,56 @@ __global__ void __launch_bounds__(128) merge_kernel(const MergeParams p) {
   if (t1 == t0) {
     if (p.mode == 1) {
       float* rec = p.records + (size_t)s * rf;
-      for (int i = threadIdx.x; i < rf; i += blockDim.x)
-        rec[i] = (i >= qdim && i < qdim + p.n_head) ? kNegBig : 0.f;
+      for (int d = threadIdx.x; d < hd; d += blockDim.x) rec[h * hd + d] = 0.f;
+      if (threadIdx.x == 0) {
+        rec[qdim + h] = kNegBig;
+        rec[qdim + p.n_head + h] = 0.f;
+      }
     }
     return;
   }
-  const int c1 = cta_of_tile(t0, p.G, T), c2 = cta_of_tile(t1 - 1, p.G, T);
+  const int G = (int)min((long long)p.G, T);  // the decode kernel's effective grid
+  const int c1 = cta_of_tile(t0, G, T), c2 = cta_of_tile(t1 - 1, G, T);
   if (c1 == c2) return;
-  const int first_slot = 2 * c1 + (cta_tile_lo(c1, p.G, T) == t0 ? 0 : 1);
+  const int first_slot = 2 * c1 + (cta_tile_lo(c1, G, T) == t0 ? 0 : 1);
   const int n_parts = 1 + (c2 - c1);
-  for (int idx = threadIdx.x; idx < qdim; idx += blockDim.x) {
-    const int h = idx / hd;
-    float M = kNegBig;
-    for (int k = 0; k < n_parts; ++k) {
-      const int slot = k == 0 ? first_slot : 2 * (c1 + k);
-      M = fmaxf(M, p.part[(size_t)slot * rf + qdim + h]);
-    }
-    float O = 0.f, L = 0.f;
-    for (int k = 0; k < n_parts; ++k) {
-      const int slot = k == 0 ? first_slot : 2 * (c1 + k);
-      const float* rec = p.part + (size_t)slot * rf;
-      const float w = ex2(rec[qdim + h] - M);
-      O = fmaf(rec[idx], w, O);
-      L = fmaf(rec[qdim + p.n_head + h], w, L);
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float M = kNegBig, O = 0.f, L = 0.f;
+    for (int k0 = 0; k0 < n_parts; k0 += MERGE_BATCH) {
+      float mv[MERGE_BATCH], lv[MERGE_BATCH], ov[MERGE_BATCH];
+#pragma unroll
+      for (int u = 0; u < MERGE_BATCH; ++u) {
+        const int k = k0 + u;
+        mv[u] = kNegBig;
+        lv[u] = 0.f;
+        ov[u] = 0.f;
+        if (k < n_parts) {
+          const float* rec = p.part + (size_t)(k == 0 ? first_slot : 2 * (c1 + k)) * rf;
+          mv[u] = rec[qdim + h];
+          lv[u] = rec[qdim + p.n_head + h];
+          ov[u] = rec[h * hd + d];
+        }
+      }
+      float Mb = M;
+#pragma unroll
+      for (int u = 0; u < MERGE_BATCH; ++u) Mb = fmaxf(Mb, mv[u]);
+      const float a = ex2(M - Mb);
+      O *= a;
+      L *= a;
+#pragma unroll
+      for (int u = 0; u < MERGE_BATCH; ++u) {
+        const float w = ex2(mv[u] - Mb);
+        O = fmaf(ov[u], w, O);
+        L = fmaf(lv[u], w, L);
+      }
+      M = Mb;
     }
     if (p.mode == 0) {
-      p.out[(size_t)s * qdim + idx] = O / L;
+      p.out[(size_t)s * qdim + h * hd + d] = O / L;
     } else {
       float* rec = p.records + (size_t)s * rf;
-      rec[idx] = O;
-      if (idx - h * hd == 0) {
+      rec[h * hd + d] = O;
+      if (d == 0) {
         rec[qdim + h] = M;
         rec[qdim + p.n_head + h] = L;
       }
@@ -647,22 +684,43 @@ __global__ void __launch_bounds__(128) merge_kernel(const MergeParams p) {
 }
 
 __global__ void __launch_bounds__(128) gather_merge_kernel(const GatherMergeParams p) {
-  const int s = blockIdx.x;
+  griddep_launch_dependents();
+  griddep_wait();
+  const int s = blockIdx.x / p.n_head, h = blockIdx.x - s * p.n_head;
   const int hd = p.head_dim, qdim = p.n_head * hd;
   const int rf = record_floats(p.n_head, hd);
-  for (int idx = threadIdx.x; idx < qdim; idx += blockDim.x) {
-    const int h = idx / hd;
-    float M = kNegBig;
-    for (int r = 0; r < p.world; ++r)
-      M = fmaxf(M, p.records[((size_t)r * p.B + s) * rf + qdim + h]);
-    float O = 0.f, L = 0.f;
-    for (int r = 0; r < p.world; ++r) {
-      const float* rec = p.records + ((size_t)r * p.B + s) * rf;
-      const float w = ex2(rec[qdim + h] - M);
-      O = fmaf(rec[idx], w, O);
-      L = fmaf(rec[qdim + p.n_head + h], w, L);
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float M = kNegBig, O = 0.f, L = 0.f;
+    for (int r0 = 0; r0 < p.world; r0 += MERGE_BATCH) {
+      float mv[MERGE_BATCH], lv[MERGE_BATCH], ov[MERGE_BATCH];
+#pragma unroll
+      for (int u = 0; u < MERGE_BATCH; ++u) {
+        const int r = r0 + u;
+        mv[u] = kNegBig;
+        lv[u] = 0.f;
+        ov[u] = 0.f;
+        if (r < p.world) {
+          const float* rec = p.records + ((size_t)r * p.B + s) * rf;
+          mv[u] = rec[qdim + h];
+          lv[u] = rec[qdim + p.n_head + h];
+          ov[u] = rec[h * hd + d];
+        }
+      }
+      float Mb = M;
+#pragma unroll
+      for (int u = 0; u < MERGE_BATCH; ++u) Mb = fmaxf(Mb, mv[u]);
+      const float a = ex2(M - Mb);
+      O *= a;
+      L *= a;
+#pragma unroll
+      for (int u = 0; u < MERGE_BATCH; ++u) {
+        const float w = ex2(mv[u] - Mb);
+        O = fmaf(ov[u], w, O);
+        L = fmaf(lv[u], w, L);
+      }
+      M = Mb;
     }
-    p.out[(size_t)s * qdim + idx] = O / L;
+    p.out[(size_t)s * qdim + h * hd + d] = O / L;
   }
 }
 
@@ -725,22 +783,53 @@ __global__ void convert_rows_kernel(void* dst, const float* src, size_t n, int d
 
 // ================================================================ launchers
 
+// Launch with programmatic stream serialization: the kernel may be
+// launched while its predecessor on the stream is still running; every
+// kernel here waits (griddepcontrol.wait) before touching memory, so the
+// overlap only hides launch latency.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*fn)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fn, std::forward<Args>(args)...);
+}
+
 cudaError_t launch_rope(const RopeParams& p, cudaStream_t st) {
   if (p.B <= 0) return cudaSuccess;
-  rope_cache_write_kernel<<<p.B, 128, 0, st>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(rope_cache_write_kernel, dim3(p.B), dim3(128), 0, st, p);
+}
+
+// Raises a kernel's dynamic shared-memory limit once per device and size.
+template <typename F>
+static cudaError_t ensure_smem(F* fn, size_t smem, size_t* cache) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (smem <= cache[dev]) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess) cache[dev] = smem;
+  return e;
 }
 
 template <int NKV>
 static cudaError_t launch_mma_nkv(const CUtensorMap& tk, const CUtensorMap& tv,
                                   const DecodeParams& p, int grid,
                                   cudaStream_t st) {
+  static size_t configured[64] = {};
   const size_t smem = MmaCfg<NKV>::smem_bytes(p.B);
-  auto kfn = decode_mma_kernel<NKV>;
-  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = ensure_smem(decode_mma_kernel<NKV>, smem, configured);
   if (e != cudaSuccess) return e;
-  kfn<<<grid, MmaCfg<NKV>::THREADS, smem, st>>>(tk, tv, p);
-  return cudaGetLastError();
+  return launch_pdl(decode_mma_kernel<NKV>, dim3(grid), dim3(MmaCfg<NKV>::THREADS), smem, st,
+                    tk, tv, p);
 }
 
 size_t decode_mma_smem(int nkv, int B) {
@@ -764,23 +853,26 @@ cudaError_t launch_decode_mma(const CUtensorMap& tk, const CUtensorMap& tv,
 
 cudaError_t launch_decode_generic(const DecodeParams& p, int dtype, int grid,
                                   cudaStream_t st) {
+  static size_t configured_f32[64] = {}, configured_bf16[64] = {};
   const size_t smem = decode_generic_smem(p.B, p.n_head, p.n_kv, p.head_dim);
   cudaError_t e;
   if (dtype == 0) {
-    e = cudaFuncSetAttribute(decode_generic_kernel<float>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    e = ensure_smem(decode_generic_kernel<float>, smem, configured_f32);
     if (e != cudaSuccess) return e;
-    decode_generic_kernel<float><<<grid, GEN_THREADS, smem, st>>>(p);
+    return launch_pdl(decode_generic_kernel<float>, dim3(grid), dim3(GEN_THREADS), smem, st, p);
   } else {
-    e = cudaFuncSetAttribute(decode_generic_kernel<__nv_bfloat16>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    e = ensure_smem(decode_generic_kernel<__nv_bfloat16>, smem, configured_bf16);
     if (e != cudaSuccess) return e;
-    decode_generic_kernel<__nv_bfloat16><<<grid, GEN_THREADS, smem, st>>>(p);
+    return launch_pdl(decode_generic_kernel<__nv_bfloat16>, dim3(grid), dim3(GEN_THREADS), smem,
+                      st, p);
   }
-  return cudaGetLastError();
 }
 
 int decode_generic_blocks_per_sm(int dtype, size_t smem) {
+  static size_t last_smem[2] = {0, 0};
+  static int last_n[2] = {0, 0};
+  const int di = dtype == 0 ? 0 : 1;
+  if (last_n[di] && last_smem[di] == smem) return last_n[di];
   int n = 0;
   if (dtype == 0) {
     cudaFuncSetAttribute(decode_generic_kernel<float>,
@@ -794,19 +886,22 @@ int decode_generic_blocks_per_sm(int dtype, size_t smem) {
                                                   GEN_THREADS, smem);
   }
   cudaGetLastError();
-  return n < 1 ? 1 : n;
+  n = n < 1 ? 1 : n;
+  last_smem[di] = smem;
+  last_n[di] = n;
+  return n;
 }
 
 cudaError_t launch_merge(const MergeParams& p, cudaStream_t st) {
   if (p.B <= 0) return cudaSuccess;
-  merge_kernel<<<p.B, 128, 0, st>>>(p);
-  return cudaGetLastError();
+  const int threads = p.head_dim <= 64 ? 64 : 128;
+  return launch_pdl(merge_kernel, dim3(p.B * p.n_head), dim3(threads), 0, st, p);
 }
 
 cudaError_t launch_gather_merge(const GatherMergeParams& p, cudaStream_t st) {
   if (p.B <= 0) return cudaSuccess;
-  gather_merge_kernel<<<p.B, 128, 0, st>>>(p);
-  return cudaGetLastError();
+  const int threads = p.head_dim <= 64 ? 64 : 128;
+  return launch_pdl(gather_merge_kernel, dim3(p.B * p.n_head), dim3(threads), 0, st, p);
 }
 
 cudaError_t launch_elem(int op, float* data, const float* aux, int dim,

@@ -5,7 +5,8 @@
 // attends over n_local(s) cache rows of this shard; they form
 // ceil(n_local(s) / TILE) tiles.  The tiles of all sequences are laid end
 // to end (tile_prefix[s] .. tile_prefix[s+1]) and CTA c of a G-CTA grid
-// takes the contiguous range [c*T/G, (c+1)*T/G), T = tile_prefix[B].  A
+// takes the contiguous range [c*T/G, (c+1)*T/G), T = tile_prefix[B], where
+// G = min(launched CTAs, T) so that every range is non-empty.  A
 // CTA's range therefore covers at most two partial sequences (its first and
 // its last segment); every sequence in between is complete.  A complete
 // segment is finished by its CTA; a partial one leaves a partial softmax
