@@ -246,6 +246,39 @@ TG_API int tg_decode_layer_splitkv(tg_context* ctx, tg_kv_cache* shard, int laye
                             const float* v_new, const int32_t* pos,
                             float* out);
 
+/* ------------------------------------------------- allocation-free decode */
+
+/* No counterpart in the reference.  Decode attention for callers that cannot
+ * allocate device memory when they run it: code recording a CUDA graph in
+ * global capture mode (allocation calls are refused there), runtimes that
+ * own a fixed memory pool and forbid the driver allocator after start-up,
+ * or an allocator hook that must not re-enter itself.  It creates no
+ * context and calls no cudaMalloc / cudaFree: the split-KV scratch (partial
+ * softmax records, tile schedule, error word) is one fixed device array of
+ * TG_NOALLOC_SCRATCH_BYTES inside the library, held by every GPU that loads
+ * the library until the process exits.
+ *
+ * Same work as tg_attention_batched on one layer: sequence s attends rows
+ * 0..past_len[s] of its cache rows [s][max_ctx][n_kv_head*head_dim] of
+ * `dtype`.  All pointers are device memory; the work is queued on
+ * cuda_stream (a cudaStream_t, 0 = legacy default stream) and the call does
+ * not wait.  n_seqs may be at most TG_NOALLOC_MAX_SEQS; larger batches are
+ * refused with TG_ERR_INVALID_ARG.  If device_status is not null, the
+ * kernels' error word (0, or 0x103 for a position outside the cache) is
+ * copied there once the work has run.
+ *
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make it before any
+ * stream capture.  All calls share the array and it keeps the last call's
+ * contents, so calls whose GPU work overlaps (other streams or threads)
+ * race: serialise them. */
+#define TG_NOALLOC_MAX_SEQS 4096
+#define TG_NOALLOC_SCRATCH_BYTES ((4u << 20) + 16896u)
+TG_API int tg_attention_noalloc(void* cuda_stream, const float* q, const void* k_cache,
+                                const void* v_cache, int dtype, int n_seqs, int max_ctx,
+                                int n_head, int n_kv_head, int head_dim,
+                                const int32_t* past_len, float* out, int* device_status);
+
 /* ------------------------------------------------- introspection */
 
 /* Kernel launches this context has issued since creation (all kinds). */

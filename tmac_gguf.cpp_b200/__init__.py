@@ -119,6 +119,9 @@ _SIGS = {
     "tg_graph_end": (C.c_int, [_vp, C.POINTER(_vp)]),
     "tg_graph_launch": (C.c_int, [_vp, _vp]),
     "tg_graph_destroy": (C.c_int, [_vp]),
+    "tg_attention_noalloc": (C.c_int, [_vp, _vp, _vp, _vp, C.c_int, C.c_int,
+                                       C.c_int, C.c_int, C.c_int, C.c_int,
+                                       _vp, _vp, _vp]),
     "tg_launch_count": (C.c_int, [_vp, C.POINTER(C.c_longlong)]),
     "tg_profile_enable": (C.c_int, [_vp, C.c_int]),
     "tg_profile_read": (C.c_int, [_vp, C.POINTER(C.c_double),
@@ -180,6 +183,23 @@ def shard_range(global_ctx: int, world: int, rank: int):
     per = -(-global_ctx // world)
     start = min(rank * per, global_ctx)
     return start, max(0, min(per, global_ctx - start))
+
+
+NOALLOC_MAX_SEQS = 4096
+
+
+def attention_noalloc(stream: int, q, k_cache, v_cache, dtype: int, n_seqs: int,
+                      max_ctx: int, past_len, out, device_status=None,
+                      n_head: int = N_HEAD, n_kv_head: int = N_KV_HEAD,
+                      head_dim: int = HEAD_DIM) -> None:
+    """tg_attention_noalloc: decode attention that allocates nothing, for
+    callers that cannot call cudaMalloc when they run it (global-mode graph
+    capture, fixed-pool runtimes, allocator hooks).  Device buffers only;
+    queued on `stream` without waiting."""
+    _check(lib().tg_attention_noalloc(C.c_void_p(stream), _ptr(q), _ptr(k_cache),
+                                      _ptr(v_cache), dtype, n_seqs, max_ctx, n_head,
+                                      n_kv_head, head_dim, _ptr(past_len), _ptr(out),
+                                      _ptr(device_status)))
 
 
 def comm_unique_id() -> bytes:

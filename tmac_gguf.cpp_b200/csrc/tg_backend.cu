@@ -1460,3 +1460,12 @@ int tg_kv_uses_tensor_cores(tg_kv_cache* kv, int* out) {
 }
 
 }  // extern "C"
+
+namespace tg {
+// Records the message tg_last_error() returns on this thread, for entry
+// points implemented in other files of the library.
+int set_last_error(int code, const char* msg) {
+  t_err = msg;
+  return code;
+}
+}  // namespace tg
