@@ -1,0 +1,96 @@
+"""Split-KV decode across the GPUs of one box, checked against the oracle.
+
+Run under torch.distributed.run, one rank per GPU:
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P tests/splitkv_worker.py
+
+Every rank builds its shard of the same seeded caches (positions
+shard_range(ctx, N, rank) of every sequence), runs the RoPE + owner
+cache-write + split-KV attention + NCCL all-gather + merge through the C ABI
+(tg_decode_layer_splitkv) and compares the replicated output with the CPU
+oracle.  Exit status 0 on success on every rank.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+
+
+def main() -> int:
+    import torch
+    import torch.distributed as dist
+    from conftest import load_package
+    import cases
+
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    tg = load_package()
+    be = tg.CudaBackend(local)
+    uid = [tg.comm_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    be.comm_init(uid[0], rank, world, timeout_ms=60000)
+
+    ok = True
+    for bf16, tol in ((True, 2e-3), (False, 1e-4)):
+        positions = [9000, 777, 12345, 0, world * 64]
+        B = len(positions)
+        gctx = max(positions) + 1
+        start, length = tg.shard_range(gctx, world, rank)
+        kv = tg.KVCache(be, 1, B, max(length, 1), shard_start=start, global_ctx=gctx,
+                        dtype=tg.DTYPE_BF16 if bf16 else tg.DTYPE_F32)
+        Q = np.zeros((B, cases.QD), np.float32)
+        K = np.zeros((B, cases.KD), np.float32)
+        V = np.zeros((B, cases.KD), np.float32)
+        refs = []
+        for i, p in enumerate(positions):
+            q, k_new, v_new, kc, vc = cases.decode_inputs(77, p, bf16, seq=i)
+            lo, hi = start, min(start + length, p)      # rows before the new token
+            if hi > lo:
+                kv.write_rows(0, i, 0, kc[lo:hi], vc[lo:hi])
+            Q[i], K[i], V[i] = q, k_new, v_new
+            refs.append(cases.oracle_decode(77, p, bf16, seq=i))
+        out = np.zeros((B, cases.QD), np.float32)
+        kv.decode_layer_splitkv(0, Q, K, V, np.array(positions, np.int32), out)
+        for i, p in enumerate(positions):
+            qr, kr, _, kc, vc, ctx = refs[i]
+            err = float(np.abs(out[i] - ctx).max())
+            same_q = np.array_equal(Q[i].view(np.uint32), qr.view(np.uint32))
+            if err > tol or not same_q:
+                print(f"rank {rank}: seq {i} pos {p} bf16={bf16} err={err} rope_ok={same_q}")
+                ok = False
+            if start <= p < start + length:          # this rank owns the new row
+                krow, _ = kv.read_rows(0, i, p - start, 1)
+                want = cases.O.pack_bf16(kc[p]) if bf16 else kc[p]
+                if not np.array_equal(krow[0], want):
+                    print(f"rank {rank}: cache-write mismatch seq {i}")
+                    ok = False
+        # all ranks hold the same output
+        t = torch.from_numpy(out.copy())
+        gathered = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(gathered, t)
+        if not all(torch.equal(gathered[0], g) for g in gathered):
+            print(f"rank {rank}: outputs differ across ranks")
+            ok = False
+        kv.destroy()
+    be.comm_destroy()
+    be.shutdown()
+    flag = torch.tensor([1 if ok else 0])
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    dist.destroy_process_group()
+    if rank == 0:
+        print("splitkv worker:", "PASS" if flag.item() == 1 else "FAIL", f"world={world}")
+    return 0 if flag.item() == 1 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
