@@ -59,6 +59,10 @@ WORKLOADS = {
     # BASELINE config 1
     "cfg1": dict(B=1, ctx=256, layers=24, dtype="f32", split=False,
                  desc="config1: single sequence, pos=255, fp32 KV, 24 layers"),
+    # BASELINE config 5
+    "prefill": dict(B=16, ctx=2048, layers=1, dtype="bf16", split=False, prefill=True,
+                    desc="config5: causal prefill, B=16 per GPU, S=2048, 14Q/2KV heads, d=64, "
+                         "RoPE in fp32 then bf16 q/k/v, fp32 accumulate, tcgen05"),
 }
 
 
@@ -86,6 +90,14 @@ def peaks():
         d = json.load(open(p))
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["bf16_tflops"]), "measured (burst)"
+    return 1590.0, "fallback"
 
 
 def positions(wl, seed=1234):
@@ -248,6 +260,127 @@ def run_reference_arm(args, wl, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def prefill_flops(B, S, n_head=N_HEAD, hd=HD):
+    """Algorithmic causal FLOPs: query t attends t+1 keys; QK and PV are 2
+    FLOPs per multiply-add each."""
+    return 4.0 * hd * n_head * B * S * (S + 1) / 2.0
+
+
+def run_prefill_bench(args, wl, rank, world, local, be, tg, barrier, max_over_ranks, sampler):
+    import torch
+    B, S = wl["B"], wl["ctx"]
+    kv = tg.KVCache(be, 1, B, S, dtype=tg.DTYPE_BF16)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(2000 + rank)
+    q = torch.randn(B, S, QD, device="cuda", generator=g)
+    k = torch.randn(B, S, KD, device="cuda", generator=g)
+    v = torch.randn(B, S, KD, device="cuda", generator=g)
+    out = torch.zeros(B, S, QD, device="cuda")
+    stream = torch.cuda.ExternalStream(be.stream())
+    kv.prefill(0, B, S, q, k, v, out)
+    be.synchronize()
+    be.graph_begin()
+    kv.prefill(0, B, S, q, k, v, out)
+    graph = be.graph_end()
+    for _ in range(args.warmup):
+        graph.launch()
+    be.synchronize()
+    barrier()
+    launches0 = be.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    e0.record(stream)
+    for _ in range(args.steps):
+        graph.launch()
+    e1.record(stream)
+    be.synchronize()
+    t1 = time.time()
+    launches = be.launch_count() - launches0
+    barrier()
+    ms_step = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    clocks = sampler.stop(t0, t1) if sampler else None
+    flops = prefill_flops(B, S)
+    value = flops * world / (ms_step * 1e-3) / 1e12
+    be.profile_enable(True)
+    be.graph_begin()
+    kv.prefill(0, B, S, q, k, v, out)
+    gprof = be.graph_end()
+    be.profile_enable(False)
+    kms, kn = 0.0, 0
+    for _ in range(max(3, min(args.steps, 20))):
+        gprof.launch()
+        a, n = be.profile_read()
+        kms += a
+        kn += n
+    gprof.destroy()
+    k_ms = kms / max(kn, 1)
+    peak, peak_kind = tensor_peak()
+    achieved = flops / (k_ms * 1e-3) / 1e12
+    achieved = -max_over_ranks(-achieved) if world > 1 else achieved
+    # end to end: fp32 inputs from pinned host memory, output back to host
+    qh = torch.randn(B, S, QD).pin_memory()
+    kh = torch.randn(B, S, KD).pin_memory()
+    vh = torch.randn(B, S, KD).pin_memory()
+    oh = torch.zeros(B, S, QD).pin_memory()
+    for _ in range(2):
+        kv.prefill(0, B, S, qh, kh, vh, oh)
+    barrier()
+    n_e2e = max(3, args.steps // 4)
+    t = time.perf_counter()
+    for _ in range(n_e2e):
+        kv.prefill(0, B, S, qh, kh, vh, oh)
+    e2e_s = max_over_ranks(time.perf_counter() - t)
+    e2e = flops * world * n_e2e / e2e_s / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        O = load_oracle()
+        if O.ref_available():
+            Ss = 1024
+            qs = O.round_bf16(O.normal(11, Ss * QD)).reshape(Ss, QD)
+            ks = O.round_bf16(O.normal(12, Ss * KD)).reshape(Ss, KD)
+            vs = O.round_bf16(O.normal(13, Ss * KD)).reshape(Ss, KD)
+            kc = np.zeros_like(ks)
+            vc = np.zeros_like(vs)
+            ctx_o = np.empty(QD, np.float32)
+            R = O.ref()
+            tt = time.perf_counter()
+            for t_ in range(Ss):
+                qq = np.ascontiguousarray(qs[t_])
+                R.tgref_cache_write_attention(qq, np.ascontiguousarray(ks[t_]),
+                                              np.ascontiguousarray(vs[t_]), ctx_o,
+                                              kc.reshape(-1), vc.reshape(-1), t_)
+            dt = time.perf_counter() - tt
+            cpu = {"value": prefill_flops(1, Ss) / dt / 1e12, "unit": "TFLOP/s", "cores": 1,
+                   "kind": "reference",
+                   "sample": f"1 sequence x {Ss} tokens processed token by token by the "
+                             f"reference code (tmac_gguf.cpp:1090-1128), single-threaded, "
+                             f"{dt:.2f} s"}
+    if rank == 0:
+        line = {
+            "metric": "causal prefill attention TFLOP/s (algorithmic causal FLOPs / time)",
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": wl["desc"], "batch": B, "seq_len": S, "n_head": N_HEAD,
+                       "n_kv_head": N_KV, "head_dim": HD,
+                       "parallelism": f"sequence-partitioned x{world}",
+                       "l2": "inputs 151 MB fp32 per step > L2"},
+            "gpu_launches": launches,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "peak_kind": peak_kind,
+                         "kernel": "prefill_attn_kernel", "flops_per_launch": flops,
+                         "launch_ms": k_ms, "traffic": None},
+            "e2e": {"value": e2e, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": B * S * (QD + 2 * KD) * 4,
+                    "d2h_bytes_per_step": B * S * QD * 4},
+            "clocks": clocks, "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    graph.destroy()
+    kv.destroy()
+
+
 # ---------------------------------------------------------------- GPU arm
 
 def main():
@@ -281,6 +414,26 @@ def main():
                                 device_id=torch.device("cuda", local))
     tg = load_package()
     be = tg.CudaBackend(local)
+    if wl.get("prefill"):
+        def barrier_p():
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+
+        def max_p(x):
+            if world == 1:
+                return x
+            t = torch.tensor([x], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+        sampler = ClockSampler(set(range(world))) if local == 0 else None
+        time.sleep(0.3 if sampler else 0)
+        run_prefill_bench(args, wl, rank, world, local, be, tg, barrier_p, max_p, sampler)
+        be.shutdown()
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     split = wl["split"] and world > 1
     if split:
         uid = [tg.comm_unique_id() if rank == 0 else None]

@@ -207,6 +207,22 @@ TG_API int tg_decode_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_se
                     float* q, float* k_new, const float* v_new,
                     const int32_t* pos, float* out);
 
+/* ------------------------------------------------- prefill */
+
+/* Causal prefill of one layer for n_seqs prompts of S tokens (positions
+ * 0..S-1).  The reference runs a prompt token by token (process_prompt,
+ * tmac_gguf.cpp:1621-1658: one decode step per position); this computes the
+ * same attention for all S positions at once on the tcgen05 tensor cores.
+ * q [n_seqs][S][n_head*head_dim], k/v [n_seqs][S][n_kv*head_dim] are fp32
+ * and un-rotated; RoPE is applied in fp32 exactly as apply_rope
+ * (tmac_gguf.cpp:990-1016) and the rotated q, k and v are rounded to bf16.
+ * The k and v rows are written to the cache (rows 0..S-1 of each
+ * sequence), so decode can continue from position S.  out
+ * [n_seqs][S][n_head*head_dim] fp32.  Needs a bf16 cache with head_dim 64
+ * that is not a split-KV shard, and S <= max_ctx. */
+TG_API int tg_prefill_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, int S,
+                            const float* q, const float* k, const float* v, float* out);
+
 /* ------------------------------------------------- split-KV across GPUs */
 
 /* NCCL unique id (128 bytes) for tg_comm_init; call on one rank and share

@@ -61,13 +61,21 @@ def oracle_decode(seed: int, pos: int, bf16: bool = False, seq: int = 0,
     return q, k, v_new, kc, vc, ctx
 
 
+def prefill_raw(seed: int, S: int, seq: int = 0):
+    """Un-rotated fp32 prefill inputs q [S][896], k/v [S][128] ~ N(0,1)."""
+    q = O.normal(O.derive_seed(seed, 0, seq, T_Q), S * QD).reshape(S, QD)
+    k = O.normal(O.derive_seed(seed, 0, seq, T_KNEW), S * KD).reshape(S, KD)
+    v = O.normal(O.derive_seed(seed, 0, seq, T_VNEW), S * KD).reshape(S, KD)
+    return q, k, v
+
+
 def prefill_inputs(seed: int, S: int, seq: int = 0):
     """Prefill inputs: q/k/v ~ N(0,1), RoPE applied to q and k in binary32 at
     positions 0..S-1 with the reference formula, then all three rounded to
     bf16.  Returns float32 arrays q [S][896], k/v [S][128] (bf16 values)."""
-    q = O.normal(O.derive_seed(seed, 0, seq, T_Q), S * QD).reshape(S, QD)
-    k = O.normal(O.derive_seed(seed, 0, seq, T_KNEW), S * KD).reshape(S, KD)
-    v = O.normal(O.derive_seed(seed, 0, seq, T_VNEW), S * KD).reshape(S, KD)
+    q, k, v = prefill_raw(seed, S, seq)
+    q = q.copy()
+    k = k.copy()
     for t in range(S):
         q[t] = O.rope_heads(q[t], O.N_HEAD, O.HEAD_DIM, t)
         k[t] = O.rope_heads(k[t], O.N_KV_HEAD, O.HEAD_DIM, t)

@@ -412,6 +412,11 @@ def test_errors_are_reported(tg, backend, cases):
         kv.attention(0, q, bad, out)                            # device-side check
     assert e.value.status == tg.TG_ERR_DEVICE
     kv.attention(0, q, np.array([3, 5], np.int32), out)         # context recovers
+    # a device view that is only 4-byte aligned is refused before any launch
+    qmis = torch.zeros(2 * 896 + 1, device="cuda")[1:].view(2, 896)
+    with pytest.raises(tg.TGError) as e:
+        kv.attention(0, qmis, np.array([3, 5], np.int32), out)
+    assert e.value.status == tg.TG_ERR_INVALID_ARG
     with pytest.raises(tg.TGError) as e:
         backend.elem_op(1, np.zeros(4, np.float32), np.zeros(4, np.float32), 4)
     assert e.value.status == tg.TG_ERR_UNSUPPORTED

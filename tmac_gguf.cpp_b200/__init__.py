@@ -111,6 +111,8 @@ _SIGS = {
                                        _vp]),
     "tg_decode_layer_splitkv": (C.c_int, [_vp, _vp, C.c_int, C.c_int, _vp,
                                           _vp, _vp, _vp, _vp]),
+    "tg_prefill_layer": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.c_int, _vp, _vp,
+                                   _vp, _vp]),
     "tg_attention_records": (C.c_int, [_vp, _vp, C.c_int, C.c_int, _vp, _vp,
                                        _vp]),
     "tg_merge_records": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_int,
@@ -456,6 +458,11 @@ class KVCache:
         past_len = _as_i32(past_len)
         _check(lib().tg_attention_splitkv(self.backend.handle, self._h, layer,
                                           n, _ptr(q), _ptr(past_len), _ptr(out)))
+
+    def prefill(self, layer: int, n_seqs: int, S: int, q, k, v, out) -> None:
+        """Causal prefill of positions 0..S-1 (tg_prefill_layer)."""
+        _check(lib().tg_prefill_layer(self.backend.handle, self._h, layer, n_seqs,
+                                      S, _ptr(q), _ptr(k), _ptr(v), _ptr(out)))
 
     def attention_records(self, layer: int, q, past_len, records) -> None:
         """Softmax records of this shard (see tg_attention_records)."""

@@ -159,6 +159,7 @@ struct tg_context {
   float* recv = nullptr;     size_t recv_cap = 0;    // floats
 
   char* arena = nullptr;     size_t arena_cap = 0, arena_off = 0;
+  uint16_t* qbf = nullptr;   size_t qbf_cap = 0;     // prefill: rotated bf16 q
   std::vector<PendingCopy> pending;  // device -> host copies of staged outputs
   std::vector<void*> graveyard;      // device buffers freed at the next sync
 
@@ -198,6 +199,9 @@ struct tg_kv_cache {
   bool tmap_ok = false;
   alignas(64) CUtensorMap tmk;
   alignas(64) CUtensorMap tmv;
+  bool tmap128_ok = false;        // 128-row boxes for the prefill kernel
+  alignas(64) CUtensorMap tmk128;
+  alignas(64) CUtensorMap tmv128;
   int global_ctx = 0;
 };
 
@@ -557,6 +561,14 @@ int get_table(tg_context* ctx, float base, int head_dim, int need_len, RopeTable
   return TG_OK;
 }
 
+// The kernels move q, k and outputs as float2 / float4: device pointers must
+// be 8-byte aligned (host pointers are staged into aligned buffers).
+int check_align8(const void* p, const char* what) {
+  if (p && (reinterpret_cast<uintptr_t>(p) & 7))
+    return fail(TG_ERR_INVALID_ARG, "%s must be 8-byte aligned", what);
+  return TG_OK;
+}
+
 int check_shape(int n_head, int n_kv, int hd) {
   if (n_head <= 0 || n_kv <= 0 || hd <= 0 || hd % 2 || hd > 128 || n_head % n_kv)
     return fail(TG_ERR_INVALID_ARG, "unsupported shape n_head=%d n_kv_head=%d head_dim=%d", n_head,
@@ -584,6 +596,8 @@ int generic_grid(tg_context* ctx, int dtype, size_t smem) {
 int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const float* q,
                const int* past_dev, int past_scalar, float* out, int mode) {
   const tg_kv_desc& d = kv->d;
+  TG_TRY(check_align8(q, "q"));
+  TG_TRY(check_align8(out, "out"));
   const int rf = tg::record_floats(d.n_head, d.head_dim);
   tg::DecodeParams p{};
   p.q = q;
@@ -603,6 +617,10 @@ int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const f
   p.scale_log2 = kLog2e / sqrtf((float)d.head_dim);
   p.mode = mode;
   p.err = ctx->d_err;
+  p.aligned16 = ((reinterpret_cast<uintptr_t>(p.k) | reinterpret_cast<uintptr_t>(p.v)) % 16 == 0 &&
+                 (kv->row_elems * kv->esize) % 16 == 0)
+                    ? 1
+                    : 0;
 
   const bool mma = mma_eligible(kv);
   int grid;
@@ -663,6 +681,8 @@ int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const f
 int run_rope(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, float* q, float* k,
              const float* v, const int* pos_dev) {
   const tg_kv_desc& d = kv->d;
+  TG_TRY(check_align8(q, "q"));
+  TG_TRY(check_align8(k, "k_new"));
   RopeTable* t = nullptr;
   TG_TRY(get_table(ctx, d.rope_base, d.head_dim, kv->global_ctx, &t));
   tg::RopeParams rp{};
@@ -786,6 +806,7 @@ int tg_shutdown(tg_context* ctx) {
   cudaFree(ctx->records);
   cudaFree(ctx->recv);
   cudaFree(ctx->arena);
+  cudaFree(ctx->qbf);
   cudaFree(ctx->d_err);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -937,6 +958,7 @@ int tg_rope_op(tg_context* ctx, float* data, int n_heads, int head_dim, int pos,
                 n_heads, head_dim, pos);
   char* d = nullptr;
   TG_TRY(resolve(ctx, data, (size_t)n_heads * head_dim * 4, true, &d));
+  TG_TRY(check_align8(d, "data"));
   RopeTable* t = nullptr;
   TG_TRY(get_table(ctx, base, head_dim, pos + 1, &t));
   tg::RopeParams rp{};
@@ -1058,6 +1080,14 @@ int tg_kv_create(tg_context* ctx, const tg_kv_desc* desc, tg_kv_cache** out) {
                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
       kv->tmap_ok = (r1 == CUDA_SUCCESS && r2 == CUDA_SUCCESS);
+      cuuint32_t box128[2] = {64, 128};
+      CUresult r3 = enc(&kv->tmk128, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv->k, gdim, gstride,
+                        box128, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      CUresult r4 = enc(&kv->tmv128, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv->v, gdim, gstride,
+                        box128, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      kv->tmap128_ok = (r3 == CUDA_SUCCESS && r4 == CUDA_SUCCESS);
     }
   }
   RopeTable* t = nullptr;
@@ -1420,6 +1450,100 @@ int tg_decode_layer_splitkv(tg_context* ctx, tg_kv_cache* kv, int layer, int n_s
                   static_cast<const float*>(dv), static_cast<const int*>(dp)));
   TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
                       static_cast<const int*>(dp), static_cast<float*>(dout)));
+  return finish_call(ctx);
+}
+
+// ------------------------------------------------ prefill
+
+int tg_prefill_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, int S,
+                     const float* q, const float* k, const float* v, float* out) {
+  TG_TRY(check_kv_call(ctx, kv, layer, n_seqs));
+  if (!q || !k || !v || !out) return fail(TG_ERR_INVALID_ARG, "null argument");
+  if (n_seqs == 0 || S == 0) return TG_OK;
+  const tg_kv_desc& d = kv->d;
+  if (d.dtype != TG_DTYPE_BF16 || d.head_dim != 64 || !kv->tmap128_ok)
+    return fail(TG_ERR_UNSUPPORTED, "prefill needs a bf16 cache with head_dim 64");
+  if (d.shard_start != 0) return fail(TG_ERR_UNSUPPORTED, "prefill on a split-KV shard");
+  if (S < 0 || S > d.max_ctx)
+    return fail(TG_ERR_INVALID_ARG, "prefill length %d outside [1, %d]", S, d.max_ctx);
+  if ((long long)n_seqs * S * d.n_head >= (1LL << 31))
+    return fail(TG_ERR_INVALID_ARG, "prefill of %d x %d positions is too large", n_seqs, S);
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return fail(TG_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+  const size_t qd = (size_t)d.n_head * d.head_dim, kd = kv->row_elems;
+  const size_t rows = (size_t)n_seqs * S;
+  const void *dq = nullptr, *dk = nullptr, *dv = nullptr;
+  void* dout = nullptr;
+  TG_TRY(stage_in(ctx, q, rows * qd * 4, &dq));
+  TG_TRY(stage_in(ctx, k, rows * kd * 4, &dk));
+  TG_TRY(stage_in(ctx, v, rows * kd * 4, &dv));
+  TG_TRY(stage_out(ctx, out, rows * qd * 4, false, &dout));
+  RopeTable* t = nullptr;
+  TG_TRY(get_table(ctx, d.rope_base, d.head_dim, S, &t));
+  TG_TRY(ensure_buf(ctx, &ctx->qbf, &ctx->qbf_cap, rows * qd));
+
+  tg::PrefillRopeParams rp{};
+  rp.q = static_cast<const float*>(dq);
+  rp.k = static_cast<const float*>(dk);
+  rp.v = static_cast<const float*>(dv);
+  rp.cs = t->d;
+  rp.q_bf16 = ctx->qbf;
+  rp.k_cache = reinterpret_cast<uint16_t*>(static_cast<char*>(kv->k) +
+                                           (size_t)layer * kv->layer_elems * kv->esize);
+  rp.v_cache = reinterpret_cast<uint16_t*>(static_cast<char*>(kv->v) +
+                                           (size_t)layer * kv->layer_elems * kv->esize);
+  rp.B = n_seqs;
+  rp.S = S;
+  rp.n_head = d.n_head;
+  rp.n_kv = d.n_kv_head;
+  rp.head_dim = d.head_dim;
+  rp.max_ctx = d.max_ctx;
+  cudaError_t e = tg::launch_prefill_rope(rp, ctx->stream);
+  if (e != cudaSuccess) return fail(TG_ERR_CUDA, "prefill rope launch: %s", cudaGetErrorString(e));
+  ctx->launches++;
+
+  // Rotated q as {64, n_head, rows}: one box = 128 positions of one head.
+  alignas(64) CUtensorMap tq;
+  cuuint64_t gdim[3] = {64, (cuuint64_t)d.n_head, (cuuint64_t)rows};
+  cuuint64_t gstride[2] = {128, (cuuint64_t)d.n_head * 128};
+  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ctx->qbf, gdim, gstride, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TG_ERR_CUDA, "q tensor map rejected (%d)", (int)r);
+  tg::PrefillParams pp{};
+  pp.out = static_cast<float*>(dout);
+  pp.err = ctx->d_err;
+  pp.row0 = (long long)layer * d.n_seqs * d.max_ctx;
+  pp.B = n_seqs;
+  pp.S = S;
+  pp.n_head = d.n_head;
+  pp.n_kv = d.n_kv_head;
+  pp.group = d.n_head / d.n_kv_head;
+  pp.max_ctx = d.max_ctx;
+  pp.n_qt = (S + 127) / 128;
+  pp.scale_log2 = kLog2e / sqrtf((float)d.head_dim);
+  const long long items = (long long)n_seqs * d.n_head * pp.n_qt;
+  const int grid = (int)(items < ctx->num_sms ? items : ctx->num_sms);
+  cudaEvent_t ev_stop = nullptr;
+  if (ctx->prof_on) {
+    while (ctx->prof_ev.size() < ctx->prof_used + 2) {
+      cudaEvent_t ev;
+      TG_CUDA(cudaEventCreate(&ev));
+      ctx->prof_ev.push_back(ev);
+    }
+    TG_CUDA(cudaEventRecordWithFlags(ctx->prof_ev[ctx->prof_used], ctx->stream,
+                                     ctx->capturing ? cudaEventRecordExternal : 0));
+    ev_stop = ctx->prof_ev[ctx->prof_used + 1];
+    ctx->prof_used += 2;
+  }
+  e = tg::launch_prefill_attn(tq, kv->tmk128, kv->tmv128, pp, grid, ctx->stream);
+  if (e != cudaSuccess) return fail(TG_ERR_CUDA, "prefill attention launch: %s", cudaGetErrorString(e));
+  ctx->launches++;
+  if (ev_stop)
+    TG_CUDA(cudaEventRecordWithFlags(ev_stop, ctx->stream,
+                                     ctx->capturing ? cudaEventRecordExternal : 0));
   return finish_call(ctx);
 }
 

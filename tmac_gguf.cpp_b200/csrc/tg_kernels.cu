@@ -41,16 +41,35 @@ __global__ void __launch_bounds__(128) rope_cache_write_kernel(const RopeParams 
   const int hd = p.head_dim, half = hd >> 1;
   const float* cs = p.cs + (size_t)pos * hd;  // [half][cos, sin]
 
+  // Every thread first loads up to RU pairs (and their cos/sin), then
+  // rotates and stores them: one memory latency per batch, not per pair.
+  constexpr int RU = 4;
   if (p.q) {
     float* q = p.q + (size_t)s * p.n_head * hd;
-    for (int i = threadIdx.x; i < p.n_head * half; i += blockDim.x) {
-      const int h = i / half, j = i - h * half;
-      const int idx = h * hd + 2 * j;
-      const float x0 = q[idx], x1 = q[idx + 1];
-      const float c = cs[2 * j], sn = cs[2 * j + 1];
-      // x0*c - x1*s and x0*s + x1*c, each product and sum rounded once.
-      q[idx] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
-      q[idx + 1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    const int n_pairs = p.n_head * half;
+    for (int b0 = 0; b0 < n_pairs; b0 += blockDim.x * RU) {
+      float2 x[RU], c2[RU];
+#pragma unroll
+      for (int u = 0; u < RU; ++u) {
+        const int i = b0 + u * blockDim.x + threadIdx.x;
+        if (i < n_pairs) {
+          const int h = i / half, j = i - h * half;
+          x[u] = *reinterpret_cast<const float2*>(q + h * hd + 2 * j);
+          c2[u] = *reinterpret_cast<const float2*>(cs + 2 * j);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < RU; ++u) {
+        const int i = b0 + u * blockDim.x + threadIdx.x;
+        if (i < n_pairs) {
+          const int h = i / half, j = i - h * half;
+          // x0*c - x1*s and x0*s + x1*c, each product and sum rounded once.
+          float2 y;
+          y.x = __fsub_rn(__fmul_rn(x[u].x, c2[u].x), __fmul_rn(x[u].y, c2[u].y));
+          y.y = __fadd_rn(__fmul_rn(x[u].x, c2[u].y), __fmul_rn(x[u].y, c2[u].x));
+          *reinterpret_cast<float2*>(q + h * hd + 2 * j) = y;
+        }
+      }
     }
   }
 
@@ -61,24 +80,36 @@ __global__ void __launch_bounds__(128) rope_cache_write_kernel(const RopeParams 
 
   if (p.k) {
     float* k = p.k + (size_t)s * kdim;
-    for (int i = threadIdx.x; i < p.n_kv * half; i += blockDim.x) {
-      const int h = i / half, j = i - h * half;
-      const int idx = h * hd + 2 * j;
-      const float x0 = k[idx], x1 = k[idx + 1];
-      const float c = cs[2 * j], sn = cs[2 * j + 1];
-      const float r0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
-      const float r1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
-      k[idx] = r0;
-      k[idx + 1] = r1;
-      if (write) {
-        if (p.dtype == 0) {
-          float* kc = static_cast<float*>(p.k_cache) + row;
-          kc[idx] = r0;
-          kc[idx + 1] = r1;
-        } else {
-          __nv_bfloat16* kc = static_cast<__nv_bfloat16*>(p.k_cache) + row;
-          kc[idx] = __float2bfloat16_rn(r0);
-          kc[idx + 1] = __float2bfloat16_rn(r1);
+    const int n_pairs = p.n_kv * half;
+    for (int b0 = 0; b0 < n_pairs; b0 += blockDim.x * RU) {
+      float2 x[RU], c2[RU];
+#pragma unroll
+      for (int u = 0; u < RU; ++u) {
+        const int i = b0 + u * blockDim.x + threadIdx.x;
+        if (i < n_pairs) {
+          const int h = i / half, j = i - h * half;
+          x[u] = *reinterpret_cast<const float2*>(k + h * hd + 2 * j);
+          c2[u] = *reinterpret_cast<const float2*>(cs + 2 * j);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < RU; ++u) {
+        const int i = b0 + u * blockDim.x + threadIdx.x;
+        if (i < n_pairs) {
+          const int h = i / half, j = i - h * half;
+          const int idx = h * hd + 2 * j;
+          const float r0 = __fsub_rn(__fmul_rn(x[u].x, c2[u].x), __fmul_rn(x[u].y, c2[u].y));
+          const float r1 = __fadd_rn(__fmul_rn(x[u].x, c2[u].y), __fmul_rn(x[u].y, c2[u].x));
+          *reinterpret_cast<float2*>(k + idx) = make_float2(r0, r1);
+          if (write) {
+            if (p.dtype == 0) {
+              *reinterpret_cast<float2*>(static_cast<float*>(p.k_cache) + row + idx) =
+                  make_float2(r0, r1);
+            } else {
+              *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p.k_cache) + row +
+                                                 idx) = __floats2bfloat162_rn(r0, r1);
+            }
+          }
         }
       }
     }
@@ -491,7 +522,7 @@ size_t decode_generic_smem(int B, int n_head, int n_kv, int hd) {
 }
 
 template <typename Elem>
-__global__ void __launch_bounds__(GEN_THREADS) decode_generic_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(GEN_THREADS, 4) decode_generic_kernel(const DecodeParams p) {
   extern __shared__ float gsm[];
   const GenLayout Ly = gen_layout(p.B, p.n_head, p.n_kv, p.head_dim);
   float* q_s = gsm + Ly.q_off;
@@ -529,7 +560,24 @@ __global__ void __launch_bounds__(GEN_THREADS) decode_generic_kernel(const Decod
     while (prefix[s + 1] <= t) ++s;
     if (new_seg) {
       seg_lo = t;
-      for (int i = tid; i < qdim; i += GEN_THREADS) q_s[i] = p.q[(size_t)s * qdim + i];
+      const float* qsrc = p.q + (size_t)s * qdim;
+      if ((qdim & 3) == 0 && (reinterpret_cast<uintptr_t>(qsrc) & 15) == 0) {
+        // All of this thread's 16-byte loads first, then the stores.
+        constexpr int QU = 8;  // 8 x 128 x 4 floats covers n_head*head_dim <= 4096
+        float4 r[QU];
+#pragma unroll
+        for (int u = 0; u < QU; ++u) {
+          const int e = tid + u * GEN_THREADS;
+          if (e < (qdim >> 2)) r[u] = reinterpret_cast<const float4*>(qsrc)[e];
+        }
+#pragma unroll
+        for (int u = 0; u < QU; ++u) {
+          const int e = tid + u * GEN_THREADS;
+          if (e < (qdim >> 2)) reinterpret_cast<float4*>(q_s)[e] = r[u];
+        }
+      } else {
+        for (int i = tid; i < qdim; i += GEN_THREADS) q_s[i] = qsrc[i];
+      }
       for (int h = tid; h < p.n_head; h += GEN_THREADS) {
         m_s[h] = -INFINITY;
         l_s[h] = 0.f;
@@ -541,11 +589,47 @@ __global__ void __launch_bounds__(GEN_THREADS) decode_generic_kernel(const Decod
     const int n_loc = local_rows(past_of(p, s), p.shard_start, p.max_ctx);
     const int nv = min(GEN_TILE, n_loc - j * GEN_TILE);
     const size_t row0 = (size_t)s * p.max_ctx + (size_t)j * GEN_TILE;
-    // Stage the valid rows of K and V as fp32 with a padded row stride.
-    for (int e = tid; e < nv * kdim; e += GEN_THREADS) {
-      const int rr = e / kdim, cc = e - rr * kdim;
-      k_s[rr * rp + cc] = to_f32(kbase[(row0 + rr) * kdim + cc]);
-      v_s[rr * rp + cc] = to_f32(vbase[(row0 + rr) * kdim + cc]);
+    // Stage the valid rows of K and V as fp32 with a padded row stride.  With
+    // 16-byte aligned rows, every 16-byte load of a batch is issued before
+    // any of them is used, so a tile costs one memory latency, not one per
+    // loop trip.
+    if (p.aligned16) {
+      constexpr int VEC = 16 / sizeof(Elem);
+      constexpr int UNROLL = 4;
+      const int nvec = nv * kdim / VEC;
+      const uint4* ksrc = reinterpret_cast<const uint4*>(kbase + row0 * kdim);
+      const uint4* vsrc = reinterpret_cast<const uint4*>(vbase + row0 * kdim);
+      for (int b0 = 0; b0 < nvec; b0 += GEN_THREADS * UNROLL) {
+        uint4 kr[UNROLL], vr[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+          const int e = b0 + u * GEN_THREADS + tid;
+          if (e < nvec) {
+            kr[u] = ksrc[e];
+            vr[u] = vsrc[e];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+          const int e = b0 + u * GEN_THREADS + tid;
+          if (e < nvec) {
+            const int idx = e * VEC, rr = idx / kdim, cc = idx - rr * kdim;
+            const Elem* ke = reinterpret_cast<const Elem*>(&kr[u]);
+            const Elem* ve = reinterpret_cast<const Elem*>(&vr[u]);
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+              k_s[rr * rp + cc + i] = to_f32(ke[i]);
+              v_s[rr * rp + cc + i] = to_f32(ve[i]);
+            }
+          }
+        }
+      }
+    } else {
+      for (int e = tid; e < nv * kdim; e += GEN_THREADS) {
+        const int rr = e / kdim, cc = e - rr * kdim;
+        k_s[rr * rp + cc] = to_f32(kbase[(row0 + rr) * kdim + cc]);
+        v_s[rr * rp + cc] = to_f32(vbase[(row0 + rr) * kdim + cc]);
+      }
     }
     __syncthreads();
     // Scores and the online-softmax update: warp w owns heads w, w+4, ...
@@ -555,9 +639,16 @@ __global__ void __launch_bounds__(GEN_THREADS) decode_generic_kernel(const Decod
       if (lane < nv) {
         const float* qh = q_s + h * hd;
         const float* kr = k_s + lane * rp + kv * hd;
-        float a = 0.f;
-        for (int d = 0; d < hd; ++d) a = fmaf(qh[d], kr[d], a);
-        sc = a * p.scale_log2;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int d = 0;
+        for (; d + 3 < hd; d += 4) {
+          a0 = fmaf(qh[d], kr[d], a0);
+          a1 = fmaf(qh[d + 1], kr[d + 1], a1);
+          a2 = fmaf(qh[d + 2], kr[d + 2], a2);
+          a3 = fmaf(qh[d + 3], kr[d + 3], a3);
+        }
+        for (; d < hd; ++d) a0 = fmaf(qh[d], kr[d], a0);
+        sc = ((a0 + a1) + (a2 + a3)) * p.scale_log2;
       }
       const float mx = warp_max(sc);
       const float m_old = m_s[h];

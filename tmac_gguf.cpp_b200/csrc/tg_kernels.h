@@ -36,4 +36,14 @@ cudaError_t launch_fill_normal(void* out, size_t n, int dtype, uint64_t seed,
 cudaError_t launch_convert_rows(void* dst, const float* src, size_t n,
                                 int dtype, int num_sms, cudaStream_t st);
 
+// Prefill (tg_prefill.cu).  The attention kernel needs a bf16 cache with
+// head_dim 64 and S a positive length; tq is a 3-D map of the rotated bf16 q
+// ({64, n_head, B*S}, box {64, 1, 128}), tk / tv 2-D maps of the cache with
+// 128-row boxes.
+cudaError_t launch_prefill_rope(const PrefillRopeParams& p, cudaStream_t st);
+cudaError_t launch_prefill_attn(const CUtensorMap& tq, const CUtensorMap& tk,
+                                const CUtensorMap& tv, const PrefillParams& p, int grid,
+                                cudaStream_t st);
+size_t prefill_attn_smem();
+
 }  // namespace tg

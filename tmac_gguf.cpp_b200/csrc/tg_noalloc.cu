@@ -104,6 +104,8 @@ extern "C" TG_API int tg_attention_noalloc(void* cuda_stream, const float* q, co
                                            int* device_status) {
   if (!q || !k_cache || !v_cache || !past_len || !out)
     return err(TG_ERR_INVALID_ARG, "tg_attention_noalloc: null buffer");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 7)
+    return err(TG_ERR_INVALID_ARG, "tg_attention_noalloc: q and out must be 8-byte aligned");
   if (dtype != TG_DTYPE_F32 && dtype != TG_DTYPE_BF16)
     return err(TG_ERR_INVALID_ARG, "tg_attention_noalloc: dtype %d", dtype);
   if (n_head <= 0 || n_kv_head <= 0 || head_dim <= 0 || head_dim % 2 || head_dim > 128 ||
@@ -156,6 +158,10 @@ extern "C" TG_API int tg_attention_noalloc(void* cuda_stream, const float* q, co
   p.shard_start = 0;
   p.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
   p.mode = 0;
+  p.aligned16 = ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) %
+                     16 == 0)
+                    ? 1
+                    : 0;
 
   const bool mma = dtype == TG_DTYPE_BF16 && head_dim == 64 &&
                    (n_kv_head == 1 || n_kv_head == 2 || n_kv_head == 4) &&

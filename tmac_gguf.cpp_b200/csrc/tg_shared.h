@@ -79,6 +79,7 @@ struct DecodeParams {
   float scale_log2;      // log2(e) / sqrt(head_dim)
   int mode;              // 0: normalised output, 1: records (split-KV)
   int past_len_scalar;   // used for every sequence when past_len == null
+  int aligned16;         // k and v rows start on 16-byte boundaries
 };
 
 TG_HD int past_of(const DecodeParams& p, int s) {
@@ -113,6 +114,27 @@ struct RopeParams {
   int B, n_head, n_kv, head_dim;
   int max_ctx, shard_start, dtype;  // dtype: 0 f32, 1 bf16
   int* err;
+};
+
+// Prefill: RoPE of positions 0..S-1 + bf16 rounding + cache rows.
+struct PrefillRopeParams {
+  const float* q;        // [B][S][n_head*head_dim] un-rotated
+  const float* k;        // [B][S][n_kv*head_dim] un-rotated
+  const float* v;        // [B][S][n_kv*head_dim]
+  const float* cs;       // RoPE table
+  uint16_t* q_bf16;      // [B][S][n_head][head_dim] rotated, bf16 bits
+  uint16_t* k_cache;     // layer base of the bf16 cache
+  uint16_t* v_cache;
+  int B, S, n_head, n_kv, head_dim, max_ctx;
+};
+
+// Prefill: causal attention of positions 0..S-1 over cache rows 0..S-1.
+struct PrefillParams {
+  float* out;            // [B][S][n_head][64] fp32
+  int* err;
+  long long row0;        // TMA row of (this layer, sequence 0, row 0)
+  int B, S, n_head, n_kv, group, max_ctx, n_qt;
+  float scale_log2;
 };
 
 }  // namespace tg
