@@ -119,11 +119,15 @@ def algo_bytes_step(wl, pos):
 
 
 def kernel_bytes_launch(wl, pos, shard_start, shard_len, split):
-    """Algorithmic bytes of one decode-attention launch on one rank."""
+    """Algorithmic bytes of one decode launch on one rank: this shard's K and
+    V rows read once, the new row written by its owner, q read and the
+    output written (the fused kernel does RoPE, cache-write and attention)."""
     s_kv = 2 if wl["dtype"] == "bf16" else 4
-    n_loc = np.clip(pos.astype(np.int64) + 1 - shard_start, 0, shard_len)
-    out_b = N_HEAD * (HD + 2) * 4 if split else QD * 4
-    return int(np.sum(n_loc * 2 * KD * s_kv) + len(pos) * (QD * 4 + out_b))
+    p1 = pos.astype(np.int64) + 1
+    n_loc = np.clip(p1 - shard_start, 0, shard_len)
+    owner = (pos >= shard_start) & (pos < shard_start + shard_len)
+    return int(np.sum(n_loc * 2 * KD * s_kv) + int(owner.sum()) * 2 * KD * s_kv
+               + len(pos) * 2 * QD * 4)
 
 
 class ClockSampler:
@@ -589,7 +593,7 @@ def main():
             "gpu_launches": launches,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak,
                          "unit": "GB/s", "frac": achieved / hbm_peak,
-                         "peak_kind": peak_kind, "kernel": "decode_mma_kernel"
+                         "peak_kind": peak_kind, "kernel": "decode_fused_kernel"
                          if kv.uses_tensor_cores() else "decode_generic_kernel",
                          "bytes_per_launch": k_bytes, "launch_ms": k_avg_ms,
                          "traffic": None},

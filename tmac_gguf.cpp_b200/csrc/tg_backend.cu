@@ -175,6 +175,16 @@ struct tg_context {
   int rank = 0, world = 1;
   int timeout_ms = 60000;
 
+
+  // Peer-memory exchange of split-KV records (IPC-mapped receive buffers).
+  bool p2p_ready = false, p2p_failed = false;
+  int p2p_bcap = 0, p2p_rf = 0, p2p_heads = 0;
+  float* recv_local = nullptr;
+  unsigned* flags_local = nullptr;  // flags, then the epoch word and the done counter
+  float* recv_peer[tg::kMaxPeers] = {};
+  unsigned* flags_peer[tg::kMaxPeers] = {};
+  unsigned char* nccl_stage = nullptr;  // small device staging for handle exchange
+
   std::vector<tg_kv_cache*> caches;  // freed by tg_shutdown if still alive
 
   // Optional CUDA-event timing of each decode-attention kernel launch.
@@ -251,10 +261,11 @@ int check_device_error(tg_context* ctx) {
   TG_CUDA(cudaMemcpy(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
   if (h != 0) {
     TG_CUDA(cudaMemset(ctx->d_err, 0, sizeof(int)));
-    const char* what = h == tg::kDevErrBadPos      ? "position outside the cache / RoPE table"
-                       : h == tg::kDevErrWaitFull  ? "bounded wait for a K/V tile expired"
-                       : h == tg::kDevErrWaitEmpty ? "bounded wait for a free stage expired"
-                                                   : "device error";
+    const char* what = h == tg::kDevErrBadPos         ? "position outside the cache / RoPE table"
+                       : h == tg::kDevErrWaitFull     ? "bounded wait for a K/V tile expired"
+                       : h == tg::kDevErrWaitEmpty    ? "bounded wait for a free stage expired"
+                       : h == tg::kDevErrPeerTimeout  ? "another GPU's softmax record did not arrive"
+                                                      : "device error";
     return fail(TG_ERR_DEVICE, "kernel reported 0x%x: %s", h, what);
   }
   return TG_OK;
@@ -708,6 +719,212 @@ int run_rope(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, float* q,
   return TG_OK;
 }
 
+// All-gather `bytes` per rank through NCCL on the context stream and wait.
+int nccl_allgather_bytes(tg_context* ctx, const void* dsend, void* drecv, size_t bytes) {
+  ncclResult_t r = nccl().AllGather(dsend, drecv, bytes, ncclUint8, ctx->comm, ctx->stream);
+  if (r == ncclInProgress) {
+    const auto t0 = std::chrono::steady_clock::now();
+    do {
+      nccl().CommGetAsyncError(ctx->comm, &r);
+      const double ms = std::chrono::duration<double, std::milli>(
+                            std::chrono::steady_clock::now() - t0)
+                            .count();
+      if (r == ncclInProgress && ms > ctx->timeout_ms) break;
+    } while (r == ncclInProgress);
+  }
+  if (r != ncclSuccess)
+    return fail(TG_ERR_COMM, "ncclAllGather: %s",
+                r == ncclInProgress ? "timeout" : nccl().GetErrorString(r));
+  return wait_stream(ctx);
+}
+
+void p2p_release(tg_context* ctx) {
+  if (!ctx->p2p_ready && !ctx->recv_local) return;
+  cudaStreamSynchronize(ctx->stream);
+  for (int r = 0; r < tg::kMaxPeers; ++r) {
+    if (ctx->recv_peer[r]) cudaIpcCloseMemHandle(ctx->recv_peer[r]);
+    if (ctx->flags_peer[r]) cudaIpcCloseMemHandle(ctx->flags_peer[r]);
+    ctx->recv_peer[r] = nullptr;
+    ctx->flags_peer[r] = nullptr;
+  }
+  cudaFree(ctx->recv_local);
+  cudaFree(ctx->flags_local);
+  ctx->recv_local = nullptr;
+  ctx->flags_local = nullptr;
+  ctx->p2p_ready = false;
+  ctx->p2p_bcap = 0;
+}
+
+// Collective: every rank of the communicator calls this with the same B.
+// Allocates this GPU's receive buffers [2][world][B][rf] and flags
+// [2][world][B][n_head] (+ epoch word and CTA counter), shares
+// their IPC handles over NCCL, maps every peer's, and agrees with all ranks
+// whether peer memory can be used (otherwise all ranks use the NCCL path).
+int ensure_p2p(tg_context* ctx, int B, int n_head, int rf) {
+  if (ctx->p2p_failed) return TG_ERR_UNSUPPORTED;
+  if (ctx->p2p_ready && B <= ctx->p2p_bcap && rf == ctx->p2p_rf && n_head == ctx->p2p_heads)
+    return TG_OK;
+  if (ctx->capturing)
+    return fail(TG_ERR_STATE, "peer buffers must be set up before graph capture");
+  if (ctx->world > tg::kMaxPeers) {
+    ctx->p2p_failed = true;
+    return TG_ERR_UNSUPPORTED;
+  }
+  TG_TRY(wait_stream(ctx));
+  p2p_release(ctx);
+  const int W = ctx->world;
+  const size_t recv_bytes = (size_t)2 * W * B * rf * sizeof(float);
+  const size_t nflags = (size_t)2 * W * B * n_head;
+  TG_CUDA(cudaMalloc(&ctx->recv_local, recv_bytes));
+  TG_CUDA(cudaMalloc(&ctx->flags_local, (nflags + 64) * sizeof(unsigned)));
+  TG_CUDA(cudaMemsetAsync(ctx->recv_local, 0, recv_bytes, ctx->stream));
+  TG_CUDA(cudaMemsetAsync(ctx->flags_local, 0, (nflags + 64) * sizeof(unsigned), ctx->stream));
+  if (!ctx->nccl_stage) TG_CUDA(cudaMalloc(&ctx->nccl_stage, 2 * 128 * (tg::kMaxPeers + 1)));
+  // Handles of this rank: [recv handle | flags handle].
+  unsigned char h[2 * sizeof(cudaIpcMemHandle_t)];
+  cudaIpcMemHandle_t hr, hf;
+  TG_CUDA(cudaIpcGetMemHandle(&hr, ctx->recv_local));
+  TG_CUDA(cudaIpcGetMemHandle(&hf, ctx->flags_local));
+  std::memcpy(h, &hr, sizeof(hr));
+  std::memcpy(h + sizeof(hr), &hf, sizeof(hf));
+  const size_t hb = sizeof(h);
+  TG_CUDA(cudaMemcpyAsync(ctx->nccl_stage, h, hb, cudaMemcpyHostToDevice, ctx->stream));
+  TG_TRY(nccl_allgather_bytes(ctx, ctx->nccl_stage, ctx->nccl_stage + hb, hb));
+  std::vector<unsigned char> all((size_t)W * hb);
+  TG_CUDA(cudaMemcpy(all.data(), ctx->nccl_stage + hb, all.size(), cudaMemcpyDeviceToHost));
+  unsigned char ok = 1;
+  for (int r = 0; r < W && ok; ++r) {
+    if (r == ctx->rank) continue;
+    cudaIpcMemHandle_t pr, pf;
+    std::memcpy(&pr, all.data() + r * hb, sizeof(pr));
+    std::memcpy(&pf, all.data() + r * hb + sizeof(pr), sizeof(pf));
+    void *a = nullptr, *b2 = nullptr;
+    if (cudaIpcOpenMemHandle(&a, pr, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess ||
+        cudaIpcOpenMemHandle(&b2, pf, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      if (a) cudaIpcCloseMemHandle(a);
+      ok = 0;
+      break;
+    }
+    ctx->recv_peer[r] = static_cast<float*>(a);
+    ctx->flags_peer[r] = static_cast<unsigned*>(b2);
+  }
+  // Consensus: peer memory only if every rank mapped every peer.  This
+  // exchange also orders every rank's zeroing before any peer store.
+  TG_CUDA(cudaMemcpyAsync(ctx->nccl_stage, &ok, 1, cudaMemcpyHostToDevice, ctx->stream));
+  TG_TRY(nccl_allgather_bytes(ctx, ctx->nccl_stage, ctx->nccl_stage + 128, 1));
+  std::vector<unsigned char> oks(W);
+  TG_CUDA(cudaMemcpy(oks.data(), ctx->nccl_stage + 128, W, cudaMemcpyDeviceToHost));
+  for (int r = 0; r < W; ++r)
+    if (!oks[r]) ok = 0;
+  if (!ok) {
+    p2p_release(ctx);
+    ctx->p2p_failed = true;
+    return TG_ERR_UNSUPPORTED;
+  }
+  ctx->p2p_ready = true;
+  ctx->p2p_bcap = B;
+  ctx->p2p_rf = rf;
+  ctx->p2p_heads = n_head;
+  return TG_OK;
+}
+
+// The decode step on the tensor-core path (bf16 cache): the decode kernel
+// and, PDL-chained behind it, the merge kernel.  mode 0: normalised output;
+// 1: per-sequence records to `records`; 2: exchange with the other GPUs of
+// the communicator (peer memory, set up by ensure_p2p) and output.
+int run_fused(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const float* q_in,
+              float* q_out, float* k_io, const float* v_new, const int* pos, float* out,
+              float* records, int mode, bool rope, bool new_row) {
+  const tg_kv_desc& d = kv->d;
+  TG_TRY(check_align8(q_in, "q"));
+  TG_TRY(check_align8(q_out, "q"));
+  TG_TRY(check_align8(k_io, "k_new"));
+  TG_TRY(check_align8(out, "out"));
+  const int rf = tg::record_floats(d.n_head, d.head_dim);
+  RopeTable* t = nullptr;
+  TG_TRY(get_table(ctx, d.rope_base, d.head_dim, kv->global_ctx, &t));
+  const int grid = ctx->num_sms;
+  const size_t smem = tg::decode_fused_smem(d.n_kv_head, B);
+  if (smem > 227 * 1024)
+    return fail(TG_ERR_INVALID_ARG, "batch of %d sequences exceeds the shared-memory schedule", B);
+  TG_TRY(ensure_buf(ctx, &ctx->part, &ctx->part_cap, (size_t)2 * grid * rf));
+  TG_TRY(ensure_buf(ctx, &ctx->sched, &ctx->sched_cap, (size_t)B + 1));
+  if (mode == 2) {  // records of sequences finished inside one CTA
+    TG_TRY(ensure_buf(ctx, &ctx->records, &ctx->rec_cap, (size_t)B * rf));
+    records = ctx->records;
+  }
+  tg::FusedParams p{};
+  p.q_in = q_in;
+  p.q_out = q_out;
+  p.k_io = k_io;
+  p.v_new = v_new;
+  p.pos = pos;
+  p.cs = t->d;
+  p.table_len = kv->global_ctx;
+  p.kc_layer = reinterpret_cast<uint16_t*>(static_cast<char*>(kv->k) +
+                                           (size_t)layer * kv->layer_elems * kv->esize);
+  p.vc_layer = reinterpret_cast<uint16_t*>(static_cast<char*>(kv->v) +
+                                           (size_t)layer * kv->layer_elems * kv->esize);
+  p.out = out;
+  p.records = records;
+  p.part = ctx->part;
+  p.sched = ctx->sched;
+  p.err = ctx->d_err;
+  p.row0 = (long long)layer * d.n_seqs * d.max_ctx;
+  p.B = B;
+  p.n_head = d.n_head;
+  p.n_kv = d.n_kv_head;
+  p.group = d.n_head / d.n_kv_head;
+  p.max_ctx = d.max_ctx;
+  p.shard_start = d.shard_start;
+  p.scale_log2 = kLog2e / sqrtf((float)d.head_dim);
+  p.mode = mode;
+  p.rope = rope ? 1 : 0;
+  p.new_row = new_row ? 1 : 0;
+  p.grid = grid;
+  // Merge kernel: one CTA per (sequence, head); in mode 2 a persistent grid
+  // that stays resident beside the decode kernel (its CTAs wait on peers).
+  const int items = B * d.n_head;
+  const int mgrid = mode == 2 ? std::min(items, 2 * ctx->num_sms) : items;
+  if (mode == 2) {
+    p.world = ctx->world;
+    p.rank = ctx->rank;
+    p.b_cap = ctx->p2p_bcap;
+    p.recv_local = ctx->recv_local;
+    p.flags_local = ctx->flags_local;
+    for (int r = 0; r < ctx->world; ++r) {
+      p.recv_peer[r] = ctx->recv_peer[r];
+      p.flags_peer[r] = ctx->flags_peer[r];
+    }
+    const size_t nflags = (size_t)2 * ctx->world * ctx->p2p_bcap * ctx->p2p_heads;
+    p.epoch = ctx->flags_local + nflags;
+    p.done_ctas = reinterpret_cast<int*>(ctx->flags_local + nflags + 32);
+  }
+  cudaEvent_t ev_stop = nullptr;
+  if (ctx->prof_on) {
+    while (ctx->prof_ev.size() < ctx->prof_used + 2) {
+      cudaEvent_t ev;
+      TG_CUDA(cudaEventCreate(&ev));
+      ctx->prof_ev.push_back(ev);
+    }
+    TG_CUDA(cudaEventRecordWithFlags(ctx->prof_ev[ctx->prof_used], ctx->stream,
+                                     ctx->capturing ? cudaEventRecordExternal : 0));
+    ev_stop = ctx->prof_ev[ctx->prof_used + 1];
+    ctx->prof_used += 2;
+  }
+  cudaError_t e = tg::launch_decode_fused(kv->tmk, kv->tmv, p, grid, ctx->stream);
+  if (e != cudaSuccess) return fail(TG_ERR_CUDA, "fused decode launch: %s", cudaGetErrorString(e));
+  ctx->launches++;
+  if (ev_stop)
+    TG_CUDA(cudaEventRecordWithFlags(ev_stop, ctx->stream,
+                                     ctx->capturing ? cudaEventRecordExternal : 0));
+  e = tg::launch_merge_exchange(p, mgrid, ctx->stream);
+  if (e != cudaSuccess) return fail(TG_ERR_CUDA, "merge launch: %s", cudaGetErrorString(e));
+  ctx->launches++;
+  return TG_OK;
+}
+
 int check_kv_call(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs) {
   if (!ctx || !kv) return fail(TG_ERR_INVALID_ARG, "null context or cache");
   if (kv->ctx != ctx) return fail(TG_ERR_INVALID_ARG, "cache belongs to another context");
@@ -787,10 +1004,12 @@ int tg_shutdown(tg_context* ctx) {
   if (!ctx) return TG_OK;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+  p2p_release(ctx);
   if (ctx->comm) {
     nccl().CommDestroy(ctx->comm);
     ctx->comm = nullptr;
   }
+  cudaFree(ctx->nccl_stage);
   free_graveyard(ctx);
   for (tg_kv_cache* kv : ctx->caches) {
     cudaFree(kv->k);
@@ -1235,8 +1454,13 @@ int tg_attention_batched(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs
   TG_TRY(stage_in(ctx, q, qb, &dq));
   TG_TRY(stage_in(ctx, past_len, (size_t)n_seqs * 4, &dp));
   TG_TRY(stage_out(ctx, out, qb, false, &dout));
-  TG_TRY(run_decode(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
-                    static_cast<const int*>(dp), 0, static_cast<float*>(dout), 0));
+  if (mma_eligible(kv))
+    TG_TRY(run_fused(ctx, kv, layer, n_seqs, static_cast<const float*>(dq), nullptr, nullptr,
+                     nullptr, static_cast<const int*>(dp), static_cast<float*>(dout), nullptr,
+                     0, false, false));
+  else
+    TG_TRY(run_decode(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
+                      static_cast<const int*>(dp), 0, static_cast<float*>(dout), 0));
   return finish_call(ctx);
 }
 
@@ -1256,6 +1480,13 @@ int tg_decode_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, flo
   TG_TRY(stage_in(ctx, v_new, kb, &dv));
   TG_TRY(stage_in(ctx, pos, (size_t)n_seqs * 4, &dp));
   TG_TRY(stage_out(ctx, out, qb, false, &dout));
+  if (mma_eligible(kv)) {
+    TG_TRY(run_fused(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
+                     static_cast<float*>(dq), static_cast<float*>(dk),
+                     static_cast<const float*>(dv), static_cast<const int*>(dp),
+                     static_cast<float*>(dout), nullptr, 0, true, true));
+    return finish_call(ctx);
+  }
   TG_TRY(run_rope(ctx, kv, layer, n_seqs, static_cast<float*>(dq), static_cast<float*>(dk),
                   static_cast<const float*>(dv), static_cast<const int*>(dp)));
   TG_TRY(run_decode(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
@@ -1315,6 +1546,8 @@ int tg_comm_destroy(tg_context* ctx) {
   TG_TRY(set_device(ctx));
   if (!ctx->comm) return TG_OK;
   cudaStreamSynchronize(ctx->stream);
+  p2p_release(ctx);
+  ctx->p2p_failed = false;
   nccl().CommDestroy(ctx->comm);
   ctx->comm = nullptr;
   ctx->world = 1;
@@ -1323,11 +1556,31 @@ int tg_comm_destroy(tg_context* ctx) {
 }
 
 namespace {
-int splitkv_core(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, const float* dq,
-                 const int* dp, float* dout) {
+int splitkv_core(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, float* dq,
+                 float* dk, const float* dv, const int* dp, float* dout, bool rope_new) {
   const tg_kv_desc& d = kv->d;
   const int rf = tg::record_floats(d.n_head, d.head_dim);
-  TG_TRY(run_decode(ctx, kv, layer, n_seqs, dq, dp, 0, nullptr, 1));
+  const bool fused = mma_eligible(kv);
+  if (fused && ctx->world == 1)  // one GPU: no exchange at all
+    return run_fused(ctx, kv, layer, n_seqs, dq, rope_new ? dq : nullptr, rope_new ? dk : nullptr,
+                     dv, dp, dout, nullptr, 0, rope_new, rope_new);
+  if (fused && ctx->world > 1) {
+    const int rc = ensure_p2p(ctx, n_seqs, d.n_head, rf);
+    if (rc == TG_OK)
+      return run_fused(ctx, kv, layer, n_seqs, dq, rope_new ? dq : nullptr,
+                       rope_new ? dk : nullptr, dv, dp, dout, nullptr, 2, rope_new, rope_new);
+    if (rc != TG_ERR_UNSUPPORTED) return rc;
+    t_err.clear();  // no peer memory between these GPUs: NCCL all-gather below
+  }
+  // Records of this shard, all-gathered over NCCL, merged on every rank.
+  TG_TRY(ensure_buf(ctx, &ctx->records, &ctx->rec_cap, (size_t)n_seqs * rf));
+  if (fused) {
+    TG_TRY(run_fused(ctx, kv, layer, n_seqs, dq, rope_new ? dq : nullptr, rope_new ? dk : nullptr,
+                     dv, dp, nullptr, ctx->records, 1, rope_new, rope_new));
+  } else {
+    if (rope_new) TG_TRY(run_rope(ctx, kv, layer, n_seqs, dq, dk, dv, dp));
+    TG_TRY(run_decode(ctx, kv, layer, n_seqs, dq, dp, 0, nullptr, 1));
+  }
   const size_t count = (size_t)n_seqs * rf;
   TG_TRY(ensure_buf(ctx, &ctx->recv, &ctx->recv_cap, count * ctx->world));
   if (ctx->world > 1) {
@@ -1380,8 +1633,9 @@ int tg_attention_splitkv(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs
   TG_TRY(stage_in(ctx, q, qb, &dq));
   TG_TRY(stage_in(ctx, past_len, (size_t)n_seqs * 4, &dp));
   TG_TRY(stage_out(ctx, out, qb, false, &dout));
-  TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
-                      static_cast<const int*>(dp), static_cast<float*>(dout)));
+  TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, const_cast<float*>(static_cast<const float*>(dq)),
+                      nullptr, nullptr, static_cast<const int*>(dp), static_cast<float*>(dout),
+                      false));
   return finish_call(ctx);
 }
 
@@ -1398,6 +1652,13 @@ int tg_attention_records(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs
   TG_TRY(stage_in(ctx, q, qb, &dq));
   TG_TRY(stage_in(ctx, past_len, (size_t)n_seqs * 4, &dp));
   TG_TRY(stage_out(ctx, records, (size_t)n_seqs * rf * 4, false, &drec));
+  if (mma_eligible(kv)) {
+    TG_TRY(run_fused(ctx, kv, layer, n_seqs, static_cast<const float*>(dq), nullptr, nullptr,
+                     nullptr, static_cast<const int*>(dp), nullptr, static_cast<float*>(drec), 1,
+                     false, false));
+    return finish_call(ctx);
+  }
+  TG_TRY(ensure_buf(ctx, &ctx->records, &ctx->rec_cap, (size_t)n_seqs * rf));
   TG_TRY(run_decode(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
                     static_cast<const int*>(dp), 0, nullptr, 1));
   TG_CUDA(cudaMemcpyAsync(drec, ctx->records, (size_t)n_seqs * rf * 4, cudaMemcpyDeviceToDevice,
@@ -1446,10 +1707,9 @@ int tg_decode_layer_splitkv(tg_context* ctx, tg_kv_cache* kv, int layer, int n_s
   TG_TRY(stage_in(ctx, v_new, kb, &dv));
   TG_TRY(stage_in(ctx, pos, (size_t)n_seqs * 4, &dp));
   TG_TRY(stage_out(ctx, out, qb, false, &dout));
-  TG_TRY(run_rope(ctx, kv, layer, n_seqs, static_cast<float*>(dq), static_cast<float*>(dk),
-                  static_cast<const float*>(dv), static_cast<const int*>(dp)));
-  TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
-                      static_cast<const int*>(dp), static_cast<float*>(dout)));
+  TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, static_cast<float*>(dq), static_cast<float*>(dk),
+                      static_cast<const float*>(dv), static_cast<const int*>(dp),
+                      static_cast<float*>(dout), true));
   return finish_call(ctx);
 }
 

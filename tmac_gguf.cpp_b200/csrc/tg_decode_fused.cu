@@ -1,0 +1,687 @@
+// tg_decode_fused.cu -- the decode step of one layer over a bf16 cache in two
+// PDL-chained launches: RoPE of q and k (tmac_gguf.cpp:990-1016), the
+// cache-write of the new row (tmac_gguf.cpp:1090-1091) and GQA attention
+// (tmac_gguf.cpp:1093-1128) in the decode kernel; the split-KV merge, the
+// write-back of the rotated q / k and -- across the GPUs of one box -- the
+// exchange of per-GPU softmax records over peer memory in the merge kernel.
+//
+// Decode kernel (same tile schedule and tensor-core inner loop as
+// decode_mma_kernel in tg_kernels.cu):
+//  * consumers rotate q on the fly from the raw q and the host-libm cos/sin
+//    table when a sequence starts (bit-identical to the RoPE kernel);
+//  * the warp whose rows hold a sequence's new position overwrites that row
+//    of the TMA-staged K and V tile with the rotated k and the new v (bf16,
+//    RNE) and stores it to the cache, so no separate cache-write launch and
+//    no ordering between a writer kernel and the TMA loads is needed;
+//  * a sequence that lies within one CTA is finished there (output, or its
+//    record for the exchange); the pieces of a split sequence go to the
+//    CTA's two partial-record slots.
+// Merge kernel: one item per (sequence, head), spread over many SMs so the
+// tail of the step is short; in mode 2 (split-KV across GPUs) it stores its
+// record slice into every GPU's receive buffer (NVLink peer stores),
+// publishes an epoch-tagged flag with release semantics at system scope,
+// waits (bounded) for the flags of all GPUs and merges.  Receive buffers
+// alternate between launches (epoch parity) because a GPU can be at most one
+// launch ahead of the others.
+//
+// Every wait is bounded (mbarriers, peer flags); on expiry the error word is
+// set and the kernel still reaches its end.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <utility>
+
+#include "tg_device.cuh"
+#include "tg_kernels.h"
+#include "tg_shared.h"
+
+namespace tg {
+
+template <int NKV>
+struct FusedCfg {
+  static constexpr int TILE = 64;
+  // 128 KB ring: enough K/V in flight per SM to cover loaded HBM latency
+  // (a pure TMA stream of this tiling reaches the copy peak with it).
+  static constexpr int STAGES = (128 * 1024) / (2 * NKV * TILE * 128);
+  // Consumer warps per KV head: each takes RW rows of every tile.  Four (16
+  // rows) give every SM sub-partition two or more warps to interleave; with
+  // four KV heads, two (32 rows) keep the CTA within the register file.
+  static constexpr int WPH = NKV >= 4 ? 2 : 4;
+  static constexpr int RW = TILE / WPH;
+  static constexpr int NT = RW / 8;   // n-tiles of 8 rows in S = q K^T
+  static constexpr int KP = RW / 16;  // k-steps of 16 rows in O += P V
+  static constexpr int CWARPS = WPH * NKV;
+  static constexpr int CTHREADS = 32 * CWARPS;
+  static constexpr int THREADS = CTHREADS + 32;
+  static constexpr int BOX = TILE * 128;
+  static constexpr int STAGE_BYTES = 2 * NKV * BOX;
+  static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+  static constexpr int MRG_FLOATS = 8 * 64 + 16;
+  static constexpr int OFF_MRG = OFF_BAR + 2 * STAGES * 8;
+  static constexpr int OFF_WTOT = OFF_MRG + CWARPS * MRG_FLOATS * 4;
+  static constexpr int OFF_PREFIX = OFF_WTOT + 32 * 4;
+  static constexpr size_t smem_bytes(int B) { return 1024 + (size_t)OFF_PREFIX + (size_t)(B + 1) * 4; }
+};
+
+// Bound of a wait for another GPU's record: about 5 s of SM clock, long
+// enough for host-side launch skew between ranks.
+constexpr long long kPeerWaitCycles = 10000000000LL;
+constexpr long long kPeerWaitPolls = 1LL << 28;
+
+__device__ __forceinline__ void cons_sync(int n) {
+  asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory");
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// x0*c - x1*s, x0*s + x1*c with one rounding per product and sum
+// (tmac_gguf.cpp:999-1000 without contraction).
+__device__ __forceinline__ float2 rot(float2 x, float2 c) {
+  return make_float2(__fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(x.y, c.y)),
+                     __fadd_rn(__fmul_rn(x.x, c.y), __fmul_rn(x.y, c.x)));
+}
+
+// Tile prefix over sequences, as build_tile_prefix in tg_kernels.cu.
+__device__ void fused_prefix(const FusedParams& p, int* prefix, int* warp_tot) {
+  const int NT = blockDim.x, t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int chunk = (p.B + NT - 1) / NT;
+  const int b0 = min(t * chunk, p.B), b1 = min(b0 + chunk, p.B);
+  int sum = 0;
+  for (int s = b0; s < b1; ++s) {
+    const int pl = p.pos[s];
+    int tiles = 0;
+    if (pl < 0 || pl >= p.table_len || (p.mode == 0 && pl >= p.shard_start + p.max_ctx)) {
+      record_error(p.err, kDevErrBadPos);
+    } else {
+      const int n = local_rows(pl, p.shard_start, p.max_ctx);
+      tiles = (n + 63) / 64;
+    }
+    prefix[s + 1] = tiles;
+    sum += tiles;
+  }
+  int incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) warp_tot[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    const int nw = (NT + 31) >> 5;
+    const int v = lane < nw ? warp_tot[lane] : 0;
+    int inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += u;
+    }
+    if (lane < nw) warp_tot[lane] = inc - v;
+  }
+  __syncthreads();
+  int run = warp_tot[w] + incl - sum;
+  if (t == 0) prefix[0] = 0;
+  for (int s = b0; s < b1; ++s) {
+    run += prefix[s + 1];
+    prefix[s + 1] = run;
+  }
+  __syncthreads();
+}
+
+template <int NKV>
+__global__ void __launch_bounds__(FusedCfg<NKV>::THREADS, 1)
+    decode_fused_kernel(const __grid_constant__ CUtensorMap tmk,
+                        const __grid_constant__ CUtensorMap tmv, const FusedParams p) {
+  using Cfg = FusedCfg<NKV>;
+  constexpr int TILE = Cfg::TILE, STAGES = Cfg::STAGES, NCT = Cfg::CTHREADS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  float* mrg = reinterpret_cast<float*>(smem + Cfg::OFF_MRG);
+  int* warp_tot = reinterpret_cast<int*>(smem + Cfg::OFF_WTOT);
+  int* prefix = reinterpret_cast<int*>(smem + Cfg::OFF_PREFIX);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qdim = p.n_head * 64;
+  const int rf = record_floats(p.n_head, 64);
+
+  griddep_launch_dependents();
+  griddep_wait();
+  fused_prefix(p, prefix, warp_tot);
+  const long long T = prefix[p.B];
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i <= p.B; i += blockDim.x) p.sched[i] = prefix[i];
+  const int G = (int)min((long long)gridDim.x, T), cta = blockIdx.x;
+  const bool active = cta < G;
+  long long t_lo = 0, t_hi = 0;
+  if (active) {
+    t_lo = cta_tile_lo(cta, G, T);
+    t_hi = cta_tile_lo(cta + 1, G, T);
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], Cfg::CWARPS);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (active && warp == Cfg::CWARPS) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmk);
+      tma_prefetch_desc(&tmv);
+      const int tlo = (int)t_lo, thi = (int)t_hi;
+      int issued = 0, st = 0, s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = tlo; t < thi && ok; ++s) {
+        while (prefix[s + 1] <= t) ++s;
+        const int s_end = min(thi, prefix[s + 1]);
+        // TMA row of tile t: row0 + s*max_ctx + (t - prefix[s])*TILE (< 2^31,
+        // checked when the cache is created).
+        const int y0 = (int)(p.row0 + (long long)s * p.max_ctx) - prefix[s] * TILE;
+        for (; t < s_end; ++t) {
+          if (!mbar_wait(&empty[st], ph ^ 1u, p.err, kDevErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* stage = smem + st * Cfg::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[st], Cfg::STAGE_BYTES);
+          const int y = y0 + t * TILE;
+#pragma unroll
+          for (int g = 0; g < NKV; ++g) {
+            tma_load_2d(stage + g * Cfg::BOX, &tmk, &full[st], 64 * g, y);
+            tma_load_2d(stage + (NKV + g) * Cfg::BOX, &tmv, &full[st], 64 * g, y);
+          }
+          ++issued;
+          if (++st == STAGES) {
+            st = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // Drain: every issued load lands before the CTA exits.
+      for (int k2 = max(0, issued - STAGES); k2 < issued; ++k2)
+        mbar_wait(&full[k2 % STAGES], (uint32_t)((k2 / STAGES) & 1), p.err, kDevErrWaitFull);
+    }
+    __syncwarp();
+  } else if (active) {
+    // ------------------------------------------------------------ consumers
+    constexpr int WPH = Cfg::WPH, RW = Cfg::RW, NT = Cfg::NT, KP = Cfg::KP;
+    const int g = warp / WPH, hf = warp % WPH;
+    const int r = lane >> 2, qd = lane & 3;
+    const bool row_ok = r < p.group;
+    const float sl2 = p.scale_log2;
+    float* my_mrg = mrg + warp * Cfg::MRG_FLOATS;
+
+    uint32_t qa[4][4];
+    float o[8][4];
+    float m_run = kNegBig, l_run = 0.f;
+    bool failed = false;
+    const int tlo = (int)t_lo, thi = (int)t_hi;
+    int st = 0, s = 0;
+    uint32_t ph = 0;
+    for (int t = tlo; t < thi; ++s) {
+      // One segment: the tiles of sequence s inside [tlo, thi).  Everything
+      // per sequence lives in registers for the tile loop.
+      while (prefix[s + 1] <= t) ++s;
+      const int seg_lo = t, seq_lo = prefix[s], seq_hi = prefix[s + 1];
+      const int s_end = min(thi, seq_hi);
+      const int pos_s = p.pos[s];
+      const int n_loc = local_rows(pos_s, p.shard_start, p.max_ctx);
+      const int local_new = pos_s - p.shard_start;  // this shard's row of the new token
+      const bool has_new = p.new_row && local_new >= 0 && local_new < p.max_ctx;
+      {
+        const float* qh = p.q_in + ((size_t)s * p.n_head + (size_t)g * p.group + (row_ok ? r : 0)) * 64;
+        const float2* cs = reinterpret_cast<const float2*>(p.cs + (size_t)pos_s * 64);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const int d = 16 * kk + 8 * half + 2 * qd;
+            float2 v = make_float2(0.f, 0.f);
+            if (row_ok) {
+              v = *reinterpret_cast<const float2*>(qh + d);
+              if (p.rope) v = rot(v, cs[d >> 1]);
+            }
+            float h0, l0, h1, l1;
+            split_bf16(v.x, h0, l0);
+            split_bf16(v.y, h1, l1);
+            qa[kk][2 * half] = pack_bf16x2(h0, h1);
+            qa[kk][2 * half + 1] = pack_bf16x2(l0, l1);
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c) o[c][0] = o[c][1] = o[c][2] = o[c][3] = 0.f;
+        m_run = kNegBig;
+        l_run = 0.f;
+      }
+      for (; t < s_end; ++t) {
+      const int j = t - seq_lo;
+      const int tile_valid = min(TILE, n_loc - j * TILE);
+      const int my_valid = max(0, min(RW, tile_valid - RW * hf));
+      if (!failed && !mbar_wait(&full[st], ph, p.err, kDevErrWaitFull)) failed = true;
+
+      if (!failed && my_valid > 0) {
+        uint8_t* kbox = smem + st * Cfg::STAGE_BYTES + g * Cfg::BOX;
+        uint8_t* vbox = smem + st * Cfg::STAGE_BYTES + (NKV + g) * Cfg::BOX;
+        const int rb = RW * hf;
+        bool touched = false;
+        if (my_valid < RW) {
+          // Rows past the attended window may hold anything; zero their V so
+          // that 0-weighted rows add exactly zero.
+          for (int e = lane; e < (RW - my_valid) * 8; e += 32) {
+            const int row = rb + my_valid + (e >> 3);
+            reinterpret_cast<uint4*>(vbox + row * 128)[e & 7] = make_uint4(0, 0, 0, 0);
+          }
+          touched = true;
+        }
+        // The new token's row: rotated k and v in bf16 into the staged tile
+        // and into the cache.
+        const int r_new = local_new - j * TILE - rb;
+        if (has_new && r_new >= 0 && r_new < RW) {
+          if (lane < 8) {
+            const int row = rb + r_new;
+            const int e0 = g * 64 + lane * 8;
+            const float* kr = p.k_io + (size_t)s * p.n_kv * 64 + e0;
+            const float* vr = p.v_new + (size_t)s * p.n_kv * 64 + e0;
+            const float2* cs = reinterpret_cast<const float2*>(p.cs + (size_t)pos_s * 64);
+            uint4 kq, vq;
+            uint32_t* kw = reinterpret_cast<uint32_t*>(&kq);
+            uint32_t* vw = reinterpret_cast<uint32_t*>(&vq);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              float2 x = *reinterpret_cast<const float2*>(kr + 2 * u);
+              x = p.rope ? rot(x, cs[lane * 4 + u]) : x;
+              const __nv_bfloat162 kb = __floats2bfloat162_rn(x.x, x.y);
+              const __nv_bfloat162 vb = __floats2bfloat162_rn(vr[2 * u], vr[2 * u + 1]);
+              kw[u] = *reinterpret_cast<const uint32_t*>(&kb);
+              vw[u] = *reinterpret_cast<const uint32_t*>(&vb);
+            }
+            const int sw = (lane ^ (row & 7)) << 4;
+            *reinterpret_cast<uint4*>(kbox + row * 128 + sw) = kq;
+            *reinterpret_cast<uint4*>(vbox + row * 128 + sw) = vq;
+            const size_t crow = ((size_t)s * p.max_ctx + (pos_s - p.shard_start)) * p.n_kv * 64 + e0;
+            *reinterpret_cast<uint4*>(p.kc_layer + crow) = kq;
+            *reinterpret_cast<uint4*>(p.vc_layer + crow) = vq;
+          }
+          touched = true;
+        }
+        if (touched) {
+          fence_proxy_async_smem();
+          __syncwarp();
+        }
+        const uint32_t kb = smem_u32(kbox), vb = smem_u32(vbox);
+        // S = q . K^T for this warp's RW rows: NT n-tiles of 8 rows.
+        float sc[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          // Two accumulators (dims 0-31 / 32-63) halve the dependent chain.
+          float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+          const int row = rb + 8 * nt + (lane & 7);
+#pragma unroll
+          for (int kq = 0; kq < 2; ++kq) {
+            const int chunk = 4 * kq + (lane >> 3);
+            uint32_t b0, b1, b2, b3;
+            ldmatrix_x4(kb + row * 128 + ((chunk ^ (row & 7)) << 4), b0, b1, b2, b3);
+            mma_bf16_16816(acc[kq], qa[2 * kq], b0, b1);
+            mma_bf16_16816(acc[kq], qa[2 * kq + 1], b2, b3);
+          }
+          const int c0 = 8 * nt + 2 * qd;
+          sc[nt][0] = (c0 < my_valid) ? ((acc[0][0] + acc[0][2]) + (acc[1][0] + acc[1][2])) * sl2 : -INFINITY;
+          sc[nt][1] = (c0 + 1 < my_valid) ? ((acc[0][1] + acc[0][3]) + (acc[1][1] + acc[1][3])) * sl2 : -INFINITY;
+        }
+        // Online softmax over the RW rows (per query head = per quad).
+        float mx = sc[0][0];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mx = fmaxf(mx, fmaxf(sc[nt][0], sc[nt][1]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run, mx);
+        const float alpha = ex2(m_run - m_new);
+        m_run = m_new;
+        float pr[NT][2];
+        float lsum = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          pr[nt][0] = ex2(sc[nt][0] - m_new);
+          pr[nt][1] = ex2(sc[nt][1] - m_new);
+          lsum += pr[nt][0] + pr[nt][1];
+        }
+        l_run = l_run * alpha + lsum;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          o[c][0] *= alpha; o[c][1] *= alpha; o[c][2] *= alpha; o[c][3] *= alpha;
+        }
+        // O += P . V, KP k-steps of 16 rows.
+#pragma unroll
+        for (int kp = 0; kp < KP; ++kp) {
+          uint32_t pa[4];
+          float h0, l0, h1, l1;
+          split_bf16(pr[2 * kp][0], h0, l0);
+          split_bf16(pr[2 * kp][1], h1, l1);
+          pa[0] = pack_bf16x2(h0, h1);
+          pa[1] = pack_bf16x2(l0, l1);
+          split_bf16(pr[2 * kp + 1][0], h0, l0);
+          split_bf16(pr[2 * kp + 1][1], h1, l1);
+          pa[2] = pack_bf16x2(h0, h1);
+          pa[3] = pack_bf16x2(l0, l1);
+          const int row = rb + 16 * kp + ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+          for (int cp = 0; cp < 4; ++cp) {
+            const int chunk = 2 * cp + (lane >> 4);
+            uint32_t b0, b1, b2, b3;
+            ldmatrix_x4_trans(vb + row * 128 + ((chunk ^ (row & 7)) << 4), b0, b1, b2, b3);
+            mma_bf16_16816(o[2 * cp], pa, b0, b1);
+            mma_bf16_16816(o[2 * cp + 1], pa, b2, b3);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+      if (++st == STAGES) {
+        st = 0;
+        ph ^= 1u;
+      }
+      }
+      // Segment end: merge the WPH warps of each KV head and write out.
+      {
+        float l_tot = l_run;
+        l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 1);
+        l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 2);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int d = 8 * c + 2 * qd;
+          my_mrg[r * 64 + d] = o[c][0] + o[c][2];
+          my_mrg[r * 64 + d + 1] = o[c][1] + o[c][3];
+        }
+        if (qd == 0) {
+          my_mrg[512 + r] = m_run;
+          my_mrg[520 + r] = l_tot;
+        }
+        cons_sync(NCT);
+        const bool complete = seg_lo == seq_lo && s_end == seq_hi;
+        float* dst = complete ? (p.mode == 0 ? p.out + (size_t)s * qdim : p.records + (size_t)s * rf)
+                              : p.part + (size_t)(2 * cta + (seg_lo == tlo ? 0 : 1)) * rf;
+        const bool normalise = complete && p.mode == 0;
+        if (hf == 0 && row_ok) {
+          float M = kNegBig;
+#pragma unroll
+          for (int w = 0; w < WPH; ++w) M = fmaxf(M, my_mrg[w * Cfg::MRG_FLOATS + 512 + r]);
+          float wt[WPH];
+          float L = 0.f;
+#pragma unroll
+          for (int w = 0; w < WPH; ++w) {
+            wt[w] = ex2(my_mrg[w * Cfg::MRG_FLOATS + 512 + r] - M);
+            L = fmaf(my_mrg[w * Cfg::MRG_FLOATS + 520 + r], wt[w], L);
+          }
+          const float inv = normalise ? 1.f / L : 1.f;
+          const int h = g * p.group + r;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const int d = 8 * c + 2 * qd;
+            float2 v = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int w = 0; w < WPH; ++w) {
+              v.x = fmaf(my_mrg[w * Cfg::MRG_FLOATS + r * 64 + d], wt[w], v.x);
+              v.y = fmaf(my_mrg[w * Cfg::MRG_FLOATS + r * 64 + d + 1], wt[w], v.y);
+            }
+            v.x *= inv;
+            v.y *= inv;
+            *reinterpret_cast<float2*>(dst + h * 64 + d) = v;
+          }
+          if (!normalise && qd == 0) {
+            dst[qdim + h] = M;
+            dst[qdim + p.n_head + h] = L;
+          }
+        }
+        cons_sync(NCT);
+      }
+    }
+  }
+}
+
+
+// ------------------------------------------------------------ merge / exchange
+
+// One item per (sequence s, head h), thread d = dimension d of the head.
+// Persistent: CTA c takes items c, c + grid, ... in increasing order on every
+// GPU, and the grid is small enough to be resident, so a CTA waiting for
+// another GPU's item i only ever waits for a CTA that processes i next.
+//   1. this GPU's record slice of (s, h): the merge of the partial records of
+//      a split sequence, the complete record the decode kernel wrote, or a
+//      neutral record when this shard holds no row of s;
+//   2. mode 0: output of split sequences; mode 1: the record;
+//      mode 2: the slice is stored into every GPU's receive buffer, an
+//      epoch-tagged flag per (s, h) is released at system scope, the flags of
+//      all GPUs are awaited (bounded) and the slices merged into the output;
+//   3. with RoPE, the rotated q (and k for h < n_kv) go back to the caller.
+__global__ void __launch_bounds__(64) merge_exchange_kernel(const FusedParams p) {
+  griddep_launch_dependents();
+  griddep_wait();
+  __shared__ int fail;
+  const int d = threadIdx.x;
+  const int H = p.n_head, qdim = H * 64, rf = record_floats(H, 64);
+  const uint32_t epoch = (p.mode == 2) ? *reinterpret_cast<volatile unsigned*>(p.epoch) : 0u;
+  const long long T = p.sched[p.B];
+  const int G = (int)min((long long)p.grid, T);
+  const int items = p.B * H;
+  for (int it = blockIdx.x; it < items; it += gridDim.x) {
+    const int s = it / H, h = it - s * H;
+    const int t0 = p.sched[s], t1 = p.sched[s + 1];
+    float o = 0.f, m = kNegBig, l = 0.f;
+    bool split = false;
+    if (t1 > t0) {
+      const int c1 = cta_of_tile(t0, G, T), c2 = cta_of_tile(t1 - 1, G, T);
+      if (c1 == c2) {
+        if (p.mode != 0) {
+          const float* rec = p.records + (size_t)s * rf;
+          o = rec[h * 64 + d];
+          m = rec[qdim + h];
+          l = rec[qdim + H + h];
+        }
+      } else {
+        split = true;
+        const int first_slot = 2 * c1 + (cta_tile_lo(c1, G, T) == t0 ? 0 : 1);
+        const int n_parts = 1 + (c2 - c1);
+        float M = kNegBig;
+        for (int k0 = 0; k0 < n_parts; k0 += 8) {
+          float mv[8], lv[8], ov[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int kk = k0 + u;
+            mv[u] = kNegBig;
+            lv[u] = 0.f;
+            ov[u] = 0.f;
+            if (kk < n_parts) {
+              const float* r = p.part + (size_t)(kk == 0 ? first_slot : 2 * (c1 + kk)) * rf;
+              mv[u] = r[qdim + h];
+              lv[u] = r[qdim + H + h];
+              ov[u] = r[h * 64 + d];
+            }
+          }
+          float Mb = M;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) Mb = fmaxf(Mb, mv[u]);
+          const float a = ex2(M - Mb);
+          o *= a;
+          l *= a;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const float w = ex2(mv[u] - Mb);
+            o = fmaf(ov[u], w, o);
+            l = fmaf(lv[u], w, l);
+          }
+          M = Mb;
+        }
+        m = M;
+      }
+    }
+    if (p.mode == 0) {
+      if (split) p.out[(size_t)s * qdim + h * 64 + d] = o / l;
+    } else if (p.mode == 1) {
+      if (split || t1 == t0) {
+        float* rec = p.records + (size_t)s * rf;
+        rec[h * 64 + d] = o;
+        if (d == 0) {
+          rec[qdim + h] = m;
+          rec[qdim + H + h] = l;
+        }
+      }
+    } else {
+      const int par = (int)(epoch & 1);
+      const size_t mine = ((size_t)(par * p.world + p.rank) * p.b_cap + s) * rf;
+      for (int r = 0; r < p.world; ++r) {
+        float* dst = (r == p.rank ? p.recv_local : p.recv_peer[r]) + mine;
+        dst[h * 64 + d] = o;
+        if (d == 0) {
+          dst[qdim + h] = m;
+          dst[qdim + H + h] = l;
+        }
+      }
+      __threadfence_system();
+      if (d == 0) fail = 0;
+      __syncthreads();
+      const size_t fmine = ((size_t)(par * p.world + p.rank) * p.b_cap + s) * H + h;
+      if (d < p.world)
+        st_release_sys((d == p.rank ? p.flags_local : p.flags_peer[d]) + fmine, epoch + 1u);
+      if (d < p.world) {
+        const unsigned* f = p.flags_local + ((size_t)(par * p.world + d) * p.b_cap + s) * H + h;
+        bool got = false;
+        const long long c0 = clock64();
+        for (long long n = 0; n < kPeerWaitPolls; ++n) {
+          if (ld_acquire_sys(f) == epoch + 1u) {
+            got = true;
+            break;
+          }
+          if (clock64() - c0 > kPeerWaitCycles) break;
+          __nanosleep(32);
+        }
+        if (!got) {
+          record_error(p.err, kDevErrPeerTimeout);
+          fail = 1;
+        }
+      }
+      __syncthreads();
+      if (!fail) {
+        // Slices written by other GPUs are read through L2 (__ldcg), where
+        // their NVLink stores land.
+        const float* base = p.recv_local + ((size_t)(par * p.world) * p.b_cap + s) * rf;
+        const size_t stride = (size_t)p.b_cap * rf;
+        float M = kNegBig;
+        for (int r = 0; r < p.world; ++r) M = fmaxf(M, __ldcg(base + r * stride + qdim + h));
+        float O = 0.f, L = 0.f;
+        for (int r = 0; r < p.world; ++r) {
+          const float* rr = base + r * stride;
+          const float w = ex2(__ldcg(rr + qdim + h) - M);
+          O = fmaf(__ldcg(rr + h * 64 + d), w, O);
+          L = fmaf(__ldcg(rr + qdim + H + h), w, L);
+        }
+        p.out[(size_t)s * qdim + h * 64 + d] = O / L;
+      }
+    }
+    const int pos_s = p.pos[s];
+    if (p.rope && pos_s >= 0 && pos_s < p.table_len) {
+      // All readers of the raw q / k of s have finished (previous kernel).
+      const float2 c = reinterpret_cast<const float2*>(p.cs + (size_t)pos_s * 64)[d >> 1];
+      const float* qi = p.q_in + (size_t)s * qdim + h * 64;
+      const float2 xq = make_float2(qi[d & ~1], qi[d | 1]);
+      float2 xk = make_float2(0.f, 0.f);
+      const bool has_k = p.k_io && h < p.n_kv;
+      float* kk = has_k ? p.k_io + (size_t)s * p.n_kv * 64 + h * 64 : nullptr;
+      if (has_k) xk = make_float2(kk[d & ~1], kk[d | 1]);
+      __syncthreads();  // every pair is read before any element is overwritten
+      const float2 rq = rot(xq, c);
+      p.q_out[(size_t)s * qdim + h * 64 + d] = (d & 1) ? rq.y : rq.x;
+      if (has_k) {
+        const float2 rk = rot(xk, c);
+        kk[d] = (d & 1) ? rk.y : rk.x;
+      }
+    }
+    __syncthreads();
+  }
+  if (p.mode == 2 && threadIdx.x == 0) {
+    __threadfence();
+    const int old = atomicAdd(p.done_ctas, 1);
+    if (old == (int)gridDim.x - 1) {
+      *reinterpret_cast<volatile unsigned*>(p.epoch) = epoch + 1u;
+      *reinterpret_cast<volatile int*>(p.done_ctas) = 0;
+      __threadfence();
+    }
+  }
+}
+
+// ---------------------------------------------------------------- launch
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl_f(void (*fn)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fn, std::forward<Args>(args)...);
+}
+
+template <int NKV>
+static cudaError_t launch_fused_nkv(const CUtensorMap& tk, const CUtensorMap& tv,
+                                    const FusedParams& p, int grid, cudaStream_t st) {
+  static size_t configured[64] = {};
+  const size_t smem = FusedCfg<NKV>::smem_bytes(p.B);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (smem > configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(decode_fused_kernel<NKV>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = smem;
+  }
+  return launch_pdl_f(decode_fused_kernel<NKV>, dim3(grid), dim3(FusedCfg<NKV>::THREADS), smem,
+                      st, tk, tv, p);
+}
+
+size_t decode_fused_smem(int nkv, int B) {
+  switch (nkv) {
+    case 1: return FusedCfg<1>::smem_bytes(B);
+    case 2: return FusedCfg<2>::smem_bytes(B);
+    case 4: return FusedCfg<4>::smem_bytes(B);
+    default: return 0;
+  }
+}
+
+cudaError_t launch_merge_exchange(const FusedParams& p, int grid, cudaStream_t st) {
+  if (p.B <= 0) return cudaSuccess;
+  return launch_pdl_f(merge_exchange_kernel, dim3(grid), dim3(64), 0, st, p);
+}
+
+cudaError_t launch_decode_fused(const CUtensorMap& tk, const CUtensorMap& tv,
+                                const FusedParams& p, int grid, cudaStream_t st) {
+  switch (p.n_kv) {
+    case 1: return launch_fused_nkv<1>(tk, tv, p, grid, st);
+    case 2: return launch_fused_nkv<2>(tk, tv, p, grid, st);
+    case 4: return launch_fused_nkv<4>(tk, tv, p, grid, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace tg

@@ -213,7 +213,9 @@ __device__ __forceinline__ SegDest segment_dest(const DecodeParams& p, int s,
 template <int NKV>
 struct MmaCfg {
   static constexpr int TILE = 64;                 // cache rows per stage
-  static constexpr int STAGES = 4;
+  // 128 KB ring: enough K/V in flight per SM to cover loaded HBM latency
+  // (a pure TMA stream of this tiling reaches the copy peak with it).
+  static constexpr int STAGES = (128 * 1024) / (2 * NKV * TILE * 128);
   static constexpr int CWARPS = 2 * NKV;          // consumer warps
   static constexpr int THREADS = 32 * (CWARPS + 1);
   static constexpr int BOX = TILE * 128;          // one KV head's rows: 64 bf16

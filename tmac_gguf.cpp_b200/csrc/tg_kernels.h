@@ -36,6 +36,13 @@ cudaError_t launch_fill_normal(void* out, size_t n, int dtype, uint64_t seed,
 cudaError_t launch_convert_rows(void* dst, const float* src, size_t n,
                                 int dtype, int num_sms, cudaStream_t st);
 
+// Fused decode step (tg_decode_fused.cu): bf16 cache, head_dim 64,
+// n_kv in {1, 2, 4}, at most 8 query heads per KV head.
+cudaError_t launch_decode_fused(const CUtensorMap& tk, const CUtensorMap& tv,
+                                const FusedParams& p, int grid, cudaStream_t st);
+cudaError_t launch_merge_exchange(const FusedParams& p, int grid, cudaStream_t st);
+size_t decode_fused_smem(int nkv, int B);
+
 // Prefill (tg_prefill.cu).  The attention kernel needs a bf16 cache with
 // head_dim 64 and S a positive length; tq is a 3-D map of the rotated bf16 q
 // ({64, n_head, B*S}, box {64, 1, 128}), tk / tv 2-D maps of the cache with

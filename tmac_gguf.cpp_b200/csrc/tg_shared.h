@@ -31,7 +31,10 @@ enum DeviceError : int {
   kDevErrWaitEmpty = 0x102,  // producer timed out waiting for a free stage
   kDevErrBadPos = 0x103,     // position outside the RoPE table / cache
   kDevErrTooManySeqs = 0x104,
+  kDevErrPeerTimeout = 0x105,  // a peer GPU's softmax record did not arrive in time
 };
+
+constexpr int kMaxPeers = 8;
 
 constexpr float kNegBig = -1.0e30f;  // finite "minus infinity" for m
 
@@ -135,6 +138,41 @@ struct PrefillParams {
   long long row0;        // TMA row of (this layer, sequence 0, row 0)
   int B, S, n_head, n_kv, group, max_ctx, n_qt;
   float scale_log2;
+};
+
+// Decode step of one layer in two launches (tg_decode_fused.cu): the decode
+// kernel (RoPE, the new K/V row, split-KV attention) and the merge kernel
+// (split sequences, the write-back of rotated q / k and, across GPUs, the
+// exchange and merge of per-GPU softmax records over peer memory).
+struct FusedParams {
+  const float* q_in;       // [B][n_head*64] raw (rope) or already rotated
+  float* q_out;            // rotated q written by the CTA finishing a sequence (or null)
+  float* k_io;             // [B][n_kv*64] raw new k, rotated in place (new_row)
+  const float* v_new;      // [B][n_kv*64] new v (new_row)
+  const int* pos;          // [B] global position of each sequence's current token
+  const float* cs;         // RoPE table [table_len][64] (cos, sin pairs)
+  int table_len;
+  uint16_t* kc_layer;      // layer base of the bf16 caches (new-row writes)
+  uint16_t* vc_layer;
+  float* out;              // [B][n_head*64] normalised output (modes 0, 2)
+  float* records;          // [B][record_floats] (mode 1)
+  float* part;             // [2*G][record_floats] partial records
+  int* sched;              // [B+1] tile prefix (written by CTA 0)
+  int* err;
+  long long row0;
+  int B, n_head, n_kv, group, max_ctx, shard_start;
+  float scale_log2;
+  int mode;                // 0 output, 1 records, 2 peer exchange + output
+  int rope, new_row;
+  int grid;                // CTAs of the decode launch (merge kernel)
+  // mode 2
+  int world, rank, b_cap;  // receive buffers hold b_cap sequences
+  float* recv_local;       // [2][world][b_cap][record_floats] on this GPU
+  float* recv_peer[kMaxPeers];
+  unsigned* flags_local;   // [2][world][b_cap][n_head]
+  unsigned* flags_peer[kMaxPeers];
+  unsigned* epoch;         // launch counter of the exchange on this GPU
+  int* done_ctas;          // CTAs finished in this launch
 };
 
 }  // namespace tg
