@@ -59,21 +59,26 @@ def main() -> int:
                 kv.write_rows(0, i, 0, kc[lo:hi], vc[lo:hi])
             Q[i], K[i], V[i] = q, k_new, v_new
             refs.append(cases.oracle_decode(77, p, bf16, seq=i))
-        out = np.zeros((B, cases.QD), np.float32)
-        kv.decode_layer_splitkv(0, Q, K, V, np.array(positions, np.int32), out)
-        for i, p in enumerate(positions):
-            qr, kr, _, kc, vc, ctx = refs[i]
-            err = float(np.abs(out[i] - ctx).max())
-            same_q = np.array_equal(Q[i].view(np.uint32), qr.view(np.uint32))
-            if err > tol or not same_q:
-                print(f"rank {rank}: seq {i} pos {p} bf16={bf16} err={err} rope_ok={same_q}")
-                ok = False
-            if start <= p < start + length:          # this rank owns the new row
-                krow, _ = kv.read_rows(0, i, p - start, 1)
-                want = cases.O.pack_bf16(kc[p]) if bf16 else kc[p]
-                if not np.array_equal(krow[0], want):
-                    print(f"rank {rank}: cache-write mismatch seq {i}")
+        # Three steps from the same inputs: the peer-memory exchange
+        # alternates its receive buffers and flags between launches.
+        for it in range(3):
+            Qi, Ki = Q.copy(), K.copy()
+            out = np.zeros((B, cases.QD), np.float32)
+            kv.decode_layer_splitkv(0, Qi, Ki, V, np.array(positions, np.int32), out)
+            for i, p in enumerate(positions):
+                qr, kr, _, kc, vc, ctx = refs[i]
+                err = float(np.abs(out[i] - ctx).max())
+                same_q = np.array_equal(Qi[i].view(np.uint32), qr.view(np.uint32))
+                if err > tol or not same_q:
+                    print(f"rank {rank}: step {it} seq {i} pos {p} bf16={bf16} err={err} "
+                          f"rope_ok={same_q}")
                     ok = False
+                if start <= p < start + length:          # this rank owns the new row
+                    krow, _ = kv.read_rows(0, i, p - start, 1)
+                    want = cases.O.pack_bf16(kc[p]) if bf16 else kc[p]
+                    if not np.array_equal(krow[0], want):
+                        print(f"rank {rank}: cache-write mismatch seq {i}")
+                        ok = False
         # all ranks hold the same output
         t = torch.from_numpy(out.copy())
         gathered = [torch.zeros_like(t) for _ in range(world)]

@@ -90,20 +90,26 @@ __device__ __forceinline__ float2 rot(float2 x, float2 c) {
                      __fadd_rn(__fmul_rn(x.x, c.y), __fmul_rn(x.y, c.x)));
 }
 
-// Tile prefix over sequences, as build_tile_prefix in tg_kernels.cu.
+// Tiles of one sequence on this shard; 0 for a position outside the cache /
+// RoPE table (the decode kernel reports it).
+__device__ __forceinline__ int seq_tiles(const FusedParams& p, int pl) {
+  if (pl < 0 || pl >= p.table_len || (p.mode == 0 && pl >= p.shard_start + p.max_ctx)) return -1;
+  return (local_rows(pl, p.shard_start, p.max_ctx) + 63) / 64;
+}
+
+// Tile prefix over sequences, as build_tile_prefix in tg_kernels.cu.  Reads
+// only the positions, which no kernel of this library writes, so it may run
+// before the grid-dependency wait.
 __device__ void fused_prefix(const FusedParams& p, int* prefix, int* warp_tot) {
   const int NT = blockDim.x, t = threadIdx.x, lane = t & 31, w = t >> 5;
   const int chunk = (p.B + NT - 1) / NT;
   const int b0 = min(t * chunk, p.B), b1 = min(b0 + chunk, p.B);
   int sum = 0;
   for (int s = b0; s < b1; ++s) {
-    const int pl = p.pos[s];
-    int tiles = 0;
-    if (pl < 0 || pl >= p.table_len || (p.mode == 0 && pl >= p.shard_start + p.max_ctx)) {
+    int tiles = seq_tiles(p, p.pos[s]);
+    if (tiles < 0) {
       record_error(p.err, kDevErrBadPos);
-    } else {
-      const int n = local_rows(pl, p.shard_start, p.max_ctx);
-      tiles = (n + 63) / 64;
+      tiles = 0;
     }
     prefix[s + 1] = tiles;
     sum += tiles;
@@ -157,11 +163,14 @@ __global__ void __launch_bounds__(FusedCfg<NKV>::THREADS, 1)
   const int rf = record_floats(p.n_head, 64);
 
   griddep_launch_dependents();
-  griddep_wait();
+  // Before the wait for the previous kernel: the schedule (positions only)
+  // and, when the host expects that wait to be long (p.prefetch), an L2
+  // prefetch of this CTA's first tiles, so the ring fills from L2 once the
+  // wait returns.  A prefetch never returns stale data: the loads after the
+  // wait read through L2.  When the wait is short the loads follow the
+  // prefetches while they are still in flight and the step gets slower.
   fused_prefix(p, prefix, warp_tot);
   const long long T = prefix[p.B];
-  if (blockIdx.x == 0)
-    for (int i = threadIdx.x; i <= p.B; i += blockDim.x) p.sched[i] = prefix[i];
   const int G = (int)min((long long)gridDim.x, T), cta = blockIdx.x;
   const bool active = cta < G;
   long long t_lo = 0, t_hi = 0;
@@ -176,13 +185,32 @@ __global__ void __launch_bounds__(FusedCfg<NKV>::THREADS, 1)
     }
     fence_mbar_init();
   }
+  if (active && warp == Cfg::CWARPS && lane == 0) {
+    tma_prefetch_desc(&tmk);
+    tma_prefetch_desc(&tmv);
+  }
+  if (p.prefetch && active && warp == Cfg::CWARPS && lane == 0) {
+    int s = 0;
+    const int t_pf = (int)min(t_hi, t_lo + STAGES);
+    for (int t = (int)t_lo; t < t_pf; ++t) {
+      while (prefix[s + 1] <= t) ++s;
+      const int y = (int)(p.row0 + (long long)s * p.max_ctx) + (t - prefix[s]) * TILE;
+#pragma unroll
+      for (int g = 0; g < NKV; ++g) {
+        tma_prefetch_l2_2d(&tmk, 64 * g, y);
+        tma_prefetch_l2_2d(&tmv, 64 * g, y);
+      }
+    }
+  }
+  griddep_wait();
+  // The previous launch's merge kernel reads the schedule buffer.
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i <= p.B; i += blockDim.x) p.sched[i] = prefix[i];
   __syncthreads();
 
   if (active && warp == Cfg::CWARPS) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      tma_prefetch_desc(&tmk);
-      tma_prefetch_desc(&tmv);
       const int tlo = (int)t_lo, thi = (int)t_hi;
       int issued = 0, st = 0, s = 0;
       uint32_t ph = 0;
@@ -448,6 +476,19 @@ __global__ void __launch_bounds__(FusedCfg<NKV>::THREADS, 1)
             dst[qdim + p.n_head + h] = L;
           }
         }
+        if (complete && p.rope) {
+          // Only this CTA read the raw q of s (segment start) and k of its new
+          // row (tile loop), and the barrier above ordered those reads: the
+          // rotated pairs go back to the caller, one thread per pair.
+          const float2* cs2 = reinterpret_cast<const float2*>(p.cs + (size_t)pos_s * 64);
+          const float2* qi = reinterpret_cast<const float2*>(p.q_in + (size_t)s * qdim);
+          float2* qo = reinterpret_cast<float2*>(p.q_out + (size_t)s * qdim);
+          for (int e = threadIdx.x; e < qdim / 2; e += NCT) qo[e] = rot(qi[e], cs2[e & 31]);
+          if (p.k_io) {
+            float2* kk = reinterpret_cast<float2*>(p.k_io + (size_t)s * p.n_kv * 64);
+            for (int e = threadIdx.x; e < p.n_kv * 32; e += NCT) kk[e] = rot(kk[e], cs2[e & 31]);
+          }
+        }
         cons_sync(NCT);
       }
     }
@@ -457,10 +498,13 @@ __global__ void __launch_bounds__(FusedCfg<NKV>::THREADS, 1)
 
 // ------------------------------------------------------------ merge / exchange
 
-// One item per (sequence s, head h), thread d = dimension d of the head.
-// Persistent: CTA c takes items c, c + grid, ... in increasing order on every
-// GPU, and the grid is small enough to be resident, so a CTA waiting for
-// another GPU's item i only ever waits for a CTA that processes i next.
+constexpr int kMaxMergeGroups = 4;
+constexpr int kPartBatch = 16;  // parts per group per load round
+
+// One item per (sequence s, head h) and 64 * GROUPS threads: thread d of
+// group grp handles dimension d of parts grp, grp + GROUPS, ...  Every part's
+// m, l and o are loaded in the same round (kPartBatch per group) and merged
+// online, then the groups are combined through shared memory.
 //   1. this GPU's record slice of (s, h): the merge of the partial records of
 //      a split sequence, the complete record the decode kernel wrote, or a
 //      neutral record when this shard holds no row of s;
@@ -468,72 +512,141 @@ __global__ void __launch_bounds__(FusedCfg<NKV>::THREADS, 1)
 //      mode 2: the slice is stored into every GPU's receive buffer, an
 //      epoch-tagged flag per (s, h) is released at system scope, the flags of
 //      all GPUs are awaited (bounded) and the slices merged into the output;
-//   3. with RoPE, the rotated q (and k for h < n_kv) go back to the caller.
-__global__ void __launch_bounds__(64) merge_exchange_kernel(const FusedParams p) {
-  griddep_launch_dependents();
-  griddep_wait();
+//   3. with RoPE, the rotated q (and k for h < n_kv) of the sequences that
+//      the decode kernel did not finish inside one CTA go back to the caller.
+// In mode 2 the grid is persistent: CTA c takes items c, c + grid, ... in
+// increasing order on every GPU, and the grid is small enough to be
+// resident, so a CTA waiting for another GPU's item i only ever waits for a
+// CTA that processes i next.
+template <int GROUPS>
+__global__ void __launch_bounds__(64 * GROUPS) merge_exchange_kernel(const FusedParams p) {
+  __shared__ float o_grp[GROUPS][64];
+  __shared__ float ml_grp[GROUPS][2];
+  __shared__ int pre[64 * GROUPS + 1];
+  __shared__ int wsum[2 * GROUPS];
   __shared__ int fail;
-  const int d = threadIdx.x;
+  const int tid = threadIdx.x, d = tid & 63, grp = tid >> 6;
+  griddep_launch_dependents();
+  // With at most one sequence per thread, the tile prefix is rebuilt from the
+  // positions before the wait (as the decode kernel does); otherwise the
+  // decode kernel's copy is read after it.
+  const bool local_sched = p.B <= 64 * GROUPS;
+  if (local_sched) {
+    const int lane = tid & 31, w = tid >> 5;
+    const int tiles = tid < p.B ? max(seq_tiles(p, p.pos[tid]), 0) : 0;
+    int incl = tiles;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) wsum[w] = incl;
+    __syncthreads();
+    int off = 0;
+    for (int i = 0; i < w; ++i) off += wsum[i];
+    if (tid < p.B) pre[tid + 1] = off + incl;
+    if (tid == 0) pre[0] = 0;
+    __syncthreads();
+  }
+  griddep_wait();
+  const int* sched = local_sched ? pre : p.sched;
   const int H = p.n_head, qdim = H * 64, rf = record_floats(H, 64);
   const uint32_t epoch = (p.mode == 2) ? *reinterpret_cast<volatile unsigned*>(p.epoch) : 0u;
-  const long long T = p.sched[p.B];
-  const int G = (int)min((long long)p.grid, T);
+  const int T = sched[p.B];
+  const int G = min(p.grid, T);
   const int items = p.B * H;
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
     const int s = it / H, h = it - s * H;
-    const int t0 = p.sched[s], t1 = p.sched[s + 1];
-    float o = 0.f, m = kNegBig, l = 0.f;
-    bool split = false;
-    if (t1 > t0) {
-      const int c1 = cta_of_tile(t0, G, T), c2 = cta_of_tile(t1 - 1, G, T);
-      if (c1 == c2) {
-        if (p.mode != 0) {
-          const float* rec = p.records + (size_t)s * rf;
-          o = rec[h * 64 + d];
-          m = rec[qdim + h];
-          l = rec[qdim + H + h];
-        }
-      } else {
-        split = true;
-        const int first_slot = 2 * c1 + (cta_tile_lo(c1, G, T) == t0 ? 0 : 1);
-        const int n_parts = 1 + (c2 - c1);
-        float M = kNegBig;
-        for (int k0 = 0; k0 < n_parts; k0 += 8) {
-          float mv[8], lv[8], ov[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int kk = k0 + u;
-            mv[u] = kNegBig;
-            lv[u] = 0.f;
-            ov[u] = 0.f;
-            if (kk < n_parts) {
-              const float* r = p.part + (size_t)(kk == 0 ? first_slot : 2 * (c1 + kk)) * rf;
-              mv[u] = r[qdim + h];
-              lv[u] = r[qdim + H + h];
-              ov[u] = r[h * 64 + d];
-            }
-          }
-          float Mb = M;
-#pragma unroll
-          for (int u = 0; u < 8; ++u) Mb = fmaxf(Mb, mv[u]);
-          const float a = ex2(M - Mb);
-          o *= a;
-          l *= a;
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const float w = ex2(mv[u] - Mb);
-            o = fmaf(ov[u], w, o);
-            l = fmaf(lv[u], w, l);
-          }
-          M = Mb;
-        }
-        m = M;
+    const int t0 = sched[s], t1 = sched[s + 1];
+    const int c1 = t1 > t0 ? cta_of_tile(t0, G, T) : 0;
+    const int c2 = t1 > t0 ? cta_of_tile(t1 - 1, G, T) : 0;
+    const bool split = t1 > t0 && c1 != c2;
+    if (p.mode == 0 && !split) continue;  // finished by the decode kernel
+    const int pos_s = p.pos[s];
+    const bool rope = p.rope && (split || t1 == t0) && grp == 0 && pos_s >= 0 &&
+                      pos_s < p.table_len;
+    const bool has_k = rope && p.k_io && h < p.n_kv;
+    // Raw q / k pair of this thread, loaded with everything else.
+    float2 xq = make_float2(0.f, 0.f), xk = make_float2(0.f, 0.f), cs = make_float2(0.f, 0.f);
+    if (rope) {
+      const float* qi = p.q_in + (size_t)s * qdim + h * 64;
+      xq = make_float2(qi[d & ~1], qi[d | 1]);
+      cs = reinterpret_cast<const float2*>(p.cs + (size_t)pos_s * 64)[d >> 1];
+      if (has_k) {
+        const float* kk = p.k_io + (size_t)s * p.n_kv * 64 + h * 64;
+        xk = make_float2(kk[d & ~1], kk[d | 1]);
       }
     }
+    float o = 0.f, m = kNegBig, l = 0.f;  // this GPU's record slice (group 0)
+    if (split) {
+      const int first_slot = 2 * c1 + (cta_tile_lo(c1, G, T) == t0 ? 0 : 1);
+      const int n_parts = 1 + (c2 - c1);
+      float mg = kNegBig, lg = 0.f, og = 0.f;
+      for (int k0 = grp; k0 < n_parts; k0 += GROUPS * kPartBatch) {
+        float mv[kPartBatch], lv[kPartBatch], ov[kPartBatch];
+#pragma unroll
+        for (int u = 0; u < kPartBatch; ++u) {
+          const int kk = k0 + u * GROUPS;
+          mv[u] = kNegBig;
+          lv[u] = 0.f;
+          ov[u] = 0.f;
+          if (kk < n_parts) {
+            const float* r = p.part + (size_t)(kk == 0 ? first_slot : 2 * (c1 + kk)) * rf;
+            mv[u] = r[qdim + h];
+            lv[u] = r[qdim + H + h];
+            ov[u] = r[h * 64 + d];
+          }
+        }
+        float Mb = mg;
+#pragma unroll
+        for (int u = 0; u < kPartBatch; ++u) Mb = fmaxf(Mb, mv[u]);
+        const float a = ex2(mg - Mb);
+        og *= a;
+        lg *= a;
+#pragma unroll
+        for (int u = 0; u < kPartBatch; ++u) {
+          const float w = ex2(mv[u] - Mb);
+          og = fmaf(ov[u], w, og);
+          lg = fmaf(lv[u], w, lg);
+        }
+        mg = Mb;
+      }
+      if (GROUPS > 1) {
+        o_grp[grp][d] = og;
+        if (d == 0) {
+          ml_grp[grp][0] = mg;
+          ml_grp[grp][1] = lg;
+        }
+        __syncthreads();
+        if (grp == 0) {
+          float M = kNegBig;
+#pragma unroll
+          for (int g2 = 0; g2 < GROUPS; ++g2) M = fmaxf(M, ml_grp[g2][0]);
+          o = 0.f;
+          l = 0.f;
+#pragma unroll
+          for (int g2 = 0; g2 < GROUPS; ++g2) {
+            const float w = ex2(ml_grp[g2][0] - M);
+            o = fmaf(o_grp[g2][d], w, o);
+            l = fmaf(ml_grp[g2][1], w, l);
+          }
+          m = M;
+        }
+      } else {
+        o = og;
+        m = mg;
+        l = lg;
+      }
+    } else if (t1 > t0 && p.mode != 0 && grp == 0) {
+      const float* rec = p.records + (size_t)s * rf;
+      o = rec[h * 64 + d];
+      m = rec[qdim + h];
+      l = rec[qdim + H + h];
+    }
     if (p.mode == 0) {
-      if (split) p.out[(size_t)s * qdim + h * 64 + d] = o / l;
+      if (grp == 0) p.out[(size_t)s * qdim + h * 64 + d] = o / l;
     } else if (p.mode == 1) {
-      if (split || t1 == t0) {
+      if ((split || t1 == t0) && grp == 0) {
         float* rec = p.records + (size_t)s * rf;
         rec[h * 64 + d] = o;
         if (d == 0) {
@@ -544,22 +657,25 @@ __global__ void __launch_bounds__(64) merge_exchange_kernel(const FusedParams p)
     } else {
       const int par = (int)(epoch & 1);
       const size_t mine = ((size_t)(par * p.world + p.rank) * p.b_cap + s) * rf;
-      for (int r = 0; r < p.world; ++r) {
-        float* dst = (r == p.rank ? p.recv_local : p.recv_peer[r]) + mine;
-        dst[h * 64 + d] = o;
-        if (d == 0) {
-          dst[qdim + h] = m;
-          dst[qdim + H + h] = l;
+      if (grp == 0) {
+        for (int r = 0; r < p.world; ++r) {
+          float* dst = (r == p.rank ? p.recv_local : p.recv_peer[r]) + mine;
+          dst[h * 64 + d] = o;
+          if (d == 0) {
+            dst[qdim + h] = m;
+            dst[qdim + H + h] = l;
+          }
         }
       }
-      __threadfence_system();
-      if (d == 0) fail = 0;
+      if (tid == 0) fail = 0;
+      // The slice's stores (group 0) happen before the flag stores (one
+      // thread per GPU) through the barrier and the system-scope fence.
       __syncthreads();
       const size_t fmine = ((size_t)(par * p.world + p.rank) * p.b_cap + s) * H + h;
-      if (d < p.world)
-        st_release_sys((d == p.rank ? p.flags_local : p.flags_peer[d]) + fmine, epoch + 1u);
-      if (d < p.world) {
-        const unsigned* f = p.flags_local + ((size_t)(par * p.world + d) * p.b_cap + s) * H + h;
+      if (tid < p.world) {
+        __threadfence_system();
+        st_release_sys((tid == p.rank ? p.flags_local : p.flags_peer[tid]) + fmine, epoch + 1u);
+        const unsigned* f = p.flags_local + ((size_t)(par * p.world + tid) * p.b_cap + s) * H + h;
         bool got = false;
         const long long c0 = clock64();
         for (long long n = 0; n < kPeerWaitPolls; ++n) {
@@ -576,42 +692,47 @@ __global__ void __launch_bounds__(64) merge_exchange_kernel(const FusedParams p)
         }
       }
       __syncthreads();
-      if (!fail) {
+      if (!fail && grp == 0) {
         // Slices written by other GPUs are read through L2 (__ldcg), where
         // their NVLink stores land.
         const float* base = p.recv_local + ((size_t)(par * p.world) * p.b_cap + s) * rf;
         const size_t stride = (size_t)p.b_cap * rf;
+        float mv[kMaxPeers], lv[kMaxPeers], ov[kMaxPeers];
         float M = kNegBig;
-        for (int r = 0; r < p.world; ++r) M = fmaxf(M, __ldcg(base + r * stride + qdim + h));
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r) {
+          mv[r] = kNegBig;
+          lv[r] = 0.f;
+          ov[r] = 0.f;
+          if (r < p.world) {
+            const float* rr = base + r * stride;
+            mv[r] = __ldcg(rr + qdim + h);
+            lv[r] = __ldcg(rr + qdim + H + h);
+            ov[r] = __ldcg(rr + h * 64 + d);
+          }
+          M = fmaxf(M, mv[r]);
+        }
         float O = 0.f, L = 0.f;
-        for (int r = 0; r < p.world; ++r) {
-          const float* rr = base + r * stride;
-          const float w = ex2(__ldcg(rr + qdim + h) - M);
-          O = fmaf(__ldcg(rr + h * 64 + d), w, O);
-          L = fmaf(__ldcg(rr + qdim + H + h), w, L);
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r) {
+          const float w = ex2(mv[r] - M);
+          O = fmaf(ov[r], w, O);
+          L = fmaf(lv[r], w, L);
         }
         p.out[(size_t)s * qdim + h * 64 + d] = O / L;
       }
     }
-    const int pos_s = p.pos[s];
-    if (p.rope && pos_s >= 0 && pos_s < p.table_len) {
-      // All readers of the raw q / k of s have finished (previous kernel).
-      const float2 c = reinterpret_cast<const float2*>(p.cs + (size_t)pos_s * 64)[d >> 1];
-      const float* qi = p.q_in + (size_t)s * qdim + h * 64;
-      const float2 xq = make_float2(qi[d & ~1], qi[d | 1]);
-      float2 xk = make_float2(0.f, 0.f);
-      const bool has_k = p.k_io && h < p.n_kv;
-      float* kk = has_k ? p.k_io + (size_t)s * p.n_kv * 64 + h * 64 : nullptr;
-      if (has_k) xk = make_float2(kk[d & ~1], kk[d | 1]);
-      __syncthreads();  // every pair is read before any element is overwritten
-      const float2 rq = rot(xq, c);
+    if (rope) {
+      // All readers of the raw q / k of s have finished (previous kernel);
+      // each thread writes only the element of the pair it owns.
+      const float2 rq = rot(xq, cs);
       p.q_out[(size_t)s * qdim + h * 64 + d] = (d & 1) ? rq.y : rq.x;
       if (has_k) {
-        const float2 rk = rot(xk, c);
-        kk[d] = (d & 1) ? rk.y : rk.x;
+        const float2 rk = rot(xk, cs);
+        p.k_io[(size_t)s * p.n_kv * 64 + h * 64 + d] = (d & 1) ? rk.y : rk.x;
       }
     }
-    __syncthreads();
+    if (GROUPS > 1 || p.mode == 2) __syncthreads();
   }
   if (p.mode == 2 && threadIdx.x == 0) {
     __threadfence();
@@ -669,9 +790,13 @@ size_t decode_fused_smem(int nkv, int B) {
   }
 }
 
-cudaError_t launch_merge_exchange(const FusedParams& p, int grid, cudaStream_t st) {
+cudaError_t launch_merge_exchange(const FusedParams& p, int grid, int groups, cudaStream_t st) {
   if (p.B <= 0) return cudaSuccess;
-  return launch_pdl_f(merge_exchange_kernel, dim3(grid), dim3(64), 0, st, p);
+  if (groups == kMaxMergeGroups)
+    return launch_pdl_f(merge_exchange_kernel<kMaxMergeGroups>, dim3(grid),
+                        dim3(64 * kMaxMergeGroups), 0, st, p);
+  if (groups == 1) return launch_pdl_f(merge_exchange_kernel<1>, dim3(grid), dim3(64), 0, st, p);
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_decode_fused(const CUtensorMap& tk, const CUtensorMap& tv,

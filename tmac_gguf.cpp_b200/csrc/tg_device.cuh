@@ -105,6 +105,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap,
       : "memory");
 }
 
+// Prefetch of one 2-D tile into L2 (no shared memory, no completion).  Same
+// coordinate rule as tma_load_2d.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(
                    reinterpret_cast<uint64_t>(tmap))

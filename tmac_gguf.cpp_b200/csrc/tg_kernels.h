@@ -40,7 +40,10 @@ cudaError_t launch_convert_rows(void* dst, const float* src, size_t n,
 // n_kv in {1, 2, 4}, at most 8 query heads per KV head.
 cudaError_t launch_decode_fused(const CUtensorMap& tk, const CUtensorMap& tv,
                                 const FusedParams& p, int grid, cudaStream_t st);
-cudaError_t launch_merge_exchange(const FusedParams& p, int grid, cudaStream_t st);
+// groups: 1 (64 threads per item, many items) or 4 (256 threads, few items or
+// the persistent peer-exchange grid).
+constexpr int kMergeGroupsWide = 4;
+cudaError_t launch_merge_exchange(const FusedParams& p, int grid, int groups, cudaStream_t st);
 size_t decode_fused_smem(int nkv, int B);
 
 // Prefill (tg_prefill.cu).  The attention kernel needs a bf16 cache with

@@ -165,6 +165,7 @@ struct FusedParams {
   int mode;                // 0 output, 1 records, 2 peer exchange + output
   int rope, new_row;
   int grid;                // CTAs of the decode launch (merge kernel)
+  int prefetch;            // L2 prefetch of the first tiles before the grid-dependency wait
   // mode 2
   int world, rank, b_cap;  // receive buffers hold b_cap sequences
   float* recv_local;       // [2][world][b_cap][record_floats] on this GPU
