@@ -6,9 +6,11 @@ seq-steps/s at 1/2/4/8 B200.  Default workload = BASELINE config 4, the one
 the metric's "at 1/2/4/8 B200" is quoted on: long-context split-KV
 flash-decoding, batch 4, context 131072, 14 Q / 2 KV heads, head_dim 64,
 bf16 KV ~ N(0,1); the KV sequence is sharded evenly over the N GPUs and the
-per-shard softmax partials are all-gathered over NCCL and merged.  A step
-is one decode step of all 24 Qwen2-0.5B layers: per layer RoPE on q/k, the
-owner's cache-write of the new row, split-KV attention and the merge.
+per-shard softmax records are exchanged over NVLink peer memory inside the
+merge kernel (--exchange nccl: all-gathered over NCCL instead) and merged on
+every GPU.  A step is one decode step of all 24 Qwen2-0.5B layers: per layer
+RoPE on q/k, the owner's cache-write of the new row, split-KV attention, the
+exchange and the merge.
 
   value       whole-job algorithmic bytes / step time, inputs resident in HBM
   e2e         the same through the C ABI with pinned HOST buffers, every
@@ -48,7 +50,7 @@ WORKLOADS = {
     # BASELINE config 4
     "longctx": dict(B=4, ctx=131072, layers=24, dtype="bf16", split=True,
                     desc="config4: long-context split-KV decode, B=4, ctx=131072, bf16 KV, "
-                         "KV sharded over the GPUs, NCCL all-gather merge"),
+                         "KV sharded over the GPUs, softmax records exchanged and merged"),
     # BASELINE config 3
     "batched": dict(B=256, ctx=4096, layers=24, dtype="bf16", split=False,
                     desc="config3: batched decode, B=256 per GPU, ctx=4096, bf16 KV, "
@@ -395,6 +397,8 @@ def main():
     ap.add_argument("--impl", default="tg", choices=["tg", "reference"])
     ap.add_argument("--workload", default="longctx", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="auto", choices=["auto", "peer", "nccl"],
+                    help="split-KV record exchange for N > 1 (tg_comm_set_exchange)")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layers per step (small profiling cases)")
     args = ap.parse_args()
@@ -443,6 +447,8 @@ def main():
         uid = [tg.comm_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         be.comm_init(uid[0], rank, world, timeout_ms=120000)
+        be.set_exchange({"auto": tg.EXCHANGE_AUTO, "peer": tg.EXCHANGE_PEER,
+                         "nccl": tg.EXCHANGE_NCCL}[args.exchange])
 
     B, L = wl["B"], wl["layers"]
     pos = positions(wl)
@@ -587,7 +593,10 @@ def main():
                        "head_dim": HD, "parallelism": f"split-kv x{world}" if wl["split"]
                        else f"sequence-partitioned x{world}",
                        "l2": "inputs larger than L2: %.0f MB of KV per GPU per step"
-                             % (algo_bytes_step(wl, pos) / max(world if wl["split"] else 1, 1) / 1e6)},
+                             % (algo_bytes_step(wl, pos) / max(world if wl["split"] else 1, 1) / 1e6),
+                       "exchange": ({tg.EXCHANGE_PEER: "nvlink peer stores in the merge kernel",
+                                     tg.EXCHANGE_NCCL: "ncclAllGather + merge kernel"}
+                                    .get(be.exchange, "none") if split else "none")},
             "seq_steps_per_s": seqs_step / (ms_step * 1e-3),
             "hbm_frac_of_measured": value / (hbm_peak * world),
             "gpu_launches": launches,

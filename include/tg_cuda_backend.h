@@ -234,11 +234,24 @@ TG_API int tg_comm_init(tg_context* ctx, const void* id, int rank, int world,
                  int timeout_ms);
 TG_API int tg_comm_destroy(tg_context* ctx);
 
+/* How the ranks exchange their softmax records in the split-KV calls. */
+#define TG_EXCHANGE_AUTO 0  /* peer memory when every GPU maps every other's, else NCCL */
+#define TG_EXCHANGE_PEER 1  /* NVLink peer stores + flags inside the merge kernel */
+#define TG_EXCHANGE_NCCL 2  /* ncclAllGather of the records, then a merge kernel */
+/* Choose the exchange (collective: every rank passes the same value before
+ * its next split-KV call).  TG_EXCHANGE_PEER fails with TG_ERR_UNSUPPORTED
+ * at the next call if peer memory cannot be set up on some rank. */
+TG_API int tg_comm_set_exchange(tg_context* ctx, int exchange);
+/* The exchange the last split-KV call used: TG_EXCHANGE_PEER,
+ * TG_EXCHANGE_NCCL, or TG_EXCHANGE_AUTO before the first call. */
+TG_API int tg_comm_exchange(tg_context* ctx, int* exchange);
+
 /* Split-KV (flash-decoding) step across the world: each rank holds a shard
  * of every sequence's positions (its kv cache's [shard_start,
  * shard_start+max_ctx)), computes the softmax partials of its shard, the
- * ranks all-gather them over NCCL and every rank merges the same result
- * into out.  Inputs and outputs are replicated on all ranks. */
+ * ranks exchange them (peer memory or NCCL, see above) and every rank
+ * merges the same result into out.  Inputs and outputs are replicated on
+ * all ranks. */
 TG_API int tg_attention_splitkv(tg_context* ctx, tg_kv_cache* shard, int layer,
                          int n_seqs, const float* q, const int32_t* past_len,
                          float* out);

@@ -6,9 +6,11 @@ Run under torch.distributed.run, one rank per GPU:
 
 Every rank builds its shard of the same seeded caches (positions
 shard_range(ctx, N, rank) of every sequence), runs the RoPE + owner
-cache-write + split-KV attention + NCCL all-gather + merge through the C ABI
+cache-write + split-KV attention + record exchange + merge through the C ABI
 (tg_decode_layer_splitkv) and compares the replicated output with the CPU
-oracle.  Exit status 0 on success on every rank.
+oracle, under the automatic exchange (peer memory for the bf16 cache when
+the GPUs map each other's memory) and the NCCL all-gather.  Exit status 0
+on success on every rank.
 """
 from __future__ import annotations
 
@@ -41,7 +43,10 @@ def main() -> int:
     be.comm_init(uid[0], rank, world, timeout_ms=60000)
 
     ok = True
-    for bf16, tol in ((True, 2e-3), (False, 1e-4)):
+    cases_run = [(ex, bf16, tol) for ex in (tg.EXCHANGE_AUTO, tg.EXCHANGE_NCCL)
+                 for bf16, tol in ((True, 2e-3), (False, 1e-4))]
+    for ex, bf16, tol in cases_run:
+        be.set_exchange(ex)
         positions = [9000, 777, 12345, 0, world * 64]
         B = len(positions)
         gctx = max(positions) + 1
@@ -79,6 +84,15 @@ def main() -> int:
                     if not np.array_equal(krow[0], want):
                         print(f"rank {rank}: cache-write mismatch seq {i}")
                         ok = False
+        used = be.exchange
+        if rank == 0:
+            print(f"exchange requested {ex} used {used} bf16={bf16}")
+        if ex == tg.EXCHANGE_NCCL and used != tg.EXCHANGE_NCCL:
+            print(f"rank {rank}: NCCL exchange requested, {used} used")
+            ok = False
+        if not bf16 and used == tg.EXCHANGE_PEER:
+            print(f"rank {rank}: fp32 cache cannot use the peer exchange")
+            ok = False
         # all ranks hold the same output
         t = torch.from_numpy(out.copy())
         gathered = [torch.zeros_like(t) for _ in range(world)]

@@ -40,6 +40,9 @@ TG_ERR_STATE = 8
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
+
+# split-KV record exchange (tg_comm_set_exchange)
+EXCHANGE_AUTO, EXCHANGE_PEER, EXCHANGE_NCCL = 0, 1, 2
 REGION_MIRROR = 0
 REGION_DEVICE_OWNED = 1
 
@@ -128,6 +131,8 @@ _SIGS = {
     "tg_profile_enable": (C.c_int, [_vp, C.c_int]),
     "tg_profile_read": (C.c_int, [_vp, C.POINTER(C.c_double),
                                   C.POINTER(C.c_longlong)]),
+    "tg_comm_set_exchange": (C.c_int, [_vp, C.c_int]),
+    "tg_comm_exchange": (C.c_int, [_vp, C.POINTER(C.c_int)]),
     "tg_kv_uses_tensor_cores": (C.c_int, [_vp, C.POINTER(C.c_int)]),
 }
 
@@ -325,6 +330,18 @@ class CudaBackend:
                   timeout_ms: int = 60000) -> None:
         buf = C.create_string_buffer(uid, 128)
         _check(lib().tg_comm_init(self._h, buf, rank, world, timeout_ms))
+
+    def set_exchange(self, exchange: int) -> None:
+        """EXCHANGE_AUTO / EXCHANGE_PEER / EXCHANGE_NCCL (collective: the same
+        value on every rank before the next split-KV call)."""
+        _check(lib().tg_comm_set_exchange(self._h, exchange))
+
+    @property
+    def exchange(self) -> int:
+        """The exchange the last split-KV call used."""
+        v = C.c_int()
+        _check(lib().tg_comm_exchange(self._h, C.byref(v)))
+        return v.value
 
     def comm_destroy(self) -> None:
         _check(lib().tg_comm_destroy(self._h))

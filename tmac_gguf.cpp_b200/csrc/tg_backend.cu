@@ -178,11 +178,12 @@ struct tg_context {
 
   // Peer-memory exchange of split-KV records (IPC-mapped receive buffers).
   bool p2p_ready = false, p2p_failed = false;
+  int exchange_pref = TG_EXCHANGE_AUTO;  // tg_comm_set_exchange
+  int exchange_used = TG_EXCHANGE_AUTO;  // last split-KV call
   int p2p_bcap = 0, p2p_rf = 0, p2p_heads = 0;
-  float* recv_local = nullptr;
-  unsigned* flags_local = nullptr;  // flags, then the epoch word and the done counter
-  float* recv_peer[tg::kMaxPeers] = {};
-  unsigned* flags_peer[tg::kMaxPeers] = {};
+  unsigned long long* xchg_local = nullptr;  // peer-exchange receive words
+  unsigned* xchg_ctl = nullptr;              // exchange epoch word (this GPU only)
+  unsigned long long* xchg_peer[tg::kMaxPeers] = {};
   unsigned char* nccl_stage = nullptr;  // small device staging for handle exchange
 
   std::vector<tg_kv_cache*> caches;  // freed by tg_shutdown if still alive
@@ -739,27 +740,25 @@ int nccl_allgather_bytes(tg_context* ctx, const void* dsend, void* drecv, size_t
 }
 
 void p2p_release(tg_context* ctx) {
-  if (!ctx->p2p_ready && !ctx->recv_local) return;
+  if (!ctx->p2p_ready && !ctx->xchg_local) return;
   cudaStreamSynchronize(ctx->stream);
   for (int r = 0; r < tg::kMaxPeers; ++r) {
-    if (ctx->recv_peer[r]) cudaIpcCloseMemHandle(ctx->recv_peer[r]);
-    if (ctx->flags_peer[r]) cudaIpcCloseMemHandle(ctx->flags_peer[r]);
-    ctx->recv_peer[r] = nullptr;
-    ctx->flags_peer[r] = nullptr;
+    if (ctx->xchg_peer[r]) cudaIpcCloseMemHandle(ctx->xchg_peer[r]);
+    ctx->xchg_peer[r] = nullptr;
   }
-  cudaFree(ctx->recv_local);
-  cudaFree(ctx->flags_local);
-  ctx->recv_local = nullptr;
-  ctx->flags_local = nullptr;
+  cudaFree(ctx->xchg_local);
+  cudaFree(ctx->xchg_ctl);
+  ctx->xchg_local = nullptr;
+  ctx->xchg_ctl = nullptr;
   ctx->p2p_ready = false;
   ctx->p2p_bcap = 0;
 }
 
 // Collective: every rank of the communicator calls this with the same B.
-// Allocates this GPU's receive buffers [2][world][B][rf] and flags
-// [2][world][B][n_head] (+ epoch word and CTA counter), shares
-// their IPC handles over NCCL, maps every peer's, and agrees with all ranks
-// whether peer memory can be used (otherwise all ranks use the NCCL path).
+// Allocates this GPU's receive words [2][world][B][n_head][kXchgWords],
+// shares their IPC handle over NCCL, maps every peer's, and agrees with all
+// ranks whether peer memory can be used (otherwise all ranks use the NCCL
+// path).
 int ensure_p2p(tg_context* ctx, int B, int n_head, int rf) {
   if (ctx->p2p_failed) return TG_ERR_UNSUPPORTED;
   if (ctx->p2p_ready && B <= ctx->p2p_bcap && rf == ctx->p2p_rf && n_head == ctx->p2p_heads)
@@ -773,41 +772,31 @@ int ensure_p2p(tg_context* ctx, int B, int n_head, int rf) {
   TG_TRY(wait_stream(ctx));
   p2p_release(ctx);
   const int W = ctx->world;
-  const size_t recv_bytes = (size_t)2 * W * B * rf * sizeof(float);
-  const size_t nflags = (size_t)2 * W * B * n_head;
-  TG_CUDA(cudaMalloc(&ctx->recv_local, recv_bytes));
-  TG_CUDA(cudaMalloc(&ctx->flags_local, (nflags + 64) * sizeof(unsigned)));
-  TG_CUDA(cudaMemsetAsync(ctx->recv_local, 0, recv_bytes, ctx->stream));
-  TG_CUDA(cudaMemsetAsync(ctx->flags_local, 0, (nflags + 64) * sizeof(unsigned), ctx->stream));
+  const size_t xbytes = (size_t)2 * W * B * n_head * tg::kXchgWords * sizeof(unsigned long long);
+  TG_CUDA(cudaMalloc(&ctx->xchg_local, xbytes));
+  TG_CUDA(cudaMalloc(&ctx->xchg_ctl, 64 * sizeof(unsigned)));
+  TG_CUDA(cudaMemsetAsync(ctx->xchg_local, 0, xbytes, ctx->stream));
+  TG_CUDA(cudaMemsetAsync(ctx->xchg_ctl, 0, 64 * sizeof(unsigned), ctx->stream));
   if (!ctx->nccl_stage) TG_CUDA(cudaMalloc(&ctx->nccl_stage, 2 * 128 * (tg::kMaxPeers + 1)));
-  // Handles of this rank: [recv handle | flags handle].
-  unsigned char h[2 * sizeof(cudaIpcMemHandle_t)];
-  cudaIpcMemHandle_t hr, hf;
-  TG_CUDA(cudaIpcGetMemHandle(&hr, ctx->recv_local));
-  TG_CUDA(cudaIpcGetMemHandle(&hf, ctx->flags_local));
-  std::memcpy(h, &hr, sizeof(hr));
-  std::memcpy(h + sizeof(hr), &hf, sizeof(hf));
-  const size_t hb = sizeof(h);
-  TG_CUDA(cudaMemcpyAsync(ctx->nccl_stage, h, hb, cudaMemcpyHostToDevice, ctx->stream));
+  cudaIpcMemHandle_t hx;
+  TG_CUDA(cudaIpcGetMemHandle(&hx, ctx->xchg_local));
+  const size_t hb = sizeof(hx);
+  TG_CUDA(cudaMemcpyAsync(ctx->nccl_stage, &hx, hb, cudaMemcpyHostToDevice, ctx->stream));
   TG_TRY(nccl_allgather_bytes(ctx, ctx->nccl_stage, ctx->nccl_stage + hb, hb));
   std::vector<unsigned char> all((size_t)W * hb);
   TG_CUDA(cudaMemcpy(all.data(), ctx->nccl_stage + hb, all.size(), cudaMemcpyDeviceToHost));
   unsigned char ok = 1;
   for (int r = 0; r < W && ok; ++r) {
     if (r == ctx->rank) continue;
-    cudaIpcMemHandle_t pr, pf;
+    cudaIpcMemHandle_t pr;
     std::memcpy(&pr, all.data() + r * hb, sizeof(pr));
-    std::memcpy(&pf, all.data() + r * hb + sizeof(pr), sizeof(pf));
-    void *a = nullptr, *b2 = nullptr;
-    if (cudaIpcOpenMemHandle(&a, pr, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess ||
-        cudaIpcOpenMemHandle(&b2, pf, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    void* a = nullptr;
+    if (cudaIpcOpenMemHandle(&a, pr, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
       cudaGetLastError();
-      if (a) cudaIpcCloseMemHandle(a);
       ok = 0;
       break;
     }
-    ctx->recv_peer[r] = static_cast<float*>(a);
-    ctx->flags_peer[r] = static_cast<unsigned*>(b2);
+    ctx->xchg_peer[r] = static_cast<unsigned long long*>(a);
   }
   // Consensus: peer memory only if every rank mapped every peer.  This
   // exchange also orders every rank's zeroing before any peer store.
@@ -899,15 +888,9 @@ int run_fused(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const fl
     p.world = ctx->world;
     p.rank = ctx->rank;
     p.b_cap = ctx->p2p_bcap;
-    p.recv_local = ctx->recv_local;
-    p.flags_local = ctx->flags_local;
-    for (int r = 0; r < ctx->world; ++r) {
-      p.recv_peer[r] = ctx->recv_peer[r];
-      p.flags_peer[r] = ctx->flags_peer[r];
-    }
-    const size_t nflags = (size_t)2 * ctx->world * ctx->p2p_bcap * ctx->p2p_heads;
-    p.epoch = ctx->flags_local + nflags;
-    p.done_ctas = reinterpret_cast<int*>(ctx->flags_local + nflags + 32);
+    p.xchg_local = ctx->xchg_local;
+    for (int r = 0; r < ctx->world; ++r) p.xchg_peer[r] = ctx->xchg_peer[r];
+    p.epoch = ctx->xchg_ctl;
   }
   cudaEvent_t ev_stop = nullptr;
   if (ctx->prof_on) {
@@ -1550,12 +1533,27 @@ int tg_comm_init(tg_context* ctx, const void* id, int rank, int world, int timeo
   return TG_OK;
 }
 
+int tg_comm_set_exchange(tg_context* ctx, int exchange) {
+  if (!ctx) return fail(TG_ERR_INVALID_ARG, "null context");
+  if (exchange < TG_EXCHANGE_AUTO || exchange > TG_EXCHANGE_NCCL)
+    return fail(TG_ERR_INVALID_ARG, "exchange %d is not TG_EXCHANGE_AUTO / PEER / NCCL", exchange);
+  ctx->exchange_pref = exchange;
+  return TG_OK;
+}
+
+int tg_comm_exchange(tg_context* ctx, int* exchange) {
+  if (!ctx || !exchange) return fail(TG_ERR_INVALID_ARG, "null argument");
+  *exchange = ctx->exchange_used;
+  return TG_OK;
+}
+
 int tg_comm_destroy(tg_context* ctx) {
   TG_TRY(set_device(ctx));
   if (!ctx->comm) return TG_OK;
   cudaStreamSynchronize(ctx->stream);
   p2p_release(ctx);
   ctx->p2p_failed = false;
+  ctx->exchange_used = TG_EXCHANGE_AUTO;
   nccl().CommDestroy(ctx->comm);
   ctx->comm = nullptr;
   ctx->world = 1;
@@ -1572,14 +1570,21 @@ int splitkv_core(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, float*
   if (fused && ctx->world == 1)  // one GPU: no exchange at all
     return run_fused(ctx, kv, layer, n_seqs, dq, rope_new ? dq : nullptr, rope_new ? dk : nullptr,
                      dv, dp, dout, nullptr, 0, rope_new, rope_new);
-  if (fused && ctx->world > 1) {
-    const int rc = ensure_p2p(ctx, n_seqs, d.n_head, rf);
-    if (rc == TG_OK)
+  if (ctx->world > 1 && ctx->exchange_pref != TG_EXCHANGE_NCCL) {
+    const int rc = fused ? ensure_p2p(ctx, n_seqs, d.n_head, rf) : TG_ERR_UNSUPPORTED;
+    if (rc == TG_OK) {
+      ctx->exchange_used = TG_EXCHANGE_PEER;
       return run_fused(ctx, kv, layer, n_seqs, dq, rope_new ? dq : nullptr,
                        rope_new ? dk : nullptr, dv, dp, dout, nullptr, 2, rope_new, rope_new);
+    }
     if (rc != TG_ERR_UNSUPPORTED) return rc;
+    if (ctx->exchange_pref == TG_EXCHANGE_PEER)
+      return fail(TG_ERR_UNSUPPORTED,
+                  "peer-memory exchange needs a bf16 tensor-core cache and peer access "
+                  "between every pair of GPUs");
     t_err.clear();  // no peer memory between these GPUs: NCCL all-gather below
   }
+  if (ctx->world > 1) ctx->exchange_used = TG_EXCHANGE_NCCL;
   // Records of this shard, all-gathered over NCCL, merged on every rank.
   TG_TRY(ensure_buf(ctx, &ctx->records, &ctx->rec_cap, (size_t)n_seqs * rf));
   if (fused) {

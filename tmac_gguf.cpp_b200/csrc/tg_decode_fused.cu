@@ -18,13 +18,13 @@
 //    CTA's two partial-record slots.
 // Merge kernel: one item per (sequence, head), spread over many SMs so the
 // tail of the step is short; in mode 2 (split-KV across GPUs) it stores its
-// record slice into every GPU's receive buffer (NVLink peer stores),
-// publishes an epoch-tagged flag with release semantics at system scope,
-// waits (bounded) for the flags of all GPUs and merges.  Receive buffers
-// alternate between launches (epoch parity) because a GPU can be at most one
-// launch ahead of the others.
+// record slice into every GPU's receive words over NVLink, each 4-byte value
+// packed with the launch's epoch tag into one 8-byte store, so receivers poll
+// the data itself (bounded) and need no fence or flag; then it merges.
+// Receive words alternate between launches (epoch parity) because a GPU can
+// be at most one launch ahead of the others.
 //
-// Every wait is bounded (mbarriers, peer flags); on expiry the error word is
+// Every wait is bounded (mbarriers, peer words); on expiry the error word is
 // set and the kernel still reaches its end.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -74,12 +74,12 @@ __device__ __forceinline__ void cons_sync(int n) {
   asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory");
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -203,9 +203,13 @@ __global__ void __launch_bounds__(FusedCfg<NKV>::THREADS, 1)
     }
   }
   griddep_wait();
-  // The previous launch's merge kernel reads the schedule buffer.
-  if (blockIdx.x == 0)
+  // The previous launch's merge kernel has finished: it read the schedule
+  // buffer and, in mode 2, the exchange epoch, which advances here once per
+  // launch (the merge kernel of this launch reads it after its own wait).
+  if (blockIdx.x == 0) {
     for (int i = threadIdx.x; i <= p.B; i += blockDim.x) p.sched[i] = prefix[i];
+    if (p.mode == 2 && threadIdx.x == 0) *p.epoch += 1u;
+  }
   __syncthreads();
 
   if (active && warp == Cfg::CWARPS) {
@@ -509,9 +513,9 @@ constexpr int kPartBatch = 16;  // parts per group per load round
 //      a split sequence, the complete record the decode kernel wrote, or a
 //      neutral record when this shard holds no row of s;
 //   2. mode 0: output of split sequences; mode 1: the record;
-//      mode 2: the slice is stored into every GPU's receive buffer, an
-//      epoch-tagged flag per (s, h) is released at system scope, the flags of
-//      all GPUs are awaited (bounded) and the slices merged into the output;
+//      mode 2: the slice is stored into every GPU's receive words, each
+//      value tagged with the launch's epoch, the words of all GPUs are
+//      awaited (bounded) and the slices merged into the output;
 //   3. with RoPE, the rotated q (and k for h < n_kv) of the sequences that
 //      the decode kernel did not finish inside one CTA go back to the caller.
 // In mode 2 the grid is persistent: CTA c takes items c, c + grid, ... in
@@ -524,13 +528,19 @@ __global__ void __launch_bounds__(64 * GROUPS) merge_exchange_kernel(const Fused
   __shared__ float ml_grp[GROUPS][2];
   __shared__ int pre[64 * GROUPS + 1];
   __shared__ int wsum[2 * GROUPS];
-  __shared__ int fail;
   const int tid = threadIdx.x, d = tid & 63, grp = tid >> 6;
   griddep_launch_dependents();
   // With at most one sequence per thread, the tile prefix is rebuilt from the
   // positions before the wait (as the decode kernel does); otherwise the
   // decode kernel's copy is read after it.
   const bool local_sched = p.B <= 64 * GROUPS;
+  // The RoPE row of this CTA's first item (the table is written only when
+  // it is created).
+  const int s_first = blockIdx.x / p.n_head;
+  const int pos_first = s_first < p.B ? p.pos[s_first] : -1;
+  float2 cs_first = make_float2(0.f, 0.f);
+  if (p.rope && pos_first >= 0 && pos_first < p.table_len)
+    cs_first = reinterpret_cast<const float2*>(p.cs + (size_t)pos_first * 64)[d >> 1];
   if (local_sched) {
     const int lane = tid & 31, w = tid >> 5;
     const int tiles = tid < p.B ? max(seq_tiles(p, p.pos[tid]), 0) : 0;
@@ -562,7 +572,8 @@ __global__ void __launch_bounds__(64 * GROUPS) merge_exchange_kernel(const Fused
     const int c2 = t1 > t0 ? cta_of_tile(t1 - 1, G, T) : 0;
     const bool split = t1 > t0 && c1 != c2;
     if (p.mode == 0 && !split) continue;  // finished by the decode kernel
-    const int pos_s = p.pos[s];
+    const bool first = it == (int)blockIdx.x;
+    const int pos_s = first ? pos_first : p.pos[s];
     const bool rope = p.rope && (split || t1 == t0) && grp == 0 && pos_s >= 0 &&
                       pos_s < p.table_len;
     const bool has_k = rope && p.k_io && h < p.n_kv;
@@ -571,7 +582,7 @@ __global__ void __launch_bounds__(64 * GROUPS) merge_exchange_kernel(const Fused
     if (rope) {
       const float* qi = p.q_in + (size_t)s * qdim + h * 64;
       xq = make_float2(qi[d & ~1], qi[d | 1]);
-      cs = reinterpret_cast<const float2*>(p.cs + (size_t)pos_s * 64)[d >> 1];
+      cs = first ? cs_first : reinterpret_cast<const float2*>(p.cs + (size_t)pos_s * 64)[d >> 1];
       if (has_k) {
         const float* kk = p.k_io + (size_t)s * p.n_kv * 64 + h * 64;
         xk = make_float2(kk[d & ~1], kk[d | 1]);
@@ -655,71 +666,68 @@ __global__ void __launch_bounds__(64 * GROUPS) merge_exchange_kernel(const Fused
         }
       }
     } else {
+      // Peer exchange: each value travels with its epoch tag in one 8-byte
+      // store (single-copy atomic), so a receiver that sees the tag sees the
+      // value -- no fence and no separate flag.  Receive words alternate
+      // between launches by epoch parity (a GPU is at most one launch ahead).
       const int par = (int)(epoch & 1);
-      const size_t mine = ((size_t)(par * p.world + p.rank) * p.b_cap + s) * rf;
+      const unsigned long long tag = (unsigned long long)epoch << 32;  // epoch >= 1
+      const size_t item_words = (size_t)kXchgWords;
+      const size_t mine = (((size_t)(par * p.world + p.rank) * p.b_cap + s) * H + h) * item_words;
       if (grp == 0) {
+        const unsigned long long wo = tag | __float_as_uint(o);
+        const unsigned long long wm = tag | __float_as_uint(m);
+        const unsigned long long wl = tag | __float_as_uint(l);
         for (int r = 0; r < p.world; ++r) {
-          float* dst = (r == p.rank ? p.recv_local : p.recv_peer[r]) + mine;
-          dst[h * 64 + d] = o;
+          unsigned long long* dst = (r == p.rank ? p.xchg_local : p.xchg_peer[r]) + mine;
+          st_relaxed_sys_u64(dst + d, wo);
           if (d == 0) {
-            dst[qdim + h] = m;
-            dst[qdim + H + h] = l;
+            st_relaxed_sys_u64(dst + 64, wm);
+            st_relaxed_sys_u64(dst + 65, wl);
           }
         }
-      }
-      if (tid == 0) fail = 0;
-      // The slice's stores (group 0) happen before the flag stores (one
-      // thread per GPU) through the barrier and the system-scope fence.
-      __syncthreads();
-      const size_t fmine = ((size_t)(par * p.world + p.rank) * p.b_cap + s) * H + h;
-      if (tid < p.world) {
-        __threadfence_system();
-        st_release_sys((tid == p.rank ? p.flags_local : p.flags_peer[tid]) + fmine, epoch + 1u);
-        const unsigned* f = p.flags_local + ((size_t)(par * p.world + tid) * p.b_cap + s) * H + h;
-        bool got = false;
-        const long long c0 = clock64();
-        for (long long n = 0; n < kPeerWaitPolls; ++n) {
-          if (ld_acquire_sys(f) == epoch + 1u) {
-            got = true;
-            break;
-          }
-          if (clock64() - c0 > kPeerWaitCycles) break;
-          __nanosleep(32);
-        }
-        if (!got) {
-          record_error(p.err, kDevErrPeerTimeout);
-          fail = 1;
-        }
-      }
-      __syncthreads();
-      if (!fail && grp == 0) {
-        // Slices written by other GPUs are read through L2 (__ldcg), where
-        // their NVLink stores land.
-        const float* base = p.recv_local + ((size_t)(par * p.world) * p.b_cap + s) * rf;
-        const size_t stride = (size_t)p.b_cap * rf;
+        // Gather: this thread's dimension and every GPU's m and l.
+        const unsigned long long* base =
+            p.xchg_local + (((size_t)(par * p.world) * p.b_cap + s) * H + h) * item_words;
+        const size_t stride = (size_t)p.b_cap * H * item_words;
         float mv[kMaxPeers], lv[kMaxPeers], ov[kMaxPeers];
-        float M = kNegBig;
+        unsigned pending = (1u << p.world) - 1u;
+        const long long c0 = clock64();
+        for (long long n = 0; pending && n < kPeerWaitPolls; ++n) {
 #pragma unroll
-        for (int r = 0; r < kMaxPeers; ++r) {
-          mv[r] = kNegBig;
-          lv[r] = 0.f;
-          ov[r] = 0.f;
-          if (r < p.world) {
-            const float* rr = base + r * stride;
-            mv[r] = __ldcg(rr + qdim + h);
-            lv[r] = __ldcg(rr + qdim + H + h);
-            ov[r] = __ldcg(rr + h * 64 + d);
+          for (int r = 0; r < kMaxPeers; ++r) {
+            if (!(pending >> r & 1u)) continue;
+            const unsigned long long* rr = base + r * stride;
+            const unsigned long long x = ld_relaxed_sys_u64(rr + d);
+            const unsigned long long y = ld_relaxed_sys_u64(rr + 64);
+            const unsigned long long z = ld_relaxed_sys_u64(rr + 65);
+            if ((x >> 32) == (tag >> 32) && (y >> 32) == (tag >> 32) && (z >> 32) == (tag >> 32)) {
+              ov[r] = __uint_as_float((unsigned)x);
+              mv[r] = __uint_as_float((unsigned)y);
+              lv[r] = __uint_as_float((unsigned)z);
+              pending &= ~(1u << r);
+            }
           }
-          M = fmaxf(M, mv[r]);
+          if (pending && clock64() - c0 > kPeerWaitCycles) break;
         }
-        float O = 0.f, L = 0.f;
+        if (pending) {
+          record_error(p.err, kDevErrPeerTimeout);
+        } else {
+          float M = kNegBig;
 #pragma unroll
-        for (int r = 0; r < kMaxPeers; ++r) {
-          const float w = ex2(mv[r] - M);
-          O = fmaf(ov[r], w, O);
-          L = fmaf(lv[r], w, L);
+          for (int r = 0; r < kMaxPeers; ++r)
+            if (r < p.world) M = fmaxf(M, mv[r]);
+          float O = 0.f, L = 0.f;
+#pragma unroll
+          for (int r = 0; r < kMaxPeers; ++r) {
+            if (r < p.world) {
+              const float w = ex2(mv[r] - M);
+              O = fmaf(ov[r], w, O);
+              L = fmaf(lv[r], w, L);
+            }
+          }
+          p.out[(size_t)s * qdim + h * 64 + d] = O / L;
         }
-        p.out[(size_t)s * qdim + h * 64 + d] = O / L;
       }
     }
     if (rope) {
@@ -732,16 +740,7 @@ __global__ void __launch_bounds__(64 * GROUPS) merge_exchange_kernel(const Fused
         p.k_io[(size_t)s * p.n_kv * 64 + h * 64 + d] = (d & 1) ? rk.y : rk.x;
       }
     }
-    if (GROUPS > 1 || p.mode == 2) __syncthreads();
-  }
-  if (p.mode == 2 && threadIdx.x == 0) {
-    __threadfence();
-    const int old = atomicAdd(p.done_ctas, 1);
-    if (old == (int)gridDim.x - 1) {
-      *reinterpret_cast<volatile unsigned*>(p.epoch) = epoch + 1u;
-      *reinterpret_cast<volatile int*>(p.done_ctas) = 0;
-      __threadfence();
-    }
+    if (GROUPS > 1) __syncthreads();
   }
 }
 

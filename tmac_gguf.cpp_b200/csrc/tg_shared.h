@@ -35,6 +35,8 @@ enum DeviceError : int {
 };
 
 constexpr int kMaxPeers = 8;
+// Words per (sequence, head) in the peer exchange: o[64], m, l.
+constexpr int kXchgWords = 66;
 
 constexpr float kNegBig = -1.0e30f;  // finite "minus infinity" for m
 
@@ -168,12 +170,11 @@ struct FusedParams {
   int prefetch;            // L2 prefetch of the first tiles before the grid-dependency wait
   // mode 2
   int world, rank, b_cap;  // receive buffers hold b_cap sequences
-  float* recv_local;       // [2][world][b_cap][record_floats] on this GPU
-  float* recv_peer[kMaxPeers];
-  unsigned* flags_local;   // [2][world][b_cap][n_head]
-  unsigned* flags_peer[kMaxPeers];
-  unsigned* epoch;         // launch counter of the exchange on this GPU
-  int* done_ctas;          // CTAs finished in this launch
+  // Receive words [2][world][b_cap][n_head][kXchgWords] on this GPU and
+  // mapped from every peer: each word = (epoch tag << 32) | float bits.
+  unsigned long long* xchg_local;
+  unsigned long long* xchg_peer[kMaxPeers];
+  unsigned* epoch;         // exchange launches on this GPU (advanced by the decode kernel)
 };
 
 }  // namespace tg
