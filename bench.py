@@ -68,6 +68,21 @@ WORKLOADS = {
 }
 
 
+# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
+# capture on a B200 at N = 1 (the committed summary named beside each).  For a
+# KV shard of 1/N of the context the launch streams 1/N of the rows, so the
+# figure is scaled by the shard's share of the rows.
+NCU_TRAFFIC = {
+    "longctx": (268508928 + 3666176, "profiles/decode_fused_longctx.md"),
+    "prefill": (75751936 + 67844352, "profiles/prefill_attn_config5.md"),
+}
+
+
+def ncu_traffic(workload, share=1.0):
+    t = NCU_TRAFFIC.get(workload)
+    return None if t is None else t[0] * share
+
+
 def load_package():
     name = "tmac_gguf_cpp_b200"
     if name in sys.modules:
@@ -376,7 +391,8 @@ def run_prefill_bench(args, wl, rank, world, local, be, tg, barrier, max_over_ra
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                          "unit": "TFLOP/s", "frac": achieved / peak, "peak_kind": peak_kind,
                          "kernel": "prefill_attn_kernel", "flops_per_launch": flops,
-                         "launch_ms": k_ms, "traffic": None},
+                         "launch_ms": k_ms, "traffic": ncu_traffic(args.workload),
+                         "traffic_unit": "bytes per launch (ncu dram__bytes_read + write)"},
             "e2e": {"value": e2e, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": B * S * (QD + 2 * KD) * 4,
                     "d2h_bytes_per_step": B * S * QD * 4},
@@ -605,7 +621,9 @@ def main():
                          "peak_kind": peak_kind, "kernel": "decode_fused_kernel"
                          if kv.uses_tensor_cores() else "decode_generic_kernel",
                          "bytes_per_launch": k_bytes, "launch_ms": k_avg_ms,
-                         "traffic": None},
+                         "traffic": ncu_traffic(args.workload,
+                                                shard_len / wl["ctx"] if wl["split"] else 1.0),
+                         "traffic_unit": "bytes per launch (ncu dram__bytes_read + write)"},
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "clocks": clocks,
