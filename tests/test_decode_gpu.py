@@ -269,6 +269,80 @@ def test_device_arrays_and_batched_attention(tg, backend, cases):
     np.testing.assert_allclose(od.cpu().numpy(), out_host, atol=1e-6, rtol=0)
 
 
+def _fill_same(kv_list, cases, positions, bf16, seed, layers):
+    """Write the same rows 0..pos-1 of every layer into each cache; return
+    the per-layer raw inputs (Q, K, V) and the oracle results."""
+    B = len(positions)
+    inputs, refs = [], []
+    for layer in range(layers):
+        Q = np.zeros((B, cases.QD), np.float32)
+        K = np.zeros((B, cases.KD), np.float32)
+        V = np.zeros((B, cases.KD), np.float32)
+        lrefs = []
+        for i, pos in enumerate(positions):
+            q, k_new, v_new, kc, vc = cases.decode_inputs(seed, pos, bf16, seq=i, layer=layer)
+            for kv in kv_list:
+                if pos > 0:
+                    kv.write_rows(layer, i, 0, kc[:pos], vc[:pos])
+            Q[i], K[i], V[i] = q, k_new, v_new
+            lrefs.append(cases.oracle_decode(seed, pos, bf16, seq=i, layer=layer))
+        inputs.append((Q, K, V))
+        refs.append(lrefs)
+    return inputs, refs
+
+
+@pytest.mark.parametrize("splitkv", [False, True])
+def test_pinned_host_buffers_match_pageable(tg, backend, O, cases, splitkv):
+    """Host buffers in page-locked memory take the direct path (inputs packed
+    into one copy per call, outputs written by the kernels through the
+    buffers' device addresses); results are bit-identical to pageable numpy
+    buffers and within the bar of the oracle.  Long positions split
+    sequences across CTAs, so the merge kernel's writes are covered too."""
+    import torch
+    positions = [0, 33, 4095, 9000]
+    layers = 2
+    max_ctx = max(positions) + 1
+    kv_a = tg.KVCache(backend, layers, len(positions), max_ctx, dtype=tg.DTYPE_BF16)
+    kv_b = tg.KVCache(backend, layers, len(positions), max_ctx, dtype=tg.DTYPE_BF16)
+    inputs, refs = _fill_same([kv_a, kv_b], cases, positions, True, 31, layers)
+    pos_np = np.array(positions, np.int32)
+    pos_pin = torch.from_numpy(pos_np.copy()).pin_memory()
+    res_a, res_b = [], []
+    backend.metal_batch_begin()
+    for layer in range(layers):
+        Q, K, V = (x.copy() for x in inputs[layer])
+        out = np.zeros_like(Q)
+        (kv_a.decode_layer_splitkv if splitkv else kv_a.decode_layer)(layer, Q, K, V, pos_np, out)
+        res_a.append((Q, K, out))
+        Qp, Kp, Vp = (torch.from_numpy(x.copy()).pin_memory() for x in inputs[layer])
+        outp = torch.zeros(Qp.shape, dtype=torch.float32).pin_memory()
+        (kv_b.decode_layer_splitkv if splitkv else kv_b.decode_layer)(layer, Qp, Kp, Vp,
+                                                                     pos_pin, outp)
+        res_b.append((Qp, Kp, outp))
+    backend.metal_batch_end()
+    for layer in range(layers):
+        Q, K, out = res_a[layer]
+        Qp, Kp, outp = (t.numpy() for t in res_b[layer])
+        assert np.array_equal(bits(Qp), bits(Q)), layer       # rotated q written back
+        assert np.array_equal(bits(Kp), bits(K)), layer       # rotated k written back
+        assert np.array_equal(bits(outp), bits(out)), layer   # same kernels, same bits
+        for i, pos in enumerate(positions):
+            qr, kr, vr, kc, vc, ctx = refs[layer][i]
+            assert np.array_equal(bits(Qp[i]), bits(qr)), (layer, pos)
+            ka, va = kv_a.read_rows(layer, i, pos, 1)
+            kb, vb = kv_b.read_rows(layer, i, pos, 1)
+            assert np.array_equal(kb, ka) and np.array_equal(vb, va)
+            assert np.array_equal(kb[0], O.pack_bf16(kc[pos])), (layer, pos)
+            assert maxabs(outp[i], ctx) <= BF16_TOL, (layer, pos)
+    # outside a batch the call returns with the host outputs valid
+    Q, K, V = (torch.from_numpy(x.copy()).pin_memory() for x in inputs[0])
+    outp = torch.zeros(Q.shape, dtype=torch.float32).pin_memory()
+    kv_c = tg.KVCache(backend, 1, len(positions), max_ctx, dtype=tg.DTYPE_BF16)
+    _fill_same([kv_c], cases, positions, True, 31, 1)
+    kv_c.decode_layer(0, Q, K, V, pos_pin, outp)
+    assert np.array_equal(bits(outp.numpy()), bits(res_a[0][2]))
+
+
 # ------------------------------------------------------ split-KV on one GPU
 
 def test_splitkv_world1_equals_batched(tg, backend, cases):

@@ -161,6 +161,16 @@ struct tg_context {
   char* arena = nullptr;     size_t arena_cap = 0, arena_off = 0;
   uint16_t* qbf = nullptr;   size_t qbf_cap = 0;     // prefill: rotated bf16 q
   std::vector<PendingCopy> pending;  // device -> host copies of staged outputs
+  // Host inputs of the current call, moved to the arena by commit_inputs.
+  struct PackEntry {
+    char* dev;
+    const char* host;
+    size_t bytes;
+  };
+  std::vector<PackEntry> pack;
+
+  char* hpin = nullptr;      size_t hpin_cap = 0, hpin_off = 0;
+  std::vector<char*> hpin_old;  // outgrown pinned blocks, freed at the next sync
   std::vector<void*> graveyard;      // device buffers freed at the next sync
 
   std::vector<RopeTable> tables;
@@ -238,6 +248,8 @@ bool is_device_ptr(const void* p) {
 void free_graveyard(tg_context* ctx) {
   for (void* p : ctx->graveyard) cudaFree(p);
   ctx->graveyard.clear();
+  for (char* p : ctx->hpin_old) cudaFreeHost(p);
+  ctx->hpin_old.clear();
 }
 
 template <typename T>
@@ -320,35 +332,148 @@ int arena_alloc(tg_context* ctx, size_t bytes, void** out) {
   return TG_OK;
 }
 
-int stage_in(tg_context* ctx, const void* p, size_t bytes, const void** dev) {
-  if (!p || bytes == 0 || is_device_ptr(p)) {
-    *dev = p;
-    return TG_OK;
+// Inputs up to this size are packed; larger ones are copied on their own.
+constexpr size_t kPackMaxBytes = size_t(1) << 20;
+
+
+// Pinned host staging for packed inputs (linear; reset when the stream is
+// idle, so a block is never rewritten while a copy from it may be pending).
+int hpin_alloc(tg_context* ctx, size_t bytes, char** out) {
+  bytes = (bytes + 255) & ~size_t(255);
+  if (ctx->hpin_off + bytes > ctx->hpin_cap) {
+    size_t n = ctx->hpin_cap * 2;
+    if (n < bytes * 2) n = bytes * 2;
+    if (n < (size_t(1) << 20)) n = size_t(1) << 20;
+    char* nb = nullptr;
+    TG_CUDA(cudaHostAlloc(&nb, n, cudaHostAllocDefault));
+    if (ctx->hpin) ctx->hpin_old.push_back(ctx->hpin);
+    ctx->hpin = nb;
+    ctx->hpin_cap = n;
+    ctx->hpin_off = 0;
   }
+  *out = ctx->hpin + ctx->hpin_off;
+  ctx->hpin_off += bytes;
+  return TG_OK;
+}
+
+// Where a pointer lives: device memory, page-locked host memory (with the
+// device address of it), or pageable host memory.  One driver query.
+struct PtrInfo {
+  bool device = false;
+  void* alias = nullptr;
+};
+PtrInfo classify(const void* p) {
+  PtrInfo r;
+  if (!p) return r;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return r;
+  }
+  r.device = a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+  if (a.type == cudaMemoryTypeHost) r.alias = a.devicePointer;
+  return r;
+}
+
+// A host input of the current call: gets its arena slot now; the bytes move
+// at commit_inputs.
+int pack_input(tg_context* ctx, const void* p, size_t bytes, void** dev) {
   if (ctx->capturing)
     return fail(TG_ERR_STATE, "host pointers cannot be used inside a graph capture");
   ctx->call_staged = true;
   void* d = nullptr;
   TG_TRY(arena_alloc(ctx, bytes, &d));
-  TG_CUDA(cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  ctx->pack.push_back({static_cast<char*>(d), static_cast<const char*>(p), bytes});
   *dev = d;
   return TG_OK;
 }
 
-// Output (copy_in = false) or in/out (copy_in = true) buffer.
-int stage_out(tg_context* ctx, void* p, size_t bytes, bool copy_in, void** dev) {
-  if (!p || bytes == 0 || is_device_ptr(p)) {
+// Moves the current call's host inputs to their arena slots: packed into
+// page-locked staging on the CPU and moved by one copy-engine transfer per
+// run of consecutive slots (measured faster end to end than a kernel that
+// reads page-locked inputs over the host link, which would spare the copy
+// node between kernels).
+int commit_inputs(tg_context* ctx) {
+  if (ctx->pack.empty()) return TG_OK;
+  std::vector<char*> stage(ctx->pack.size());
+  for (size_t i = 0; i < ctx->pack.size(); ++i) {
+    TG_TRY(hpin_alloc(ctx, ctx->pack[i].bytes, &stage[i]));
+    std::memcpy(stage[i], ctx->pack[i].host, ctx->pack[i].bytes);
+  }
+  size_t i = 0;
+  while (i < ctx->pack.size()) {
+    char* d0 = ctx->pack[i].dev;
+    char* h0 = stage[i];
+    size_t run = 0, j = i;
+    for (; j < ctx->pack.size(); ++j) {
+      if (ctx->pack[j].dev != d0 + run || stage[j] != h0 + run) break;
+      run += (ctx->pack[j].bytes + 255) & ~size_t(255);
+    }
+    const size_t bytes = (size_t)(ctx->pack[j - 1].dev - d0) + ctx->pack[j - 1].bytes;
+    TG_CUDA(cudaMemcpyAsync(d0, h0, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    i = j;
+  }
+  ctx->pack.clear();
+  return TG_OK;
+}
+
+int stage_in(tg_context* ctx, const void* p, size_t bytes, const void** dev) {
+  const PtrInfo pi = bytes ? classify(p) : PtrInfo{};
+  if (!p || bytes == 0 || pi.device) {
     *dev = p;
+    return TG_OK;
+  }
+  void* d = nullptr;
+  if (bytes > kPackMaxBytes) {  // bulk data (cache rows): one copy of its own
+    if (ctx->capturing)
+      return fail(TG_ERR_STATE, "host pointers cannot be used inside a graph capture");
+    ctx->call_staged = true;
+    TG_TRY(commit_inputs(ctx));
+    TG_TRY(arena_alloc(ctx, bytes, &d));
+    TG_CUDA(cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  } else {
+    TG_TRY(pack_input(ctx, p, bytes, &d));
+  }
+  *dev = d;
+  return TG_OK;
+}
+
+// Output (copy_in = false) or in/out (copy_in = true) buffer.  dev_in is
+// what kernels read, *dev what they write.  Pinned host memory is written
+// directly through its device alias when dev_in is given (the kernel takes
+// separate in / out pointers); otherwise host buffers get an arena copy and
+// a device->host copy when the call finishes.
+int stage_out(tg_context* ctx, void* p, size_t bytes, bool copy_in, void** dev,
+              const void** dev_in = nullptr) {
+  const PtrInfo pi = bytes ? classify(p) : PtrInfo{};
+  if (!p || bytes == 0 || pi.device) {
+    *dev = p;
+    if (dev_in) *dev_in = p;
     return TG_OK;
   }
   if (ctx->capturing)
     return fail(TG_ERR_STATE, "host pointers cannot be used inside a graph capture");
   ctx->call_staged = true;
+  if (dev_in && pi.alias) {
+    *dev = pi.alias;
+    if (copy_in) {
+      void* d = nullptr;
+      TG_TRY(pack_input(ctx, p, bytes, &d));
+      *dev_in = d;
+    } else {
+      *dev_in = pi.alias;
+    }
+    return TG_OK;
+  }
   void* d = nullptr;
-  TG_TRY(arena_alloc(ctx, bytes, &d));
-  if (copy_in) TG_CUDA(cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  if (copy_in) {
+    TG_TRY(pack_input(ctx, p, bytes, &d));
+  } else {
+    TG_TRY(arena_alloc(ctx, bytes, &d));
+  }
   ctx->pending.push_back({p, d, bytes});
   *dev = d;
+  if (dev_in) *dev_in = d;
   return TG_OK;
 }
 
@@ -358,6 +483,7 @@ int stage_out(tg_context* ctx, void* p, size_t bytes, bool copy_in, void** dev) 
 // any stream-ordered CUDA work, and device-side errors surface at the next
 // tg_synchronize / tg_batch_end.
 int finish_call(tg_context* ctx) {
+  TG_TRY(commit_inputs(ctx));
   const bool staged = ctx->call_staged;
   ctx->call_staged = false;
   for (const PendingCopy& c : ctx->pending)
@@ -366,6 +492,7 @@ int finish_call(tg_context* ctx) {
   if (ctx->in_batch || !staged) return TG_OK;
   TG_TRY(wait_stream(ctx));
   ctx->arena_off = 0;
+  ctx->hpin_off = 0;
   free_graveyard(ctx);
   return check_device_error(ctx);
 }
@@ -510,6 +637,7 @@ int flush_regions(tg_context* ctx) {
     }
   }
   ctx->arena_off = 0;
+  ctx->hpin_off = 0;
   ctx->call_staged = false;
   free_graveyard(ctx);
   return check_device_error(ctx);
@@ -607,6 +735,7 @@ int generic_grid(tg_context* ctx, int dtype, size_t smem) {
 // writes per-sequence records to ctx->records.
 int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const float* q,
                const int* past_dev, int past_scalar, float* out, int mode) {
+  TG_TRY(commit_inputs(ctx));
   const tg_kv_desc& d = kv->d;
   TG_TRY(check_align8(q, "q"));
   TG_TRY(check_align8(out, "out"));
@@ -692,6 +821,7 @@ int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const f
 
 int run_rope(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, float* q, float* k,
              const float* v, const int* pos_dev) {
+  TG_TRY(commit_inputs(ctx));
   const tg_kv_desc& d = kv->d;
   TG_TRY(check_align8(q, "q"));
   TG_TRY(check_align8(k, "k_new"));
@@ -824,11 +954,13 @@ int ensure_p2p(tg_context* ctx, int B, int n_head, int rf) {
 // the communicator (peer memory, set up by ensure_p2p) and output.
 int run_fused(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const float* q_in,
               float* q_out, float* k_io, const float* v_new, const int* pos, float* out,
-              float* records, int mode, bool rope, bool new_row) {
+              float* records, int mode, bool rope, bool new_row, float* k_out = nullptr) {
+  TG_TRY(commit_inputs(ctx));
   const tg_kv_desc& d = kv->d;
   TG_TRY(check_align8(q_in, "q"));
   TG_TRY(check_align8(q_out, "q"));
   TG_TRY(check_align8(k_io, "k_new"));
+  TG_TRY(check_align8(k_out, "k_new"));
   TG_TRY(check_align8(out, "out"));
   const int rf = tg::record_floats(d.n_head, d.head_dim);
   RopeTable* t = nullptr;
@@ -847,6 +979,7 @@ int run_fused(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const fl
   p.q_in = q_in;
   p.q_out = q_out;
   p.k_io = k_io;
+  p.k_out = k_out ? k_out : k_io;
   p.v_new = v_new;
   p.pos = pos;
   p.cs = t->d;
@@ -1016,6 +1149,7 @@ int tg_shutdown(tg_context* ctx) {
   cudaFree(ctx->records);
   cudaFree(ctx->recv);
   cudaFree(ctx->arena);
+  if (ctx->hpin) cudaFreeHost(ctx->hpin);
   cudaFree(ctx->qbf);
   cudaFree(ctx->d_err);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
@@ -1068,6 +1202,7 @@ int tg_synchronize(tg_context* ctx) {
   TG_TRY(wait_stream(ctx));
   if (!ctx->in_batch) {
     ctx->arena_off = 0;
+    ctx->hpin_off = 0;
     free_graveyard(ctx);
   }
   return check_device_error(ctx);
@@ -1385,6 +1520,7 @@ int tg_kv_write_rows(tg_kv_cache* kv, int layer, int seq, int row0, int n_rows,
     if (!src[i]) continue;
     const void* ds = nullptr;
     TG_TRY(stage_in(ctx, src[i], n * 4, &ds));
+    TG_TRY(commit_inputs(ctx));
     cudaError_t e = tg::launch_convert_rows(dst[i], static_cast<const float*>(ds), n,
                                             kv->d.dtype, ctx->num_sms, ctx->stream);
     if (e != cudaSuccess) return fail(TG_ERR_CUDA, "convert launch: %s", cudaGetErrorString(e));
@@ -1465,17 +1601,20 @@ int tg_decode_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, flo
   const size_t qb = (size_t)n_seqs * d.n_head * d.head_dim * 4;
   const size_t kb = (size_t)n_seqs * kv->row_elems * 4;
   void *dq = nullptr, *dk = nullptr, *dout = nullptr;
-  const void *dv = nullptr, *dp = nullptr;
-  TG_TRY(stage_out(ctx, q, qb, true, &dq));
-  TG_TRY(stage_out(ctx, k_new, kb, true, &dk));
+  const void *dv = nullptr, *dp = nullptr, *dq_in = nullptr, *dk_in = nullptr, *dout_in = nullptr;
+  // The tensor-core path reads staged copies and writes pinned host outputs
+  // directly; the CUDA-core path works in place.
+  const bool split_io = mma_eligible(kv);
+  TG_TRY(stage_out(ctx, q, qb, true, &dq, split_io ? &dq_in : nullptr));
+  TG_TRY(stage_out(ctx, k_new, kb, true, &dk, split_io ? &dk_in : nullptr));
   TG_TRY(stage_in(ctx, v_new, kb, &dv));
   TG_TRY(stage_in(ctx, pos, (size_t)n_seqs * 4, &dp));
-  TG_TRY(stage_out(ctx, out, qb, false, &dout));
-  if (mma_eligible(kv)) {
-    TG_TRY(run_fused(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
-                     static_cast<float*>(dq), static_cast<float*>(dk),
+  TG_TRY(stage_out(ctx, out, qb, false, &dout, split_io ? &dout_in : nullptr));
+  if (split_io) {
+    TG_TRY(run_fused(ctx, kv, layer, n_seqs, static_cast<const float*>(dq_in),
+                     static_cast<float*>(dq), const_cast<float*>(static_cast<const float*>(dk_in)),
                      static_cast<const float*>(dv), static_cast<const int*>(dp),
-                     static_cast<float*>(dout), nullptr, 0, true, true));
+                     static_cast<float*>(dout), nullptr, 0, true, true, static_cast<float*>(dk)));
     return finish_call(ctx);
   }
   TG_TRY(run_rope(ctx, kv, layer, n_seqs, static_cast<float*>(dq), static_cast<float*>(dk),
@@ -1562,20 +1701,29 @@ int tg_comm_destroy(tg_context* ctx) {
 }
 
 namespace {
+// dq / dk are read; dq_out / dk_out receive the rotated q / k (the same
+// buffers unless the caller's pinned host memory is written directly, which
+// only the tensor-core path does).
 int splitkv_core(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, float* dq,
-                 float* dk, const float* dv, const int* dp, float* dout, bool rope_new) {
+                 float* dk, const float* dv, const int* dp, float* dout, bool rope_new,
+                 float* dq_out = nullptr, float* dk_out = nullptr) {
+  TG_TRY(commit_inputs(ctx));
+  if (!dq_out) dq_out = dq;
+  if (!dk_out) dk_out = dk;
   const tg_kv_desc& d = kv->d;
   const int rf = tg::record_floats(d.n_head, d.head_dim);
   const bool fused = mma_eligible(kv);
   if (fused && ctx->world == 1)  // one GPU: no exchange at all
-    return run_fused(ctx, kv, layer, n_seqs, dq, rope_new ? dq : nullptr, rope_new ? dk : nullptr,
-                     dv, dp, dout, nullptr, 0, rope_new, rope_new);
+    return run_fused(ctx, kv, layer, n_seqs, dq, rope_new ? dq_out : nullptr,
+                     rope_new ? dk : nullptr, dv, dp, dout, nullptr, 0, rope_new, rope_new,
+                     rope_new ? dk_out : nullptr);
   if (ctx->world > 1 && ctx->exchange_pref != TG_EXCHANGE_NCCL) {
     const int rc = fused ? ensure_p2p(ctx, n_seqs, d.n_head, rf) : TG_ERR_UNSUPPORTED;
     if (rc == TG_OK) {
       ctx->exchange_used = TG_EXCHANGE_PEER;
-      return run_fused(ctx, kv, layer, n_seqs, dq, rope_new ? dq : nullptr,
-                       rope_new ? dk : nullptr, dv, dp, dout, nullptr, 2, rope_new, rope_new);
+      return run_fused(ctx, kv, layer, n_seqs, dq, rope_new ? dq_out : nullptr,
+                       rope_new ? dk : nullptr, dv, dp, dout, nullptr, 2, rope_new, rope_new,
+                       rope_new ? dk_out : nullptr);
     }
     if (rc != TG_ERR_UNSUPPORTED) return rc;
     if (ctx->exchange_pref == TG_EXCHANGE_PEER)
@@ -1588,9 +1736,12 @@ int splitkv_core(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, float*
   // Records of this shard, all-gathered over NCCL, merged on every rank.
   TG_TRY(ensure_buf(ctx, &ctx->records, &ctx->rec_cap, (size_t)n_seqs * rf));
   if (fused) {
-    TG_TRY(run_fused(ctx, kv, layer, n_seqs, dq, rope_new ? dq : nullptr, rope_new ? dk : nullptr,
-                     dv, dp, nullptr, ctx->records, 1, rope_new, rope_new));
+    TG_TRY(run_fused(ctx, kv, layer, n_seqs, dq, rope_new ? dq_out : nullptr,
+                     rope_new ? dk : nullptr, dv, dp, nullptr, ctx->records, 1, rope_new,
+                     rope_new, rope_new ? dk_out : nullptr));
   } else {
+    if (dq_out != dq || dk_out != dk)
+      return fail(TG_ERR_STATE, "separate q / k outputs need the tensor-core path");
     if (rope_new) TG_TRY(run_rope(ctx, kv, layer, n_seqs, dq, dk, dv, dp));
     TG_TRY(run_decode(ctx, kv, layer, n_seqs, dq, dp, 0, nullptr, 1));
   }
@@ -1627,6 +1778,7 @@ int splitkv_core(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, float*
   g.B = n_seqs;
   g.n_head = d.n_head;
   g.head_dim = d.head_dim;
+  TG_TRY(commit_inputs(ctx));
   cudaError_t e = tg::launch_gather_merge(g, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "gather merge: %s", cudaGetErrorString(e));
   ctx->launches++;
@@ -1698,6 +1850,7 @@ int tg_merge_records(tg_context* ctx, int n_parts, int n_seqs, int n_head, int h
   g.B = n_seqs;
   g.n_head = n_head;
   g.head_dim = head_dim;
+  TG_TRY(commit_inputs(ctx));
   cudaError_t e = tg::launch_gather_merge(g, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "gather merge: %s", cudaGetErrorString(e));
   ctx->launches++;
@@ -1714,15 +1867,24 @@ int tg_decode_layer_splitkv(tg_context* ctx, tg_kv_cache* kv, int layer, int n_s
   const size_t qb = (size_t)n_seqs * d.n_head * d.head_dim * 4;
   const size_t kb = (size_t)n_seqs * kv->row_elems * 4;
   void *dq = nullptr, *dk = nullptr, *dout = nullptr;
-  const void *dv = nullptr, *dp = nullptr;
-  TG_TRY(stage_out(ctx, q, qb, true, &dq));
-  TG_TRY(stage_out(ctx, k_new, kb, true, &dk));
+  const void *dv = nullptr, *dp = nullptr, *dq_in = nullptr, *dk_in = nullptr, *dout_in = nullptr;
+  // The tensor-core path reads staged copies and writes pinned host outputs
+  // directly; the others work in place.
+  const bool split_io = mma_eligible(kv);
+  TG_TRY(stage_out(ctx, q, qb, true, &dq, split_io ? &dq_in : nullptr));
+  TG_TRY(stage_out(ctx, k_new, kb, true, &dk, split_io ? &dk_in : nullptr));
   TG_TRY(stage_in(ctx, v_new, kb, &dv));
   TG_TRY(stage_in(ctx, pos, (size_t)n_seqs * 4, &dp));
-  TG_TRY(stage_out(ctx, out, qb, false, &dout));
-  TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, static_cast<float*>(dq), static_cast<float*>(dk),
+  TG_TRY(stage_out(ctx, out, qb, false, &dout, split_io ? &dout_in : nullptr));
+  if (!split_io) {
+    dq_in = dq;
+    dk_in = dk;
+  }
+  TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, const_cast<float*>(static_cast<const float*>(dq_in)),
+                      const_cast<float*>(static_cast<const float*>(dk_in)),
                       static_cast<const float*>(dv), static_cast<const int*>(dp),
-                      static_cast<float*>(dout), true));
+                      static_cast<float*>(dout), true, static_cast<float*>(dq),
+                      static_cast<float*>(dk)));
   return finish_call(ctx);
 }
 
@@ -1771,6 +1933,7 @@ int tg_prefill_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, in
   rp.n_kv = d.n_kv_head;
   rp.head_dim = d.head_dim;
   rp.max_ctx = d.max_ctx;
+  TG_TRY(commit_inputs(ctx));
   cudaError_t e = tg::launch_prefill_rope(rp, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "prefill rope launch: %s", cudaGetErrorString(e));
   ctx->launches++;

@@ -489,8 +489,9 @@ __global__ void __launch_bounds__(FusedCfg<NKV>::THREADS, 1)
           float2* qo = reinterpret_cast<float2*>(p.q_out + (size_t)s * qdim);
           for (int e = threadIdx.x; e < qdim / 2; e += NCT) qo[e] = rot(qi[e], cs2[e & 31]);
           if (p.k_io) {
-            float2* kk = reinterpret_cast<float2*>(p.k_io + (size_t)s * p.n_kv * 64);
-            for (int e = threadIdx.x; e < p.n_kv * 32; e += NCT) kk[e] = rot(kk[e], cs2[e & 31]);
+            const float2* ki = reinterpret_cast<const float2*>(p.k_io + (size_t)s * p.n_kv * 64);
+            float2* ko = reinterpret_cast<float2*>(p.k_out + (size_t)s * p.n_kv * 64);
+            for (int e = threadIdx.x; e < p.n_kv * 32; e += NCT) ko[e] = rot(ki[e], cs2[e & 31]);
           }
         }
         cons_sync(NCT);
@@ -737,7 +738,7 @@ __global__ void __launch_bounds__(64 * GROUPS) merge_exchange_kernel(const Fused
       p.q_out[(size_t)s * qdim + h * 64 + d] = (d & 1) ? rq.y : rq.x;
       if (has_k) {
         const float2 rk = rot(xk, cs);
-        p.k_io[(size_t)s * p.n_kv * 64 + h * 64 + d] = (d & 1) ? rk.y : rk.x;
+        p.k_out[(size_t)s * p.n_kv * 64 + h * 64 + d] = (d & 1) ? rk.y : rk.x;
       }
     }
     if (GROUPS > 1) __syncthreads();

@@ -149,7 +149,8 @@ struct PrefillParams {
 struct FusedParams {
   const float* q_in;       // [B][n_head*64] raw (rope) or already rotated
   float* q_out;            // rotated q written by the CTA finishing a sequence (or null)
-  float* k_io;             // [B][n_kv*64] raw new k, rotated in place (new_row)
+  float* k_io;             // [B][n_kv*64] raw new k (new_row)
+  float* k_out;            // [B][n_kv*64] rotated k (k_io, or a separate buffer)
   const float* v_new;      // [B][n_kv*64] new v (new_row)
   const int* pos;          // [B] global position of each sequence's current token
   const float* cs;         // RoPE table [table_len][64] (cos, sin pairs)
