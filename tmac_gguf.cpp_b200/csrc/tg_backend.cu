@@ -160,6 +160,7 @@ struct tg_context {
 
   char* arena = nullptr;     size_t arena_cap = 0, arena_off = 0;
   uint16_t* qbf = nullptr;   size_t qbf_cap = 0;     // prefill: rotated bf16 q
+  uint16_t* vh = nullptr;     size_t vh_cap = 0;   // prefill: fp16 copy of v
   std::vector<PendingCopy> pending;  // device -> host copies of staged outputs
   // Host inputs of the current call, moved to the arena by commit_inputs.
   struct PackEntry {
@@ -1151,6 +1152,7 @@ int tg_shutdown(tg_context* ctx) {
   cudaFree(ctx->arena);
   if (ctx->hpin) cudaFreeHost(ctx->hpin);
   cudaFree(ctx->qbf);
+  cudaFree(ctx->vh);
   cudaFree(ctx->d_err);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -1916,6 +1918,7 @@ int tg_prefill_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, in
   RopeTable* t = nullptr;
   TG_TRY(get_table(ctx, d.rope_base, d.head_dim, S, &t));
   TG_TRY(ensure_buf(ctx, &ctx->qbf, &ctx->qbf_cap, rows * qd));
+  TG_TRY(ensure_buf(ctx, &ctx->vh, &ctx->vh_cap, rows * kd));
 
   tg::PrefillRopeParams rp{};
   rp.q = static_cast<const float*>(dq);
@@ -1933,6 +1936,7 @@ int tg_prefill_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, in
   rp.n_kv = d.n_kv_head;
   rp.head_dim = d.head_dim;
   rp.max_ctx = d.max_ctx;
+  rp.v_f16 = ctx->vh;
   TG_TRY(commit_inputs(ctx));
   cudaError_t e = tg::launch_prefill_rope(rp, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "prefill rope launch: %s", cudaGetErrorString(e));
@@ -1948,6 +1952,16 @@ int tg_prefill_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, in
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TG_ERR_CUDA, "q tensor map rejected (%d)", (int)r);
+  // fp16 v as {n_kv*64, rows}: one box = 128 positions of one KV head.
+  alignas(64) CUtensorMap tvh;
+  cuuint64_t vdim[2] = {(cuuint64_t)kd, (cuuint64_t)rows};
+  cuuint64_t vstride[1] = {(cuuint64_t)kd * 2};
+  cuuint32_t vbox[2] = {64, 128};
+  cuuint32_t vestr[2] = {1, 1};
+  r = enc(&tvh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ctx->vh, vdim, vstride, vbox, vestr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TG_ERR_CUDA, "v tensor map rejected (%d)", (int)r);
   tg::PrefillParams pp{};
   pp.out = static_cast<float*>(dout);
   pp.err = ctx->d_err;
@@ -1960,7 +1974,7 @@ int tg_prefill_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, in
   pp.max_ctx = d.max_ctx;
   pp.n_qt = (S + 127) / 128;
   pp.scale_log2 = kLog2e / sqrtf((float)d.head_dim);
-  const long long items = (long long)n_seqs * d.n_head * pp.n_qt;
+  const long long items = (long long)n_seqs * d.n_head * ((pp.n_qt + 1) / 2);  // tile pairs
   const int grid = (int)(items < ctx->num_sms ? items : ctx->num_sms);
   cudaEvent_t ev_stop = nullptr;
   if (ctx->prof_on) {
@@ -1974,7 +1988,7 @@ int tg_prefill_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, in
     ev_stop = ctx->prof_ev[ctx->prof_used + 1];
     ctx->prof_used += 2;
   }
-  e = tg::launch_prefill_attn(tq, kv->tmk128, kv->tmv128, pp, grid, ctx->stream);
+  e = tg::launch_prefill_attn(tq, kv->tmk128, tvh, pp, grid, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "prefill attention launch: %s", cudaGetErrorString(e));
   ctx->launches++;
   if (ev_stop)

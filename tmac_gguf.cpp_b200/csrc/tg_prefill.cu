@@ -15,27 +15,12 @@
 //                         persistent over (sequence, query head, 128-row
 //                         query tile) items, most expensive first.
 //
-// prefill_attn_kernel roles (320 threads):
-//   warp 0      TMA producer: the item's Q tile (128 x 64 bf16) and a ring of
-//               K/V tiles (128 positions x 64 bf16 each), 128B swizzle.
-//   warp 1      owns TMEM (512 columns) and one thread issues tcgen05.mma:
-//               S = Q.K^T (M128 N128 K64) into one of two TMEM S buffers,
-//               O += P.V (M128 N64 K128) into the TMEM O accumulator.
-//   warps 2-9   softmax / correction / epilogue: query row i (TMEM lane i)
-//               belongs to two threads, one per half of the S columns.  Each
-//               reads its half row with tcgen05.ld, masks causally, trades
-//               its half-row maximum with the partner through shared memory,
-//               computes the online softmax, rescales its half of the O row
-//               in TMEM and writes its half of P to shared memory as bf16 hi
-//               and lo parts; the MMA issues P_hi.V and P_lo.V, so the
-//               probabilities keep ~15 mantissa bits.
-//
-// Every mbarrier wait is bounded.  A failed wait records the error word and
-// raises a CTA abort flag; every role then leaves its loop, so all threads
-// reach the final barrier, issued TMA loads and MMAs are drained (bounded)
-// and the TMEM columns are freed before exit.
+// prefill_attn_kernel works on pairs of adjacent query tiles so that the
+// tensor core computes one tile's products while the other tile's softmax
+// runs (roles below, at the kernel).
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -203,7 +188,14 @@ __global__ void __launch_bounds__(128) prefill_rope_kernel(const PrefillRopePara
     kc[idx] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
     kc[idx + 1] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)));
   }
-  for (int i = threadIdx.x; i < kdim; i += blockDim.x) vc[i] = __float2bfloat16_rn(v[i]);
+  // v: bf16 into the cache, and fp16 of the same bf16 value (exact) as the
+  // operand of the attention's P.V products.
+  __half* vh = reinterpret_cast<__half*>(p.v_f16) + (size_t)row * kdim;
+  for (int i = threadIdx.x; i < kdim; i += blockDim.x) {
+    const __nv_bfloat16 b = __float2bfloat16_rn(v[i]);
+    vc[i] = b;
+    vh[i] = __float2half_rn(__bfloat162float(b));
+  }
 }
 
 // ------------------------------------------------------------ attention
@@ -211,23 +203,29 @@ __global__ void __launch_bounds__(128) prefill_rope_kernel(const PrefillRopePara
 constexpr int PF_M = 128;          // query rows per tile (TMEM lanes)
 constexpr int PF_N = 128;          // cache rows per K/V tile
 constexpr int PF_STAGES = 2;       // K/V ring depth
-constexpr int PF_THREADS = 320;   // TMA warp, MMA warp, 8 softmax warps
-constexpr int PF_TILE_BYTES = PF_M * 128;  // 128 rows x 64 bf16
-constexpr int PF_OFF_Q = 0;
-constexpr int PF_OFF_K = PF_OFF_Q + PF_TILE_BYTES;
-constexpr int PF_OFF_V = PF_OFF_K + PF_STAGES * PF_TILE_BYTES;
-// P: two buffers (steps alternate), each a hi and a lo part of 2 K-blocks.
-constexpr int PF_P_BYTES = 2 * PF_TILE_BYTES;  // one part: 128 rows x 128 bf16
-constexpr int PF_OFF_P = PF_OFF_V + PF_STAGES * PF_TILE_BYTES;
+constexpr int PF_THREADS = 320;    // TMA warp, MMA warp, 2 softmax warpgroups
+constexpr int PF_TILE_BYTES = 128 * 128;   // 128 rows x 64 16-bit values (Q, K, V tiles)
+constexpr int PF_P_BYTES = 2 * PF_TILE_BYTES;  // P: 128 rows x 128 fp16, two K-blocks
+constexpr int PF_OFF_Q = 0;                                       // [2 slots]
+constexpr int PF_OFF_K = PF_OFF_Q + 2 * PF_TILE_BYTES;            // [stages]
+constexpr int PF_OFF_V = PF_OFF_K + PF_STAGES * PF_TILE_BYTES;    // [stages], fp16
+constexpr int PF_OFF_P = PF_OFF_V + PF_STAGES * PF_TILE_BYTES;    // [slot][buffer]
 constexpr int PF_OFF_BAR = PF_OFF_P + 2 * 2 * PF_P_BYTES;
-// barriers: q_full, q_empty, kv_full[S], kv_empty[S], s_full[2], s_free[2], p_full,
-// o_done[2] (per P buffer), xbar[4] (row-statistics exchange within a lane quarter)
-constexpr int PF_NBAR = 2 + 2 * PF_STAGES + 2 + 2 + 1 + 2 + 4;
-constexpr int PF_OFF_XCH = PF_OFF_BAR + PF_NBAR * 8;       // float [2 parity][2 half][128]
-constexpr int PF_OFF_MISC = PF_OFF_XCH + 2 * 2 * 128 * 4;  // tmem base, abort flag
+// barriers: q_full, q_empty, kv_full[S], kv_empty[S], s_full[2], s_free[2],
+// p_full[2][2], pv_done[2][2]
+constexpr int PF_NBAR = 2 + 2 * PF_STAGES + 2 + 2 + 4 + 4;
+constexpr int PF_OFF_MISC = PF_OFF_BAR + PF_NBAR * 8;  // tmem base, abort flag
 constexpr size_t PF_SMEM = 1024 + PF_OFF_MISC + 16;
 constexpr uint32_t PF_TMEM_COLS = 512;
-constexpr uint32_t PF_COL_S0 = 0, PF_COL_S1 = 128, PF_COL_O = 256;
+// TMEM columns: S of slot x at 128x, O of slot x at 256 + 64x.
+__device__ __forceinline__ uint32_t pf_col_s(int x) { return (uint32_t)(128 * x); }
+__device__ __forceinline__ uint32_t pf_col_o(int x) { return (uint32_t)(256 + 64 * x); }
+
+// Instruction descriptor, kind::f16 with fp16 A and B (P.V), fp32 accumulator.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool b_mn_major) {
+  return (1u << 4) | (b_mn_major ? (1u << 16) : 0u) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
 
 __device__ __forceinline__ bool pf_wait(uint64_t* bar, uint32_t parity, int* err,
                                         volatile int* abort_flag) {
@@ -239,29 +237,67 @@ __device__ __forceinline__ bool pf_wait(uint64_t* bar, uint32_t parity, int* err
 
 // Warp-uniform wait: every lane polls (and so acquires the phase itself),
 // then the warp agrees on one verdict, so no lane can fall out of step with a
-// warp-collective tcgen05 instruction or leave its partner waiting.
+// warp-collective tcgen05 instruction.
 __device__ __forceinline__ bool pf_wait_warp(uint64_t* bar, uint32_t parity, int* err,
-                                             volatile int* abort_flag, int lane) {
-  (void)lane;
+                                             volatile int* abort_flag) {
   const bool got = pf_wait(bar, parity, err, abort_flag);
   return __all_sync(0xffffffffu, got) != 0;
 }
 
+// A work item is a pair of adjacent query tiles (2m, 2m+1) of one (sequence,
+// head): slot 0 and slot 1.  Both walk the same causal K/V tiles 0..2m+1 in
+// lockstep (slot 0 skips the last), so they share every K/V load.
 struct PfItem {
-  int b, h, qt;
+  int b, h, m;
+  int qa, qb;        // query tiles of slot 0 / slot 1
+  bool b_active;     // slot 1 exists (the last pair of an odd tile count has one tile)
+  int nkv;           // K/V tiles the pair walks
 };
 
 __device__ __forceinline__ PfItem pf_item(const PrefillParams& p, int idx) {
-  // Most expensive query tiles (most causal K/V tiles) first.
+  // Most expensive pairs (most causal K/V tiles) first.
+  const int n_qp = (p.n_qt + 1) >> 1;
   const int bh = p.B * p.n_head;
   PfItem it;
-  it.qt = p.n_qt - 1 - idx / bh;
+  it.m = n_qp - 1 - idx / bh;
   const int r = idx - (idx / bh) * bh;
   it.b = r / p.n_head;
   it.h = r - it.b * p.n_head;
+  it.qa = 2 * it.m;
+  it.qb = 2 * it.m + 1;
+  it.b_active = it.qb < p.n_qt;
+  it.nkv = it.b_active ? it.qb + 1 : it.qa + 1;
   return it;
 }
 
+// Steps (K/V tiles) of slot x in an item.
+__device__ __forceinline__ int pf_steps(const PfItem& it, int x) {
+  return x == 0 ? it.qa + 1 : (it.b_active ? it.qb + 1 : 0);
+}
+
+// Roles (320 threads):
+//   warp 0      TMA producer: both Q tiles of an item (128 x 64 bf16 each)
+//               and a ring of K (bf16, the cache) and V (fp16 copy) tiles of
+//               128 positions, 128B swizzle, no multicast.
+//   warp 1      owns TMEM (512 columns); one thread issues tcgen05.mma.  Per
+//               slot, S = Q.K^T (M128 N128 K64, bf16) goes into the slot's S
+//               columns as soon as the softmax has read the previous S, and
+//               O += P.V (M128 N64 K128, fp16) follows each P, so the tensor
+//               core works while either slot's softmax runs.
+//   warps 2-5   softmax of slot 0, warps 6-9 softmax of slot 1: thread r of
+//               a warpgroup owns query row r (TMEM lane r) and all 128 S
+//               columns, so a row's maximum and sum never leave the thread.
+//               It reads its S row into registers with tcgen05.ld and
+//               releases the S columns at once, masks causally, keeps a
+//               lazily moved exponent base (O is rescaled in TMEM only when
+//               the row maximum grows by more than 2^8), writes P in fp16
+//               (11 significant bits; v is fp16-exact) into the slot's P
+//               buffer for the step, and at the item's end normalises its O
+//               row.
+// Every mbarrier wait is bounded.  A failed wait records the error word and
+// raises a CTA abort flag; every role then leaves its loop, so all threads
+// reach the final barrier, issued TMA loads and MMAs are drained (bounded)
+// and the TMEM columns are freed before exit.
 __global__ void __launch_bounds__(PF_THREADS, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tmq,
                         const __grid_constant__ CUtensorMap tmk,
@@ -274,17 +310,15 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   uint64_t* q_empty = bars + 1;
   uint64_t* kv_full = bars + 2;
   uint64_t* kv_empty = bars + 2 + PF_STAGES;
-  uint64_t* s_full = bars + 2 + 2 * PF_STAGES;
-  uint64_t* s_free = s_full + 2;
-  uint64_t* p_full = s_free + 2;
-  uint64_t* o_done = p_full + 1;  // [2]: P.V of the steps using P buffer 0 / 1
-  uint64_t* xbar = o_done + 2;
-  float* xch = reinterpret_cast<float*>(smem + PF_OFF_XCH);
+  uint64_t* s_full = bars + 2 + 2 * PF_STAGES;  // [slot]: Q.K^T done
+  uint64_t* s_free = s_full + 2;                // [slot]: S read (4 warps)
+  uint64_t* p_full = s_free + 2;                // [slot * 2 + buffer]: P written (4 warps)
+  uint64_t* pv_done = p_full + 4;               // [slot * 2 + buffer]: P.V done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PF_OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + PF_OFF_MISC + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_items = p.B * p.n_head * p.n_qt;
+  const int n_items = p.B * p.n_head * ((p.n_qt + 1) >> 1);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -295,12 +329,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 8);
+      mbar_init(&s_free[i], 4);
     }
-    mbar_init(p_full, 8);
-    mbar_init(&o_done[0], 1);
-    mbar_init(&o_done[1], 1);
-    for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], 64);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&p_full[i], 4);
+      mbar_init(&pv_done[i], 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -319,7 +353,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   const uint32_t sQ = smem_u32(smem + PF_OFF_Q);
   const uint32_t sK = smem_u32(smem + PF_OFF_K);
   const uint32_t sV = smem_u32(smem + PF_OFF_V);
-  const uint32_t sP = smem_u32(smem + PF_OFF_P);  // buffer b part h at b*2*PF_P_BYTES + h*PF_P_BYTES
+  const uint32_t sP = smem_u32(smem + PF_OFF_P);  // (slot x, buffer b) at (2x + b) * PF_P_BYTES
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -332,12 +366,15 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
       for (int idx = blockIdx.x; idx < n_items; idx += gridDim.x, ++it_n) {
         const PfItem it = pf_item(p, idx);
         if (!pf_wait(q_empty, (uint32_t)((it_n & 1) ^ 1), p.err, abort_flag)) break;
-        mbar_arrive_expect_tx(q_full, PF_TILE_BYTES);
-        tma_load_3d(smem + PF_OFF_Q, &tmq, q_full, 0, it.h, it.b * p.S + it.qt * PF_M);
+        mbar_arrive_expect_tx(q_full, 2 * PF_TILE_BYTES);
+        // Slot 1's tile of a one-tile pair reads rows past this sequence
+        // (another sequence's, or the map's zero fill); nothing uses them.
+        tma_load_3d(smem + PF_OFF_Q, &tmq, q_full, 0, it.h, it.b * p.S + it.qa * PF_M);
+        tma_load_3d(smem + PF_OFF_Q + PF_TILE_BYTES, &tmq, q_full, 0, it.h,
+                    it.b * p.S + it.qb * PF_M);
         const int g = it.h / p.group;
-        const int nkv = it.qt + 1;
         bool ok = true;
-        for (int j = 0; j < nkv; ++j, ++kvi) {
+        for (int j = 0; j < it.nkv; ++j, ++kvi) {
           const int st = (int)(kvi % PF_STAGES);
           const uint32_t ph = (uint32_t)((kvi / PF_STAGES) & 1);
           if (!pf_wait(&kv_empty[st], ph ^ 1u, p.err, abort_flag)) {
@@ -345,9 +382,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             break;
           }
           mbar_arrive_expect_tx(&kv_full[st], 2 * PF_TILE_BYTES);
-          const int y = (int)(p.row0 + (long long)it.b * p.max_ctx + (long long)j * PF_N);
-          tma_load_2d(smem + PF_OFF_K + st * PF_TILE_BYTES, &tmk, &kv_full[st], 64 * g, y);
-          tma_load_2d(smem + PF_OFF_V + st * PF_TILE_BYTES, &tmv, &kv_full[st], 64 * g, y);
+          const int yk = (int)(p.row0 + (long long)it.b * p.max_ctx + (long long)j * PF_N);
+          const int yv = it.b * p.S + j * PF_N;  // rows past the sequence are never weighted
+          tma_load_2d(smem + PF_OFF_K + st * PF_TILE_BYTES, &tmk, &kv_full[st], 64 * g, yk);
+          tma_load_2d(smem + PF_OFF_V + st * PF_TILE_BYTES, &tmv, &kv_full[st], 64 * g, yv);
         }
         if (!ok) break;
       }
@@ -363,71 +401,87 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t IDESC_QK = idesc_bf16(PF_M, PF_N, false);
-      constexpr uint32_t IDESC_PV = idesc_bf16(PF_M, 64, true);
-      long long kvi = 0, sc = 0;  // K/V ring slot counter, S step counter
+      constexpr uint32_t IDESC_PV = idesc_f16(PF_M, 64, true);
+      // Shared-memory descriptors of the region bases, built once: a
+      // descriptor's address field is (byte address >> 4), so an operand at
+      // base + off is the base descriptor + off / 16 (every offset here is a
+      // multiple of 16 and the region stays below 256 KB, inside the field).
+      const uint64_t dq0 = smem_desc_sw128(sQ, 16, 1024);
+      const uint64_t dk0 = smem_desc_sw128(sK, 16, 1024);
+      const uint64_t dv0 = smem_desc_sw128(sV, PF_TILE_BYTES, 1024);
+      const uint64_t dp0 = smem_desc_sw128(sP, 16, 1024);
+      long long kvi = 0;
+      long long nq[2] = {0, 0};  // Q.K^T issued per slot (S uses)
+      long long np[2] = {0, 0};  // P.V issued per slot (P buffer uses)
       int it_n = 0;
-      bool issued_any = false;
-      auto issue_qk = [&](long long step, long long slot) -> bool {
-        const int st = (int)(slot % PF_STAGES);
-        if (!pf_wait(&kv_full[st], (uint32_t)((slot / PF_STAGES) & 1), p.err, abort_flag))
-          return false;
-        const int sb = (int)(step & 1);
-        if (!pf_wait(&s_free[sb], (uint32_t)(((step >> 1) & 1) ^ 1), p.err, abort_flag))
+      bool issued_any = false, ok = true;
+      // S = Q.K^T of slot x from ring slot st; waits until the softmax has
+      // read the slot's previous S.
+      auto issue_qk = [&](int x, int st) -> bool {
+        if (nq[x] > 0 &&
+            !pf_wait(&s_free[x], (uint32_t)((nq[x] - 1) & 1), p.err, abort_flag))
           return false;
         tc_fence_after();
-        const uint32_t d = tmem + (sb ? PF_COL_S1 : PF_COL_S0);
+        const uint64_t a0 = dq0 + (uint64_t)(x * (PF_TILE_BYTES >> 4));
+        const uint64_t b0 = dk0 + (uint64_t)(st * (PF_TILE_BYTES >> 4));
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t a = smem_desc_sw128(sQ + kk * 32, 16, 1024);
-          const uint64_t b = smem_desc_sw128(sK + st * PF_TILE_BYTES + kk * 32, 16, 1024);
-          umma_f16(d, a, b, IDESC_QK, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[sb]);
+        for (int kk = 0; kk < 4; ++kk)  // 32 bytes along K per step: +2
+          umma_f16(tmem + pf_col_s(x), a0 + 2 * kk, b0 + 2 * kk, IDESC_QK, kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[x]);
+        ++nq[x];
         issued_any = true;
         return true;
       };
-      for (int idx = blockIdx.x; idx < n_items; idx += gridDim.x, ++it_n) {
-        const PfItem it = pf_item(p, idx);
-        const int nkv = it.qt + 1;
-        if (!pf_wait(q_full, (uint32_t)(it_n & 1), p.err, abort_flag)) break;
+      // O += P.V of slot x: P buffer np&1 (K-major, two 64-column blocks),
+      // V from ring slot st (MN-major, 16 rows = +128 per step).
+      auto issue_pv = [&](int x, int st, bool first) -> bool {
+        const int b = (int)(np[x] & 1);
+        if (!pf_wait(&p_full[x * 2 + b], (uint32_t)((np[x] >> 1) & 1), p.err, abort_flag))
+          return false;
         tc_fence_after();
-        if (!issue_qk(sc, kvi)) break;
-        bool ok = true;
-        for (int j = 0; j < nkv; ++j) {
-          const long long step = sc + j, slot = kvi + j;
-          if (j + 1 < nkv) {
-            if (!issue_qk(step + 1, slot + 1)) {
+        const uint64_t pa = dp0 + (uint64_t)(((x * 2 + b) * PF_P_BYTES) >> 4);
+        const uint64_t vb = dv0 + (uint64_t)(st * (PF_TILE_BYTES >> 4));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16(tmem + pf_col_o(x), pa + (uint64_t)((kk >> 2) * (PF_TILE_BYTES >> 4) + 2 * (kk & 3)),
+                   vb + 128 * kk, IDESC_PV, (!first || kk > 0) ? 1u : 0u);
+        umma_commit(&pv_done[x * 2 + b]);
+        ++np[x];
+        return true;
+      };
+      for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x, ++it_n) {
+        const PfItem it = pf_item(p, idx);
+        const int n0 = pf_steps(it, 0), n1 = pf_steps(it, 1);
+        if (!pf_wait(q_full, (uint32_t)(it_n & 1), p.err, abort_flag)) break;
+        if (!pf_wait(&kv_full[(int)(kvi % PF_STAGES)], (uint32_t)((kvi / PF_STAGES) & 1), p.err,
+                     abort_flag))
+          break;
+        tc_fence_after();
+        ok = issue_qk(0, (int)(kvi % PF_STAGES));
+        if (ok && n1 > 0) ok = issue_qk(1, (int)(kvi % PF_STAGES));
+        for (int j = 0; j < it.nkv && ok; ++j) {
+          const long long slot = kvi + j;
+          const int st = (int)(slot % PF_STAGES), st1 = (int)((slot + 1) % PF_STAGES);
+          // The next Q.K^T of each slot as soon as its S has been read ...
+          if (j + 1 < it.nkv) {
+            if (!pf_wait(&kv_full[st1], (uint32_t)(((slot + 1) / PF_STAGES) & 1), p.err,
+                         abort_flag)) {
               ok = false;
               break;
             }
-          } else {
-            umma_commit(q_empty);  // the item's last Q.K^T has been issued
+            tc_fence_after();
+            if (j + 1 < n0) ok = issue_qk(0, st1);
+            if (ok && j + 1 < n1) ok = issue_qk(1, st1);
+            if (!ok) break;
           }
-          if (!pf_wait(p_full, (uint32_t)(step & 1), p.err, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const int st = (int)(slot % PF_STAGES);
-          const uint32_t pbuf = sP + (uint32_t)(step & 1) * 2 * PF_P_BYTES;
-#pragma unroll
-          for (int part = 0; part < 2; ++part) {
-            const uint32_t pbase = pbuf + part * PF_P_BYTES;
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint64_t a =
-                  smem_desc_sw128(pbase + (kk >> 2) * PF_TILE_BYTES + (kk & 3) * 32, 16, 1024);
-              const uint64_t b =
-                  smem_desc_sw128(sV + st * PF_TILE_BYTES + kk * 2048, PF_TILE_BYTES, 1024);
-              umma_f16(tmem + PF_COL_O, a, b, IDESC_PV, (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
-            }
-          }
-          umma_commit(&o_done[step & 1]);
-          umma_commit(&kv_empty[st]);
+          // ... and this step's P.V of each slot once its P is written.
+          if (j < n0) ok = issue_pv(0, st, j == 0);
+          if (ok && j < n1) ok = issue_pv(1, st, j == 0);
+          if (!ok) break;
+          umma_commit(&kv_empty[st]);  // both slots' products of tile j issued
+          if (j + 1 == it.nkv) umma_commit(q_empty);
         }
-        if (!ok) break;
-        sc += nkv;
-        kvi += nkv;
+        kvi += it.nkv;
       }
       // Drain: wait (bounded) until every issued MMA has completed.
       if (issued_any) {
@@ -438,152 +492,127 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax
-    // Warps 2..9: warp pairs (w, w+4) share TMEM lane quarter w%4 (query
-    // rows 32*(w%4)..+31); the first of a pair owns S columns 0-63, O
-    // columns 0-31 and P block 0, the second the other halves.
-    const int sw = warp - 2;
-    const int quarter = warp & 3;
-    const int half = sw >> 2;
-    const int row = quarter * 32 + lane;
+    const int x = (warp - 2) >> 2;          // slot of this warpgroup
+    const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;    // query row within the tile
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     const float scale = p.scale_log2;
     // The exponent base of a row (m_use, raw score units) is only moved when
     // the row's max has grown by more than kLazy in log2 units; until then
     // probabilities may reach 2^kLazy, and O and l need no rescaling.
     constexpr float kLazy = 8.f;
-    long long sc = 0;
-    uint32_t xph = 0;  // phase counter of this quarter's exchange barrier
-    // P.V of global step t used P buffer t&1; it is that buffer's use t>>1.
-    auto wait_pv = [&](long long t) -> bool {
-      return pf_wait_warp(&o_done[t & 1], (uint32_t)((t >> 1) & 1), p.err, abort_flag, lane);
-    };
+    long long xs = 0;  // this slot's steps so far (barrier phases)
     for (int idx = blockIdx.x; idx < n_items; idx += gridDim.x) {
       const PfItem it = pf_item(p, idx);
-      const int nkv = it.qt + 1;
-      const int q_pos = it.qt * PF_M + row;
+      const int nx = pf_steps(it, x);
+      if (nx == 0) continue;
+      const int qt = x == 0 ? it.qa : it.qb;
+      const int q_pos = qt * PF_M + row;
       float m_use = -INFINITY;
-      float l_run = 0.f;  // this half-row's share of the softmax sum
+      float l_run = 0.f;
       bool ok = true;
-      for (int j = 0; j < nkv; ++j) {
-        const long long step = sc + j;
-        const int sb = (int)(step & 1);
-        if (!pf_wait_warp(&s_full[sb], (uint32_t)((step >> 1) & 1), p.err, abort_flag, lane)) {
+      for (int j = 0; j < nx; ++j, ++xs) {
+        if (!pf_wait_warp(&s_full[x], (uint32_t)(xs & 1), p.err, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint32_t sv[64];
-        TG_TMEM_LD64(tmem + lane_addr + (sb ? PF_COL_S1 : PF_COL_S0) + half * 64, sv);
+        uint32_t sv[128];
+        TG_TMEM_LD64(tmem + lane_addr + pf_col_s(x), sv);
+        TG_TMEM_LD64(tmem + lane_addr + pf_col_s(x) + 64, (sv + 64));
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[sb]);
-        // Key position j*128 + half*64 + c is visible to query q_pos when it
-        // is not after it and lies inside the sequence; only the diagonal
-        // tile and a partial last tile need the mask.
-        const int k0 = j * PF_N + half * 64;
-        const int lim = min(q_pos - k0, p.S - 1 - k0);
+        if (lane == 0) mbar_arrive(&s_free[x]);  // the next Q.K^T may overwrite S
+        // Key position j*128 + c is visible to query q_pos when it is not
+        // after it and lies inside the sequence; only the diagonal tile and a
+        // partial last tile need the mask.
+        const int lim = min(q_pos - j * PF_N, p.S - 1 - j * PF_N);
         float mx = -INFINITY;
-        if (__reduce_min_sync(0xffffffffu, lim) >= 63) {
+        if (__reduce_min_sync(0xffffffffu, lim) >= 127) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c) mx = fmaxf(mx, __uint_as_float(sv[c]));
+          for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(sv[c]));
         } else {
 #pragma unroll
-          for (int c = 0; c < 64; ++c) {
+          for (int c = 0; c < 128; ++c) {
             const float s = (c <= lim) ? __uint_as_float(sv[c]) : -INFINITY;
             sv[c] = __float_as_uint(s);
             mx = fmaxf(mx, s);
           }
         }
-        // Exchange the half-row maxima with the partner warp (bounded wait).
-        float* xc = xch + (xph & 1) * 256;
-        xc[half * 128 + row] = mx;
-        mbar_arrive(&xbar[quarter]);
-        if (!pf_wait_warp(&xbar[quarter], xph & 1, p.err, abort_flag, lane)) {
-          ok = false;
-          break;
-        }
-        ++xph;
-        const float m_tile = fmaxf(mx, xc[(half ^ 1) * 128 + row]);
         float alpha = 1.f;
         if (j == 0) {
-          m_use = m_tile;
-        } else if ((m_tile - m_use) * scale > kLazy) {
-          alpha = ex2((m_use - m_tile) * scale);
-          m_use = m_tile;
+          m_use = mx;
+        } else if ((mx - m_use) * scale > kLazy) {
+          alpha = ex2((m_use - mx) * scale);
+          m_use = mx;
         }
         // O rescale: needs every earlier P.V finished (the last one issued).
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
-          if (!wait_pv(step - 1)) {
+          if (!pf_wait_warp(&pv_done[x * 2 + (int)((xs - 1) & 1)],
+                            (uint32_t)(((xs - 1) >> 1) & 1), p.err, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          uint32_t ov[32];
-          const uint32_t oaddr = tmem + lane_addr + PF_COL_O + half * 32;
-          TG_TMEM_LD32(oaddr, ov);
+#pragma unroll 1
+          for (int c0 = 0; c0 < 64; c0 += 32) {
+            uint32_t ov[32];
+            const uint32_t oaddr = tmem + lane_addr + pf_col_o(x) + c0;
+            TG_TMEM_LD32(oaddr, ov);
 #pragma unroll
-          for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
-          TG_TMEM_ST32(oaddr, ov);
+            for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
+            TG_TMEM_ST32(oaddr, ov);
+          }
         }
-        // P buffer step&1 is free once the P.V two steps back has finished.
-        if (step >= 2 && !wait_pv(step - 2)) {
+        // This step's P buffer is free once the P.V two steps back is done.
+        const int b = (int)(xs & 1);
+        if (xs >= 2 && !pf_wait_warp(&pv_done[x * 2 + b], (uint32_t)(((xs - 2) >> 1) & 1), p.err,
+                                     abort_flag)) {
           ok = false;
           break;
         }
         const float neg = -m_use * scale;
-        // p = 2^(s*scale - m); P = hi + lo with hi = p truncated to bf16 and
-        // lo = bf16(p - hi): ~2^-14 relative, packed with byte permutes.
+        // p = 2^(s*scale - m) in fp16 (RNE), 8 columns per 16-byte chunk.
         float lsum = 0.f;
-        const uint32_t pbase =
-            sP + (uint32_t)(step & 1) * 2 * PF_P_BYTES + half * PF_TILE_BYTES + row * 128;
+        const uint32_t prow = sP + (uint32_t)((x * 2 + b) * PF_P_BYTES) + row * 128;
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          uint32_t hi[4], lo[4];
+        for (int ch = 0; ch < 16; ++ch) {
+          uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int c = ch * 8 + 2 * e;
             const float p0 = ex2(fmaf(__uint_as_float(sv[c]), scale, neg));
             const float p1 = ex2(fmaf(__uint_as_float(sv[c + 1]), scale, neg));
             lsum += p0 + p1;
-            const uint32_t b0 = __float_as_uint(p0), b1 = __float_as_uint(p1);
-            const float r0 = p0 - __uint_as_float(b0 & 0xFFFF0000u);
-            const float r1 = p1 - __uint_as_float(b1 & 0xFFFF0000u);
-            hi[e] = __byte_perm(b0, b1, 0x7632);
-            lo[e] = __byte_perm(__float_as_uint(r0), __float_as_uint(r1), 0x7632);
+            const __half2 h2 = __floats2half2_rn(p0, p1);
+            w[e] = *reinterpret_cast<const uint32_t*>(&h2);
           }
-          const uint32_t off = pbase + ((ch ^ (row & 7)) << 4);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(off), "r"(hi[0]),
-                       "r"(hi[1]), "r"(hi[2]), "r"(hi[3])
-                       : "memory");
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(off + PF_P_BYTES),
-                       "r"(lo[0]), "r"(lo[1]), "r"(lo[2]), "r"(lo[3])
+          // Columns 8ch..8ch+7: K-block ch/8, 16-byte chunk ch%8 of the row.
+          const uint32_t off = prow + (ch >> 3) * PF_TILE_BYTES + (((ch & 7) ^ (row & 7)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(off), "r"(w[0]),
+                       "r"(w[1]), "r"(w[2]), "r"(w[3])
                        : "memory");
         }
         l_run = l_run * alpha + lsum;
         fence_proxy_async_smem();  // P (generic writes) before the tensor core reads it
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(p_full);
+        if (lane == 0) mbar_arrive(&p_full[x * 2 + b]);
       }
       if (!ok) break;
-      sc += nkv;
-      // Epilogue: the two halves' sums, then O / l for this warp's 32 columns.
-      if (!wait_pv(sc - 1)) break;
+      // Epilogue: the last P.V, then O / l for this row.
+      if (!pf_wait_warp(&pv_done[x * 2 + (int)((xs - 1) & 1)], (uint32_t)(((xs - 1) >> 1) & 1),
+                        p.err, abort_flag))
+        break;
       tc_fence_after();
-      float* xc = xch + (xph & 1) * 256;
-      xc[half * 128 + row] = l_run;
-      mbar_arrive(&xbar[quarter]);
-      if (!pf_wait_warp(&xbar[quarter], xph & 1, p.err, abort_flag, lane)) break;
-      ++xph;
-      const float l_tot = l_run + xc[(half ^ 1) * 128 + row];
-      uint32_t ov[32];
-      TG_TMEM_LD32(tmem + lane_addr + PF_COL_O + half * 32, ov);
+      uint32_t ov[64];
+      TG_TMEM_LD64(tmem + lane_addr + pf_col_o(x), ov);
       tc_fence_before();
       if (q_pos < p.S) {
-        const float inv = 1.f / l_tot;
-        float* dst = p.out + (((size_t)it.b * p.S + q_pos) * p.n_head + it.h) * 64 + half * 32;
+        const float inv = 1.f / l_run;
+        float* dst = p.out + (((size_t)it.b * p.S + q_pos) * p.n_head + it.h) * 64;
 #pragma unroll
-        for (int c = 0; c < 32; c += 4) {
+        for (int c = 0; c < 64; c += 4) {
           float4 w;
           w.x = __uint_as_float(ov[c]) * inv;
           w.y = __uint_as_float(ov[c + 1]) * inv;

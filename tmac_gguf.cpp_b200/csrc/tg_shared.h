@@ -130,6 +130,7 @@ struct PrefillRopeParams {
   uint16_t* q_bf16;      // [B][S][n_head][head_dim] rotated, bf16 bits
   uint16_t* k_cache;     // layer base of the bf16 cache
   uint16_t* v_cache;
+  uint16_t* v_f16;       // [B][S][n_kv*head_dim] v in fp16 bits (the P.V operand)
   int B, S, n_head, n_kv, head_dim, max_ctx;
 };
 
