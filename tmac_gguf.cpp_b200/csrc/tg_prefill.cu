@@ -527,18 +527,24 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         // after it and lies inside the sequence; only the diagonal tile and a
         // partial last tile need the mask.
         const int lim = min(q_pos - j * PF_N, p.S - 1 - j * PF_N);
-        float mx = -INFINITY;
+        // Row maximum over 8 independent running maxima (a single running
+        // maximum would be a chain of 128 dependent operations).
+        float mx8[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mx8[u] = -INFINITY;
         if (__reduce_min_sync(0xffffffffu, lim) >= 127) {
 #pragma unroll
-          for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(sv[c]));
+          for (int c = 0; c < 128; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sv[c]));
         } else {
 #pragma unroll
           for (int c = 0; c < 128; ++c) {
             const float s = (c <= lim) ? __uint_as_float(sv[c]) : -INFINITY;
             sv[c] = __float_as_uint(s);
-            mx = fmaxf(mx, s);
+            mx8[c & 7] = fmaxf(mx8[c & 7], s);
           }
         }
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         float alpha = 1.f;
         if (j == 0) {
           m_use = mx;
@@ -573,7 +579,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         }
         const float neg = -m_use * scale;
         // p = 2^(s*scale - m) in fp16 (RNE), 8 columns per 16-byte chunk.
-        float lsum = 0.f;
+        float ls4[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
         const uint32_t prow = sP + (uint32_t)((x * 2 + b) * PF_P_BYTES) + row * 128;
 #pragma unroll
         for (int ch = 0; ch < 16; ++ch) {
@@ -583,7 +589,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             const int c = ch * 8 + 2 * e;
             const float p0 = ex2(fmaf(__uint_as_float(sv[c]), scale, neg));
             const float p1 = ex2(fmaf(__uint_as_float(sv[c + 1]), scale, neg));
-            lsum += p0 + p1;
+            ls4[e] += p0 + p1;
             const __half2 h2 = __floats2half2_rn(p0, p1);
             w[e] = *reinterpret_cast<const uint32_t*>(&h2);
           }
@@ -593,6 +599,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
                        "r"(w[1]), "r"(w[2]), "r"(w[3])
                        : "memory");
         }
+        const float lsum = (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
         l_run = l_run * alpha + lsum;
         fence_proxy_async_smem();  // P (generic writes) before the tensor core reads it
         tc_fence_before();
