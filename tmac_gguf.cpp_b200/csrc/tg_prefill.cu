@@ -59,6 +59,18 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16: A is read from tensor
+// memory (row m in lane m, two 16-bit elements per 32-bit column along K).
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on `bar` once every tcgen05.mma this thread issued so far is done.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(
@@ -202,24 +214,24 @@ __global__ void __launch_bounds__(128) prefill_rope_kernel(const PrefillRopePara
 
 constexpr int PF_M = 128;          // query rows per tile (TMEM lanes)
 constexpr int PF_N = 128;          // cache rows per K/V tile
-constexpr int PF_STAGES = 2;       // K/V ring depth
+constexpr int PF_STAGES = 4;       // K/V ring depth
 constexpr int PF_THREADS = 320;    // TMA warp, MMA warp, 2 softmax warpgroups
 constexpr int PF_TILE_BYTES = 128 * 128;   // 128 rows x 64 16-bit values (Q, K, V tiles)
-constexpr int PF_P_BYTES = 2 * PF_TILE_BYTES;  // P: 128 rows x 128 fp16, two K-blocks
 constexpr int PF_OFF_Q = 0;                                       // [2 slots]
 constexpr int PF_OFF_K = PF_OFF_Q + 2 * PF_TILE_BYTES;            // [stages]
 constexpr int PF_OFF_V = PF_OFF_K + PF_STAGES * PF_TILE_BYTES;    // [stages], fp16
-constexpr int PF_OFF_P = PF_OFF_V + PF_STAGES * PF_TILE_BYTES;    // [slot][buffer]
-constexpr int PF_OFF_BAR = PF_OFF_P + 2 * 2 * PF_P_BYTES;
-// barriers: q_full, q_empty, kv_full[S], kv_empty[S], s_full[2], s_free[2],
-// p_full[2][2], pv_done[2][2]
-constexpr int PF_NBAR = 2 + 2 * PF_STAGES + 2 + 2 + 4 + 4;
+constexpr int PF_OFF_BAR = PF_OFF_V + PF_STAGES * PF_TILE_BYTES;
+// barriers: q_full, q_empty, kv_full[S], kv_empty[S], and per slot s_full,
+// s_free, p_full, pv_done
+constexpr int PF_NBAR = 2 + 2 * PF_STAGES + 4 * 2;
 constexpr int PF_OFF_MISC = PF_OFF_BAR + PF_NBAR * 8;  // tmem base, abort flag
 constexpr size_t PF_SMEM = 1024 + PF_OFF_MISC + 16;
 constexpr uint32_t PF_TMEM_COLS = 512;
-// TMEM columns: S of slot x at 128x, O of slot x at 256 + 64x.
+// TMEM columns: S of slot x at 128x, O of slot x at 256 + 64x, P of slot x
+// (128 fp16 per row, two per column) at 384 + 64x.
 __device__ __forceinline__ uint32_t pf_col_s(int x) { return (uint32_t)(128 * x); }
 __device__ __forceinline__ uint32_t pf_col_o(int x) { return (uint32_t)(256 + 64 * x); }
+__device__ __forceinline__ uint32_t pf_col_p(int x) { return (uint32_t)(384 + 64 * x); }
 
 // Instruction descriptor, kind::f16 with fp16 A and B (P.V), fp32 accumulator.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool b_mn_major) {
@@ -282,18 +294,18 @@ __device__ __forceinline__ int pf_steps(const PfItem& it, int x) {
 //   warp 1      owns TMEM (512 columns); one thread issues tcgen05.mma.  Per
 //               slot, S = Q.K^T (M128 N128 K64, bf16) goes into the slot's S
 //               columns as soon as the softmax has read the previous S, and
-//               O += P.V (M128 N64 K128, fp16) follows each P, so the tensor
-//               core works while either slot's softmax runs.
+//               O += P.V (M128 N64 K128, fp16, P read from TMEM) follows each
+//               P, so the tensor core works while either slot's softmax runs.
 //   warps 2-5   softmax of slot 0, warps 6-9 softmax of slot 1: thread r of
 //               a warpgroup owns query row r (TMEM lane r) and all 128 S
 //               columns, so a row's maximum and sum never leave the thread.
 //               It reads its S row into registers with tcgen05.ld and
 //               releases the S columns at once, masks causally, keeps a
 //               lazily moved exponent base (O is rescaled in TMEM only when
-//               the row maximum grows by more than 2^8), writes P in fp16
-//               (11 significant bits; v is fp16-exact) into the slot's P
-//               buffer for the step, and at the item's end normalises its O
-//               row.
+//               the row maximum grows by more than 2^8), writes its row of P
+//               in fp16 (11 significant bits; v is fp16-exact) into the
+//               slot's P columns of TMEM, and at the item's end normalises
+//               its O row.
 // Every mbarrier wait is bounded.  A failed wait records the error word and
 // raises a CTA abort flag; every role then leaves its loop, so all threads
 // reach the final barrier, issued TMA loads and MMAs are drained (bounded)
@@ -312,8 +324,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   uint64_t* kv_empty = bars + 2 + PF_STAGES;
   uint64_t* s_full = bars + 2 + 2 * PF_STAGES;  // [slot]: Q.K^T done
   uint64_t* s_free = s_full + 2;                // [slot]: S read (4 warps)
-  uint64_t* p_full = s_free + 2;                // [slot * 2 + buffer]: P written (4 warps)
-  uint64_t* pv_done = p_full + 4;               // [slot * 2 + buffer]: P.V done
+  uint64_t* p_full = s_free + 2;                // [slot]: P written to TMEM (4 warps)
+  uint64_t* pv_done = p_full + 2;               // [slot]: P.V done (P and O free)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PF_OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + PF_OFF_MISC + 4);
 
@@ -330,8 +342,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 4);
-    }
-    for (int i = 0; i < 4; ++i) {
       mbar_init(&p_full[i], 4);
       mbar_init(&pv_done[i], 1);
     }
@@ -353,7 +363,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   const uint32_t sQ = smem_u32(smem + PF_OFF_Q);
   const uint32_t sK = smem_u32(smem + PF_OFF_K);
   const uint32_t sV = smem_u32(smem + PF_OFF_V);
-  const uint32_t sP = smem_u32(smem + PF_OFF_P);  // (slot x, buffer b) at (2x + b) * PF_P_BYTES
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -409,7 +418,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
       const uint64_t dq0 = smem_desc_sw128(sQ, 16, 1024);
       const uint64_t dk0 = smem_desc_sw128(sK, 16, 1024);
       const uint64_t dv0 = smem_desc_sw128(sV, PF_TILE_BYTES, 1024);
-      const uint64_t dp0 = smem_desc_sw128(sP, 16, 1024);
       long long kvi = 0;
       long long nq[2] = {0, 0};  // Q.K^T issued per slot (S uses)
       long long np[2] = {0, 0};  // P.V issued per slot (P buffer uses)
@@ -432,20 +440,17 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         issued_any = true;
         return true;
       };
-      // O += P.V of slot x: P buffer np&1 (K-major, two 64-column blocks),
-      // V from ring slot st (MN-major, 16 rows = +128 per step).
+      // O += P.V of slot x: P from the slot's TMEM columns (16 keys = 8
+      // columns per step), V from ring slot st (MN-major, 16 rows = +128).
       auto issue_pv = [&](int x, int st, bool first) -> bool {
-        const int b = (int)(np[x] & 1);
-        if (!pf_wait(&p_full[x * 2 + b], (uint32_t)((np[x] >> 1) & 1), p.err, abort_flag))
-          return false;
+        if (!pf_wait(&p_full[x], (uint32_t)(np[x] & 1), p.err, abort_flag)) return false;
         tc_fence_after();
-        const uint64_t pa = dp0 + (uint64_t)(((x * 2 + b) * PF_P_BYTES) >> 4);
         const uint64_t vb = dv0 + (uint64_t)(st * (PF_TILE_BYTES >> 4));
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_f16(tmem + pf_col_o(x), pa + (uint64_t)((kk >> 2) * (PF_TILE_BYTES >> 4) + 2 * (kk & 3)),
-                   vb + 128 * kk, IDESC_PV, (!first || kk > 0) ? 1u : 0u);
-        umma_commit(&pv_done[x * 2 + b]);
+          umma_f16_ts(tmem + pf_col_o(x), tmem + pf_col_p(x) + 8 * kk, vb + 128 * kk, IDESC_PV,
+                      (!first || kk > 0) ? 1u : 0u);
+        umma_commit(&pv_done[x]);
         ++np[x];
         return true;
       };
@@ -552,14 +557,16 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
           alpha = ex2((m_use - mx) * scale);
           m_use = mx;
         }
-        // O rescale: needs every earlier P.V finished (the last one issued).
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
-          if (!pf_wait_warp(&pv_done[x * 2 + (int)((xs - 1) & 1)],
-                            (uint32_t)(((xs - 1) >> 1) & 1), p.err, abort_flag)) {
+        // The previous P.V of this slot must be done before its P columns
+        // are rewritten or its O row rescaled.
+        if (j > 0 || xs > 0) {
+          if (!pf_wait_warp(&pv_done[x], (uint32_t)((xs - 1) & 1), p.err, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
+        }
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
           for (int c0 = 0; c0 < 64; c0 += 32) {
             uint32_t ov[32];
@@ -570,47 +577,33 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             TG_TMEM_ST32(oaddr, ov);
           }
         }
-        // This step's P buffer is free once the P.V two steps back is done.
-        const int b = (int)(xs & 1);
-        if (xs >= 2 && !pf_wait_warp(&pv_done[x * 2 + b], (uint32_t)(((xs - 2) >> 1) & 1), p.err,
-                                     abort_flag)) {
-          ok = false;
-          break;
-        }
         const float neg = -m_use * scale;
-        // p = 2^(s*scale - m) in fp16 (RNE), 8 columns per 16-byte chunk.
+        // p = 2^(s*scale - m) in fp16 (RNE), two per TMEM column, written in
+        // two stores of 32 columns.
         float ls4[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
-        const uint32_t prow = sP + (uint32_t)((x * 2 + b) * PF_P_BYTES) + row * 128;
 #pragma unroll
-        for (int ch = 0; ch < 16; ++ch) {
-          uint32_t w[4];
+        for (int half = 0; half < 2; ++half) {
+          uint32_t w[32];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int c = ch * 8 + 2 * e;
+          for (int e = 0; e < 32; ++e) {
+            const int c = half * 64 + 2 * e;
             const float p0 = ex2(fmaf(__uint_as_float(sv[c]), scale, neg));
             const float p1 = ex2(fmaf(__uint_as_float(sv[c + 1]), scale, neg));
-            ls4[e] += p0 + p1;
+            ls4[e & 3] += p0 + p1;
             const __half2 h2 = __floats2half2_rn(p0, p1);
             w[e] = *reinterpret_cast<const uint32_t*>(&h2);
           }
-          // Columns 8ch..8ch+7: K-block ch/8, 16-byte chunk ch%8 of the row.
-          const uint32_t off = prow + (ch >> 3) * PF_TILE_BYTES + (((ch & 7) ^ (row & 7)) << 4);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(off), "r"(w[0]),
-                       "r"(w[1]), "r"(w[2]), "r"(w[3])
-                       : "memory");
+          TG_TMEM_ST32(tmem + lane_addr + pf_col_p(x) + 32 * half, w);
         }
         const float lsum = (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
         l_run = l_run * alpha + lsum;
-        fence_proxy_async_smem();  // P (generic writes) before the tensor core reads it
-        tc_fence_before();
+        tc_fence_before();  // the P stores (waited) before the MMA that reads them
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[x * 2 + b]);
+        if (lane == 0) mbar_arrive(&p_full[x]);
       }
       if (!ok) break;
       // Epilogue: the last P.V, then O / l for this row.
-      if (!pf_wait_warp(&pv_done[x * 2 + (int)((xs - 1) & 1)], (uint32_t)(((xs - 1) >> 1) & 1),
-                        p.err, abort_flag))
-        break;
+      if (!pf_wait_warp(&pv_done[x], (uint32_t)((xs - 1) & 1), p.err, abort_flag)) break;
       tc_fence_after();
       uint32_t ov[64];
       TG_TMEM_LD64(tmem + lane_addr + pf_col_o(x), ov);
