@@ -215,7 +215,14 @@ __global__ void __launch_bounds__(128) prefill_rope_kernel(const PrefillRopePara
 constexpr int PF_M = 128;          // query rows per tile (TMEM lanes)
 constexpr int PF_N = 128;          // cache rows per K/V tile
 constexpr int PF_STAGES = 4;       // K/V ring depth
-constexpr int PF_THREADS = 320;    // TMA warp, MMA warp, 2 softmax warpgroups
+constexpr int PF_THREADS = 384;    // producer warpgroup (TMA, MMA, 2 idle warps), 2 softmax warpgroups
+// Register split (setmaxnreg): the launch gives 384 x 168 = 64512; the
+// producer warpgroup drops to 80 and the softmax warpgroups rise to 208:
+// 128 x 80 + 256 x 208 = 63488.  Per sub-partition (three warps, one of each
+// warpgroup) 80 + 208 + 208 registers per thread, 15872 of its 16384.  With
+// these no role spills.
+constexpr int PF_REG_PRODUCER = 80;
+constexpr int PF_REG_SOFTMAX = 208;
 constexpr int PF_TILE_BYTES = 128 * 128;   // 128 rows x 64 16-bit values (Q, K, V tiles)
 constexpr int PF_OFF_Q = 0;                                       // [2 slots]
 constexpr int PF_OFF_K = PF_OFF_Q + 2 * PF_TILE_BYTES;            // [stages]
@@ -287,7 +294,7 @@ __device__ __forceinline__ int pf_steps(const PfItem& it, int x) {
   return x == 0 ? it.qa + 1 : (it.b_active ? it.qb + 1 : 0);
 }
 
-// Roles (320 threads):
+// Roles (384 threads, three warpgroups):
 //   warp 0      TMA producer: both Q tiles of an item (128 x 64 bf16 each)
 //               and a ring of K (bf16, the cache) and V (fp16 copy) tiles of
 //               128 positions, 128B swizzle, no multicast.
@@ -296,7 +303,8 @@ __device__ __forceinline__ int pf_steps(const PfItem& it, int x) {
 //               columns as soon as the softmax has read the previous S, and
 //               O += P.V (M128 N64 K128, fp16, P read from TMEM) follows each
 //               P, so the tensor core works while either slot's softmax runs.
-//   warps 2-5   softmax of slot 0, warps 6-9 softmax of slot 1: thread r of
+//   warps 2-3   idle (complete the producer warpgroup for the register split)
+//   warps 4-7   softmax of slot 0, warps 8-11 softmax of slot 1: thread r of
 //               a warpgroup owns query row r (TMEM lane r) and all 128 S
 //               columns, so a row's maximum and sum never leave the thread.
 //               It reads its S row into registers with tcgen05.ld and
@@ -364,6 +372,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   const uint32_t sK = smem_u32(smem + PF_OFF_K);
   const uint32_t sV = smem_u32(smem + PF_OFF_V);
 
+  if (warp < 4) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(PF_REG_PRODUCER));
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -495,9 +505,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
       }
     }
     __syncwarp();
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(PF_REG_SOFTMAX));
     // ------------------------------------------------------------ softmax
-    const int x = (warp - 2) >> 2;          // slot of this warpgroup
+    const int x = (warp - 4) >> 2;          // slot of this warpgroup
     const int quarter = warp & 3;           // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;    // query row within the tile
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
