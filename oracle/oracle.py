@@ -4,8 +4,10 @@ Two libraries are wrapped here:
 
 * ``liboracle.so``: the plain-C restatement (``tg_oracle.c``) of the
   reference's CPU hot path -- RoPE (tmac_gguf.cpp:990-1016), the KV
-  cache-write (:1090-1091) and the GQA decode attention (:1093-1128) -- plus
-  the seeded input generator shared by every test and benchmark.
+  cache-write (:1090-1091), the GQA decode attention (:1093-1128) and the
+  quantized Q/K/V projection with its bias adds (:220-248, :311-328,
+  :402-415, :476-513, :1046-1081) -- plus the seeded input generators
+  shared by every test and benchmark.
 * ``_ref/libref.so``: the reference's own lines of that path, compiled from
   the reference tree by ``oracle/Makefile``.  The restatement is pinned
   bit-for-bit against it (tests/test_oracle.py) and against the golden
@@ -33,6 +35,11 @@ ROPE_BASE = 1000000.0
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+
+# Weight types (tmac_gguf.cpp:177-182) and bytes per 32-element block.
+TYPE_F32, TYPE_Q5_0, TYPE_Q8_0 = 0, 6, 8
+BLOCK_BYTES = {TYPE_Q5_0: 22, TYPE_Q8_0: 34}
 
 _lib = None
 _ref = None
@@ -79,6 +86,18 @@ def lib():
                                        C.POINTER(C.c_float), _f32p, _f32p]
         L.tgo_merge_partials.argtypes = [C.c_int, _f32p, _f32p, _f32p, C.c_int,
                                          _f32p]
+        L.tgo_f16_to_f32.restype = C.c_float
+        L.tgo_f16_to_f32.argtypes = [C.c_uint16]
+        L.tgo_dequant.restype = C.c_float
+        L.tgo_dequant.argtypes = [C.c_int, _u8p, C.c_uint64]
+        L.tgo_matmul_q.argtypes = [C.c_int, _u8p, _f32p, _f32p, C.c_int, C.c_int]
+        L.tgo_qkv_step.argtypes = [C.c_int, _u8p, C.c_int, _u8p, C.c_int, _u8p,
+                                   C.c_void_p, C.c_void_p, C.c_void_p, _f32p,
+                                   _f32p, _f32p, _f32p, C.c_int, C.c_int,
+                                   C.c_int, C.c_int, C.c_int, C.c_float,
+                                   C.c_void_p, C.c_void_p]
+        L.tgo_fill_qblocks.argtypes = [C.c_int, C.c_uint64, _u8p, C.c_size_t,
+                                       C.c_float]
         _lib = L
     return _lib
 
@@ -106,6 +125,14 @@ def ref():
         R.tgref_attention_units_mt.argtypes = [
             C.c_int, C.c_void_p, C.c_long, C.POINTER(C.c_void_p),
             C.POINTER(C.c_void_p), _i32p, C.c_void_p, C.c_int]
+        R.tgref_f16_to_f32.restype = C.c_float
+        R.tgref_f16_to_f32.argtypes = [C.c_uint16]
+        R.tgref_matmul.argtypes = [C.c_int, _u8p, _f32p, _f32p, C.c_int, C.c_int]
+        R.tgref_qkv_layer.restype = C.c_int
+        R.tgref_qkv_layer.argtypes = [C.c_int, _u8p, C.c_int, _u8p, C.c_int, _u8p,
+                                      C.c_void_p, C.c_void_p, C.c_void_p, _f32p,
+                                      _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
+                                      C.c_int]
         _ref = R
     return _ref
 
@@ -138,6 +165,16 @@ def pack_bf16(x: np.ndarray) -> np.ndarray:
     out = np.empty(x.shape, dtype=np.uint16)
     lib().tgo_pack_bf16(x.reshape(-1), out.reshape(-1), x.size)
     return out
+
+
+def qblocks(wtype: int, seed: int, rows: int, cols: int,
+            d_scale: float = 0.004) -> np.ndarray:
+    """Synthetic weight rows of a block type: uint8 [rows, row_bytes]."""
+    nb = rows * (cols // 32)
+    out = np.empty(nb * BLOCK_BYTES[wtype], dtype=np.uint8)
+    lib().tgo_fill_qblocks(wtype, C.c_uint64(seed & 0xFFFFFFFFFFFFFFFF), out, nb,
+                           d_scale)
+    return out.reshape(rows, -1)
 
 
 def derive_seed(seed: int, layer: int, seq: int, tag: int = 0) -> int:
@@ -202,6 +239,51 @@ def prefill_causal(q, k, v, n_head=N_HEAD, n_kv_head=N_KV_HEAD,
     return out
 
 
+def _ptr(a):
+    return None if a is None else np.ascontiguousarray(a, np.float32).ctypes.data
+
+
+def matmul_q(wtype: int, w: np.ndarray, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """matmul's CPU loop (tmac_gguf.cpp:508-512): y = W x, j-ordered sums."""
+    y = np.empty(rows, dtype=np.float32)
+    lib().tgo_matmul_q(wtype, np.ascontiguousarray(w, np.uint8).reshape(-1),
+                       np.ascontiguousarray(x, np.float32).reshape(-1), y, rows, cols)
+    return y
+
+
+def dequant_rows(wtype: int, w: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """The dequantised weight matrix [rows, cols] (tmac_gguf.cpp:240-248,
+    :311-328), element by element."""
+    flat = np.ascontiguousarray(w, np.uint8).reshape(-1)
+    L = lib()
+    return np.array([L.tgo_dequant(wtype, flat, i) for i in range(rows * cols)],
+                    dtype=np.float32).reshape(rows, cols)
+
+
+def qkv_step(wq, wk, wv, bq, bk, bv, x, pos, q_type=TYPE_Q5_0, k_type=TYPE_Q5_0,
+             v_type=TYPE_Q5_0, n_head=N_HEAD, n_kv_head=N_KV_HEAD, head_dim=HEAD_DIM,
+             base=ROPE_BASE, k_cache=None, v_cache=None):
+    """tmac_gguf.cpp:1046-1091 for one sequence: projections, bias adds,
+    RoPE at pos and (when caches are given, updated in place) the
+    cache-write.  Returns (q, k, v)."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    cols = x.size
+    qd, kd = n_head * head_dim, n_kv_head * head_dim
+    q = np.empty(qd, np.float32)
+    k = np.empty(kd, np.float32)
+    v = np.empty(kd, np.float32)
+    keep = [np.ascontiguousarray(b, np.float32) if b is not None else None
+            for b in (bq, bk, bv)]
+    lib().tgo_qkv_step(q_type, np.ascontiguousarray(wq, np.uint8).reshape(-1), k_type,
+                       np.ascontiguousarray(wk, np.uint8).reshape(-1), v_type,
+                       np.ascontiguousarray(wv, np.uint8).reshape(-1),
+                       *[_ptr(b) for b in keep], x, q, k, v, n_head, n_kv_head,
+                       head_dim, cols, pos, base,
+                       None if k_cache is None else k_cache.ctypes.data,
+                       None if v_cache is None else v_cache.ctypes.data)
+    return q, k, v
+
+
 def attention_units_mt(q: np.ndarray, k_list, v_list, pos, n_threads: int,
                        n_head=N_HEAD, n_kv_head=N_KV_HEAD, head_dim=HEAD_DIM):
     """Multi-threaded oracle over independent (sequence, layer) units."""
@@ -264,3 +346,32 @@ def ref_attention_units_mt(q: np.ndarray, k_list, v_list, pos, n_threads: int):
     if rc != 0:
         raise RuntimeError("tgref_attention_units_mt failed")
     return out
+
+
+def ref_matmul(wtype: int, w: np.ndarray, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """The reference's matmul (tmac_gguf.cpp:476-514, CPU loop)."""
+    y = np.empty(rows, dtype=np.float32)
+    ref().tgref_matmul(wtype, np.ascontiguousarray(w, np.uint8).reshape(-1),
+                       np.ascontiguousarray(x, np.float32).reshape(-1), y, rows, cols)
+    return y
+
+
+def ref_qkv_layer(wq, wk, wv, bq, bk, bv, x, k_cache, v_cache, pos,
+                  q_type=TYPE_Q5_0, k_type=TYPE_Q5_0, v_type=TYPE_Q5_0):
+    """The reference's tmac_gguf.cpp:1045-1128 for one sequence (Qwen2-0.5B
+    shape): returns (q, k, v, context); the caches are updated in place."""
+    q = np.empty(N_HEAD * HEAD_DIM, np.float32)
+    k = np.empty(N_KV_HEAD * HEAD_DIM, np.float32)
+    v = np.empty(N_KV_HEAD * HEAD_DIM, np.float32)
+    out = np.empty(N_HEAD * HEAD_DIM, np.float32)
+    keep = [np.ascontiguousarray(b, np.float32) if b is not None else None
+            for b in (bq, bk, bv)]
+    rc = ref().tgref_qkv_layer(q_type, np.ascontiguousarray(wq, np.uint8).reshape(-1),
+                               k_type, np.ascontiguousarray(wk, np.uint8).reshape(-1),
+                               v_type, np.ascontiguousarray(wv, np.uint8).reshape(-1),
+                               *[_ptr(b) for b in keep],
+                               np.ascontiguousarray(x, np.float32).reshape(-1), q, k, v,
+                               out, k_cache.reshape(-1), v_cache.reshape(-1), pos)
+    if rc != 0:
+        raise RuntimeError("tgref_qkv_layer failed")
+    return q, k, v, out

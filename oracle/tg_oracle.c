@@ -4,6 +4,9 @@
  *   RoPE            tmac_gguf.cpp:990-1016   (apply_rope)
  *   cache-write     tmac_gguf.cpp:1090-1091
  *   GQA attention   tmac_gguf.cpp:1093-1128
+ *   Q/K/V projection f16_to_f32 :220-232, dequant_q8_0 :240-248,
+ *                   dequant_q5_0 :311-328, read_tensor :402-415, matmul's
+ *                   CPU loop :508-512, bias adds :1067-1081
  * Build: oracle/Makefile (gcc -O2 -ffp-contract=off, no -march=native).
  */
 #include "tg_oracle.h"
@@ -313,4 +316,139 @@ void tgo_merge_partials(int n_parts, const float *m, const float *l,
     for (int d = 0; d < head_dim; d++) out[d] += o[(size_t)i * head_dim + d] * w;
   }
   for (int d = 0; d < head_dim; d++) out[d] /= lsum;
+}
+
+/* ------------------------------------------------------------------ */
+/* quantized Q/K/V projection                                          */
+/* ------------------------------------------------------------------ */
+
+size_t tgo_qrow_bytes(int type, int cols) {
+  if (type == TGO_TYPE_F32) return (size_t)cols * 4;
+  if (type == TGO_TYPE_Q5_0) return (size_t)(cols / 32) * 22;
+  if (type == TGO_TYPE_Q8_0) return (size_t)(cols / 32) * 34;
+  return 0;
+}
+
+/* f16_to_f32 (tmac_gguf.cpp:220-232) widens exactly: a zero of either sign
+ * becomes +0 (:225), subnormals mant*2^-24 (:226), Inf keeps its sign and
+ * every NaN becomes the NAN macro (:228), normals rebias the exponent
+ * (:230).  Restated with the bit pattern built directly. */
+float tgo_f16_to_f32(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h >> 15) << 31;
+  const uint32_t e = (h >> 10) & 0x1fu, m = h & 0x3ffu;
+  uint32_t u;
+  if (e == 0) {
+    if (m == 0) return 0.0f;
+    const float f = (float)m * 0x1p-24f; /* exact: m < 2^10 */
+    return sign ? -f : f;
+  }
+  if (e == 0x1fu) {
+    if (m) return NAN;
+    u = sign | 0x7f800000u;
+  } else {
+    u = sign | ((e + 112u) << 23) | (m << 13);
+  }
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+float tgo_dequant(int type, const uint8_t *w, uint64_t idx) {
+  if (type == TGO_TYPE_F32) {
+    float f;
+    memcpy(&f, w + idx * 4, 4);
+    return f;
+  }
+  const uint64_t blk = idx / 32, j = idx % 32;
+  if (type == TGO_TYPE_Q8_0) {
+    /* :243-247: d at bytes 0-1 (little endian), int8 values from byte 2. */
+    const uint8_t *b = w + blk * 34;
+    const float d = tgo_f16_to_f32((uint16_t)(b[0] | (b[1] << 8)));
+    return (float)(int8_t)b[2 + j] * d;
+  }
+  if (type == TGO_TYPE_Q5_0) {
+    /* :314-327: d, then the 32 high bits, then 16 bytes holding elements
+     * j (low nibble) and j+16 (high nibble). */
+    const uint8_t *b = w + blk * 22;
+    const float d = tgo_f16_to_f32((uint16_t)(b[0] | (b[1] << 8)));
+    const uint32_t qh = (uint32_t)b[2] | ((uint32_t)b[3] << 8) | ((uint32_t)b[4] << 16) |
+                        ((uint32_t)b[5] << 24);
+    const uint8_t byte = b[6 + (j < 16 ? j : j - 16)];
+    const uint32_t lo = j < 16 ? (byte & 0xfu) : (byte >> 4);
+    const int q = (int)((((qh >> j) & 1u) << 4) | lo) - 16;
+    return d * (float)q;
+  }
+  return 0.0f;
+}
+
+void tgo_matmul_q(int type, const uint8_t *w, const float *x, float *y, int rows, int cols) {
+  for (int i = 0; i < rows; i++) {
+    float sum = 0.0f;
+    for (int j = 0; j < cols; j++)
+      sum += tgo_dequant(type, w, (uint64_t)j + (uint64_t)i * (uint64_t)cols) * x[j];
+    y[i] = sum;
+  }
+}
+
+void tgo_qkv_step(int q_type, const uint8_t *wq, int k_type, const uint8_t *wk, int v_type,
+                  const uint8_t *wv, const float *bq, const float *bk, const float *bv,
+                  const float *x, float *q, float *k, float *v, int n_head, int n_kv_head,
+                  int head_dim, int cols, int pos, float base, float *k_cache,
+                  float *v_cache) {
+  const int qd = n_head * head_dim, kd = n_kv_head * head_dim;
+  /* :1046-1064 the three projections of the same input */
+  tgo_matmul_q(q_type, wq, x, q, qd, cols);
+  tgo_matmul_q(k_type, wk, x, k, kd, cols);
+  tgo_matmul_q(v_type, wv, x, v, kd, cols);
+  /* :1067-1081 bias adds, each present bias added element by element */
+  if (bq)
+    for (int i = 0; i < qd; i++) q[i] += bq[i];
+  if (bk)
+    for (int i = 0; i < kd; i++) k[i] += bk[i];
+  if (bv)
+    for (int i = 0; i < kd; i++) v[i] += bv[i];
+  /* :1085-1088 RoPE; :1090-1091 cache-write */
+  tgo_apply_rope(q, k, n_head, n_kv_head, head_dim, pos, base);
+  if (k_cache && v_cache) tgo_cache_write(k_cache, v_cache, k, v, n_kv_head, head_dim, pos);
+}
+
+/* Round a positive or negative binary32 in the half normal range to an
+ * IEEE half (nearest even); out-of-range magnitudes clamp to the smallest
+ * or largest normal half.  Used only to make synthetic scales. */
+static uint16_t f32_to_f16_clamped(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  const uint32_t sign = (u >> 16) & 0x8000u;
+  int32_t e = (int32_t)((u >> 23) & 0xffu) - 127 + 15;
+  const uint32_t m = u & 0x7fffffu;
+  if (e <= 0) return (uint16_t)(sign | 0x0400u);
+  if (e >= 31) return (uint16_t)(sign | 0x7bffu);
+  uint32_t r = m >> 13;
+  const uint32_t rem = m & 0x1fffu;
+  if (rem > 0x1000u || (rem == 0x1000u && (r & 1u))) {
+    if (++r == 0x400u) {
+      r = 0;
+      if (++e >= 31) return (uint16_t)(sign | 0x7bffu);
+    }
+  }
+  return (uint16_t)(sign | ((uint32_t)e << 10) | r);
+}
+
+void tgo_fill_qblocks(int type, uint64_t seed, uint8_t *out, size_t n_blocks, float d_scale) {
+  uint64_t s = seed;
+  const size_t bs = type == TGO_TYPE_Q5_0 ? 22 : 34;
+  for (size_t b = 0; b < n_blocks; b++) {
+    uint8_t *blk = out + b * bs;
+    const uint64_t a = tgo_splitmix64(&s);
+    const double u = (double)(a >> 11) * (1.0 / 9007199254740992.0);
+    float d = (float)((double)d_scale * (0.5 + u));
+    if (a & 1u) d = -d;
+    const uint16_t h = f32_to_f16_clamped(d);
+    blk[0] = (uint8_t)(h & 0xffu);
+    blk[1] = (uint8_t)(h >> 8);
+    for (size_t i = 2; i < bs; i += 8) {
+      uint64_t r = tgo_splitmix64(&s);
+      for (size_t k = 0; k < 8 && i + k < bs; k++, r >>= 8) blk[i + k] = (uint8_t)(r & 0xffu);
+    }
+  }
 }

@@ -111,6 +111,54 @@ void tgo_prefill_causal(const float *q, const float *k, const float *v,
                         float *out, int S, int n_head, int n_kv_head,
                         int head_dim, int t_begin, int t_end);
 
+/* ---- quantized Q/K/V projection (tmac_gguf.cpp:220-248, 311-328,
+ *      402-415, 476-513 and the layer step :1046-1091) ---- */
+
+/* Weight types (tmac_gguf.cpp:177-182) and their 32-element blocks:
+ * Q8_0 = fp16 d + 32 int8 (34 bytes), value d*q;
+ * Q5_0 = fp16 d + 32 high bits + 16 bytes of nibbles (22 bytes), value
+ * d*(((hi<<4)|lo) - 16), element j < 16 in the low nibble of byte j,
+ * element j >= 16 in the high nibble of byte j-16. */
+#define TGO_TYPE_F32 0
+#define TGO_TYPE_Q5_0 6
+#define TGO_TYPE_Q8_0 8
+
+/* Bytes of one row of `cols` elements (cols a multiple of 32); 0 for an
+ * unknown type. */
+size_t tgo_qrow_bytes(int type, int cols);
+
+/* f16_to_f32 (tmac_gguf.cpp:220-232): exact widening of an IEEE half. */
+float tgo_f16_to_f32(uint16_t h);
+
+/* dequant_q8_0 / dequant_q5_0 (tmac_gguf.cpp:240-248, :311-328): element
+ * idx of a row-major block array. */
+float tgo_dequant(int type, const uint8_t *w, uint64_t idx);
+
+/* matmul's CPU loop (tmac_gguf.cpp:508-512 with read_tensor :402-415):
+ * y[i] = sum over j of dequant(w, j + i*cols) * x[j], summed in j order in
+ * binary32. */
+void tgo_matmul_q(int type, const uint8_t *w, const float *x, float *y,
+                  int rows, int cols);
+
+/* The layer step from the normed hidden state to the cache
+ * (forward_layer_with_cache, tmac_gguf.cpp:1046-1091): q/k/v = W x
+ * (q rows n_head*head_dim, k/v rows n_kv_head*head_dim, `cols` inputs),
+ * + bias (skipped where the bias pointer is NULL), RoPE of q and k at pos,
+ * then the k and v rows written at row pos of k_cache / v_cache (skipped
+ * when the caches are NULL).  q, k, v receive the final vectors. */
+void tgo_qkv_step(int q_type, const uint8_t *wq, int k_type,
+                  const uint8_t *wk, int v_type, const uint8_t *wv,
+                  const float *bq, const float *bk, const float *bv,
+                  const float *x, float *q, float *k, float *v, int n_head,
+                  int n_kv_head, int head_dim, int cols, int pos, float base,
+                  float *k_cache, float *v_cache);
+
+/* Synthetic weight blocks from `seed`: scales d = fp16(d_scale * (0.5 +
+ * u)), u uniform in [0, 1); the quant bytes uniform.  n_blocks blocks of
+ * `type` are written to out. */
+void tgo_fill_qblocks(int type, uint64_t seed, uint8_t *out, size_t n_blocks,
+                      float d_scale);
+
 /* ---- multi-threaded CPU baseline (not in the reference) ---- */
 
 /* Attention for n_units independent (sequence, layer) units, fanned out

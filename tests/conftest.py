@@ -64,3 +64,9 @@ def backend(tg):
 def golden():
     import numpy as np
     return np.load(os.path.join(ROOT, "tests", "golden", "golden_ref.npz"))
+
+
+@pytest.fixture(scope="session")
+def golden_qkv():
+    import numpy as np
+    return np.load(os.path.join(ROOT, "tests", "golden", "golden_qkv.npz"))

@@ -80,3 +80,34 @@ def prefill_inputs(seed: int, S: int, seq: int = 0):
         q[t] = O.rope_heads(q[t], O.N_HEAD, O.HEAD_DIM, t)
         k[t] = O.rope_heads(k[t], O.N_KV_HEAD, O.HEAD_DIM, t)
     return O.round_bf16(q), O.round_bf16(k), O.round_bf16(v)
+
+
+# tensor tags of the Q/K/V projection inputs
+T_WQ, T_WK, T_WV, T_BQ, T_BK, T_BV, T_X = 21, 22, 23, 24, 25, 26, 27
+# d scale per weight type: keeps |q|, |k|, |v| of order 1 for N(0,1) inputs.
+D_SCALE = {O.TYPE_Q5_0: 0.004, O.TYPE_Q8_0: 0.0005}
+
+
+def qkv_weights(seed: int, v_type: int = O.TYPE_Q5_0, bias: bool = True,
+                layer: int = 0, cols: int = QD):
+    """One layer's projection weights as the model file holds them: W_q
+    (QD rows) and W_k (KD rows) in Q5_0, W_v (KD rows) in v_type, each row
+    of `cols` inputs in 32-element blocks; fp32 biases ~ 0.1 N(0,1), or None
+    (a model without biases).  Returns (wq, wk, wv, bq, bk, bv)."""
+    wq = O.qblocks(O.TYPE_Q5_0, O.derive_seed(seed, layer, 0, T_WQ), QD, cols,
+                   D_SCALE[O.TYPE_Q5_0])
+    wk = O.qblocks(O.TYPE_Q5_0, O.derive_seed(seed, layer, 0, T_WK), KD, cols,
+                   D_SCALE[O.TYPE_Q5_0])
+    wv = O.qblocks(v_type, O.derive_seed(seed, layer, 0, T_WV), KD, cols,
+                   D_SCALE[v_type])
+    if not bias:
+        return wq, wk, wv, None, None, None
+    bq = (O.normal(O.derive_seed(seed, layer, 0, T_BQ), QD) * np.float32(0.1)).astype(np.float32)
+    bk = (O.normal(O.derive_seed(seed, layer, 0, T_BK), KD) * np.float32(0.1)).astype(np.float32)
+    bv = (O.normal(O.derive_seed(seed, layer, 0, T_BV), KD) * np.float32(0.1)).astype(np.float32)
+    return wq, wk, wv, bq, bk, bv
+
+
+def qkv_x(seed: int, n_seqs: int = 1, cols: int = QD, layer: int = 0):
+    """Normed hidden states x [n_seqs][cols] ~ N(0,1)."""
+    return O.normal(O.derive_seed(seed, layer, 0, T_X), n_seqs * cols).reshape(n_seqs, cols)

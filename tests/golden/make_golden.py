@@ -2,7 +2,11 @@
 
 The outputs come from oracle/_ref/libref.so, i.e. tmac_gguf.cpp:990-1016
 (apply_rope) and :1090-1128 (cache-write + GQA attention) compiled from the
-reference tree by oracle/Makefile.  Inputs are regenerated from the seeds
+reference tree by oracle/Makefile.  golden_qkv.npz holds the reference's
+layer step from the normed hidden state (:1045-1128: quantized Q/K/V
+projections, bias adds, RoPE, cache-write, attention) with weights decoded
+by its own f16_to_f32 / dequant_q5_0 / dequant_q8_0 / read_tensor / matmul
+(:220-415, :476-514).  Inputs are regenerated from the seeds
 recorded in the file (tests/golden/cases.py), so the fixture stays small.
 
 Run from the repository root where the reference tree is mounted:
@@ -21,6 +25,7 @@ import cases  # noqa: E402
 from cases import O  # noqa: E402
 
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden_ref.npz")
+OUT_QKV = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden_qkv.npz")
 
 ROPE_POS = [0, 1, 2, 17, 255, 4095, 131071]
 DECODE_POS = [0, 1, 7, 15, 16, 17, 63, 64, 100, 255]
@@ -97,9 +102,48 @@ def main() -> None:
     data["prefill_in_sha"] = np.array(_sha(q, k, v))
     data["prefill_out"] = pout
 
-    np.savez_compressed(OUT, **data)
-    print(f"wrote {OUT} ({os.path.getsize(OUT)} bytes)")
+    _save(OUT, data)
+
+
+QKV_CASES = [  # (v weight type, biases present, position)
+    (6, True, 0), (6, True, 5), (6, True, 63), (8, True, 17), (8, False, 40),
+    (6, False, 1),
+]
+
+
+def main_qkv() -> None:
+    data = {"seed": np.int64(SEED), "cases": np.array(QKV_CASES, dtype=np.int32)}
+    outs = {k: [] for k in ("q", "k", "v", "ctx", "sha")}
+    for i, (vt, bias, pos) in enumerate(QKV_CASES):
+        wq, wk, wv, bq, bk, bv = cases.qkv_weights(SEED + i, vt, bias)
+        x = cases.qkv_x(SEED + i)[0]
+        kc = np.zeros((pos + 1, cases.KD), np.float32)
+        vc = np.zeros((pos + 1, cases.KD), np.float32)
+        if pos > 0:
+            kc[:pos] = O.normal(O.derive_seed(SEED + i, 0, 0, cases.T_KC), pos * cases.KD).reshape(pos, -1)
+            vc[:pos] = O.normal(O.derive_seed(SEED + i, 0, 0, cases.T_VC), pos * cases.KD).reshape(pos, -1)
+        outs["sha"].append(_sha(wq, wk, wv, *(b for b in (bq, bk, bv) if b is not None), x, kc, vc))
+        q, k, v, ctx = O.ref_qkv_layer(wq, wk, wv, bq, bk, bv, x, kc, vc, pos, v_type=vt)
+        for key, val in (("q", q), ("k", k), ("v", v), ("ctx", ctx)):
+            outs[key].append(val)
+    for key in ("q", "k", "v", "ctx"):
+        data[f"qkv_{key}"] = np.stack(outs[key])
+    data["qkv_in_sha"] = np.array(outs["sha"])
+    _save(OUT_QKV, data)
+
+
+def _save(path, data) -> None:
+    """Write the fixture unless an identical one is already there."""
+    if os.path.exists(path):
+        old = np.load(path)
+        if set(old.files) == set(data) and all(
+                np.array_equal(old[k], np.asarray(data[k])) for k in data):
+            print(f"{path} unchanged")
+            return
+    np.savez_compressed(path, **data)
+    print(f"wrote {path} ({os.path.getsize(path)} bytes)")
 
 
 if __name__ == "__main__":
     main()
+    main_qkv()
