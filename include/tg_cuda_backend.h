@@ -149,6 +149,50 @@ TG_API int tg_attention_op(tg_context* ctx, const float* Q, const float* K_cache
                     const float* V_cache, float* output, int n_head,
                     int n_kv_head, int head_dim, int past_len);
 
+/* ------------------------------------------------- Q/K/V projection */
+
+/* Weight block types (tmac_gguf.cpp:177-182), GGML's 32-element blocks:
+ * Q5_0 = fp16 d, 32 high bits, 16 bytes of nibbles (22 bytes); element j
+ * < 16 in the low nibble of byte j, j >= 16 in the high nibble of byte
+ * j-16; value d*(((hi<<4)|lo) - 16) (dequant_q5_0, :311-328).  Q8_0 =
+ * fp16 d, 32 int8 (34 bytes); value d*q (dequant_q8_0, :240-248).  Rows
+ * are row-major runs of cols/32 blocks (read_tensor, :402-415). */
+#define TG_WTYPE_Q5_0 6
+#define TG_WTYPE_Q8_0 8
+
+/* fused_qkv_op (metal_backend.hpp:456-489; kernel_fused_qkv.metal:8-70):
+ * y_q = W_q x, y_k = W_k x, y_v = W_v x for one input vector of `cols`
+ * values (a multiple of 32); W_q / W_k are Q5_0, W_v is Q5_0 or Q8_0
+ * (v_is_q8).  Host or device pointers, weights at least 2-byte aligned;
+ * host weight arrays are best registered (tg_register_host,
+ * TG_REGION_DEVICE_OWNED) so that they are uploaded once.  The kernel
+ * reads the weights before it waits for the kernel launched just before
+ * it on the stream, which therefore must not write them. */
+TG_API int tg_fused_qkv_op(tg_context* ctx, const uint8_t* W_q, const uint8_t* W_k,
+                           const uint8_t* W_v, const float* x, float* y_q, float* y_k,
+                           float* y_v, int q_rows, int k_rows, int v_rows, int cols,
+                           int v_is_q8);
+
+/* matmul_q5_0 / matmul_q8_0 (metal_backend.hpp:320-338; the CPU path
+ * matmul, tmac_gguf.cpp:476-513): y = W x for a rows x cols weight of
+ * wtype (TG_WTYPE_*).  Pointer rules as tg_fused_qkv_op. */
+TG_API int tg_matmul_q(tg_context* ctx, int wtype, int rows, int cols, const uint8_t* w,
+                       const float* x, float* y);
+
+/* One layer's projection weights: W_q has n_head*head_dim rows, W_k and
+ * W_v n_kv_head*head_dim rows of `cols` inputs.  Device pointers or
+ * registered host arrays; a NULL bias is a bias the model does not have. */
+typedef struct tg_qkv_weights {
+  int q_type, k_type, v_type; /* TG_WTYPE_* */
+  int cols;
+  const void* w_q;
+  const void* w_k;
+  const void* w_v;
+  const float* b_q;
+  const float* b_k;
+  const float* b_v;
+} tg_qkv_weights;
+
 /* ------------------------------------------------- device KV caches */
 
 /* A device-resident cache replacing the static g_k_cache / g_v_cache
@@ -206,6 +250,24 @@ TG_API int tg_attention_batched(tg_context* ctx, tg_kv_cache* kv, int layer,
 TG_API int tg_decode_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs,
                     float* q, float* k_new, const float* v_new,
                     const int32_t* pos, float* out);
+
+/* The layer step from the normed hidden state to the cache
+ * (forward_layer_with_cache, tmac_gguf.cpp:1046-1091; the fused_qkv_op +
+ * elem_op(0) x3 + rope_op x2 + elem_op(2) x2 of :1479-1493) in one launch:
+ * q/k/v = W x + bias, RoPE of q and k at pos[s], the k and v rows written
+ * into the cache at pos[s] (when this cache or shard holds it), rotated q
+ * to q_out [n_seqs][n_head*head_dim].  x [n_seqs][w->cols]. */
+TG_API int tg_qkv_rope_cache_write(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs,
+                                   const tg_qkv_weights* w, const float* x,
+                                   const int32_t* pos, float* q_out);
+
+/* tg_qkv_rope_cache_write followed by decode attention over rows
+ * 0..pos[s]: the layer from x to the attention context out
+ * [n_seqs][n_head*head_dim] (tmac_gguf.cpp:1046-1128), two kernels chained
+ * by programmatic dependent launch plus the split-sequence merge. */
+TG_API int tg_decode_layer_x(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs,
+                             const tg_qkv_weights* w, const float* x, const int32_t* pos,
+                             float* out);
 
 /* ------------------------------------------------- prefill */
 

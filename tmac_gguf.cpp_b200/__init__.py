@@ -40,6 +40,7 @@ TG_ERR_STATE = 8
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
+WTYPE_Q5_0, WTYPE_Q8_0 = 6, 8  # GGML block types (TG_WTYPE_*)
 
 # split-KV record exchange (tg_comm_set_exchange)
 EXCHANGE_AUTO, EXCHANGE_PEER, EXCHANGE_NCCL = 0, 1, 2
@@ -70,6 +71,13 @@ class tg_kv_desc(C.Structure):
                 ("n_kv_head", C.c_int), ("head_dim", C.c_int),
                 ("dtype", C.c_int), ("shard_start", C.c_int),
                 ("global_ctx", C.c_int), ("rope_base", C.c_float)]
+
+
+class tg_qkv_weights(C.Structure):
+    _fields_ = [("q_type", C.c_int), ("k_type", C.c_int), ("v_type", C.c_int),
+                ("cols", C.c_int), ("w_q", C.c_void_p), ("w_k", C.c_void_p),
+                ("w_v", C.c_void_p), ("b_q", C.c_void_p), ("b_k", C.c_void_p),
+                ("b_v", C.c_void_p)]
 
 
 _vp = C.c_void_p
@@ -134,6 +142,13 @@ _SIGS = {
     "tg_comm_set_exchange": (C.c_int, [_vp, C.c_int]),
     "tg_comm_exchange": (C.c_int, [_vp, C.POINTER(C.c_int)]),
     "tg_kv_uses_tensor_cores": (C.c_int, [_vp, C.POINTER(C.c_int)]),
+    "tg_fused_qkv_op": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, C.c_int,
+                                  C.c_int, C.c_int, C.c_int, C.c_int]),
+    "tg_matmul_q": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp]),
+    "tg_qkv_rope_cache_write": (C.c_int, [_vp, _vp, C.c_int, C.c_int,
+                                          C.POINTER(tg_qkv_weights), _vp, _vp, _vp]),
+    "tg_decode_layer_x": (C.c_int, [_vp, _vp, C.c_int, C.c_int,
+                                    C.POINTER(tg_qkv_weights), _vp, _vp, _vp]),
 }
 
 _lib: Optional[C.CDLL] = None
@@ -325,6 +340,19 @@ class CudaBackend:
                                      _ptr(V_cache), _ptr(output), n_head,
                                      n_kv_head, head_dim, past_len))
 
+    def fused_qkv_op(self, W_q, W_k, W_v, x, y_q, y_k, y_v, q_rows: int,
+                     k_rows: int, v_rows: int, cols: int, v_is_q8: bool) -> None:
+        """metal_backend::fused_qkv_op (metal_backend.hpp:456): y_m = W_m x,
+        W_q / W_k Q5_0, W_v Q5_0 or Q8_0."""
+        _check(lib().tg_fused_qkv_op(self._h, _ptr(W_q), _ptr(W_k), _ptr(W_v),
+                                     _ptr(x), _ptr(y_q), _ptr(y_k), _ptr(y_v),
+                                     q_rows, k_rows, v_rows, cols,
+                                     1 if v_is_q8 else 0))
+
+    def matmul_q(self, wtype: int, rows: int, cols: int, w, x, y) -> None:
+        """metal_backend::matmul_q5_0 / matmul_q8_0 (metal_backend.hpp:320-338)."""
+        _check(lib().tg_matmul_q(self._h, wtype, rows, cols, _ptr(w), _ptr(x), _ptr(y)))
+
     # -- split-KV communicator ----------------------------------------------
     def comm_init(self, uid: bytes, rank: int, world: int,
                   timeout_ms: int = 60000) -> None:
@@ -470,6 +498,23 @@ class KVCache:
                                      _ptr(q), _ptr(k_new), _ptr(v_new),
                                      _ptr(pos), _ptr(out)))
 
+    def qkv_rope_cache_write(self, layer: int, weights: "QKVWeights", x, pos,
+                             q_out) -> None:
+        """Projection + bias + RoPE + cache-write from x (tg_qkv_rope_cache_write)."""
+        n = len(pos)
+        pos = _as_i32(pos)
+        _check(lib().tg_qkv_rope_cache_write(self.backend.handle, self._h, layer, n,
+                                             C.byref(weights.desc), _ptr(x), _ptr(pos),
+                                             _ptr(q_out)))
+
+    def decode_layer_x(self, layer: int, weights: "QKVWeights", x, pos, out) -> None:
+        """The layer from the normed hidden state x to the attention output
+        (tg_decode_layer_x)."""
+        n = len(pos)
+        pos = _as_i32(pos)
+        _check(lib().tg_decode_layer_x(self.backend.handle, self._h, layer, n,
+                                       C.byref(weights.desc), _ptr(x), _ptr(pos), _ptr(out)))
+
     def attention_splitkv(self, layer: int, q, past_len, out) -> None:
         n = len(past_len)
         past_len = _as_i32(past_len)
@@ -506,3 +551,16 @@ def _as_i32(x):
     if hasattr(x, "data_ptr"):
         return x
     return np.ascontiguousarray(np.asarray(x), dtype=np.int32)
+
+
+class QKVWeights:
+    """One layer's projection weights for tg_qkv_rope_cache_write /
+    tg_decode_layer_x: block arrays (numpy uint8 or device tensors / device
+    addresses) and optional fp32 biases.  The arrays are kept referenced."""
+
+    def __init__(self, w_q, w_k, w_v, cols: int, q_type: int = WTYPE_Q5_0,
+                 k_type: int = WTYPE_Q5_0, v_type: int = WTYPE_Q5_0,
+                 b_q=None, b_k=None, b_v=None):
+        self._keep = (w_q, w_k, w_v, b_q, b_k, b_v)
+        self.desc = tg_qkv_weights(q_type, k_type, v_type, cols, _ptr(w_q), _ptr(w_k),
+                                   _ptr(w_v), _ptr(b_q), _ptr(b_k), _ptr(b_v))

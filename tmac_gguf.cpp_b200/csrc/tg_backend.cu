@@ -161,6 +161,7 @@ struct tg_context {
   char* arena = nullptr;     size_t arena_cap = 0, arena_off = 0;
   uint16_t* qbf = nullptr;   size_t qbf_cap = 0;     // prefill: rotated bf16 q
   uint16_t* vh = nullptr;     size_t vh_cap = 0;   // prefill: fp16 copy of v
+  float* qx = nullptr;        size_t qx_cap = 0;   // decode from x: rotated q
   std::vector<PendingCopy> pending;  // device -> host copies of staged outputs
   // Host inputs of the current call, moved to the arena by commit_inputs.
   struct PackEntry {
@@ -1050,6 +1051,118 @@ int run_fused(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const fl
   return TG_OK;
 }
 
+// ------------------------------------------------ Q/K/V projection
+
+size_t qrow_bytes(int wtype, int cols) {
+  return (size_t)(cols / 32) * (size_t)tg::wtype_block_bytes(wtype);
+}
+
+int check_qkv_cols(int cols) {
+  if (cols <= 0 || cols % 32)
+    return fail(TG_ERR_INVALID_ARG, "cols %d must be a positive multiple of 32", cols);
+  if (cols > tg::qkv_max_cols())
+    return fail(TG_ERR_INVALID_ARG, "cols %d exceeds the projection kernel's %d", cols,
+                tg::qkv_max_cols());
+  return TG_OK;
+}
+
+int check_wtype(int t, const char* what) {
+  if (t != TG_WTYPE_Q5_0 && t != TG_WTYPE_Q8_0)
+    return fail(TG_ERR_UNSUPPORTED, "%s: weight type %d (only Q5_0 = 6 and Q8_0 = 8)", what, t);
+  return TG_OK;
+}
+
+// Blocks hold 16-bit fields: weight arrays must be 2-byte aligned.
+int check_align2(const void* p, const char* what) {
+  if (p && (reinterpret_cast<uintptr_t>(p) & 1))
+    return fail(TG_ERR_INVALID_ARG, "%s must be 2-byte aligned", what);
+  return TG_OK;
+}
+
+// Device address of a weight or bias array: device pointers pass through,
+// registered host arrays use their mirror, other host arrays are staged
+// for this call.
+int weight_ptr(tg_context* ctx, const void* p, size_t bytes, const void** dev) {
+  if (!p) {
+    *dev = nullptr;
+    return TG_OK;
+  }
+  if (is_device_ptr(p)) {
+    *dev = p;
+    return TG_OK;
+  }
+  if (find_region(ctx, static_cast<const char*>(p), bytes)) {
+    char* d = nullptr;
+    TG_TRY(resolve(ctx, p, bytes, false, &d));
+    *dev = d;
+    return TG_OK;
+  }
+  return stage_in(ctx, p, bytes, dev);
+}
+
+int run_qkv(tg_context* ctx, tg::QkvParams& p) {
+  TG_TRY(commit_inputs(ctx));
+  for (int m = 0; m < 3; ++m) p.tiles[m] = (p.rows[m] + tg::kQkvRows - 1) / tg::kQkvRows;
+  p.err = ctx->d_err;
+  cudaError_t e = tg::launch_qkv(p, ctx->stream);
+  if (e != cudaSuccess) return fail(TG_ERR_CUDA, "qkv launch: %s", cudaGetErrorString(e));
+  ctx->launches++;
+  return TG_OK;
+}
+
+// Mode-1 projection of one layer on device x / pos: bias, RoPE, cache-write,
+// rotated q into dq_out.
+int qkv_layer_core(tg_context* ctx, const tg_kv_cache* kv, int layer, int n,
+                   const tg_qkv_weights* w, const float* dx, const int* dpos, float* dq_out) {
+  const tg_kv_desc& d = kv->d;
+  const int qrows = d.n_head * d.head_dim, krows = d.n_kv_head * d.head_dim;
+  TG_TRY(check_qkv_cols(w->cols));
+  TG_TRY(check_wtype(w->q_type, "w_q"));
+  TG_TRY(check_wtype(w->k_type, "w_k"));
+  TG_TRY(check_wtype(w->v_type, "w_v"));
+  if (!w->w_q || !w->w_k || !w->w_v) return fail(TG_ERR_INVALID_ARG, "null weight pointer");
+  const void *wq = nullptr, *wk = nullptr, *wv = nullptr;
+  const void *bq = nullptr, *bk = nullptr, *bv = nullptr;
+  TG_TRY(weight_ptr(ctx, w->w_q, (size_t)qrows * qrow_bytes(w->q_type, w->cols), &wq));
+  TG_TRY(weight_ptr(ctx, w->w_k, (size_t)krows * qrow_bytes(w->k_type, w->cols), &wk));
+  TG_TRY(weight_ptr(ctx, w->w_v, (size_t)krows * qrow_bytes(w->v_type, w->cols), &wv));
+  TG_TRY(weight_ptr(ctx, w->b_q, (size_t)qrows * 4, &bq));
+  TG_TRY(weight_ptr(ctx, w->b_k, (size_t)krows * 4, &bk));
+  TG_TRY(weight_ptr(ctx, w->b_v, (size_t)krows * 4, &bv));
+  TG_TRY(check_align2(wq, "w_q"));
+  TG_TRY(check_align2(wk, "w_k"));
+  TG_TRY(check_align2(wv, "w_v"));
+  TG_TRY(check_align8(dq_out, "q_out"));
+  RopeTable* t = nullptr;
+  TG_TRY(get_table(ctx, d.rope_base, d.head_dim, kv->global_ctx, &t));
+  tg::QkvParams p{};
+  const void* ws[3] = {wq, wk, wv};
+  const void* bs[3] = {bq, bk, bv};
+  const int types[3] = {w->q_type, w->k_type, w->v_type};
+  const int rows[3] = {qrows, krows, krows};
+  for (int m = 0; m < 3; ++m) {
+    p.w[m] = static_cast<const uint8_t*>(ws[m]);
+    p.bias[m] = static_cast<const float*>(bs[m]);
+    p.wtype[m] = types[m];
+    p.rows[m] = rows[m];
+  }
+  p.cols = w->cols;
+  p.x = dx;
+  p.B = n;
+  p.mode = 1;
+  p.q_out = dq_out;
+  p.pos = dpos;
+  p.cs = t->d;
+  p.table_len = kv->global_ctx;
+  p.head_dim = d.head_dim;
+  p.k_cache = static_cast<char*>(kv->k) + (size_t)layer * kv->layer_elems * kv->esize;
+  p.v_cache = static_cast<char*>(kv->v) + (size_t)layer * kv->layer_elems * kv->esize;
+  p.dtype = d.dtype;
+  p.max_ctx = d.max_ctx;
+  p.shard_start = d.shard_start;
+  return run_qkv(ctx, p);
+}
+
 int check_kv_call(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs) {
   if (!ctx || !kv) return fail(TG_ERR_INVALID_ARG, "null context or cache");
   if (kv->ctx != ctx) return fail(TG_ERR_INVALID_ARG, "cache belongs to another context");
@@ -1153,6 +1266,7 @@ int tg_shutdown(tg_context* ctx) {
   if (ctx->hpin) cudaFreeHost(ctx->hpin);
   cudaFree(ctx->qbf);
   cudaFree(ctx->vh);
+  cudaFree(ctx->qx);
   cudaFree(ctx->d_err);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -1623,6 +1737,129 @@ int tg_decode_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, flo
                   static_cast<const float*>(dv), static_cast<const int*>(dp)));
   TG_TRY(run_decode(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
                     static_cast<const int*>(dp), 0, static_cast<float*>(dout), 0));
+  return finish_call(ctx);
+}
+
+// ------------------------------------------------ Q/K/V projection
+
+int tg_fused_qkv_op(tg_context* ctx, const uint8_t* W_q, const uint8_t* W_k, const uint8_t* W_v,
+                    const float* x, float* y_q, float* y_k, float* y_v, int q_rows, int k_rows,
+                    int v_rows, int cols, int v_is_q8) {
+  TG_TRY(set_device(ctx));
+  if (q_rows < 0 || k_rows < 0 || v_rows < 0)
+    return fail(TG_ERR_INVALID_ARG, "fused_qkv_op: negative row count");
+  TG_TRY(check_qkv_cols(cols));
+  const uint8_t* W[3] = {W_q, W_k, W_v};
+  float* Y[3] = {y_q, y_k, y_v};
+  const int R[3] = {q_rows, k_rows, v_rows};
+  const int T[3] = {TG_WTYPE_Q5_0, TG_WTYPE_Q5_0, v_is_q8 ? TG_WTYPE_Q8_0 : TG_WTYPE_Q5_0};
+  if (!x) return fail(TG_ERR_INVALID_ARG, "fused_qkv_op: null x");
+  for (int m = 0; m < 3; ++m)
+    if (R[m] > 0 && (!W[m] || !Y[m]))
+      return fail(TG_ERR_INVALID_ARG, "fused_qkv_op: null weight or output");
+  if (R[0] + R[1] + R[2] == 0) return TG_OK;
+  // Every mirror first, then the addresses (see ensure_region).
+  TG_TRY(ensure_region(ctx, x, (size_t)cols * 4));
+  for (int m = 0; m < 3; ++m) {
+    if (!R[m]) continue;
+    TG_TRY(ensure_region(ctx, W[m], (size_t)R[m] * qrow_bytes(T[m], cols)));
+    TG_TRY(ensure_region(ctx, Y[m], (size_t)R[m] * 4));
+  }
+  tg::QkvParams p{};
+  char* dx = nullptr;
+  TG_TRY(resolve(ctx, x, (size_t)cols * 4, false, &dx));
+  for (int m = 0; m < 3; ++m) {
+    p.wtype[m] = T[m];
+    if (!R[m]) continue;
+    char *dw = nullptr, *dy = nullptr;
+    TG_TRY(resolve(ctx, W[m], (size_t)R[m] * qrow_bytes(T[m], cols), false, &dw));
+    TG_TRY(resolve(ctx, Y[m], (size_t)R[m] * 4, true, &dy));
+    TG_TRY(check_align2(dw, "weights"));
+    p.w[m] = reinterpret_cast<const uint8_t*>(dw);
+    p.y[m] = reinterpret_cast<float*>(dy);
+    p.rows[m] = R[m];
+  }
+  p.cols = cols;
+  p.x = reinterpret_cast<const float*>(dx);
+  p.B = 1;
+  p.mode = 0;
+  TG_TRY(run_qkv(ctx, p));
+  return finish_compat(ctx);
+}
+
+int tg_matmul_q(tg_context* ctx, int wtype, int rows, int cols, const uint8_t* w, const float* x,
+                float* y) {
+  TG_TRY(set_device(ctx));
+  TG_TRY(check_wtype(wtype, "matmul_q"));
+  TG_TRY(check_qkv_cols(cols));
+  if (rows < 0) return fail(TG_ERR_INVALID_ARG, "matmul_q: negative rows");
+  if (!w || !x || !y) return fail(TG_ERR_INVALID_ARG, "matmul_q: null argument");
+  if (rows == 0) return TG_OK;
+  const size_t wb = (size_t)rows * qrow_bytes(wtype, cols);
+  TG_TRY(ensure_region(ctx, w, wb));
+  TG_TRY(ensure_region(ctx, x, (size_t)cols * 4));
+  TG_TRY(ensure_region(ctx, y, (size_t)rows * 4));
+  char *dw = nullptr, *dx = nullptr, *dy = nullptr;
+  TG_TRY(resolve(ctx, w, wb, false, &dw));
+  TG_TRY(resolve(ctx, x, (size_t)cols * 4, false, &dx));
+  TG_TRY(resolve(ctx, y, (size_t)rows * 4, true, &dy));
+  TG_TRY(check_align2(dw, "weights"));
+  tg::QkvParams p{};
+  p.w[0] = reinterpret_cast<const uint8_t*>(dw);
+  p.wtype[0] = p.wtype[1] = p.wtype[2] = wtype;
+  p.rows[0] = rows;
+  p.y[0] = reinterpret_cast<float*>(dy);
+  p.cols = cols;
+  p.x = reinterpret_cast<const float*>(dx);
+  p.B = 1;
+  p.mode = 0;
+  TG_TRY(run_qkv(ctx, p));
+  return finish_compat(ctx);
+}
+
+int tg_qkv_rope_cache_write(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs,
+                            const tg_qkv_weights* w, const float* x, const int32_t* pos,
+                            float* q_out) {
+  TG_TRY(check_kv_call(ctx, kv, layer, n_seqs));
+  if (!w || !x || !pos || !q_out) return fail(TG_ERR_INVALID_ARG, "null argument");
+  if (n_seqs == 0) return TG_OK;
+  TG_TRY(check_qkv_cols(w->cols));
+  TG_TRY(check_host_pos(pos, n_seqs, kv->global_ctx, "pos"));
+  const tg_kv_desc& d = kv->d;
+  const void *dx = nullptr, *dp = nullptr;
+  void* dq = nullptr;
+  TG_TRY(stage_in(ctx, x, (size_t)n_seqs * w->cols * 4, &dx));
+  TG_TRY(stage_in(ctx, pos, (size_t)n_seqs * 4, &dp));
+  TG_TRY(stage_out(ctx, q_out, (size_t)n_seqs * d.n_head * d.head_dim * 4, false, &dq));
+  TG_TRY(qkv_layer_core(ctx, kv, layer, n_seqs, w, static_cast<const float*>(dx),
+                        static_cast<const int*>(dp), static_cast<float*>(dq)));
+  return finish_call(ctx);
+}
+
+int tg_decode_layer_x(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs,
+                      const tg_qkv_weights* w, const float* x, const int32_t* pos, float* out) {
+  TG_TRY(check_kv_call(ctx, kv, layer, n_seqs));
+  if (!w || !x || !pos || !out) return fail(TG_ERR_INVALID_ARG, "null argument");
+  if (n_seqs == 0) return TG_OK;
+  TG_TRY(check_qkv_cols(w->cols));
+  TG_TRY(check_host_pos(pos, n_seqs, kv->d.shard_start + kv->d.max_ctx, "pos"));
+  const tg_kv_desc& d = kv->d;
+  const size_t qb = (size_t)n_seqs * d.n_head * d.head_dim * 4;
+  const void *dx = nullptr, *dp = nullptr;
+  void* dout = nullptr;
+  TG_TRY(stage_in(ctx, x, (size_t)n_seqs * w->cols * 4, &dx));
+  TG_TRY(stage_in(ctx, pos, (size_t)n_seqs * 4, &dp));
+  TG_TRY(stage_out(ctx, out, qb, false, &dout));
+  TG_TRY(ensure_buf(ctx, &ctx->qx, &ctx->qx_cap, qb / 4));
+  TG_TRY(qkv_layer_core(ctx, kv, layer, n_seqs, w, static_cast<const float*>(dx),
+                        static_cast<const int*>(dp), ctx->qx));
+  if (mma_eligible(kv))
+    TG_TRY(run_fused(ctx, kv, layer, n_seqs, ctx->qx, nullptr, nullptr, nullptr,
+                     static_cast<const int*>(dp), static_cast<float*>(dout), nullptr, 0, false,
+                     false));
+  else
+    TG_TRY(run_decode(ctx, kv, layer, n_seqs, ctx->qx, static_cast<const int*>(dp), 0,
+                      static_cast<float*>(dout), 0));
   return finish_call(ctx);
 }
 

@@ -56,4 +56,10 @@ cudaError_t launch_prefill_attn(const CUtensorMap& tq, const CUtensorMap& tk,
                                 cudaStream_t st);
 size_t prefill_attn_smem();
 
+// Q/K/V projection (tg_qkv.cu): kQkvRows weight rows per CTA, cols a multiple
+// of 32 up to qkv_max_cols().
+cudaError_t launch_qkv(const QkvParams& p, cudaStream_t st);
+size_t qkv_smem(int cols);
+int qkv_max_cols();
+
 }  // namespace tg

@@ -179,4 +179,43 @@ struct FusedParams {
   unsigned* epoch;         // exchange launches on this GPU (advanced by the decode kernel)
 };
 
+
+// Q/K/V projection of one layer (tg_qkv.cu): y_m = W_m x (+ bias) for the
+// three weight matrices m = 0 (q), 1 (k), 2 (v) and B input vectors, with
+// weights in the model file's 32-element blocks (GGML Q5_0 / Q8_0).  Mode 0
+// writes y_m; mode 1 is the layer step of tmac_gguf.cpp:1067-1091: bias,
+// RoPE of q and k at pos[s], the k / v rows into the cache, rotated q out.
+constexpr int kWTypeQ5_0 = 6;   // 22-byte blocks: fp16 d, 32 high bits, 16 nibble bytes
+constexpr int kWTypeQ8_0 = 8;   // 34-byte blocks: fp16 d, 32 int8
+constexpr int kQkvRows = 8;     // weight rows per CTA (one warp each)
+constexpr int kQkvChunk = 256;  // sequences per epilogue pass
+
+TG_HD int wtype_block_bytes(int t) {
+  return t == kWTypeQ5_0 ? 22 : (t == kWTypeQ8_0 ? 34 : 0);
+}
+
+struct QkvParams {
+  const uint8_t* w[3];     // row-major rows of cols/32 blocks
+  const float* bias[3];    // or null (a model without that bias)
+  float* y[3];             // mode 0: [B][rows[m]]
+  int wtype[3];
+  int rows[3];             // 0 rows: matrix absent
+  int tiles[3];            // CTAs of each matrix: ceil(rows / kQkvRows)
+  int cols;                // inputs, a multiple of 32
+  const float* x;          // [B][cols]
+  int B;
+  int mode;
+  // mode 1
+  float* q_out;            // [B][rows[0]] rotated q
+  float* k_out;            // optional [B][rows[1]]: the rotated k row
+  float* v_out;            // optional [B][rows[2]]: the v row
+  const int* pos;          // [B] global position of each sequence's token
+  const float* cs;         // RoPE table [table_len][head_dim] (cos, sin pairs)
+  int table_len, head_dim;
+  void* k_cache;           // layer base of the caches, [n_seqs][max_ctx][rows[1]]
+  void* v_cache;
+  int dtype, max_ctx, shard_start;
+  int* err;
+};
+
 }  // namespace tg
