@@ -21,7 +21,8 @@ exchange and the merge.
               tmac_gguf.cpp:990-1016 / :1090-1128) on a bounded sample
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W]
-                       [--impl tg|reference] [--workload longctx|batched|cfg2|cfg1]
+                       [--impl tg|reference]
+                       [--workload longctx|batched|cfg2|cfg1|prefill|qkv|qkv_batched]
 For N > 1 launch with torch.distributed.run (one rank per GPU).
 """
 from __future__ import annotations
@@ -61,6 +62,15 @@ WORKLOADS = {
     # BASELINE config 1
     "cfg1": dict(B=1, ctx=256, layers=24, dtype="f32", split=False,
                  desc="config1: single sequence, pos=255, fp32 KV, 24 layers"),
+    # config 1 and config 3 entered from the normed hidden state: the Q/K/V
+    # projection (Q5_0 q/k, Q8_0 v), biases, RoPE and cache-write fused in
+    # one kernel ahead of attention (tmac_gguf.cpp:1046-1128)
+    "qkv": dict(B=1, ctx=256, layers=24, dtype="f32", split=False, qkv=True,
+                desc="config1 from x: Q5_0/Q8_0 q/k/v projection + bias + RoPE + cache-write "
+                     "+ attention, B=1, pos=255, fp32 KV, 24 layers"),
+    "qkv_batched": dict(B=256, ctx=4096, layers=24, dtype="bf16", split=False, qkv=True,
+                        desc="config3 from x: Q5_0/Q8_0 q/k/v projection + bias + RoPE + "
+                             "cache-write + attention, B=256, ctx=4096, bf16 KV, 24 layers"),
     # BASELINE config 5
     "prefill": dict(B=16, ctx=2048, layers=1, dtype="bf16", split=False, prefill=True,
                     desc="config5: causal prefill, B=16 per GPU, S=2048, 14Q/2KV heads, d=64, "
@@ -133,6 +143,33 @@ def algo_bytes_step(wl, pos):
     n = pos.astype(np.int64) + 1
     per_layer = int(np.sum(n * 2 * KD * s_kv + 2 * KD * s_kv + 2 * QD * 4))
     return per_layer * wl["layers"]
+
+
+L2_BYTES = 126 * 1024 * 1024  # B200 L2
+
+
+def qkv_weight_bytes():
+    """Bytes of one layer's projection weights: W_q and W_k in Q5_0 (22-byte
+    blocks of 32), W_v in Q8_0 (34-byte blocks)."""
+    nb = QD // 32
+    return (QD + KD) * nb * 22 + KD * nb * 34
+
+
+def qkv_kernel_bytes(wl, B):
+    """Algorithmic bytes of one projection launch: the weights once, x read,
+    rotated q written, the new k / v rows written."""
+    s_kv = 2 if wl["dtype"] == "bf16" else 4
+    return qkv_weight_bytes() + B * (QD * 4 + QD * 4 + 2 * KD * s_kv)
+
+
+def synth_qblocks(rng, wtype, rows, cols, d_scale):
+    """Random GGML blocks (Q5_0 = 6, Q8_0 = 8) with finite fp16 scales."""
+    bs = 22 if wtype == 6 else 34
+    nb = rows * (cols // 32)
+    blk = rng.integers(0, 256, size=(nb, bs), dtype=np.uint8)
+    d = (d_scale * rng.uniform(0.5, 1.5, nb) * rng.choice([-1.0, 1.0], nb)).astype(np.float16)
+    blk[:, 0:2] = d.view(np.uint8).reshape(nb, 2)
+    return blk.reshape(rows, -1)
 
 
 def kernel_bytes_launch(wl, pos, shard_start, shard_len, split):
@@ -238,6 +275,40 @@ def time_reference_cpu(O, wl, n_units, n_threads, reps=1):
     return unit_bytes(wl, ps) / best / 1e9, best, int(np.sum(ps + 1))
 
 
+def qkv_cpu_weights(O):
+    """One layer's projection weights for the CPU legs (Q5_0 q/k, Q8_0 v)."""
+    return (O.qblocks(O.TYPE_Q5_0, 101, QD, QD, 0.004), O.qblocks(O.TYPE_Q5_0, 102, KD, QD, 0.004),
+            O.qblocks(O.TYPE_Q8_0, 103, KD, QD, 0.0005), O.normal(104, QD) * np.float32(0.1),
+            O.normal(105, KD) * np.float32(0.1), O.normal(106, KD) * np.float32(0.1))
+
+
+def run_reference_qkv_units(O, W, x, ks, vs, ps, n_threads):
+    """The reference's layer step from x (tmac_gguf.cpp:1045-1128: quantized
+    projections, biases, RoPE, cache-write, attention) on every unit,
+    fanned out over n_threads (ctypes drops the GIL during each call)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    def one(u):
+        O.ref_qkv_layer(*W, x[u], ks[u], vs[u], int(ps[u]), v_type=O.TYPE_Q8_0)
+
+    if n_threads <= 1:
+        for u in range(len(ps)):
+            one(u)
+        return
+    with ThreadPoolExecutor(n_threads) as ex:
+        list(ex.map(one, range(len(ps))))
+
+
+def time_reference_qkv_cpu(O, wl, n_units, n_threads):
+    x, ks, vs, ps = cpu_units(O, wl, n_units)
+    W = qkv_cpu_weights(O)
+    t = time.perf_counter()
+    run_reference_qkv_units(O, W, x, ks, vs, ps, n_threads)
+    dt = time.perf_counter() - t
+    return ((unit_bytes(wl, ps) + n_units * qkv_weight_bytes()) / dt / 1e9, dt,
+            int(np.sum(ps + 1)))
+
+
 def run_reference_arm(args, wl, rank, world):
     """--impl reference: the reference's CPU implementation of the path,
     all host threads, bounded sample per step (rank 0 only)."""
@@ -254,13 +325,24 @@ def run_reference_arm(args, wl, rank, world):
     # whole layers of the batch, enough units to keep every thread busy
     n_units = min(total_units, max(wl["B"], (threads // wl["B"]) * wl["B"]))
     q, ks, vs, ps = cpu_units(O, wl, n_units)
+    extra = 0
+    if wl.get("qkv"):
+        if kind == "reference":
+            W = qkv_cpu_weights(O)
+            run = lambda q, ks, vs, ps, nt: run_reference_qkv_units(O, W, q, ks, vs, ps, nt)
+            extra = n_units * qkv_weight_bytes()
+        else:
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the projection workloads need the reference build "
+                              "oracle/_ref/libref.so"}), flush=True)
+            return
     for _ in range(args.warmup):
         run(q, ks, vs, ps, threads)
     t = time.perf_counter()
     for _ in range(args.steps):
         run(q, ks, vs, ps, threads)
     dt = time.perf_counter() - t
-    gbs = unit_bytes(wl, ps) * args.steps / dt / 1e9
+    gbs = (unit_bytes(wl, ps) + extra) * args.steps / dt / 1e9
     sample = (f"{n_units} of the {total_units} (sequence, layer) units of one step per "
               f"timed step ({n_units // wl['B']} layer(s) x {wl['B']} sequences), fp32 "
               f"caches of the workload's values, {threads} threads")
@@ -487,9 +569,27 @@ def main():
     pos_d = torch.from_numpy(pos).cuda()
     stream = torch.cuda.ExternalStream(be.stream())
 
+    qkv = bool(wl.get("qkv"))
+    if qkv:
+        # One weight set per layer (device-resident model constants); the
+        # step's input is the normed hidden state x, in q's place.
+        rng = np.random.default_rng(77 + rank)
+        weights = []
+        for _ in range(L):
+            wq = torch.from_numpy(synth_qblocks(rng, 6, QD, QD, 0.004)).cuda()
+            wk = torch.from_numpy(synth_qblocks(rng, 6, KD, QD, 0.004)).cuda()
+            wv = torch.from_numpy(synth_qblocks(rng, 8, KD, QD, 0.0005)).cuda()
+            bq = torch.randn(QD, device="cuda", generator=g) * 0.1
+            bk = torch.randn(KD, device="cuda", generator=g) * 0.1
+            bv = torch.randn(KD, device="cuda", generator=g) * 0.1
+            weights.append(tg.QKVWeights(wq, wk, wv, QD, v_type=tg.WTYPE_Q8_0, b_q=bq,
+                                         b_k=bk, b_v=bv))
+
     def step(qs, ks, vs, ps, os_):
         for l in range(L):
-            if split:
+            if qkv:
+                kv.decode_layer_x(l, weights[l], qs[l], ps, os_[l])
+            elif split:
                 kv.decode_layer_splitkv(l, qs[l], ks[l], vs[l], ps, os_[l])
             else:
                 kv.decode_layer(l, qs[l], ks[l], vs[l], ps, os_[l])
@@ -519,41 +619,66 @@ def main():
     be.synchronize()
     sampler = ClockSampler(set(range(world))) if local == 0 else None
     time.sleep(0.3 if sampler else 0)
+    # A step whose inputs fit twice in L2 is timed alone between L2 flushes
+    # (a 512 MB write on the same stream, outside the events); larger steps
+    # stream their inputs from HBM on their own and run back to back.
+    wbytes = L * qkv_weight_bytes() if qkv else 0
+    gpu_step_bytes = algo_bytes_step(wl, pos) / (world if wl["split"] else 1) + wbytes
+    flush = gpu_step_bytes < 2 * L2_BYTES
+    flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device="cuda") if flush else None
+
+    def l2_flush():
+        if flush:
+            with torch.cuda.stream(stream):
+                flush_buf.add_(1)
+
     barrier()
     launches0 = be.launch_count()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_wall0 = time.time()
-    e0.record(stream)
-    for _ in range(args.steps):
-        graph.launch()
-    e1.record(stream)
+    if flush:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for a, b in evs:
+            l2_flush()
+            a.record(stream)
+            graph.launch()
+            b.record(stream)
+    else:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.launch()
+        e1.record(stream)
     be.synchronize()
     t_wall1 = time.time()
     launches = be.launch_count() - launches0
     barrier()
-    ms_total = max_over_ranks(e0.elapsed_time(e1))
+    ms_local = sum(a.elapsed_time(b) for a, b in evs) if flush else e0.elapsed_time(e1)
+    ms_total = max_over_ranks(ms_local)
     clocks = sampler.stop(t_wall0, t_wall1) if sampler else None
     ms_step = ms_total / args.steps
-    bytes_step = algo_bytes_step(wl, pos) * (1 if wl["split"] else world)
+    bytes_step = (algo_bytes_step(wl, pos) + wbytes) * (1 if wl["split"] else world)
     seqs_step = B * (1 if wl["split"] else world)
     value = bytes_step / (ms_step * 1e-3) / 1e9
 
     # ---- roofline: decode-kernel launches timed with CUDA events -----------
     # A second graph of the same step carries event records around every
     # decode-attention launch; each replay re-records them on the stream.
-    be.profile_enable(True)
+    be.profile_enable(tg.PROFILE_PROJECTION if qkv else tg.PROFILE_ATTENTION)
     be.graph_begin()
     step(q, kn, vn, pos_d, out)
     gprof = be.graph_end()
     be.profile_enable(False)
     kms, kn_launch = 0.0, 0
     for _ in range(max(3, min(args.steps, 50))):
+        l2_flush()
         gprof.launch()
         ms_i, n_i = be.profile_read()
         kms += ms_i
         kn_launch += n_i
     gprof.destroy()
-    k_bytes = kernel_bytes_launch(wl, pos, shard_start, shard_len, split)
+    k_bytes = (qkv_kernel_bytes(wl, B) if qkv
+               else kernel_bytes_launch(wl, pos, shard_start, shard_len, split))
     k_avg_ms = kms / max(kn_launch, 1)
     hbm_peak, peak_kind = peaks()
     achieved = k_bytes / (k_avg_ms * 1e-3) / 1e9
@@ -581,8 +706,12 @@ def main():
         e2e_step()
     e2e_s = max_over_ranks(time.perf_counter() - t)
     e2e_value = bytes_step * e2e_steps / e2e_s / 1e9
-    h2d = L * B * (QD + 2 * KD) * 4 + L * B * 4
-    d2h = L * B * (2 * QD + KD) * 4
+    if qkv:   # x in, context out; weights and caches stay on the device
+        h2d = L * B * QD * 4 + L * B * 4
+        d2h = L * B * QD * 4
+    else:
+        h2d = L * B * (QD + 2 * KD) * 4 + L * B * 4
+        d2h = L * B * (2 * QD + KD) * 4
 
     # ---- CPU baseline (rank 0, one GPU only) -------------------------------
     cpu = None
@@ -590,11 +719,16 @@ def main():
         O = load_oracle()
         if O.ref_available():
             n_units = 2 if wl["ctx"] > 8192 else 24
-            gbs, dt, npos = time_reference_cpu(O, wl, n_units, 1)
+            if qkv:
+                gbs, dt, npos = time_reference_qkv_cpu(O, wl, n_units, 1)
+            else:
+                gbs, dt, npos = time_reference_cpu(O, wl, n_units, 1)
             cpu = {"value": gbs, "unit": "GB/s", "cores": 1, "kind": "reference",
                    "sample": f"{n_units} (sequence, layer) units at the workload's positions "
                              f"({npos} cache rows, {dt:.2f} s), reference code single-threaded "
-                             "as it runs; fp32 caches of bf16-rounded values, bytes counted as "
+                             "as it runs" + ("; its layer step from x (tmac_gguf.cpp:1045-1128, "
+                                             "Q5_0/Q8_0 projections + attention)" if qkv else "")
+                             + "; fp32 caches of bf16-rounded values, bytes counted as "
                              "the workload's"}
 
     if rank == 0:
@@ -608,8 +742,10 @@ def main():
                        "layers_per_step": L, "n_head": N_HEAD, "n_kv_head": N_KV,
                        "head_dim": HD, "parallelism": f"split-kv x{world}" if wl["split"]
                        else f"sequence-partitioned x{world}",
-                       "l2": "inputs larger than L2: %.0f MB of KV per GPU per step"
-                             % (algo_bytes_step(wl, pos) / max(world if wl["split"] else 1, 1) / 1e6),
+                       "l2": ("L2 flushed between timed steps (512 MB write outside the "
+                              "events): %.1f MB of inputs per GPU per step" % (gpu_step_bytes / 1e6))
+                             if flush else "inputs larger than L2: %.0f MB per GPU per step"
+                             % (gpu_step_bytes / 1e6),
                        "exchange": ({tg.EXCHANGE_PEER: "nvlink peer stores in the merge kernel",
                                      tg.EXCHANGE_NCCL: "ncclAllGather + merge kernel"}
                                     .get(be.exchange, "none") if split else "none")},
@@ -618,8 +754,9 @@ def main():
             "gpu_launches": launches,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak,
                          "unit": "GB/s", "frac": achieved / hbm_peak,
-                         "peak_kind": peak_kind, "kernel": "decode_fused_kernel"
-                         if kv.uses_tensor_cores() else "decode_generic_kernel",
+                         "peak_kind": peak_kind, "kernel": "qkv_kernel" if qkv else
+                         ("decode_fused_kernel" if kv.uses_tensor_cores()
+                          else "decode_generic_kernel"),
                          "bytes_per_launch": k_bytes, "launch_ms": k_avg_ms,
                          "traffic": ncu_traffic(args.workload,
                                                 shard_len / wl["ctx"] if wl["split"] else 1.0),

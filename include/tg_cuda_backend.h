@@ -374,12 +374,17 @@ TG_API int tg_attention_noalloc(void* cuda_stream, const float* q, const void* k
 
 /* Kernel launches this context has issued since creation (all kinds). */
 TG_API int tg_launch_count(tg_context* ctx, long long* out);
-/* CUDA-event timing of every decode-attention kernel launch on the context
- * stream (events recorded just before and after each launch, also into a
- * graph being captured, so that replays re-record them).  Enabling resets
- * the record; tg_profile_read waits for the stream and returns the summed
- * time of the recorded launches (for a graph: of its latest replay) and
- * their number. */
+/* CUDA-event timing of kernel launches on the context stream (events
+ * recorded just before and after each launch, also into a graph being
+ * captured, so that replays re-record them).  `on` selects the kernels: a
+ * mask of TG_PROFILE_ATTENTION (the decode / prefill attention kernels; 1,
+ * so that a true value keeps its meaning) and TG_PROFILE_PROJECTION (the
+ * Q/K/V projection kernel); 0 stops recording.  Enabling resets the
+ * record; tg_profile_read waits for the stream and returns the summed time
+ * of the recorded launches (for a graph: of its latest replay) and their
+ * number. */
+#define TG_PROFILE_ATTENTION 1
+#define TG_PROFILE_PROJECTION 2
 TG_API int tg_profile_enable(tg_context* ctx, int on);
 TG_API int tg_profile_read(tg_context* ctx, double* total_ms, long long* launches);
 /* 1 if the next batched decode on `kv` uses the tensor-core kernel. */

@@ -119,6 +119,25 @@ def test_matmul_q_matches_oracle(backend, O, wtype, rows, cols):
     check_within(y, ref, sum_bound(dequant_np(O, wtype, w, rows, cols), x), "matmul_q")
 
 
+def test_matmul_q_unaligned_device_input(backend, O):
+    """x on the device at an address that is 4- but not 16-byte aligned:
+    the kernel takes its scalar-load path."""
+    import torch
+    rows, cols = 24, 896
+    w = O.qblocks(6, 93, rows, cols, 0.004)
+    x = O.normal(94, cols)
+    buf = torch.zeros(cols + 1, dtype=torch.float32, device="cuda")
+    buf[1:] = torch.from_numpy(x).cuda()
+    xd = buf[1:]
+    assert xd.data_ptr() % 16 != 0
+    wd = torch.from_numpy(w).cuda()
+    yd = torch.zeros(rows, dtype=torch.float32, device="cuda")
+    backend.matmul_q(6, rows, cols, wd, xd, yd)
+    backend.synchronize()
+    ref = O.matmul_q(6, w, x, rows, cols)
+    check_within(yd.cpu().numpy(), ref, sum_bound(dequant_np(O, 6, w, rows, cols), x), "matmul_q")
+
+
 def test_matmul_q_rejects_bad_shapes(backend, tg, O):
     w = O.qblocks(6, 1, 4, 64)
     x = O.normal(2, 64)
@@ -212,6 +231,31 @@ def test_qkv_rope_cache_write_matches_oracle(tg, backend, O, cases, bf16, vt, bi
         else:
             check_within(kr, k, bk, f"k row seq {i}")
             check_within(vr, v, bv, f"v row seq {i}")
+
+
+@pytest.mark.parametrize("bf16", [False, True], ids=["f32", "bf16"])
+@pytest.mark.parametrize("B", [37, 130])
+def test_qkv_batched_path_matches_oracle(tg, backend, O, cases, bf16, B):
+    """Batches of 9 or more sequences take the batched kernel (16 rows x 64
+    sequences per CTA); 37 leaves a partial group, 130 spans three."""
+    rng = np.random.default_rng(B)
+    positions = [int(v) for v in rng.integers(0, 300, size=B)]
+    kv, W, X, refs, bounds = _layer_case(tg, backend, O, cases, positions, bf16, 8, True,
+                                         700 + B)
+    q_out = np.zeros((B, cases.QD), np.float32)
+    kv.qkv_rope_cache_write(0, W, X, positions, q_out)
+    for i, pos in enumerate(positions):
+        q, k, v = refs[i]
+        bq, bk, bv = bounds[i]
+        check_within(q_out[i], q, bq, f"q seq {i}")
+        kr, vr = kv.read_rows(0, i, pos, 1)
+        kr = as_f32(kr).reshape(-1)
+        vr = as_f32(vr).reshape(-1)
+        slack_k = np.abs(k) * 2.0 ** -8 if bf16 else 0.0
+        slack_v = np.abs(v) * 2.0 ** -8 if bf16 else 0.0
+        check_within(kr, k, bk + slack_k, f"k row seq {i}")
+        check_within(vr, v, bv + slack_v, f"v row seq {i}")
+    kv.destroy()
 
 
 @pytest.mark.parametrize("bf16", [False, True], ids=["f32", "bf16"])

@@ -41,6 +41,7 @@ TG_ERR_STATE = 8
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 WTYPE_Q5_0, WTYPE_Q8_0 = 6, 8  # GGML block types (TG_WTYPE_*)
+PROFILE_ATTENTION, PROFILE_PROJECTION = 1, 2  # tg_profile_enable masks
 
 # split-KV record exchange (tg_comm_set_exchange)
 EXCHANGE_AUTO, EXCHANGE_PEER, EXCHANGE_NCCL = 0, 1, 2
@@ -302,8 +303,11 @@ class CudaBackend:
         _check(lib().tg_launch_count(self._h, C.byref(n)))
         return n.value
 
-    def profile_enable(self, on: bool = True) -> None:
-        _check(lib().tg_profile_enable(self._h, 1 if on else 0))
+    def profile_enable(self, on=True) -> None:
+        """True / PROFILE_ATTENTION: attention kernels; PROFILE_PROJECTION:
+        the Q/K/V projection kernel; False: off."""
+        mask = on if isinstance(on, int) and not isinstance(on, bool) else (1 if on else 0)
+        _check(lib().tg_profile_enable(self._h, mask))
 
     def profile_read(self):
         """(summed decode-kernel milliseconds, timed launches)."""

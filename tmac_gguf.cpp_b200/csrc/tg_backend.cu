@@ -201,7 +201,7 @@ struct tg_context {
   std::vector<tg_kv_cache*> caches;  // freed by tg_shutdown if still alive
 
   // Optional CUDA-event timing of each decode-attention kernel launch.
-  bool prof_on = false;
+  int prof_on = 0;  // TG_PROFILE_* mask
   std::vector<cudaEvent_t> prof_ev;  // start/stop pairs
   size_t prof_used = 0;              // events recorded since the last read
 };
@@ -733,6 +733,32 @@ int generic_grid(tg_context* ctx, int dtype, size_t smem) {
   return ctx->num_sms * per_sm;
 }
 
+// CUDA-event timing of one launch of a profiled kernel class
+// (tg_profile_enable): a start event before the launch and, through
+// prof_end, a stop event after it.  Inside a capture the records become
+// event nodes of the graph, re-recorded by every replay.
+int prof_begin(tg_context* ctx, int kind, cudaEvent_t* ev_stop) {
+  *ev_stop = nullptr;
+  if (!(ctx->prof_on & kind)) return TG_OK;
+  while (ctx->prof_ev.size() < ctx->prof_used + 2) {
+    cudaEvent_t ev;
+    TG_CUDA(cudaEventCreate(&ev));
+    ctx->prof_ev.push_back(ev);
+  }
+  TG_CUDA(cudaEventRecordWithFlags(ctx->prof_ev[ctx->prof_used], ctx->stream,
+                                   ctx->capturing ? cudaEventRecordExternal : 0));
+  *ev_stop = ctx->prof_ev[ctx->prof_used + 1];
+  ctx->prof_used += 2;
+  return TG_OK;
+}
+
+int prof_end(tg_context* ctx, cudaEvent_t ev_stop) {
+  if (ev_stop)
+    TG_CUDA(cudaEventRecordWithFlags(ev_stop, ctx->stream,
+                                     ctx->capturing ? cudaEventRecordExternal : 0));
+  return TG_OK;
+}
+
 // Core decode launch on device pointers.  mode 0 writes `out`; mode 1
 // writes per-sequence records to ctx->records.
 int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const float* q,
@@ -785,25 +811,12 @@ int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const f
   p.records = ctx->records;
 
   cudaEvent_t ev_stop = nullptr;
-  if (ctx->prof_on) {
-    while (ctx->prof_ev.size() < ctx->prof_used + 2) {
-      cudaEvent_t ev;
-      TG_CUDA(cudaEventCreate(&ev));
-      ctx->prof_ev.push_back(ev);
-    }
-    // Inside a capture, an external record becomes an event node of the graph.
-    TG_CUDA(cudaEventRecordWithFlags(ctx->prof_ev[ctx->prof_used], ctx->stream,
-                                     ctx->capturing ? cudaEventRecordExternal : 0));
-    ev_stop = ctx->prof_ev[ctx->prof_used + 1];
-    ctx->prof_used += 2;
-  }
+  TG_TRY(prof_begin(ctx, TG_PROFILE_ATTENTION, &ev_stop));
   cudaError_t e = mma ? tg::launch_decode_mma(kv->tmk, kv->tmv, p, grid, ctx->stream)
                       : tg::launch_decode_generic(p, d.dtype, grid, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
   ctx->launches++;
-  if (ev_stop)
-    TG_CUDA(cudaEventRecordWithFlags(ev_stop, ctx->stream,
-                                     ctx->capturing ? cudaEventRecordExternal : 0));
+  TG_TRY(prof_end(ctx, ev_stop));
 
   tg::MergeParams m{};
   m.part = ctx->part;
@@ -1028,23 +1041,11 @@ int run_fused(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const fl
     p.epoch = ctx->xchg_ctl;
   }
   cudaEvent_t ev_stop = nullptr;
-  if (ctx->prof_on) {
-    while (ctx->prof_ev.size() < ctx->prof_used + 2) {
-      cudaEvent_t ev;
-      TG_CUDA(cudaEventCreate(&ev));
-      ctx->prof_ev.push_back(ev);
-    }
-    TG_CUDA(cudaEventRecordWithFlags(ctx->prof_ev[ctx->prof_used], ctx->stream,
-                                     ctx->capturing ? cudaEventRecordExternal : 0));
-    ev_stop = ctx->prof_ev[ctx->prof_used + 1];
-    ctx->prof_used += 2;
-  }
+  TG_TRY(prof_begin(ctx, TG_PROFILE_ATTENTION, &ev_stop));
   cudaError_t e = tg::launch_decode_fused(kv->tmk, kv->tmv, p, grid, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "fused decode launch: %s", cudaGetErrorString(e));
   ctx->launches++;
-  if (ev_stop)
-    TG_CUDA(cudaEventRecordWithFlags(ev_stop, ctx->stream,
-                                     ctx->capturing ? cudaEventRecordExternal : 0));
+  TG_TRY(prof_end(ctx, ev_stop));
   e = tg::launch_merge_exchange(p, mgrid, mgroups, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "merge launch: %s", cudaGetErrorString(e));
   ctx->launches++;
@@ -1102,12 +1103,15 @@ int weight_ptr(tg_context* ctx, const void* p, size_t bytes, const void** dev) {
 
 int run_qkv(tg_context* ctx, tg::QkvParams& p) {
   TG_TRY(commit_inputs(ctx));
-  for (int m = 0; m < 3; ++m) p.tiles[m] = (p.rows[m] + tg::kQkvRows - 1) / tg::kQkvRows;
+  const int per = tg::qkv_use_gemm(p.B, p.cols) ? tg::kQkvGemmRows : tg::kQkvRows;
+  for (int m = 0; m < 3; ++m) p.tiles[m] = (p.rows[m] + per - 1) / per;
   p.err = ctx->d_err;
+  cudaEvent_t ev_stop = nullptr;
+  TG_TRY(prof_begin(ctx, TG_PROFILE_PROJECTION, &ev_stop));
   cudaError_t e = tg::launch_qkv(p, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "qkv launch: %s", cudaGetErrorString(e));
   ctx->launches++;
-  return TG_OK;
+  return prof_end(ctx, ev_stop);
 }
 
 // Mode-1 projection of one layer on device x / pos: bias, RoPE, cache-write,
@@ -2214,23 +2218,11 @@ int tg_prefill_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, in
   const long long items = (long long)n_seqs * d.n_head * ((pp.n_qt + 1) / 2);  // tile pairs
   const int grid = (int)(items < ctx->num_sms ? items : ctx->num_sms);
   cudaEvent_t ev_stop = nullptr;
-  if (ctx->prof_on) {
-    while (ctx->prof_ev.size() < ctx->prof_used + 2) {
-      cudaEvent_t ev;
-      TG_CUDA(cudaEventCreate(&ev));
-      ctx->prof_ev.push_back(ev);
-    }
-    TG_CUDA(cudaEventRecordWithFlags(ctx->prof_ev[ctx->prof_used], ctx->stream,
-                                     ctx->capturing ? cudaEventRecordExternal : 0));
-    ev_stop = ctx->prof_ev[ctx->prof_used + 1];
-    ctx->prof_used += 2;
-  }
+  TG_TRY(prof_begin(ctx, TG_PROFILE_ATTENTION, &ev_stop));
   e = tg::launch_prefill_attn(tq, kv->tmk128, tvh, pp, grid, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "prefill attention launch: %s", cudaGetErrorString(e));
   ctx->launches++;
-  if (ev_stop)
-    TG_CUDA(cudaEventRecordWithFlags(ev_stop, ctx->stream,
-                                     ctx->capturing ? cudaEventRecordExternal : 0));
+  TG_TRY(prof_end(ctx, ev_stop));
   return finish_call(ctx);
 }
 
@@ -2244,7 +2236,9 @@ int tg_launch_count(tg_context* ctx, long long* out) {
 
 int tg_profile_enable(tg_context* ctx, int on) {
   TG_TRY(set_device(ctx));
-  ctx->prof_on = on != 0;
+  if (on < 0 || on > (TG_PROFILE_ATTENTION | TG_PROFILE_PROJECTION))
+    return fail(TG_ERR_INVALID_ARG, "profile_enable: unknown mask %d", on);
+  ctx->prof_on = on;
   if (on) ctx->prof_used = 0;  // disabling keeps the record (a graph may replay it)
   return TG_OK;
 }

@@ -56,10 +56,14 @@ cudaError_t launch_prefill_attn(const CUtensorMap& tq, const CUtensorMap& tk,
                                 cudaStream_t st);
 size_t prefill_attn_smem();
 
-// Q/K/V projection (tg_qkv.cu): kQkvRows weight rows per CTA, cols a multiple
-// of 32 up to qkv_max_cols().
+// Q/K/V projection (tg_qkv.cu), cols a multiple of 32 up to qkv_max_cols().
+// Batches of kQkvGemmMinB or more (cols up to qkv_gemm_max_cols()) take the
+// batched kernel with kQkvGemmRows rows per CTA (qkv_use_gemm), others
+// kQkvRows; p.tiles must follow the kernel launch_qkv picks.
 cudaError_t launch_qkv(const QkvParams& p, cudaStream_t st);
 size_t qkv_smem(int cols);
 int qkv_max_cols();
+int qkv_gemm_max_cols();
+bool qkv_use_gemm(int B, int cols);
 
 }  // namespace tg

@@ -13,13 +13,28 @@
 //                written into the cache and the rotated q written out for
 //                the attention kernel.
 //
-// Decomposition: CTA c takes kQkvRows = 8 consecutive rows of one matrix and
-// every sequence.  It copies the rows' raw blocks into shared memory with
-// 16-byte loads and decodes them to fp32 there (exact: an fp16 scale times a
-// small integer), one warp per row then forms the dot products of all B
-// inputs (lanes over columns, float4 loads, a shuffle reduction), and the
-// epilogue runs over (sequence, row pair).  Weight rows are read once per
-// launch; x rows are shared by the 8 warps through L1.
+// Decomposition: CTA (c, g) takes kQkvRows = 8 consecutive rows of one matrix
+// and kQkvSeqs = 64 sequences (grid.y = ceil(B / 64)).  It copies the rows'
+// raw blocks into shared memory with 16-byte loads (all of a thread's loads
+// issued before any store).  Warp w then owns row w and lane l its 32-element
+// block l: the lane decodes the block once into 32 registers (exact: an fp16
+// scale times a small integer) and, per sequence, multiplies it with the
+// matching 32 inputs (eight float4 loads issued together), two sequences at a
+// time; a shuffle reduction over the lanes finishes each sum.  Rows longer
+// than 32 blocks loop over groups of 32 blocks and decode per sequence.  The
+// epilogue runs over (sequence, row pair).
+//
+//   qkv_gemm_kernel  the same contract for batches of kQkvGemmMinB or more
+//                sequences: a CTA covers kQkvGemmRows = 16 rows x 64
+//                sequences.  The rows are decoded once into a K-major fp32
+//                tile in shared memory, x is staged transposed 32 columns
+//                at a time (double-buffered through registers), and every
+//                thread accumulates a 4-row x 2-sequence register tile over
+//                K (one broadcast LDS.128 of weights and one LDS.64 of inputs
+//                feed 8 FMAs), so no sum needs a cross-lane reduction and
+//                each x value is read from memory once per CTA.  The
+//                epilogue works from registers (a RoPE pair is two of the
+//                thread's rows).
 //
 // PDL: the weight copy and decode come before griddepcontrol.wait, so they
 // overlap the previous kernel on the stream (weights are constants of the
@@ -45,8 +60,7 @@ constexpr int QKV_THREADS = kQkvRows * 32;
 
 struct QkvSmem {
   int raw_bytes;   // staged blocks of kQkvRows rows (16-byte multiple)
-  int w_off;       // fp32 weights [kQkvRows][cols]
-  int y_off;       // dot products [kQkvChunk][kQkvRows]
+  int y_off;       // dot products [kQkvSeqs][kQkvRows]
   int total;
 };
 
@@ -54,9 +68,8 @@ __host__ __device__ inline QkvSmem qkv_smem_layout(int cols) {
   QkvSmem L;
   const int max_row = (cols / 32) * 34;  // the larger block type
   L.raw_bytes = ((kQkvRows * max_row) + 15) & ~15;
-  L.w_off = L.raw_bytes;
-  L.y_off = L.w_off + kQkvRows * cols * 4;
-  L.total = L.y_off + kQkvChunk * kQkvRows * 4;
+  L.y_off = L.raw_bytes;
+  L.total = L.y_off + kQkvSeqs * kQkvRows * 4;
   return L;
 }
 
@@ -67,19 +80,64 @@ __device__ __forceinline__ float f16_scale(uint16_t h) {
   return __half2float(__ushort_as_half(h));
 }
 
-// Element j (0..31) of one block, decoded exactly as dequant_q5_0 /
+// The 32 values of one block, decoded exactly as dequant_q5_0 /
 // dequant_q8_0 (tmac_gguf.cpp:311-328, :240-248).  blk is 2-byte aligned.
-__device__ __forceinline__ float dequant_elem(const uint8_t* blk, int type, int j) {
+__device__ __forceinline__ void decode_block(const uint8_t* blk, int type, float (&w)[32]) {
   const uint16_t* h = reinterpret_cast<const uint16_t*>(blk);
   const float d = f16_scale(h[0]);
   if (type == kWTypeQ5_0) {
+    // qh: bit j is the high bit of element j; byte j of qs holds element j
+    // (low nibble) and element j + 16 (high nibble).
     const uint32_t qh = (uint32_t)h[1] | ((uint32_t)h[2] << 16);
-    const uint32_t byte = blk[6 + (j & 15)];
-    const uint32_t lo = j < 16 ? (byte & 0xfu) : (byte >> 4);
-    const int q = (int)((((qh >> j) & 1u) << 4) | lo) - 16;
-    return d * (float)q;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t two = h[3 + k];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int j = 2 * k + t;
+        const uint32_t byte = (two >> (8 * t)) & 0xffu;
+        w[j] = d * (float)((int)((((qh >> j) & 1u) << 4) | (byte & 0xfu)) - 16);
+        w[j + 16] = d * (float)((int)((((qh >> (j + 16)) & 1u) << 4) | (byte >> 4)) - 16);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const uint32_t two = h[1 + k];
+      w[2 * k] = (float)(int8_t)(two & 0xffu) * d;
+      w[2 * k + 1] = (float)(int8_t)(two >> 8) * d;
+    }
   }
-  return (float)(int8_t)blk[2 + j] * d;
+}
+
+// The 32 inputs of block `blk` of one x row: eight 16-byte loads (vec) or
+// 32 scalar loads, all issued before use.
+__device__ __forceinline__ void load_x32(const float* x, bool vec, float (&v)[32]) {
+  if (vec) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(x) + k);
+      v[4 * k] = f.x;
+      v[4 * k + 1] = f.y;
+      v[4 * k + 2] = f.z;
+      v[4 * k + 3] = f.w;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 32; ++k) v[k] = __ldg(x + k);
+  }
+}
+
+__device__ __forceinline__ float dot32(const float (&w)[32], const float (&v)[32]) {
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+  for (int k = 0; k < 32; k += 4) {
+    a0 = fmaf(w[k], v[k], a0);
+    a1 = fmaf(w[k + 1], v[k + 1], a1);
+    a2 = fmaf(w[k + 2], v[k + 2], a2);
+    a3 = fmaf(w[k + 3], v[k + 3], a3);
+  }
+  return (a0 + a1) + (a2 + a3);
 }
 
 // Cache element write: fp32, or bf16 rounded to nearest even.
@@ -88,55 +146,6 @@ __device__ __forceinline__ void cache_store(void* base, size_t off, int dtype, f
     static_cast<float*>(base)[off] = v;
   else
     static_cast<__nv_bfloat16*>(base)[off] = __float2bfloat16_rn(v);
-}
-
-// Dot products of one fp32 weight row with two input rows (vector path:
-// cols a multiple of 128, 16-byte aligned rows).
-__device__ __forceinline__ void dot2_vec(const float* w, const float* x0, const float* x1,
-                                         int cols, int lane, float& r0, float& r1) {
-  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-  float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
-#pragma unroll 4
-  for (int c = lane * 4; c < cols; c += 128) {
-    const float4 w4 = *reinterpret_cast<const float4*>(w + c);
-    const float4 u = __ldg(reinterpret_cast<const float4*>(x0 + c));
-    const float4 v = __ldg(reinterpret_cast<const float4*>(x1 + c));
-    a0 = fmaf(w4.x, u.x, a0);
-    a1 = fmaf(w4.y, u.y, a1);
-    a2 = fmaf(w4.z, u.z, a2);
-    a3 = fmaf(w4.w, u.w, a3);
-    b0 = fmaf(w4.x, v.x, b0);
-    b1 = fmaf(w4.y, v.y, b1);
-    b2 = fmaf(w4.z, v.z, b2);
-    b3 = fmaf(w4.w, v.w, b3);
-  }
-  r0 = (a0 + a1) + (a2 + a3);
-  r1 = (b0 + b1) + (b2 + b3);
-}
-
-__device__ __forceinline__ float dot1_vec(const float* w, const float* x0, int cols, int lane) {
-  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll 4
-  for (int c = lane * 4; c < cols; c += 128) {
-    const float4 w4 = *reinterpret_cast<const float4*>(w + c);
-    const float4 u = __ldg(reinterpret_cast<const float4*>(x0 + c));
-    a0 = fmaf(w4.x, u.x, a0);
-    a1 = fmaf(w4.y, u.y, a1);
-    a2 = fmaf(w4.z, u.z, a2);
-    a3 = fmaf(w4.w, u.w, a3);
-  }
-  return (a0 + a1) + (a2 + a3);
-}
-
-__device__ __forceinline__ float dot1_scalar(const float* w, const float* x0, int cols, int lane) {
-  float a0 = 0.f, a1 = 0.f;
-  int c = lane;
-  for (; c + 32 < cols; c += 64) {
-    a0 = fmaf(w[c], __ldg(x0 + c), a0);
-    a1 = fmaf(w[c + 32], __ldg(x0 + c + 32), a1);
-  }
-  if (c < cols) a0 = fmaf(w[c], __ldg(x0 + c), a0);
-  return a0 + a1;
 }
 
 }  // namespace
@@ -148,7 +157,6 @@ __global__ void __launch_bounds__(QKV_THREADS) qkv_kernel(const QkvParams p) {
   const int cols = p.cols;
   const QkvSmem L = qkv_smem_layout(cols);
   uint8_t* raw = qsm;
-  float* wf = reinterpret_cast<float*>(qsm + L.w_off);
   float* ys = reinterpret_cast<float*>(qsm + L.y_off);
 
   // This CTA's matrix and rows.
@@ -163,14 +171,28 @@ __global__ void __launch_bounds__(QKV_THREADS) qkv_kernel(const QkvParams p) {
   const uint8_t* src = p.w[m] + (size_t)r0 * row_bytes;
   const size_t bytes = (size_t)nr * row_bytes;
 
+  const int s_begin = blockIdx.y * kQkvSeqs, ns = min(kQkvSeqs, p.B - s_begin);
+
   // 1. Raw blocks into shared memory (before the wait: weights are
-  //    constants).  16-byte loads when the span allows, else 2-byte loads
-  //    (blocks are 2-byte aligned).
+  //    constants).  16-byte loads when the span allows, four per thread in
+  //    flight; else 2-byte loads (blocks are 2-byte aligned).
   if (((reinterpret_cast<uintptr_t>(src) | bytes) & 15) == 0) {
     const uint4* s4 = reinterpret_cast<const uint4*>(src);
     uint4* d4 = reinterpret_cast<uint4*>(raw);
     const int n4 = (int)(bytes >> 4);
-    for (int i = tid; i < n4; i += QKV_THREADS) d4[i] = __ldg(s4 + i);
+    for (int i0 = 0; i0 < n4; i0 += 4 * QKV_THREADS) {
+      uint4 r[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * QKV_THREADS + tid;
+        if (i < n4) r[u] = __ldg(s4 + i);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * QKV_THREADS + tid;
+        if (i < n4) d4[i] = r[u];
+      }
+    }
   } else {
     const uint16_t* s2 = reinterpret_cast<const uint16_t*>(src);
     uint16_t* d2 = reinterpret_cast<uint16_t*>(raw);
@@ -178,108 +200,370 @@ __global__ void __launch_bounds__(QKV_THREADS) qkv_kernel(const QkvParams p) {
     for (int i = tid; i < n2; i += QKV_THREADS) d2[i] = __ldg(s2 + i);
   }
   __syncthreads();
-  // 2. Decode to fp32 rows.
-  const int n_el = nr * cols;
-  for (int e = tid; e < n_el; e += QKV_THREADS) {
-    const int r = e / cols, c = e - r * cols;
-    wf[r * cols + c] = dequant_elem(raw + (size_t)r * row_bytes + (size_t)(c >> 5) * bs, type,
-                                    c & 31);
+  // 2. Lane l decodes block l of the warp's row (before the wait).
+  const int nb = cols >> 5;
+  const uint8_t* rowp = raw + (size_t)min(warp, nr - 1) * row_bytes;
+  float w[32];
+  const bool one_group = nb <= 32;
+  if (one_group) {
+    if (lane < nb) {
+      decode_block(rowp + (size_t)lane * bs, type, w);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) w[k] = 0.f;
+    }
+  }
+
+  griddep_wait();
+  // Epilogue inputs of this thread's first item (sequence, row or row pair),
+  // loaded now so that their latency overlaps the dot products.
+  const bool pairs = p.mode == 1 && m < 2;
+  const int per_seq = pairs ? (nr >> 1) : nr;
+  const int n_items = ns * per_seq;
+  const float* bias = p.bias[m];
+  int pre_pos = 0;
+  float pre_b0 = 0.f, pre_b1 = 0.f;
+  if (tid < n_items) {
+    const int s = tid / per_seq, r = (pairs ? 2 : 1) * (tid - s * per_seq);
+    if (p.mode == 1) pre_pos = p.pos[s_begin + s];
+    if (bias) {
+      pre_b0 = bias[r0 + r];
+      if (pairs) pre_b1 = bias[r0 + r + 1];
+    }
+  }
+  // 3. Dot products: warp = row, lane = block, two sequences at a time.
+  if (warp < nr) {
+    const bool vec = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
+    if (one_group) {
+      const bool have = lane < nb;
+      int s = 0;
+      for (; s + 1 < ns; s += 2) {
+        float v0[32], v1[32];
+        float y0 = 0.f, y1 = 0.f;
+        if (have) {
+          load_x32(p.x + (size_t)(s_begin + s) * cols + lane * 32, vec, v0);
+          load_x32(p.x + (size_t)(s_begin + s + 1) * cols + lane * 32, vec, v1);
+          y0 = dot32(w, v0);
+          y1 = dot32(w, v1);
+        }
+        y0 = warp_sum(y0);
+        y1 = warp_sum(y1);
+        if (lane == 0) {
+          ys[s * kQkvRows + warp] = y0;
+          ys[(s + 1) * kQkvRows + warp] = y1;
+        }
+      }
+      if (s < ns) {
+        float v0[32];
+        float y0 = 0.f;
+        if (have) {
+          load_x32(p.x + (size_t)(s_begin + s) * cols + lane * 32, vec, v0);
+          y0 = dot32(w, v0);
+        }
+        y0 = warp_sum(y0);
+        if (lane == 0) ys[s * kQkvRows + warp] = y0;
+      }
+    } else {
+      for (int s = 0; s < ns; ++s) {
+        float y0 = 0.f;
+        for (int g = lane; g < nb; g += 32) {
+          float v0[32];
+          load_x32(p.x + (size_t)(s_begin + s) * cols + g * 32, vec, v0);
+          decode_block(rowp + (size_t)g * bs, type, w);
+          y0 += dot32(w, v0);
+        }
+        y0 = warp_sum(y0);
+        if (lane == 0) ys[s * kQkvRows + warp] = y0;
+      }
+    }
+  }
+  const int hd = p.head_dim;
+  float2 pre_cs = make_float2(1.f, 0.f);
+  if (pairs && tid < n_items && pre_pos >= 0 && pre_pos < p.table_len) {
+    const int r = 2 * (tid - (tid / per_seq) * per_seq);
+    pre_cs = *reinterpret_cast<const float2*>(p.cs + (size_t)pre_pos * hd + (r0 + r) % hd);
+  }
+  __syncthreads();
+  // 4. Epilogue (a thread's first item uses the values loaded above).
+  if (p.mode == 0) {
+    for (int i = tid; i < ns * nr; i += QKV_THREADS) {
+      const int s = i / nr, r = i - s * nr;
+      float y = ys[s * kQkvRows + r];
+      if (bias) y = __fadd_rn(y, i == tid ? pre_b0 : bias[r0 + r]);
+      p.y[m][(size_t)(s_begin + s) * rows + r0 + r] = y;
+    }
+  } else if (m < 2) {
+    // q or k: bias, then the rotation of pairs (2i, 2i+1) of a head
+    // (tmac_gguf.cpp:1000-1003): x0*c - x1*s, x0*s + x1*c.
+    const int np = nr >> 1;
+    for (int i = tid; i < ns * np; i += QKV_THREADS) {
+      const int s = i / np, r = 2 * (i - s * np), seq = s_begin + s;
+      const bool first = i == tid;
+      float x0 = ys[s * kQkvRows + r], x1 = ys[s * kQkvRows + r + 1];
+      if (bias) {
+        x0 = __fadd_rn(x0, first ? pre_b0 : bias[r0 + r]);
+        x1 = __fadd_rn(x1, first ? pre_b1 : bias[r0 + r + 1]);
+      }
+      const int pos = first ? pre_pos : p.pos[seq];
+      if (pos < 0 || pos >= p.table_len) {
+        record_error(p.err, kDevErrBadPos);
+        continue;
+      }
+      const float2 cs = first ? pre_cs
+                              : *reinterpret_cast<const float2*>(p.cs + (size_t)pos * hd +
+                                                                 (r0 + r) % hd);
+      const float y0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+      const float y1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+      const size_t o = (size_t)seq * rows + r0 + r;
+      if (m == 0) {
+        *reinterpret_cast<float2*>(p.q_out + o) = make_float2(y0, y1);
+      } else {
+        if (p.k_out) *reinterpret_cast<float2*>(p.k_out + o) = make_float2(y0, y1);
+        const int local = pos - p.shard_start;
+        if (local >= 0 && local < p.max_ctx) {
+          const size_t co = ((size_t)seq * p.max_ctx + local) * rows + r0 + r;
+          cache_store(p.k_cache, co, p.dtype, y0);
+          cache_store(p.k_cache, co + 1, p.dtype, y1);
+        }
+      }
+    }
+  } else {
+    // v: bias, then the cache row.
+    for (int i = tid; i < ns * nr; i += QKV_THREADS) {
+      const int s = i / nr, r = i - s * nr, seq = s_begin + s;
+      const bool first = i == tid;
+      float y = ys[s * kQkvRows + r];
+      if (bias) y = __fadd_rn(y, first ? pre_b0 : bias[r0 + r]);
+      if (p.v_out) p.v_out[(size_t)seq * rows + r0 + r] = y;
+      const int pos = first ? pre_pos : p.pos[seq];
+      const int local = pos - p.shard_start;
+      if (local >= 0 && local < p.max_ctx)
+        cache_store(p.v_cache, ((size_t)seq * p.max_ctx + local) * rows + r0 + r, p.dtype, y);
+    }
+  }
+}
+
+namespace {
+
+constexpr int QG_THREADS = 128;  // 4 warps x 4 rows
+constexpr int QG_KC = 32;        // columns per x chunk (one block)
+constexpr int QG_TS = kQkvSeqs;  // sequences per CTA (2 per lane)
+
+struct QgSmem {
+  int wt_off;  // fp32 W^T [cols][kQkvGemmRows]
+  int xt_off;  // x^T [2][QG_KC][QG_TS]
+  int total;
+};
+
+__host__ __device__ inline QgSmem qkv_gemm_layout(int cols) {
+  QgSmem L;
+  const int raw = ((kQkvGemmRows * (cols / 32) * 34) + 15) & ~15;
+  L.wt_off = raw;
+  L.xt_off = L.wt_off + cols * kQkvGemmRows * 4;
+  L.total = L.xt_off + 2 * QG_KC * QG_TS * 4;
+  return L;
+}
+
+// Epilogue of one output pair (rows lr, lr+1 of the CTA; one sequence) in
+// mode 1 for q / k: bias, rotation, q_out / k cache row.
+__device__ __forceinline__ void qg_store_pair(const QkvParams& p, int m, int rows, int r, int seq,
+                                              float x0, float x1, const float* bias) {
+  if (bias) {
+    x0 = __fadd_rn(x0, bias[r]);
+    x1 = __fadd_rn(x1, bias[r + 1]);
+  }
+  const int pos = p.pos[seq];
+  if (pos < 0 || pos >= p.table_len) {
+    record_error(p.err, kDevErrBadPos);
+    return;
+  }
+  const float2 cs = *reinterpret_cast<const float2*>(p.cs + (size_t)pos * p.head_dim +
+                                                     r % p.head_dim);
+  const float y0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+  const float y1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+  const size_t o = (size_t)seq * rows + r;
+  if (m == 0) {
+    *reinterpret_cast<float2*>(p.q_out + o) = make_float2(y0, y1);
+  } else {
+    if (p.k_out) *reinterpret_cast<float2*>(p.k_out + o) = make_float2(y0, y1);
+    const int local = pos - p.shard_start;
+    if (local >= 0 && local < p.max_ctx) {
+      const size_t co = ((size_t)seq * p.max_ctx + local) * rows + r;
+      cache_store(p.k_cache, co, p.dtype, y0);
+      cache_store(p.k_cache, co + 1, p.dtype, y1);
+    }
+  }
+}
+
+// Mode 0 output, or mode 1 v row (bias, cache row, v_out).
+__device__ __forceinline__ void qg_store_one(const QkvParams& p, int m, int rows, int r, int seq,
+                                             float y, const float* bias) {
+  if (bias) y = __fadd_rn(y, bias[r]);
+  if (p.mode == 0) {
+    p.y[m][(size_t)seq * rows + r] = y;
+    return;
+  }
+  if (p.v_out) p.v_out[(size_t)seq * rows + r] = y;
+  const int local = p.pos[seq] - p.shard_start;
+  if (local >= 0 && local < p.max_ctx)
+    cache_store(p.v_cache, ((size_t)seq * p.max_ctx + local) * rows + r, p.dtype, y);
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(QG_THREADS) qkv_gemm_kernel(const QkvParams p) {
+  extern __shared__ __align__(16) unsigned char qsm[];
+  griddep_launch_dependents();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int cols = p.cols, nb = cols >> 5;
+  const QgSmem L = qkv_gemm_layout(cols);
+  uint8_t* raw = qsm;
+  float* wt = reinterpret_cast<float*>(qsm + L.wt_off);
+  float* xt = reinterpret_cast<float*>(qsm + L.xt_off);
+
+  int b = blockIdx.x, m = 0;
+  while (m < 2 && b >= p.tiles[m]) {
+    b -= p.tiles[m];
+    ++m;
+  }
+  const int rows = p.rows[m], r0 = b * kQkvGemmRows, nr = min(kQkvGemmRows, rows - r0);
+  const int type = p.wtype[m], bs = wtype_block_bytes(type);
+  const size_t row_bytes = (size_t)nb * bs;
+  const uint8_t* src = p.w[m] + (size_t)r0 * row_bytes;
+  const size_t bytes = (size_t)nr * row_bytes;
+  const int s_begin = blockIdx.y * QG_TS, ns = min(QG_TS, p.B - s_begin);
+
+  // 1. Raw blocks into shared memory (before the wait).
+  if (((reinterpret_cast<uintptr_t>(src) | bytes) & 15) == 0) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    uint4* d4 = reinterpret_cast<uint4*>(raw);
+    const int n4 = (int)(bytes >> 4);
+    for (int i0 = 0; i0 < n4; i0 += 8 * QG_THREADS) {
+      uint4 r[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * QG_THREADS + tid;
+        if (i < n4) r[u] = __ldg(s4 + i);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * QG_THREADS + tid;
+        if (i < n4) d4[i] = r[u];
+      }
+    }
+  } else {
+    const uint16_t* s2 = reinterpret_cast<const uint16_t*>(src);
+    uint16_t* d2 = reinterpret_cast<uint16_t*>(raw);
+    const int n2 = (int)(bytes >> 1);
+    for (int i = tid; i < n2; i += QG_THREADS) d2[i] = __ldg(s2 + i);
+  }
+  __syncthreads();
+  // 2. Decode into W^T [k][16] (rows past nr are zero).
+  for (int it = tid; it < kQkvGemmRows * nb; it += QG_THREADS) {
+    const int r = it & (kQkvGemmRows - 1), blk = it / kQkvGemmRows;
+    float w[32];
+    if (r < nr) {
+      decode_block(raw + (size_t)r * row_bytes + (size_t)blk * bs, type, w);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) w[j] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) wt[(blk * 32 + j) * kQkvGemmRows + r] = w[j];
   }
   __syncthreads();
 
   griddep_wait();
-  const bool vec = (cols & 127) == 0 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
-  const float* bias = p.bias[m];
-  const int hd = p.head_dim;
-  for (int s0 = 0; s0 < p.B; s0 += kQkvChunk) {
-    const int ns = min(kQkvChunk, p.B - s0);
-    // 3. Dot products: warp = row, two sequences at a time.
-    if (warp < nr) {
-      const float* wr = wf + warp * cols;
-      int s = 0;
+  // 3. K loop: x^T chunks of QG_KC columns, double-buffered through registers.
+  //    Loader thread t: sequence t % 64, columns (t / 64) * 16 .. +15.
+  const bool vec = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
+  const int ls = tid & (QG_TS - 1), lh = tid / QG_TS;
+  float4 xr[4];
+  auto load_chunk = [&](int c) {
+    if (ls < ns) {
+      const float* x = p.x + (size_t)(s_begin + ls) * cols + c * QG_KC + lh * 16;
       if (vec) {
-        for (; s + 1 < ns; s += 2) {
-          float y0, y1;
-          dot2_vec(wr, p.x + (size_t)(s0 + s) * cols, p.x + (size_t)(s0 + s + 1) * cols, cols,
-                   lane, y0, y1);
-          y0 = warp_sum(y0);
-          y1 = warp_sum(y1);
-          if (lane == 0) {
-            ys[s * kQkvRows + warp] = y0;
-            ys[(s + 1) * kQkvRows + warp] = y1;
-          }
-        }
-        if (s < ns) {
-          const float y0 = warp_sum(dot1_vec(wr, p.x + (size_t)(s0 + s) * cols, cols, lane));
-          if (lane == 0) ys[s * kQkvRows + warp] = y0;
-        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) xr[q] = __ldg(reinterpret_cast<const float4*>(x) + q);
       } else {
-        for (; s < ns; ++s) {
-          const float y0 = warp_sum(dot1_scalar(wr, p.x + (size_t)(s0 + s) * cols, cols, lane));
-          if (lane == 0) ys[s * kQkvRows + warp] = y0;
-        }
-      }
-    }
-    __syncthreads();
-    // 4. Epilogue.
-    if (p.mode == 0) {
-      for (int i = tid; i < ns * nr; i += QKV_THREADS) {
-        const int s = i / nr, r = i - s * nr;
-        float y = ys[s * kQkvRows + r];
-        if (bias) y = __fadd_rn(y, bias[r0 + r]);
-        p.y[m][(size_t)(s0 + s) * rows + r0 + r] = y;
-      }
-    } else if (m < 2) {
-      // q or k: bias, then the rotation of pairs (2i, 2i+1) of a head
-      // (tmac_gguf.cpp:1000-1003): x0*c - x1*s, x0*s + x1*c.
-      const int np = nr >> 1;
-      for (int i = tid; i < ns * np; i += QKV_THREADS) {
-        const int s = i / np, r = 2 * (i - s * np), seq = s0 + s;
-        float x0 = ys[s * kQkvRows + r], x1 = ys[s * kQkvRows + r + 1];
-        if (bias) {
-          x0 = __fadd_rn(x0, bias[r0 + r]);
-          x1 = __fadd_rn(x1, bias[r0 + r + 1]);
-        }
-        const int pos = p.pos[seq];
-        if (pos < 0 || pos >= p.table_len) {
-          record_error(p.err, kDevErrBadPos);
-          continue;
-        }
-        const int d = (r0 + r) % hd;
-        const float2 cs = *reinterpret_cast<const float2*>(p.cs + (size_t)pos * hd + d);
-        const float y0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
-        const float y1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-        const size_t o = (size_t)seq * rows + r0 + r;
-        if (m == 0) {
-          *reinterpret_cast<float2*>(p.q_out + o) = make_float2(y0, y1);
-        } else {
-          if (p.k_out) *reinterpret_cast<float2*>(p.k_out + o) = make_float2(y0, y1);
-          const int local = pos - p.shard_start;
-          if (local >= 0 && local < p.max_ctx) {
-            const size_t co = ((size_t)seq * p.max_ctx + local) * rows + r0 + r;
-            cache_store(p.k_cache, co, p.dtype, y0);
-            cache_store(p.k_cache, co + 1, p.dtype, y1);
-          }
-        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          xr[q] = make_float4(__ldg(x + 4 * q), __ldg(x + 4 * q + 1), __ldg(x + 4 * q + 2),
+                              __ldg(x + 4 * q + 3));
       }
     } else {
-      // v: bias, then the cache row.
-      for (int i = tid; i < ns * nr; i += QKV_THREADS) {
-        const int s = i / nr, r = i - s * nr, seq = s0 + s;
-        float y = ys[s * kQkvRows + r];
-        if (bias) y = __fadd_rn(y, bias[r0 + r]);
-        if (p.v_out) p.v_out[(size_t)seq * rows + r0 + r] = y;
-        const int pos = p.pos[seq];
-        const int local = pos - p.shard_start;
-        if (local >= 0 && local < p.max_ctx)
-          cache_store(p.v_cache, ((size_t)seq * p.max_ctx + local) * rows + r0 + r, p.dtype, y);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) xr[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto store_chunk = [&](int buf) {
+    float* d = xt + buf * QG_KC * QG_TS + (lh * 16) * QG_TS + ls;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      d[(4 * q + 0) * QG_TS] = xr[q].x;
+      d[(4 * q + 1) * QG_TS] = xr[q].y;
+      d[(4 * q + 2) * QG_TS] = xr[q].z;
+      d[(4 * q + 3) * QG_TS] = xr[q].w;
+    }
+  };
+  float acc[4][2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = 0.f;
+  load_chunk(0);
+  store_chunk(0);
+  __syncthreads();
+  for (int c = 0; c < nb; ++c) {
+    if (c + 1 < nb) load_chunk(c + 1);
+    const float* xb = xt + (c & 1) * QG_KC * QG_TS + lane * 2;
+    const float* wb = wt + (size_t)c * QG_KC * kQkvGemmRows + warp * 4;
+#pragma unroll 8
+    for (int k = 0; k < QG_KC; ++k) {
+      const float4 w4 = *reinterpret_cast<const float4*>(wb + k * kQkvGemmRows);
+      const float2 x2 = *reinterpret_cast<const float2*>(xb + k * QG_TS);
+      acc[0][0] = fmaf(w4.x, x2.x, acc[0][0]);
+      acc[0][1] = fmaf(w4.x, x2.y, acc[0][1]);
+      acc[1][0] = fmaf(w4.y, x2.x, acc[1][0]);
+      acc[1][1] = fmaf(w4.y, x2.y, acc[1][1]);
+      acc[2][0] = fmaf(w4.z, x2.x, acc[2][0]);
+      acc[2][1] = fmaf(w4.z, x2.y, acc[2][1]);
+      acc[3][0] = fmaf(w4.w, x2.x, acc[3][0]);
+      acc[3][1] = fmaf(w4.w, x2.y, acc[3][1]);
+    }
+    if (c + 1 < nb) store_chunk((c + 1) & 1);
+    __syncthreads();
+  }
+
+  // 4. Epilogue from registers: rows r0 + 4*warp + {0..3}, sequences
+  //    s_begin + 2*lane + {0, 1}.
+  const float* bias = p.bias[m];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int sl = 2 * lane + i;
+    if (sl >= ns) continue;
+    const int seq = s_begin + sl;
+#pragma unroll
+    for (int t = 0; t < 4; t += 2) {
+      const int lr = warp * 4 + t;
+      if (lr >= nr) continue;
+      if (p.mode == 1 && m < 2) {
+        qg_store_pair(p, m, rows, r0 + lr, seq, acc[t][i], acc[t + 1][i], bias);
+      } else {
+        qg_store_one(p, m, rows, r0 + lr, seq, acc[t][i], bias);
+        if (lr + 1 < nr) qg_store_one(p, m, rows, r0 + lr + 1, seq, acc[t + 1][i], bias);
       }
     }
-    __syncthreads();
   }
 }
 
 size_t qkv_smem(int cols) { return (size_t)qkv_smem_layout(cols).total; }
+
+int qkv_gemm_max_cols() {
+  int c = 32;
+  while (qkv_gemm_layout(c + 32).total <= 227 * 1024) c += 32;
+  return c;
+}
+
+bool qkv_use_gemm(int B, int cols) { return B >= kQkvGemmMinB && cols <= qkv_gemm_max_cols(); }
 
 int qkv_max_cols() {
   // Largest multiple of 32 whose layout fits the 227 KB opt-in limit.
@@ -291,20 +575,22 @@ int qkv_max_cols() {
 cudaError_t launch_qkv(const QkvParams& p, cudaStream_t st) {
   const int grid = p.tiles[0] + p.tiles[1] + p.tiles[2];
   if (grid <= 0 || p.B <= 0) return cudaSuccess;
-  const size_t smem = qkv_smem(p.cols);
-  static size_t configured[64] = {};
+  const bool gemm = qkv_use_gemm(p.B, p.cols);
+  const int groups = (p.B + kQkvSeqs - 1) / kQkvSeqs;
+  const size_t smem = gemm ? (size_t)qkv_gemm_layout(p.cols).total : qkv_smem(p.cols);
+  void (*fn)(const QkvParams) = gemm ? qkv_gemm_kernel : qkv_kernel;
+  static size_t configured[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (smem > configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(qkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+  if (smem > configured[gemm][dev]) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    configured[dev] = smem;
+    configured[gemm][dev] = smem;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(QKV_THREADS);
+  cfg.gridDim = dim3(grid, groups);
+  cfg.blockDim = dim3(gemm ? QG_THREADS : QKV_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -312,7 +598,7 @@ cudaError_t launch_qkv(const QkvParams& p, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, qkv_kernel, p);
+  return cudaLaunchKernelEx(&cfg, fn, p);
 }
 
 }  // namespace tg

@@ -188,7 +188,9 @@ struct FusedParams {
 constexpr int kWTypeQ5_0 = 6;   // 22-byte blocks: fp16 d, 32 high bits, 16 nibble bytes
 constexpr int kWTypeQ8_0 = 8;   // 34-byte blocks: fp16 d, 32 int8
 constexpr int kQkvRows = 8;     // weight rows per CTA (one warp each)
-constexpr int kQkvChunk = 256;  // sequences per epilogue pass
+constexpr int kQkvSeqs = 64;    // sequences per CTA (grid.y covers the batch)
+constexpr int kQkvGemmRows = 16;  // batched path: rows per CTA (4 per warp)
+constexpr int kQkvGemmMinB = 9;   // batches from this size take the batched path
 
 TG_HD int wtype_block_bytes(int t) {
   return t == kWTypeQ5_0 ? 22 : (t == kWTypeQ8_0 ? 34 : 0);
@@ -200,7 +202,7 @@ struct QkvParams {
   float* y[3];             // mode 0: [B][rows[m]]
   int wtype[3];
   int rows[3];             // 0 rows: matrix absent
-  int tiles[3];            // CTAs of each matrix: ceil(rows / kQkvRows)
+  int tiles[3];            // CTAs of each matrix: ceil(rows / rows per CTA of the path)
   int cols;                // inputs, a multiple of 32
   const float* x;          // [B][cols]
   int B;
