@@ -337,6 +337,14 @@ TG_API int tg_decode_layer_splitkv(tg_context* ctx, tg_kv_cache* shard, int laye
                             const float* v_new, const int32_t* pos,
                             float* out);
 
+/* tg_decode_layer_x on a split-KV shard: every rank projects the replicated
+ * q from x (same weights and x on every rank), the rank whose shard holds
+ * pos[s] writes the k / v row, then the split-KV attention, exchange and
+ * merge of tg_decode_layer_splitkv give every rank the full output. */
+TG_API int tg_decode_layer_splitkv_x(tg_context* ctx, tg_kv_cache* shard, int layer,
+                                     int n_seqs, const tg_qkv_weights* w, const float* x,
+                                     const int32_t* pos, float* out);
+
 /* ------------------------------------------------- allocation-free decode */
 
 /* No counterpart in the reference.  Decode attention for callers that cannot

@@ -9,8 +9,10 @@ shard_range(ctx, N, rank) of every sequence), runs the RoPE + owner
 cache-write + split-KV attention + record exchange + merge through the C ABI
 (tg_decode_layer_splitkv) and compares the replicated output with the CPU
 oracle, under the automatic exchange (peer memory for the bf16 cache when
-the GPUs map each other's memory) and the NCCL all-gather.  Exit status 0
-on success on every rank.
+the GPUs map each other's memory) and the NCCL all-gather.  The layer from
+the normed hidden state (tg_decode_layer_splitkv_x: Q/K/V projection, then
+split-KV attention) is checked against the same layer on one GPU over the
+whole cache.  Exit status 0 on success on every rank.
 """
 from __future__ import annotations
 
@@ -101,6 +103,49 @@ def main() -> int:
             print(f"rank {rank}: outputs differ across ranks")
             ok = False
         kv.destroy()
+    # The layer from the normed hidden state x (projection + split-KV
+    # attention) against the same layer on this GPU over the whole cache:
+    # the owner's new k / v row is bit-identical, the output agrees to the
+    # split-merge rounding.
+    be.set_exchange(tg.EXCHANGE_AUTO)
+    for bf16 in (True, False):
+        positions = [9000, 777, 12345, 0, world * 64]
+        B = len(positions)
+        gctx = max(positions) + 1
+        start, length = tg.shard_range(gctx, world, rank)
+        dt = tg.DTYPE_BF16 if bf16 else tg.DTYPE_F32
+        kv = tg.KVCache(be, 1, B, max(length, 1), shard_start=start, global_ctx=gctx, dtype=dt)
+        full = tg.KVCache(be, 1, B, gctx, dtype=dt)
+        for i, p in enumerate(positions):
+            _, _, _, kc, vc = cases.decode_inputs(78, p, bf16, seq=i)
+            lo, hi = start, min(start + length, p)
+            if hi > lo:
+                kv.write_rows(0, i, 0, kc[lo:hi], vc[lo:hi])
+            if p > 0:
+                full.write_rows(0, i, 0, kc[:p], vc[:p])
+        wq, wk, wv, bq, bk, bv = cases.qkv_weights(79, 8, True)
+        W = tg.QKVWeights(wq, wk, wv, 896, v_type=8, b_q=bq, b_k=bk, b_v=bv)
+        X = cases.qkv_x(80, B).copy()
+        ref = np.zeros((B, cases.QD), np.float32)
+        full.decode_layer_x(0, W, X, positions, ref)
+        for it in range(2):
+            out = np.zeros((B, cases.QD), np.float32)
+            kv.decode_layer_splitkv_x(0, W, X, positions, out)
+            err = float(np.abs(out - ref).max())
+            if err > 5e-5:
+                print(f"rank {rank}: x path step {it} bf16={bf16} err={err}")
+                ok = False
+        for i, p in enumerate(positions):
+            if start <= p < start + length:
+                a = kv.read_rows(0, i, p - start, 1)
+                b = full.read_rows(0, i, p, 1)
+                if not (np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])):
+                    print(f"rank {rank}: x path cache row mismatch seq {i}")
+                    ok = False
+        if rank == 0:
+            print(f"x path bf16={bf16} exchange {be.exchange}")
+        kv.destroy()
+        full.destroy()
     be.comm_destroy()
     be.shutdown()
     flag = torch.tensor([1 if ok else 0])

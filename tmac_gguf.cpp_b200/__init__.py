@@ -150,6 +150,8 @@ _SIGS = {
                                           C.POINTER(tg_qkv_weights), _vp, _vp, _vp]),
     "tg_decode_layer_x": (C.c_int, [_vp, _vp, C.c_int, C.c_int,
                                     C.POINTER(tg_qkv_weights), _vp, _vp, _vp]),
+    "tg_decode_layer_splitkv_x": (C.c_int, [_vp, _vp, C.c_int, C.c_int,
+                                            C.POINTER(tg_qkv_weights), _vp, _vp, _vp]),
 }
 
 _lib: Optional[C.CDLL] = None
@@ -518,6 +520,15 @@ class KVCache:
         pos = _as_i32(pos)
         _check(lib().tg_decode_layer_x(self.backend.handle, self._h, layer, n,
                                        C.byref(weights.desc), _ptr(x), _ptr(pos), _ptr(out)))
+
+    def decode_layer_splitkv_x(self, layer: int, weights: "QKVWeights", x, pos,
+                               out) -> None:
+        """The layer from x on a split-KV shard (tg_decode_layer_splitkv_x)."""
+        n = len(pos)
+        pos = _as_i32(pos)
+        _check(lib().tg_decode_layer_splitkv_x(self.backend.handle, self._h, layer, n,
+                                               C.byref(weights.desc), _ptr(x), _ptr(pos),
+                                               _ptr(out)))
 
     def attention_splitkv(self, layer: int, q, past_len, out) -> None:
         n = len(past_len)

@@ -2131,6 +2131,31 @@ int tg_decode_layer_splitkv(tg_context* ctx, tg_kv_cache* kv, int layer, int n_s
   return finish_call(ctx);
 }
 
+int tg_decode_layer_splitkv_x(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs,
+                              const tg_qkv_weights* w, const float* x, const int32_t* pos,
+                              float* out) {
+  TG_TRY(check_kv_call(ctx, kv, layer, n_seqs));
+  if (!w || !x || !pos || !out) return fail(TG_ERR_INVALID_ARG, "null argument");
+  if (n_seqs == 0) return TG_OK;
+  TG_TRY(check_qkv_cols(w->cols));
+  TG_TRY(check_host_pos(pos, n_seqs, kv->global_ctx, "pos"));
+  const tg_kv_desc& d = kv->d;
+  const size_t qb = (size_t)n_seqs * d.n_head * d.head_dim * 4;
+  const void *dx = nullptr, *dp = nullptr;
+  void* dout = nullptr;
+  TG_TRY(stage_in(ctx, x, (size_t)n_seqs * w->cols * 4, &dx));
+  TG_TRY(stage_in(ctx, pos, (size_t)n_seqs * 4, &dp));
+  TG_TRY(stage_out(ctx, out, qb, false, &dout));
+  TG_TRY(ensure_buf(ctx, &ctx->qx, &ctx->qx_cap, qb / 4));
+  // Every rank projects q (replicated); only the shard holding pos[s]
+  // writes the k / v row.
+  TG_TRY(qkv_layer_core(ctx, kv, layer, n_seqs, w, static_cast<const float*>(dx),
+                        static_cast<const int*>(dp), ctx->qx));
+  TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, ctx->qx, nullptr, nullptr,
+                      static_cast<const int*>(dp), static_cast<float*>(dout), false));
+  return finish_call(ctx);
+}
+
 // ------------------------------------------------ prefill
 
 int tg_prefill_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, int S,
