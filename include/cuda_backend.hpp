@@ -1,10 +1,11 @@
 // cuda_backend.hpp -- C++ mirror of the reference's metal_backend operator
 // surface for the attention hot path, over the C ABI of tg_cuda_backend.h.
 //
-// tmac_gguf.cpp drives RoPE, the KV cache-write and decode attention through
-// metal_backend::{init, shutdown, metal_batch_begin, metal_batch_end,
-// rope_op, elem_op, attention_op} (metal_backend.hpp:114-191, :354-453,
-// :519-520).  This header offers the same functions, with the same names,
+// tmac_gguf.cpp drives the Q/K/V projection, RoPE, the KV cache-write and
+// decode attention through metal_backend::{init, shutdown,
+// metal_batch_begin, metal_batch_end, fused_qkv_op, matmul_q5_0,
+// matmul_q8_0, rope_op, elem_op, attention_op} (metal_backend.hpp:114-191,
+// :320-338, :354-489, :519-520).  This header offers the same functions, with the same names,
 // argument order and meaning, in namespace cuda_backend, so the forward loop
 // (tmac_gguf.cpp:1490-1496, :1562-1568) switches backend with a namespace
 // alias.  Error behaviour follows the reference: init returns bool and
@@ -98,6 +99,27 @@ inline void attention_op(Context& ctx, const float* Q, const float* K_cache,
                  tg_attention_op(ctx.tg, Q, K_cache, V_cache, output, n_head, n_kv_head,
                                  head_dim, past_len),
                  "attention_op");
+}
+
+// fused_qkv_op (metal_backend.hpp:456): y_q = W_q x, y_k = W_k x, y_v = W_v x
+// with W_q / W_k in Q5_0 and W_v in Q5_0 or Q8_0 blocks.
+inline void fused_qkv_op(Context& ctx, const uint8_t* W_q, const uint8_t* W_k,
+                         const uint8_t* W_v, const float* x, float* y_q, float* y_k, float* y_v,
+                         int q_rows, int k_rows, int v_rows, int cols, bool v_is_q8) {
+  detail::report(ctx,
+                 tg_fused_qkv_op(ctx.tg, W_q, W_k, W_v, x, y_q, y_k, y_v, q_rows, k_rows,
+                                 v_rows, cols, v_is_q8 ? 1 : 0),
+                 "fused_qkv_op");
+}
+
+// matmul_q5_0 / matmul_q8_0 (metal_backend.hpp:320-338): y = W x.
+inline void matmul_q5_0(Context& ctx, int rows, int cols, const uint8_t* w, const float* x,
+                        float* y) {
+  detail::report(ctx, tg_matmul_q(ctx.tg, TG_WTYPE_Q5_0, rows, cols, w, x, y), "matmul_q5_0");
+}
+inline void matmul_q8_0(Context& ctx, int rows, int cols, const uint8_t* w, const float* x,
+                        float* y) {
+  detail::report(ctx, tg_matmul_q(ctx.tg, TG_WTYPE_Q8_0, rows, cols, w, x, y), "matmul_q8_0");
 }
 
 // Mark a host array (e.g. the static g_k_cache) as written only by GPU ops.

@@ -1,16 +1,19 @@
 // The decode step of the reference's forward loop (tmac_gguf.cpp:1453-1516,
-// forward_all_layers_fused) on Linux with this library as the attention
-// backend: per layer RMSNorm -> Q/K/V matvecs + biases -> RoPE -> cache-write
-// -> attention -> output matvec -> residual -> RMSNorm -> gate/up -> SiLU ->
-// down -> residual.  The attention-path ops (rope_op, elem_op(2),
-// attention_op inside metal_batch_begin / metal_batch_end) go through
+// forward_all_layers_fused) on Linux with this library as the backend of its
+// Metal ops: per layer RMSNorm -> fused_qkv_op (Q5_0 q/k, Q8_0 v) and the
+// three bias adds (elem_op 0) -> rope_op x2 -> elem_op(2) x2 (cache-write)
+// -> attention_op -> matmul_q5_0 (attn_output), all inside
+// metal_batch_begin / metal_batch_end, as :1468-1498 encodes them -> residual
+// -> RMSNorm -> gate/up -> SiLU -> down -> residual.  The ops go through
 // cuda_backend.hpp with the reference's arguments and host arrays; the
-// weight matvecs, norms and SiLU are host-side fp32 stubs with seeded
-// weights of Qwen2-0.5B's shapes (one weight set shared by all layers, to
-// keep the program small).  The same loop is run a second time with the
-// CPU oracle's decode step (tg_oracle.c, the restatement of
-// tmac_gguf.cpp:990-1016 and :1090-1128) in place of the backend, and the
-// hidden states after every token are compared.  Prints PASS / FAIL.
+// norms and the FFN (not on this path) are host-side fp32 stubs.  Weights
+// are seeded blocks of Qwen2-0.5B's shapes (one weight set shared by all
+// layers, to keep the program small), registered once as device-owned.
+// The same loop is run a second time with the CPU oracle in place of the
+// backend (tg_oracle.c: the restatements of matmul's CPU loop
+// :476-513 with dequant_q5_0 / dequant_q8_0, the bias adds :1067-1081 and
+// the decode step :990-1016, :1090-1128), and the hidden states after every
+// token are compared.  Prints PASS / FAIL.
 //
 // usage: forward_model_shim <n_tokens> <device_owned 0|1>
 #include <cmath>
@@ -36,8 +39,16 @@ float o_k_cache[NUM_LAYERS][MAX_SEQ_LEN][K_DIM];
 float o_v_cache[NUM_LAYERS][MAX_SEQ_LEN][K_DIM];
 
 struct Weights {
-  std::vector<float> wq, wk, wv, bq, bk, bv, wo, gate, up, down;
+  std::vector<uint8_t> wq, wk, wv, wo;  // GGML blocks: Q5_0 (q, k, o), Q8_0 (v)
+  std::vector<float> bq, bk, bv, gate, up, down;
 };
+
+void fill_blocks(std::vector<uint8_t>& w, int type, int rows, int cols, uint64_t seed,
+                 float d_scale) {
+  const size_t nb = (size_t)rows * (cols / 32);
+  w.resize(nb * (type == TGO_TYPE_Q5_0 ? 22 : 34));
+  tgo_fill_qblocks(type, seed, w.data(), nb, d_scale);
+}
 
 void fill(std::vector<float>& w, size_t n, uint64_t seed, float scale) {
   w.resize(n);
@@ -71,26 +82,32 @@ bool forward(cuda_backend::Context* ctx, const Weights& W, float* hidden, int po
   for (int layer = 0; layer < NUM_LAYERS; ++layer) {
     std::memcpy(scratch, hidden, sizeof(scratch));
     rmsnorm(scratch, HIDDEN_DIM);
-    matvec(W.wq, scratch, q, HIDDEN_DIM, HIDDEN_DIM);
-    matvec(W.wk, scratch, k, K_DIM, HIDDEN_DIM);
-    matvec(W.wv, scratch, v, K_DIM, HIDDEN_DIM);
-    for (int i = 0; i < HIDDEN_DIM; ++i) q[i] += W.bq[i];
-    for (int i = 0; i < K_DIM; ++i) k[i] += W.bk[i], v[i] += W.bv[i];
     if (ctx) {
       cuda_backend::metal_batch_begin(*ctx);
+      cuda_backend::fused_qkv_op(*ctx, W.wq.data(), W.wk.data(), W.wv.data(), scratch, q, k, v,
+                                 HIDDEN_DIM, K_DIM, K_DIM, HIDDEN_DIM, true);
+      cuda_backend::elem_op(*ctx, 0, q, W.bq.data(), HIDDEN_DIM);
+      cuda_backend::elem_op(*ctx, 0, k, W.bk.data(), K_DIM);
+      cuda_backend::elem_op(*ctx, 0, v, W.bv.data(), K_DIM);
       cuda_backend::rope_op(*ctx, q, NUM_HEADS, HEAD_DIM, pos, ROPE_BASE);
       cuda_backend::rope_op(*ctx, k, NUM_KV_HEADS, HEAD_DIM, pos, ROPE_BASE);
       cuda_backend::elem_op(*ctx, 2, &kc[layer][pos][0], k, K_DIM);
       cuda_backend::elem_op(*ctx, 2, &vc[layer][pos][0], v, K_DIM);
       cuda_backend::attention_op(*ctx, q, &kc[layer][0][0], &vc[layer][0][0], context,
                                  NUM_HEADS, NUM_KV_HEADS, HEAD_DIM, pos);
-      cuda_backend::metal_batch_end();  // context valid on the host
+      cuda_backend::matmul_q5_0(*ctx, HIDDEN_DIM, HIDDEN_DIM, W.wo.data(), context, attn_out);
+      cuda_backend::metal_batch_end();  // attn_out valid on the host
       if (ctx->last_status != TG_OK) return false;
     } else {
+      tgo_matmul_q(TGO_TYPE_Q5_0, W.wq.data(), scratch, q, HIDDEN_DIM, HIDDEN_DIM);
+      tgo_matmul_q(TGO_TYPE_Q5_0, W.wk.data(), scratch, k, K_DIM, HIDDEN_DIM);
+      tgo_matmul_q(TGO_TYPE_Q8_0, W.wv.data(), scratch, v, K_DIM, HIDDEN_DIM);
+      for (int i = 0; i < HIDDEN_DIM; ++i) q[i] += W.bq[i];
+      for (int i = 0; i < K_DIM; ++i) k[i] += W.bk[i], v[i] += W.bv[i];
       tgo_decode_step(q, k, v, &kc[layer][0][0], &vc[layer][0][0], context, NUM_HEADS,
                       NUM_KV_HEADS, HEAD_DIM, pos, ROPE_BASE, scores.data());
+      tgo_matmul_q(TGO_TYPE_Q5_0, W.wo.data(), context, attn_out, HIDDEN_DIM, HIDDEN_DIM);
     }
-    matvec(W.wo, context, attn_out, HIDDEN_DIM, HIDDEN_DIM);
     for (int i = 0; i < HIDDEN_DIM; ++i) hidden[i] += attn_out[i];
     std::memcpy(scratch, hidden, sizeof(scratch));
     rmsnorm(scratch, HIDDEN_DIM);
@@ -110,13 +127,14 @@ int main(int argc, char** argv) {
   if (n_tok < 1 || n_tok > MAX_SEQ_LEN) return 2;
   Weights W;
   const float sh = 1.0f / std::sqrt((float)HIDDEN_DIM), si = 1.0f / std::sqrt((float)INTER_DIM);
-  fill(W.wq, (size_t)HIDDEN_DIM * HIDDEN_DIM, 11, sh);
-  fill(W.wk, (size_t)K_DIM * HIDDEN_DIM, 12, sh);
-  fill(W.wv, (size_t)K_DIM * HIDDEN_DIM, 13, sh);
+  // Block scales so that a row's dot product with a unit-RMS input is O(1).
+  fill_blocks(W.wq, TGO_TYPE_Q5_0, HIDDEN_DIM, HIDDEN_DIM, 11, 0.004f);
+  fill_blocks(W.wk, TGO_TYPE_Q5_0, K_DIM, HIDDEN_DIM, 12, 0.004f);
+  fill_blocks(W.wv, TGO_TYPE_Q8_0, K_DIM, HIDDEN_DIM, 13, 0.0005f);
+  fill_blocks(W.wo, TGO_TYPE_Q5_0, HIDDEN_DIM, HIDDEN_DIM, 17, 0.004f);
   fill(W.bq, HIDDEN_DIM, 14, 0.1f);
   fill(W.bk, K_DIM, 15, 0.1f);
   fill(W.bv, K_DIM, 16, 0.1f);
-  fill(W.wo, (size_t)HIDDEN_DIM * HIDDEN_DIM, 17, sh);
   fill(W.gate, (size_t)INTER_DIM * HIDDEN_DIM, 18, sh);
   fill(W.up, (size_t)INTER_DIM * HIDDEN_DIM, 19, sh);
   fill(W.down, (size_t)HIDDEN_DIM * INTER_DIM, 20, si);
@@ -130,6 +148,10 @@ int main(int argc, char** argv) {
     cuda_backend::register_device_owned(g_ctx, g_k_cache, sizeof(g_k_cache));
     cuda_backend::register_device_owned(g_ctx, g_v_cache, sizeof(g_v_cache));
   }
+  // The model's weights: uploaded once (the reference wraps the mapped
+  // model file with no-copy buffers, metal_backend.hpp:52-65).
+  for (std::vector<uint8_t>* w : {&W.wq, &W.wk, &W.wv, &W.wo})
+    cuda_backend::register_device_owned(g_ctx, w->data(), w->size());
   std::vector<float> scores(MAX_SEQ_LEN);
   std::vector<float> hid_gpu(HIDDEN_DIM), hid_cpu(HIDDEN_DIM);
   double worst = 0.0;
