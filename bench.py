@@ -497,12 +497,18 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="auto", choices=["auto", "peer", "nccl"],
                     help="split-KV record exchange for N > 1 (tg_comm_set_exchange)")
+    ap.add_argument("--ctx", type=int, default=0,
+                    help="override the workload's context length (small cases for "
+                         "profiler captures; the reported config says so)")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layers per step (small profiling cases)")
     args = ap.parse_args()
     wl = dict(WORKLOADS[args.workload])
     if args.layers > 0:
         wl["layers"] = args.layers
+    if args.ctx > 0:
+        wl["ctx"] = args.ctx
+        wl["desc"] = wl["desc"] + f" [context overridden to {args.ctx}]"
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

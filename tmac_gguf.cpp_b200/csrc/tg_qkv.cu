@@ -349,18 +349,21 @@ constexpr int QG_THREADS = 128;  // 4 warps x 4 rows
 constexpr int QG_KC = 32;        // columns per x chunk (one block)
 constexpr int QG_TS = kQkvSeqs;  // sequences per CTA (2 per lane)
 
+// The raw blocks are dead once decoded, so the x^T buffers reuse their
+// bytes: [raw blocks | x^T [2][QG_KC][QG_TS]] then W^T [cols][16] fp32.
 struct QgSmem {
-  int wt_off;  // fp32 W^T [cols][kQkvGemmRows]
-  int xt_off;  // x^T [2][QG_KC][QG_TS]
+  int xt_off;  // 0: shares the raw blocks' bytes
+  int wt_off;
   int total;
 };
 
 __host__ __device__ inline QgSmem qkv_gemm_layout(int cols) {
   QgSmem L;
   const int raw = ((kQkvGemmRows * (cols / 32) * 34) + 15) & ~15;
-  L.wt_off = raw;
-  L.xt_off = L.wt_off + cols * kQkvGemmRows * 4;
-  L.total = L.xt_off + 2 * QG_KC * QG_TS * 4;
+  const int xt = 2 * QG_KC * QG_TS * 4;
+  L.xt_off = 0;
+  L.wt_off = raw > xt ? raw : xt;
+  L.total = L.wt_off + cols * kQkvGemmRows * 4;
   return L;
 }
 
