@@ -179,6 +179,16 @@ TG_API int tg_fused_qkv_op(tg_context* ctx, const uint8_t* W_q, const uint8_t* W
 TG_API int tg_matmul_q(tg_context* ctx, int wtype, int rows, int cols, const uint8_t* w,
                        const float* x, float* y);
 
+/* The attn_output matvec and its residual add (tmac_gguf.cpp:1497-1499:
+ * matmul of blk.N.attn_output.weight, then elem_op(0, hidden, attn_out)):
+ * hidden[s] += W_o context[s] for n_seqs sequences, W_o `rows` x `cols` in
+ * wtype blocks (Q5_0 or Q8_0: a 896-wide row is not a multiple of the 256
+ * values of a K-quant super-block).  The product sum is rounded once, then
+ * the add, as the reference does.  context [n_seqs][cols], hidden
+ * [n_seqs][rows]; pointer rules as tg_fused_qkv_op. */
+TG_API int tg_attn_output(tg_context* ctx, int n_seqs, int wtype, const void* w_o, int rows,
+                          int cols, const float* context, float* hidden);
+
 /* One layer's projection weights: W_q has n_head*head_dim rows, W_k and
  * W_v n_kv_head*head_dim rows of `cols` inputs.  Device pointers or
  * registered host arrays; a NULL bias is a bias the model does not have. */
@@ -269,6 +279,16 @@ TG_API int tg_decode_layer_x(tg_context* ctx, tg_kv_cache* kv, int layer, int n_
                              const tg_qkv_weights* w, const float* x, const int32_t* pos,
                              float* out);
 
+/* The attention block of a decode layer, from the normed hidden state x to
+ * the residual stream (tmac_gguf.cpp:1479-1499): tg_qkv_rope_cache_write,
+ * attention over rows 0..pos[s], then hidden[s] += W_o context[s]
+ * (tg_attn_output, o_type blocks; W_o square of n_head*head_dim).  The
+ * context stays on the device; hidden [n_seqs][n_head*head_dim] is read and
+ * written.  Four kernels chained by programmatic dependent launch. */
+TG_API int tg_attention_block(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs,
+                              const tg_qkv_weights* w, int o_type, const void* w_o,
+                              const float* x, const int32_t* pos, float* hidden);
+
 /* ------------------------------------------------- prefill */
 
 /* Causal prefill of one layer for n_seqs prompts of S tokens (positions
@@ -344,6 +364,14 @@ TG_API int tg_decode_layer_splitkv(tg_context* ctx, tg_kv_cache* shard, int laye
 TG_API int tg_decode_layer_splitkv_x(tg_context* ctx, tg_kv_cache* shard, int layer,
                                      int n_seqs, const tg_qkv_weights* w, const float* x,
                                      const int32_t* pos, float* out);
+
+/* tg_attention_block on a split-KV shard: the attention as
+ * tg_decode_layer_splitkv_x, then every rank applies the attn_output
+ * matvec to the replicated context (identical hidden on every rank). */
+TG_API int tg_attention_block_splitkv(tg_context* ctx, tg_kv_cache* shard, int layer,
+                                      int n_seqs, const tg_qkv_weights* w, int o_type,
+                                      const void* w_o, const float* x, const int32_t* pos,
+                                      float* hidden);
 
 /* ------------------------------------------------- allocation-free decode */
 

@@ -98,6 +98,8 @@ def lib():
                                    C.c_void_p, C.c_void_p]
         L.tgo_fill_qblocks.argtypes = [C.c_int, C.c_uint64, _u8p, C.c_size_t,
                                        C.c_float]
+        L.tgo_attn_output.argtypes = [C.c_int, _u8p, _f32p, _f32p, _f32p, C.c_int,
+                                      C.c_int, C.c_void_p]
         _lib = L
     return _lib
 
@@ -128,6 +130,11 @@ def ref():
         R.tgref_f16_to_f32.restype = C.c_float
         R.tgref_f16_to_f32.argtypes = [C.c_uint16]
         R.tgref_matmul.argtypes = [C.c_int, _u8p, _f32p, _f32p, C.c_int, C.c_int]
+        R.tgref_attention_block.restype = C.c_int
+        R.tgref_attention_block.argtypes = [
+            C.c_int, _u8p, C.c_int, _u8p, C.c_int, _u8p, C.c_void_p, C.c_void_p,
+            C.c_void_p, C.c_int, _u8p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
+            _f32p, _f32p, _f32p, C.c_int]
         R.tgref_qkv_layer.restype = C.c_int
         R.tgref_qkv_layer.argtypes = [C.c_int, _u8p, C.c_int, _u8p, C.c_int, _u8p,
                                       C.c_void_p, C.c_void_p, C.c_void_p, _f32p,
@@ -284,6 +291,16 @@ def qkv_step(wq, wk, wv, bq, bk, bv, x, pos, q_type=TYPE_Q5_0, k_type=TYPE_Q5_0,
     return q, k, v
 
 
+def attn_output(o_type: int, wo, context, original_hidden) -> np.ndarray:
+    """tmac_gguf.cpp:1129-1140: original_hidden + W_o context."""
+    context = np.ascontiguousarray(context, np.float32).reshape(-1)
+    h0 = np.ascontiguousarray(original_hidden, np.float32).reshape(-1)
+    out = np.empty_like(h0)
+    lib().tgo_attn_output(o_type, np.ascontiguousarray(wo, np.uint8).reshape(-1), context, h0,
+                          out, h0.size, context.size, None)
+    return out
+
+
 def attention_units_mt(q: np.ndarray, k_list, v_list, pos, n_threads: int,
                        n_head=N_HEAD, n_kv_head=N_KV_HEAD, head_dim=HEAD_DIM):
     """Multi-threaded oracle over independent (sequence, layer) units."""
@@ -375,3 +392,29 @@ def ref_qkv_layer(wq, wk, wv, bq, bk, bv, x, k_cache, v_cache, pos,
     if rc != 0:
         raise RuntimeError("tgref_qkv_layer failed")
     return q, k, v, out
+
+
+def ref_attention_block(wq, wk, wv, bq, bk, bv, wo, x, original_hidden, k_cache, v_cache,
+                        pos, q_type=TYPE_Q5_0, k_type=TYPE_Q5_0, v_type=TYPE_Q5_0,
+                        o_type=TYPE_Q5_0):
+    """The reference's tmac_gguf.cpp:1045-1140 for one sequence: returns
+    (hidden, q, k, v, context); the caches are updated in place."""
+    q = np.empty(N_HEAD * HEAD_DIM, np.float32)
+    k = np.empty(N_KV_HEAD * HEAD_DIM, np.float32)
+    v = np.empty(N_KV_HEAD * HEAD_DIM, np.float32)
+    ctx = np.empty(N_HEAD * HEAD_DIM, np.float32)
+    att = np.empty(N_HEAD * HEAD_DIM, np.float32)
+    hid = np.empty(N_HEAD * HEAD_DIM, np.float32)
+    keep = [np.ascontiguousarray(b, np.float32) if b is not None else None
+            for b in (bq, bk, bv)]
+    rc = ref().tgref_attention_block(
+        q_type, np.ascontiguousarray(wq, np.uint8).reshape(-1), k_type,
+        np.ascontiguousarray(wk, np.uint8).reshape(-1), v_type,
+        np.ascontiguousarray(wv, np.uint8).reshape(-1), *[_ptr(b) for b in keep], o_type,
+        np.ascontiguousarray(wo, np.uint8).reshape(-1),
+        np.ascontiguousarray(x, np.float32).reshape(-1),
+        np.ascontiguousarray(original_hidden, np.float32).reshape(-1), hid, q, k, v, ctx, att,
+        k_cache.reshape(-1), v_cache.reshape(-1), pos)
+    if rc != 0:
+        raise RuntimeError("tgref_attention_block failed")
+    return hid, q, k, v, ctx

@@ -7,6 +7,7 @@
  *   Q/K/V projection f16_to_f32 :220-232, dequant_q8_0 :240-248,
  *                   dequant_q5_0 :311-328, read_tensor :402-415, matmul's
  *                   CPU loop :508-512, bias adds :1067-1081
+ *   attn_output     matmul + residual add :1129-1140
  * Build: oracle/Makefile (gcc -O2 -ffp-contract=off, no -march=native).
  */
 #include "tg_oracle.h"
@@ -410,6 +411,16 @@ void tgo_qkv_step(int q_type, const uint8_t *wq, int k_type, const uint8_t *wk, 
   /* :1085-1088 RoPE; :1090-1091 cache-write */
   tgo_apply_rope(q, k, n_head, n_kv_head, head_dim, pos, base);
   if (k_cache && v_cache) tgo_cache_write(k_cache, v_cache, k, v, n_kv_head, head_dim, pos);
+}
+
+void tgo_attn_output(int o_type, const uint8_t *wo, const float *context,
+                     const float *original_hidden, float *hidden, int rows, int cols,
+                     float *attn_out) {
+  float *tmp = attn_out ? attn_out : (float *)malloc((size_t)rows * sizeof(float));
+  if (!tmp) return;
+  tgo_matmul_q(o_type, wo, context, tmp, rows, cols);                    /* :1135 */
+  for (int i = 0; i < rows; i++) hidden[i] = original_hidden[i] + tmp[i]; /* :1140 */
+  if (!attn_out) free(tmp);
 }
 
 /* Round a positive or negative binary32 in the half normal range to an

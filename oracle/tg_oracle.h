@@ -153,6 +153,14 @@ void tgo_qkv_step(int q_type, const uint8_t *wq, int k_type,
                   int n_kv_head, int head_dim, int cols, int pos, float base,
                   float *k_cache, float *v_cache);
 
+/* The attn_output matvec and the residual add of forward_layer_with_cache
+ * (tmac_gguf.cpp:1129-1140): attn_out = W_o context (matmul's CPU loop),
+ * then hidden[i] = original_hidden[i] + attn_out[i].  attn_out may be NULL
+ * when the caller does not need it (a rows-long scratch is used). */
+void tgo_attn_output(int o_type, const uint8_t *wo, const float *context,
+                     const float *original_hidden, float *hidden, int rows,
+                     int cols, float *attn_out);
+
 /* Synthetic weight blocks from `seed`: scales d = fp16(d_scale * (0.5 +
  * u)), u uniform in [0, 1); the quant bytes uniform.  n_blocks blocks of
  * `type` are written to out. */

@@ -2,9 +2,9 @@
 // forward_all_layers_fused) on Linux with this library as the backend of its
 // Metal ops: per layer RMSNorm -> fused_qkv_op (Q5_0 q/k, Q8_0 v) and the
 // three bias adds (elem_op 0) -> rope_op x2 -> elem_op(2) x2 (cache-write)
-// -> attention_op -> matmul_q5_0 (attn_output), all inside
-// metal_batch_begin / metal_batch_end, as :1468-1498 encodes them -> residual
-// -> RMSNorm -> gate/up -> SiLU -> down -> residual.  The ops go through
+// -> attention_op -> matmul_q5_0 (attn_output) -> elem_op(0) residual, all
+// inside metal_batch_begin / metal_batch_end, as :1468-1499 encodes them ->
+// RMSNorm -> gate/up -> SiLU -> down -> residual.  The ops go through
 // cuda_backend.hpp with the reference's arguments and host arrays; the
 // norms and the FFN (not on this path) are host-side fp32 stubs.  Weights
 // are seeded blocks of Qwen2-0.5B's shapes (one weight set shared by all
@@ -12,7 +12,8 @@
 // The same loop is run a second time with the CPU oracle in place of the
 // backend (tg_oracle.c: the restatements of matmul's CPU loop
 // :476-513 with dequant_q5_0 / dequant_q8_0, the bias adds :1067-1081 and
-// the decode step :990-1016, :1090-1128), and the hidden states after every
+// the decode step :990-1016, :1090-1128, attn_output + residual
+// :1129-1140), and the hidden states after every
 // token are compared.  Prints PASS / FAIL.
 //
 // usage: forward_model_shim <n_tokens> <device_owned 0|1>
@@ -96,7 +97,8 @@ bool forward(cuda_backend::Context* ctx, const Weights& W, float* hidden, int po
       cuda_backend::attention_op(*ctx, q, &kc[layer][0][0], &vc[layer][0][0], context,
                                  NUM_HEADS, NUM_KV_HEADS, HEAD_DIM, pos);
       cuda_backend::matmul_q5_0(*ctx, HIDDEN_DIM, HIDDEN_DIM, W.wo.data(), context, attn_out);
-      cuda_backend::metal_batch_end();  // attn_out valid on the host
+      cuda_backend::elem_op(*ctx, 0, hidden, attn_out, HIDDEN_DIM);  // residual1, :1499
+      cuda_backend::metal_batch_end();  // hidden valid on the host
       if (ctx->last_status != TG_OK) return false;
     } else {
       tgo_matmul_q(TGO_TYPE_Q5_0, W.wq.data(), scratch, q, HIDDEN_DIM, HIDDEN_DIM);
@@ -106,9 +108,9 @@ bool forward(cuda_backend::Context* ctx, const Weights& W, float* hidden, int po
       for (int i = 0; i < K_DIM; ++i) k[i] += W.bk[i], v[i] += W.bv[i];
       tgo_decode_step(q, k, v, &kc[layer][0][0], &vc[layer][0][0], context, NUM_HEADS,
                       NUM_KV_HEADS, HEAD_DIM, pos, ROPE_BASE, scores.data());
-      tgo_matmul_q(TGO_TYPE_Q5_0, W.wo.data(), context, attn_out, HIDDEN_DIM, HIDDEN_DIM);
+      tgo_attn_output(TGO_TYPE_Q5_0, W.wo.data(), context, hidden, hidden, HIDDEN_DIM,
+                      HIDDEN_DIM, attn_out);
     }
-    for (int i = 0; i < HIDDEN_DIM; ++i) hidden[i] += attn_out[i];
     std::memcpy(scratch, hidden, sizeof(scratch));
     rmsnorm(scratch, HIDDEN_DIM);
     matvec(W.gate, scratch, gate, INTER_DIM, HIDDEN_DIM);

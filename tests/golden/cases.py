@@ -83,7 +83,7 @@ def prefill_inputs(seed: int, S: int, seq: int = 0):
 
 
 # tensor tags of the Q/K/V projection inputs
-T_WQ, T_WK, T_WV, T_BQ, T_BK, T_BV, T_X = 21, 22, 23, 24, 25, 26, 27
+T_WQ, T_WK, T_WV, T_BQ, T_BK, T_BV, T_X, T_WO, T_H = 21, 22, 23, 24, 25, 26, 27, 28, 29
 # d scale per weight type: keeps |q|, |k|, |v| of order 1 for N(0,1) inputs.
 D_SCALE = {O.TYPE_Q5_0: 0.004, O.TYPE_Q8_0: 0.0005}
 
@@ -111,3 +111,13 @@ def qkv_weights(seed: int, v_type: int = O.TYPE_Q5_0, bias: bool = True,
 def qkv_x(seed: int, n_seqs: int = 1, cols: int = QD, layer: int = 0):
     """Normed hidden states x [n_seqs][cols] ~ N(0,1)."""
     return O.normal(O.derive_seed(seed, layer, 0, T_X), n_seqs * cols).reshape(n_seqs, cols)
+
+
+def attn_output_weight(seed: int, o_type: int = O.TYPE_Q5_0, layer: int = 0):
+    """W_o (QD x QD) in o_type blocks."""
+    return O.qblocks(o_type, O.derive_seed(seed, layer, 0, T_WO), QD, QD, D_SCALE[o_type])
+
+
+def residual_in(seed: int, n_seqs: int = 1, layer: int = 0):
+    """The residual stream entering the layer, [n_seqs][QD] ~ N(0,1)."""
+    return O.normal(O.derive_seed(seed, layer, 0, T_H), n_seqs * QD).reshape(n_seqs, QD)

@@ -4,9 +4,10 @@ The outputs come from oracle/_ref/libref.so, i.e. tmac_gguf.cpp:990-1016
 (apply_rope) and :1090-1128 (cache-write + GQA attention) compiled from the
 reference tree by oracle/Makefile.  golden_qkv.npz holds the reference's
 layer step from the normed hidden state (:1045-1128: quantized Q/K/V
-projections, bias adds, RoPE, cache-write, attention) with weights decoded
-by its own f16_to_f32 / dequant_q5_0 / dequant_q8_0 / read_tensor / matmul
-(:220-415, :476-514).  Inputs are regenerated from the seeds
+projections, bias adds, RoPE, cache-write, attention) and the attention
+block (:1045-1140: the same followed by the attn_output matmul and the
+residual add) with weights decoded by its own f16_to_f32 / dequant_q5_0 /
+dequant_q8_0 / read_tensor / matmul (:220-415, :476-514).  Inputs are regenerated from the seeds
 recorded in the file (tests/golden/cases.py), so the fixture stays small.
 
 Run from the repository root where the reference tree is mounted:
@@ -111,6 +112,11 @@ QKV_CASES = [  # (v weight type, biases present, position)
 ]
 
 
+BLOCK_CASES = [  # (v type, attn_output type, biases present, position)
+    (6, 6, 1, 9), (8, 8, 1, 33), (6, 8, 0, 2),
+]
+
+
 def main_qkv() -> None:
     data = {"seed": np.int64(SEED), "cases": np.array(QKV_CASES, dtype=np.int32)}
     outs = {k: [] for k in ("q", "k", "v", "ctx", "sha")}
@@ -129,6 +135,27 @@ def main_qkv() -> None:
     for key in ("q", "k", "v", "ctx"):
         data[f"qkv_{key}"] = np.stack(outs[key])
     data["qkv_in_sha"] = np.array(outs["sha"])
+    # The attention block (tmac_gguf.cpp:1045-1140): the layer step, then
+    # hidden = original_hidden + attn_output . context.
+    data["blk_cases"] = np.array(BLOCK_CASES, dtype=np.int32)
+    hid, shas = [], []
+    for i, (vt, ot, bias, pos) in enumerate(BLOCK_CASES):
+        seed = SEED + 100 + i
+        wq, wk, wv, bq, bk, bv = cases.qkv_weights(seed, vt, bias)
+        wo = cases.attn_output_weight(seed, ot)
+        x = cases.qkv_x(seed)[0]
+        h0 = cases.residual_in(seed)[0]
+        kc = np.zeros((pos + 1, cases.KD), np.float32)
+        vc = np.zeros((pos + 1, cases.KD), np.float32)
+        if pos > 0:
+            kc[:pos] = O.normal(O.derive_seed(seed, 0, 0, cases.T_KC), pos * cases.KD).reshape(pos, -1)
+            vc[:pos] = O.normal(O.derive_seed(seed, 0, 0, cases.T_VC), pos * cases.KD).reshape(pos, -1)
+        shas.append(_sha(wq, wk, wv, *(b for b in (bq, bk, bv) if b is not None), wo, x, h0, kc, vc))
+        h, *_ = O.ref_attention_block(wq, wk, wv, bq, bk, bv, wo, x, h0, kc, vc, pos,
+                                      v_type=vt, o_type=ot)
+        hid.append(h)
+    data["blk_hidden"] = np.stack(hid)
+    data["blk_in_sha"] = np.array(shas)
     _save(OUT_QKV, data)
 
 

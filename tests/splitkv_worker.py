@@ -142,8 +142,26 @@ def main() -> int:
                 if not (np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])):
                     print(f"rank {rank}: x path cache row mismatch seq {i}")
                     ok = False
+        # The attention block (projection, split attention, attn_output +
+        # residual on every rank) against the one-GPU block.
+        wo = cases.attn_output_weight(81, 6)
+        h0 = cases.residual_in(82, B)
+        hid = h0.copy()
+        kv.attention_block(0, W, wo, X, positions, hid, o_type=6, split=True)
+        full2 = tg.KVCache(be, 1, B, gctx, dtype=dt)
+        for i, p in enumerate(positions):
+            _, _, _, kc, vc = cases.decode_inputs(78, p, bf16, seq=i)
+            if p > 0:
+                full2.write_rows(0, i, 0, kc[:p], vc[:p])
+        hid_ref = h0.copy()
+        full2.attention_block(0, W, wo, X, positions, hid_ref, o_type=6)
+        full2.destroy()
+        err = float(np.abs(hid - hid_ref).max())
+        if err > 2e-4:
+            print(f"rank {rank}: attention block bf16={bf16} err={err}")
+            ok = False
         if rank == 0:
-            print(f"x path bf16={bf16} exchange {be.exchange}")
+            print(f"x path bf16={bf16} exchange {be.exchange} block err {err:.2e}")
         kv.destroy()
         full.destroy()
     be.comm_destroy()

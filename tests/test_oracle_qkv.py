@@ -59,6 +59,30 @@ def test_qkv_step_matches_reference_golden(golden_qkv, O, cases):
         assert np.array_equal(bits(kc[pos]), bits(k)) and np.array_equal(bits(vc[pos]), bits(v))
 
 
+def test_attention_block_matches_reference_golden(golden_qkv, O, cases):
+    """Projection step + attention + attn_output matmul + residual add of the
+    oracle equal the reference's tmac_gguf.cpp:1045-1140 bit for bit."""
+    seed0 = int(golden_qkv["seed"])
+    for i, (vt, ot, bias, pos) in enumerate(golden_qkv["blk_cases"]):
+        vt, ot, pos = int(vt), int(ot), int(pos)
+        seed = seed0 + 100 + i
+        wq, wk, wv, bq, bk, bv = cases.qkv_weights(seed, vt, bool(bias))
+        wo = cases.attn_output_weight(seed, ot)
+        x = cases.qkv_x(seed)[0]
+        h0 = cases.residual_in(seed)[0]
+        kc = np.zeros((pos + 1, cases.KD), np.float32)
+        vc = np.zeros((pos + 1, cases.KD), np.float32)
+        if pos > 0:
+            kc[:pos] = O.normal(O.derive_seed(seed, 0, 0, cases.T_KC), pos * cases.KD).reshape(pos, -1)
+            vc[:pos] = O.normal(O.derive_seed(seed, 0, 0, cases.T_VC), pos * cases.KD).reshape(pos, -1)
+        sha = _sha(wq, wk, wv, *(b for b in (bq, bk, bv) if b is not None), wo, x, h0, kc, vc)
+        assert sha == str(golden_qkv["blk_in_sha"][i])
+        q, k, v = O.qkv_step(wq, wk, wv, bq, bk, bv, x, pos, v_type=vt, k_cache=kc, v_cache=vc)
+        ctx = O.attention(q, kc, vc, pos)
+        hid = O.attn_output(ot, wo, ctx, h0)
+        assert np.array_equal(bits(hid), bits(golden_qkv["blk_hidden"][i])), i
+
+
 def test_f16_widening_known_answers(O):
     L = O.lib()
     known = {0x0000: 0.0, 0x8000: 0.0, 0x3c00: 1.0, 0xc000: -2.0, 0x0001: 2.0 ** -24,

@@ -1,7 +1,9 @@
 """Parity of the CUDA Q/K/V projection (tg_qkv.cu) with the CPU oracle,
 through the C ABI: fused_qkv_op / matmul_q (the reference's operator
-surface, metal_backend.hpp:320-338 and :456-489) and the fused layer step
-tg_qkv_rope_cache_write / tg_decode_layer_x (tmac_gguf.cpp:1046-1128).
+surface, metal_backend.hpp:320-338 and :456-489), the fused layer step
+tg_qkv_rope_cache_write / tg_decode_layer_x (tmac_gguf.cpp:1046-1128), the
+attn_output matvec with its residual add (tg_attn_output, :1129-1140) and
+the whole attention block (tg_attention_block, :1045-1140).
 
 Bars, written per check:
   * weight decoding is exact: the kernel's products use the dequantised
@@ -281,6 +283,53 @@ def test_decode_layer_x_matches_oracle(tg, backend, O, cases, bf16):
         ref = O.attention(q_out[i], kc, vc, pos)
         err = float(np.max(np.abs(out[i].astype(np.float64) - ref)))
         assert err <= tol, (i, pos, err)
+    kv.destroy()
+    kv2.destroy()
+
+
+@pytest.mark.parametrize("B,ot", [(1, 6), (1, 8), (20, 6)])
+def test_attn_output_matches_oracle(tg, backend, O, cases, B, ot):
+    """hidden += W_o context (tmac_gguf.cpp:1129-1140): the product within
+    the summation-order bound, then one rounding of the add.  B = 20 takes
+    the batched kernel."""
+    wo = cases.attn_output_weight(801 + B, ot)
+    ctx = O.normal(802, B * cases.QD).reshape(B, cases.QD)
+    h0 = cases.residual_in(803, B)
+    hid = h0.copy()
+    backend.attn_output(ot, wo, cases.QD, cases.QD, ctx, hid, n_seqs=B)
+    Wf = dequant_np(O, ot, wo, cases.QD, cases.QD)
+    for s in range(B):
+        ref = O.attn_output(ot, wo, ctx[s], h0[s])
+        check_within(hid[s], ref, sum_bound(Wf, ctx[s]) + ulp(ref), f"seq {s}")
+
+
+@pytest.mark.parametrize("bf16", [False, True], ids=["f32", "bf16"])
+@pytest.mark.parametrize("B", [5, 12])
+def test_attention_block_matches_oracle(tg, backend, O, cases, bf16, B):
+    """x -> projection -> attention -> hidden += W_o context in one call.
+    The attention part is checked through decode_layer_x on a copy of the
+    cache state (test_decode_layer_x_matches_oracle bounds it against the
+    oracle); hidden must equal h0 + W_o . context of that context within
+    the summation-order bound."""
+    rng = np.random.default_rng(B)
+    positions = [int(v) for v in rng.integers(0, 200, size=B)]
+    seed = 900 + B
+    kv, W, X, refs, bounds = _layer_case(tg, backend, O, cases, positions, bf16, 8, True, seed)
+    kv2, W2, X2, _, _ = _layer_case(tg, backend, O, cases, positions, bf16, 8, True, seed)
+    wo = cases.attn_output_weight(seed, 6)
+    h0 = cases.residual_in(seed, B)
+    hid = h0.copy()
+    kv.attention_block(0, W, wo, X, positions, hid, o_type=6)
+    ctx = np.zeros((B, cases.QD), np.float32)
+    kv2.decode_layer_x(0, W2, X2, positions, ctx)
+    Wf = dequant_np(O, 6, wo, cases.QD, cases.QD)
+    for s in range(B):
+        ref = O.attn_output(6, wo, ctx[s], h0[s])
+        check_within(hid[s], ref, sum_bound(Wf, ctx[s]) + ulp(ref), f"seq {s}")
+        # and the caches hold the same new rows
+        a = kv.read_rows(0, s, positions[s], 1)
+        b = kv2.read_rows(0, s, positions[s], 1)
+        assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
     kv.destroy()
     kv2.destroy()
 

@@ -152,6 +152,12 @@ _SIGS = {
                                     C.POINTER(tg_qkv_weights), _vp, _vp, _vp]),
     "tg_decode_layer_splitkv_x": (C.c_int, [_vp, _vp, C.c_int, C.c_int,
                                             C.POINTER(tg_qkv_weights), _vp, _vp, _vp]),
+    "tg_attn_output": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp]),
+    "tg_attention_block": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.POINTER(tg_qkv_weights),
+                                     C.c_int, _vp, _vp, _vp, _vp]),
+    "tg_attention_block_splitkv": (C.c_int, [_vp, _vp, C.c_int, C.c_int,
+                                             C.POINTER(tg_qkv_weights), C.c_int, _vp, _vp,
+                                             _vp, _vp]),
 }
 
 _lib: Optional[C.CDLL] = None
@@ -355,6 +361,12 @@ class CudaBackend:
                                      q_rows, k_rows, v_rows, cols,
                                      1 if v_is_q8 else 0))
 
+    def attn_output(self, wtype: int, w_o, rows: int, cols: int, context, hidden,
+                    n_seqs: int = 1) -> None:
+        """hidden += W_o context (tg_attn_output; tmac_gguf.cpp:1497-1499)."""
+        _check(lib().tg_attn_output(self._h, n_seqs, wtype, _ptr(w_o), rows, cols,
+                                    _ptr(context), _ptr(hidden)))
+
     def matmul_q(self, wtype: int, rows: int, cols: int, w, x, y) -> None:
         """metal_backend::matmul_q5_0 / matmul_q8_0 (metal_backend.hpp:320-338)."""
         _check(lib().tg_matmul_q(self._h, wtype, rows, cols, _ptr(w), _ptr(x), _ptr(y)))
@@ -520,6 +532,16 @@ class KVCache:
         pos = _as_i32(pos)
         _check(lib().tg_decode_layer_x(self.backend.handle, self._h, layer, n,
                                        C.byref(weights.desc), _ptr(x), _ptr(pos), _ptr(out)))
+
+    def attention_block(self, layer: int, weights: "QKVWeights", w_o, x, pos, hidden,
+                        o_type: int = WTYPE_Q5_0, split: bool = False) -> None:
+        """x -> projection -> attention -> hidden += W_o context
+        (tg_attention_block / tg_attention_block_splitkv)."""
+        n = len(pos)
+        pos = _as_i32(pos)
+        fn = lib().tg_attention_block_splitkv if split else lib().tg_attention_block
+        _check(fn(self.backend.handle, self._h, layer, n, C.byref(weights.desc), o_type,
+                  _ptr(w_o), _ptr(x), _ptr(pos), _ptr(hidden)))
 
     def decode_layer_splitkv_x(self, layer: int, weights: "QKVWeights", x, pos,
                                out) -> None:

@@ -162,6 +162,7 @@ struct tg_context {
   uint16_t* qbf = nullptr;   size_t qbf_cap = 0;     // prefill: rotated bf16 q
   uint16_t* vh = nullptr;     size_t vh_cap = 0;   // prefill: fp16 copy of v
   float* qx = nullptr;        size_t qx_cap = 0;   // decode from x: rotated q
+  float* cx = nullptr;        size_t cx_cap = 0;   // attention block: context
   std::vector<PendingCopy> pending;  // device -> host copies of staged outputs
   // Host inputs of the current call, moved to the arena by commit_inputs.
   struct PackEntry {
@@ -1271,6 +1272,7 @@ int tg_shutdown(tg_context* ctx) {
   cudaFree(ctx->qbf);
   cudaFree(ctx->vh);
   cudaFree(ctx->qx);
+  cudaFree(ctx->cx);
   cudaFree(ctx->d_err);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -1746,6 +1748,48 @@ int tg_decode_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, flo
 
 // ------------------------------------------------ Q/K/V projection
 
+namespace {
+// hidden[s] += W_o ctx[s] on device x / hidden (mode 2 of the projection
+// kernel); W_o resolved by weight_ptr.
+int attn_output_core(tg_context* ctx, int n, int wtype, const void* w_o, int rows, int cols,
+                     const float* dctx, float* dhidden) {
+  TG_TRY(check_wtype(wtype, "w_o"));
+  TG_TRY(check_qkv_cols(cols));
+  if (rows <= 0) return fail(TG_ERR_INVALID_ARG, "attn_output: rows %d", rows);
+  const void* dw = nullptr;
+  TG_TRY(weight_ptr(ctx, w_o, (size_t)rows * qrow_bytes(wtype, cols), &dw));
+  TG_TRY(check_align2(dw, "w_o"));
+  tg::QkvParams p{};
+  p.w[0] = static_cast<const uint8_t*>(dw);
+  p.wtype[0] = p.wtype[1] = p.wtype[2] = wtype;
+  p.rows[0] = rows;
+  p.y[0] = dhidden;
+  p.cols = cols;
+  p.x = dctx;
+  p.B = n;
+  p.mode = 2;
+  return run_qkv(ctx, p);
+}
+}  // namespace
+
+int tg_attn_output(tg_context* ctx, int n_seqs, int wtype, const void* w_o, int rows, int cols,
+                   const float* context, float* hidden) {
+  TG_TRY(set_device(ctx));
+  if (n_seqs < 0 || !w_o || !context || !hidden)
+    return fail(TG_ERR_INVALID_ARG, "attn_output: bad arguments");
+  if (n_seqs == 0) return TG_OK;
+  TG_TRY(check_wtype(wtype, "w_o"));
+  TG_TRY(check_qkv_cols(cols));
+  if (rows <= 0) return fail(TG_ERR_INVALID_ARG, "attn_output: rows %d", rows);
+  const void* dc = nullptr;
+  void* dh = nullptr;
+  TG_TRY(stage_in(ctx, context, (size_t)n_seqs * cols * 4, &dc));
+  TG_TRY(stage_out(ctx, hidden, (size_t)n_seqs * rows * 4, true, &dh));
+  TG_TRY(attn_output_core(ctx, n_seqs, wtype, w_o, rows, cols, static_cast<const float*>(dc),
+                          static_cast<float*>(dh)));
+  return finish_call(ctx);
+}
+
 int tg_fused_qkv_op(tg_context* ctx, const uint8_t* W_q, const uint8_t* W_k, const uint8_t* W_v,
                     const float* x, float* y_q, float* y_k, float* y_v, int q_rows, int k_rows,
                     int v_rows, int cols, int v_is_q8) {
@@ -2154,6 +2198,56 @@ int tg_decode_layer_splitkv_x(tg_context* ctx, tg_kv_cache* kv, int layer, int n
   TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, ctx->qx, nullptr, nullptr,
                       static_cast<const int*>(dp), static_cast<float*>(dout), false));
   return finish_call(ctx);
+}
+
+namespace {
+int attention_block(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs,
+                    const tg_qkv_weights* w, int o_type, const void* w_o, const float* x,
+                    const int32_t* pos, float* hidden, bool split) {
+  TG_TRY(check_kv_call(ctx, kv, layer, n_seqs));
+  if (!w || !w_o || !x || !pos || !hidden) return fail(TG_ERR_INVALID_ARG, "null argument");
+  if (n_seqs == 0) return TG_OK;
+  TG_TRY(check_qkv_cols(w->cols));
+  TG_TRY(check_host_pos(pos, n_seqs, split ? kv->global_ctx : kv->d.shard_start + kv->d.max_ctx,
+                        "pos"));
+  const tg_kv_desc& d = kv->d;
+  const int qdim = d.n_head * d.head_dim;
+  const size_t qb = (size_t)n_seqs * qdim * 4;
+  const void *dx = nullptr, *dp = nullptr;
+  void* dh = nullptr;
+  TG_TRY(stage_in(ctx, x, (size_t)n_seqs * w->cols * 4, &dx));
+  TG_TRY(stage_in(ctx, pos, (size_t)n_seqs * 4, &dp));
+  TG_TRY(stage_out(ctx, hidden, qb, true, &dh));
+  TG_TRY(ensure_buf(ctx, &ctx->qx, &ctx->qx_cap, qb / 4));
+  TG_TRY(ensure_buf(ctx, &ctx->cx, &ctx->cx_cap, qb / 4));
+  TG_TRY(qkv_layer_core(ctx, kv, layer, n_seqs, w, static_cast<const float*>(dx),
+                        static_cast<const int*>(dp), ctx->qx));
+  if (split) {
+    TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, ctx->qx, nullptr, nullptr,
+                        static_cast<const int*>(dp), ctx->cx, false));
+  } else if (mma_eligible(kv)) {
+    TG_TRY(run_fused(ctx, kv, layer, n_seqs, ctx->qx, nullptr, nullptr, nullptr,
+                     static_cast<const int*>(dp), ctx->cx, nullptr, 0, false, false));
+  } else {
+    TG_TRY(run_decode(ctx, kv, layer, n_seqs, ctx->qx, static_cast<const int*>(dp), 0, ctx->cx,
+                      0));
+  }
+  TG_TRY(attn_output_core(ctx, n_seqs, o_type, w_o, qdim, qdim, ctx->cx,
+                          static_cast<float*>(dh)));
+  return finish_call(ctx);
+}
+}  // namespace
+
+int tg_attention_block(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs,
+                       const tg_qkv_weights* w, int o_type, const void* w_o, const float* x,
+                       const int32_t* pos, float* hidden) {
+  return attention_block(ctx, kv, layer, n_seqs, w, o_type, w_o, x, pos, hidden, false);
+}
+
+int tg_attention_block_splitkv(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs,
+                               const tg_qkv_weights* w, int o_type, const void* w_o,
+                               const float* x, const int32_t* pos, float* hidden) {
+  return attention_block(ctx, kv, layer, n_seqs, w, o_type, w_o, x, pos, hidden, true);
 }
 
 // ------------------------------------------------ prefill

@@ -5,7 +5,9 @@
 //                blocks (GGML Q5_0 / Q8_0, tmac_gguf.cpp:240-248, :311-328;
 //                kernel_fused_qkv.metal:8-70).  Mode 0 writes y_m as
 //                fused_qkv_op / matmul_q5_0 / matmul_q8_0 do
-//                (metal_backend.hpp:320-338, :456-489).  Mode 1 fuses the
+//                (metal_backend.hpp:320-338, :456-489); mode 2 adds W x to
+//                y in place, the attn_output matvec with its residual add
+//                (tmac_gguf.cpp:1497-1499).  Mode 1 fuses the
 //                rest of the layer step up to attention
 //                (tmac_gguf.cpp:1067-1091): the bias adds, RoPE of q and k
 //                at each sequence's position (cos/sin from the host-libm
@@ -285,12 +287,15 @@ __global__ void __launch_bounds__(QKV_THREADS) qkv_kernel(const QkvParams p) {
   }
   __syncthreads();
   // 4. Epilogue (a thread's first item uses the values loaded above).
-  if (p.mode == 0) {
+  if (p.mode != 1) {
+    // Mode 0: y = W x (+ bias).  Mode 2: y += W x, the residual add of
+    // tmac_gguf.cpp:1499 (elem_op 0) rounded once after the product sum.
     for (int i = tid; i < ns * nr; i += QKV_THREADS) {
       const int s = i / nr, r = i - s * nr;
       float y = ys[s * kQkvRows + r];
       if (bias) y = __fadd_rn(y, i == tid ? pre_b0 : bias[r0 + r]);
-      p.y[m][(size_t)(s_begin + s) * rows + r0 + r] = y;
+      float* dst = p.y[m] + (size_t)(s_begin + s) * rows + r0 + r;
+      *dst = p.mode == 2 ? __fadd_rn(*dst, y) : y;
     }
   } else if (m < 2) {
     // q or k: bias, then the rotation of pairs (2i, 2i+1) of a head
@@ -398,12 +403,14 @@ __device__ __forceinline__ void qg_store_pair(const QkvParams& p, int m, int row
   }
 }
 
-// Mode 0 output, or mode 1 v row (bias, cache row, v_out).
+// Mode 0 / 2 output (2: added to y), or mode 1 v row (bias, cache row,
+// v_out).
 __device__ __forceinline__ void qg_store_one(const QkvParams& p, int m, int rows, int r, int seq,
                                              float y, const float* bias) {
   if (bias) y = __fadd_rn(y, bias[r]);
-  if (p.mode == 0) {
-    p.y[m][(size_t)seq * rows + r] = y;
+  if (p.mode != 1) {
+    float* dst = p.y[m] + (size_t)seq * rows + r;
+    *dst = p.mode == 2 ? __fadd_rn(*dst, y) : y;
     return;
   }
   if (p.v_out) p.v_out[(size_t)seq * rows + r] = y;

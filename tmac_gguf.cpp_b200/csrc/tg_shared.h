@@ -183,7 +183,8 @@ struct FusedParams {
 // Q/K/V projection of one layer (tg_qkv.cu): y_m = W_m x (+ bias) for the
 // three weight matrices m = 0 (q), 1 (k), 2 (v) and B input vectors, with
 // weights in the model file's 32-element blocks (GGML Q5_0 / Q8_0).  Mode 0
-// writes y_m; mode 1 is the layer step of tmac_gguf.cpp:1067-1091: bias,
+// writes y_m; mode 2 adds W_m x to y_m (the attn_output matvec and its
+// residual add); mode 1 is the layer step of tmac_gguf.cpp:1067-1091: bias,
 // RoPE of q and k at pos[s], the k / v rows into the cache, rotated q out.
 constexpr int kWTypeQ5_0 = 6;   // 22-byte blocks: fp16 d, 32 high bits, 16 nibble bytes
 constexpr int kWTypeQ8_0 = 8;   // 34-byte blocks: fp16 d, 32 int8
@@ -199,7 +200,7 @@ TG_HD int wtype_block_bytes(int t) {
 struct QkvParams {
   const uint8_t* w[3];     // row-major rows of cols/32 blocks
   const float* bias[3];    // or null (a model without that bias)
-  float* y[3];             // mode 0: [B][rows[m]]
+  float* y[3];             // modes 0 / 2: [B][rows[m]]
   int wtype[3];
   int rows[3];             // 0 rows: matrix absent
   int tiles[3];            // CTAs of each matrix: ceil(rows / rows per CTA of the path)
