@@ -62,15 +62,18 @@ WORKLOADS = {
     # BASELINE config 1
     "cfg1": dict(B=1, ctx=256, layers=24, dtype="f32", split=False,
                  desc="config1: single sequence, pos=255, fp32 KV, 24 layers"),
-    # config 1 and config 3 entered from the normed hidden state: the Q/K/V
-    # projection (Q5_0 q/k, Q8_0 v), biases, RoPE and cache-write fused in
-    # one kernel ahead of attention (tmac_gguf.cpp:1046-1128)
+    # config 1 and config 3 run as the whole attention block of a layer
+    # (tmac_gguf.cpp:1045-1140): the Q/K/V projection (Q5_0 q/k, Q8_0 v)
+    # with biases, RoPE and cache-write fused in one kernel, attention, and
+    # the Q5_0 attn_output matvec with its residual add into the hidden state
     "qkv": dict(B=1, ctx=256, layers=24, dtype="f32", split=False, qkv=True,
-                desc="config1 from x: Q5_0/Q8_0 q/k/v projection + bias + RoPE + cache-write "
-                     "+ attention, B=1, pos=255, fp32 KV, 24 layers"),
+                desc="config1 as attention blocks: x -> Q5_0/Q8_0 q/k/v projection + bias + "
+                     "RoPE + cache-write -> attention -> Q5_0 attn_output + residual, B=1, "
+                     "pos=255, fp32 KV, 24 layers"),
     "qkv_batched": dict(B=256, ctx=4096, layers=24, dtype="bf16", split=False, qkv=True,
-                        desc="config3 from x: Q5_0/Q8_0 q/k/v projection + bias + RoPE + "
-                             "cache-write + attention, B=256, ctx=4096, bf16 KV, 24 layers"),
+                        desc="config3 as attention blocks: x -> Q5_0/Q8_0 q/k/v projection + "
+                             "bias + RoPE + cache-write -> attention -> Q5_0 attn_output + "
+                             "residual, B=256, ctx=4096, bf16 KV, 24 layers"),
     # BASELINE config 5
     "prefill": dict(B=16, ctx=2048, layers=1, dtype="bf16", split=False, prefill=True,
                     desc="config5: causal prefill, B=16 per GPU, S=2048, 14Q/2KV heads, d=64, "
@@ -155,11 +158,22 @@ def qkv_weight_bytes():
     return (QD + KD) * nb * 22 + KD * nb * 34
 
 
+def wo_weight_bytes():
+    """Bytes of one layer's attn_output weight (Q5_0, QD x QD)."""
+    return QD * (QD // 32) * 22
+
+
 def qkv_kernel_bytes(wl, B):
     """Algorithmic bytes of one projection launch: the weights once, x read,
     rotated q written, the new k / v rows written."""
     s_kv = 2 if wl["dtype"] == "bf16" else 4
     return qkv_weight_bytes() + B * (QD * 4 + QD * 4 + 2 * KD * s_kv)
+
+
+def attn_output_bytes(B):
+    """Algorithmic bytes of one attn_output launch: W_o once, the context
+    read, the hidden state read and written."""
+    return wo_weight_bytes() + B * 3 * QD * 4
 
 
 def synth_qblocks(rng, wtype, rows, cols, d_scale):
@@ -276,20 +290,24 @@ def time_reference_cpu(O, wl, n_units, n_threads, reps=1):
 
 
 def qkv_cpu_weights(O):
-    """One layer's projection weights for the CPU legs (Q5_0 q/k, Q8_0 v)."""
+    """One layer's attention-block weights for the CPU legs (Q5_0 q/k, Q8_0
+    v, biases, Q5_0 attn_output)."""
     return (O.qblocks(O.TYPE_Q5_0, 101, QD, QD, 0.004), O.qblocks(O.TYPE_Q5_0, 102, KD, QD, 0.004),
             O.qblocks(O.TYPE_Q8_0, 103, KD, QD, 0.0005), O.normal(104, QD) * np.float32(0.1),
-            O.normal(105, KD) * np.float32(0.1), O.normal(106, KD) * np.float32(0.1))
+            O.normal(105, KD) * np.float32(0.1), O.normal(106, KD) * np.float32(0.1),
+            O.qblocks(O.TYPE_Q5_0, 107, QD, QD, 0.004))
 
 
 def run_reference_qkv_units(O, W, x, ks, vs, ps, n_threads):
-    """The reference's layer step from x (tmac_gguf.cpp:1045-1128: quantized
-    projections, biases, RoPE, cache-write, attention) on every unit,
-    fanned out over n_threads (ctypes drops the GIL during each call)."""
+    """The reference's attention block (tmac_gguf.cpp:1045-1140: quantized
+    projections, biases, RoPE, cache-write, attention, attn_output matmul,
+    residual add) on every unit, fanned out over n_threads (ctypes drops the
+    GIL during each call)."""
     from concurrent.futures import ThreadPoolExecutor
+    h0 = O.normal(108, QD)
 
     def one(u):
-        O.ref_qkv_layer(*W, x[u], ks[u], vs[u], int(ps[u]), v_type=O.TYPE_Q8_0)
+        O.ref_attention_block(*W, x[u], h0, ks[u], vs[u], int(ps[u]), v_type=O.TYPE_Q8_0)
 
     if n_threads <= 1:
         for u in range(len(ps)):
@@ -305,8 +323,8 @@ def time_reference_qkv_cpu(O, wl, n_units, n_threads):
     t = time.perf_counter()
     run_reference_qkv_units(O, W, x, ks, vs, ps, n_threads)
     dt = time.perf_counter() - t
-    return ((unit_bytes(wl, ps) + n_units * qkv_weight_bytes()) / dt / 1e9, dt,
-            int(np.sum(ps + 1)))
+    return ((unit_bytes(wl, ps) + n_units * (qkv_weight_bytes() + wo_weight_bytes() + 2 * QD * 4))
+            / dt / 1e9, dt, int(np.sum(ps + 1)))
 
 
 def run_reference_arm(args, wl, rank, world):
@@ -330,7 +348,7 @@ def run_reference_arm(args, wl, rank, world):
         if kind == "reference":
             W = qkv_cpu_weights(O)
             run = lambda q, ks, vs, ps, nt: run_reference_qkv_units(O, W, q, ks, vs, ps, nt)
-            extra = n_units * qkv_weight_bytes()
+            extra = n_units * (qkv_weight_bytes() + wo_weight_bytes() + 2 * QD * 4)
         else:
             print(json.dumps({"impl": "reference", "unavailable":
                               "the projection workloads need the reference build "
@@ -580,7 +598,7 @@ def main():
         # One weight set per layer (device-resident model constants); the
         # step's input is the normed hidden state x, in q's place.
         rng = np.random.default_rng(77 + rank)
-        weights = []
+        weights, w_out = [], []
         for _ in range(L):
             wq = torch.from_numpy(synth_qblocks(rng, 6, QD, QD, 0.004)).cuda()
             wk = torch.from_numpy(synth_qblocks(rng, 6, KD, QD, 0.004)).cuda()
@@ -590,11 +608,13 @@ def main():
             bv = torch.randn(KD, device="cuda", generator=g) * 0.1
             weights.append(tg.QKVWeights(wq, wk, wv, QD, v_type=tg.WTYPE_Q8_0, b_q=bq,
                                          b_k=bk, b_v=bv))
+            w_out.append(torch.from_numpy(synth_qblocks(rng, 6, QD, QD, 0.004)).cuda())
 
     def step(qs, ks, vs, ps, os_):
         for l in range(L):
-            if qkv:
-                kv.decode_layer_x(l, weights[l], qs[l], ps, os_[l])
+            if qkv:   # x = qs[l]; the residual stream os_[l] is read and written
+                kv.attention_block(l, weights[l], w_out[l], qs[l], ps, os_[l],
+                                   o_type=tg.WTYPE_Q5_0)
             elif split:
                 kv.decode_layer_splitkv(l, qs[l], ks[l], vs[l], ps, os_[l])
             else:
@@ -628,7 +648,7 @@ def main():
     # A step whose inputs fit twice in L2 is timed alone between L2 flushes
     # (a 512 MB write on the same stream, outside the events); larger steps
     # stream their inputs from HBM on their own and run back to back.
-    wbytes = L * qkv_weight_bytes() if qkv else 0
+    wbytes = L * (qkv_weight_bytes() + wo_weight_bytes()) if qkv else 0
     gpu_step_bytes = algo_bytes_step(wl, pos) / (world if wl["split"] else 1) + wbytes
     flush = gpu_step_bytes < 2 * L2_BYTES
     flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device="cuda") if flush else None
@@ -663,7 +683,10 @@ def main():
     ms_total = max_over_ranks(ms_local)
     clocks = sampler.stop(t_wall0, t_wall1) if sampler else None
     ms_step = ms_total / args.steps
-    bytes_step = (algo_bytes_step(wl, pos) + wbytes) * (1 if wl["split"] else world)
+    # The attention block also reads and writes the hidden state (x stands in
+    # for q in the attention bytes; the context stays on the device).
+    hbytes = L * B * 2 * QD * 4 if qkv else 0
+    bytes_step = (algo_bytes_step(wl, pos) + wbytes + hbytes) * (1 if wl["split"] else world)
     seqs_step = B * (1 if wl["split"] else world)
     value = bytes_step / (ms_step * 1e-3) / 1e9
 
@@ -683,7 +706,9 @@ def main():
         kms += ms_i
         kn_launch += n_i
     gprof.destroy()
-    k_bytes = (qkv_kernel_bytes(wl, B) if qkv
+    # Projection workloads time both projection-class launches of a layer
+    # (the Q/K/V kernel and attn_output): bytes per launch is their mean.
+    k_bytes = ((qkv_kernel_bytes(wl, B) + attn_output_bytes(B)) / 2 if qkv
                else kernel_bytes_launch(wl, pos, shard_start, shard_len, split))
     k_avg_ms = kms / max(kn_launch, 1)
     hbm_peak, peak_kind = peaks()
@@ -712,8 +737,8 @@ def main():
         e2e_step()
     e2e_s = max_over_ranks(time.perf_counter() - t)
     e2e_value = bytes_step * e2e_steps / e2e_s / 1e9
-    if qkv:   # x in, context out; weights and caches stay on the device
-        h2d = L * B * QD * 4 + L * B * 4
+    if qkv:   # x and the hidden state in, hidden out; weights and caches stay
+        h2d = L * B * QD * 4 * 2 + L * B * 4
         d2h = L * B * QD * 4
     else:
         h2d = L * B * (QD + 2 * KD) * 4 + L * B * 4
@@ -732,8 +757,9 @@ def main():
             cpu = {"value": gbs, "unit": "GB/s", "cores": 1, "kind": "reference",
                    "sample": f"{n_units} (sequence, layer) units at the workload's positions "
                              f"({npos} cache rows, {dt:.2f} s), reference code single-threaded "
-                             "as it runs" + ("; its layer step from x (tmac_gguf.cpp:1045-1128, "
-                                             "Q5_0/Q8_0 projections + attention)" if qkv else "")
+                             "as it runs" + ("; its attention block from x (tmac_gguf.cpp:"
+                                             "1045-1140: Q5_0/Q8_0 projections, attention, "
+                                             "attn_output, residual)" if qkv else "")
                              + "; fp32 caches of bf16-rounded values, bytes counted as "
                              "the workload's"}
 
@@ -760,7 +786,10 @@ def main():
             "gpu_launches": launches,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak,
                          "unit": "GB/s", "frac": achieved / hbm_peak,
-                         "peak_kind": peak_kind, "kernel": "qkv_kernel" if qkv else
+                         "peak_kind": peak_kind,
+                         "kernel": ("projection kernels (q/k/v + attn_output), "
+                                    + ("qkv_gemm_kernel" if B >= 9 else "qkv_kernel"))
+                         if qkv else
                          ("decode_fused_kernel" if kv.uses_tensor_cores()
                           else "decode_generic_kernel"),
                          "bytes_per_launch": k_bytes, "launch_ms": k_avg_ms,
