@@ -203,6 +203,41 @@ typedef struct tg_qkv_weights {
   const float* b_v;
 } tg_qkv_weights;
 
+/* ------------------------------------------------- model files */
+
+/* A TMAC model file (scripts/extract_tmac.py:6-23: "TMAC", uint64 count,
+ * then per tensor uint64 name_len, name, uint64 rows, uint64 cols, uint32
+ * GGUF type, uint64 n_bytes, data) loaded into device memory -- load_tmac
+ * (tmac_gguf.cpp:1372-1425) with the reference's 512 MB host region
+ * replaced by one device allocation (tensors at 256-byte aligned offsets).
+ * The table keeps what load_tmac keeps: names cut to 127 characters, rows
+ * (outputs), cols (inputs), type and size; the magic is read, not checked,
+ * as there.  A truncated file or an unreadable path gives
+ * TG_ERR_INVALID_ARG. */
+typedef struct tg_model tg_model;
+typedef struct tg_tensor_info {
+  const char* name;   /* NULL when tg_model_find does not find the name */
+  uint64_t rows, cols, n_bytes;
+  uint32_t type;      /* GGUF type code: 0 F32, 6 Q5_0, 8 Q8_0, ... */
+  const void* data;   /* device address */
+} tg_tensor_info;
+
+TG_API int tg_model_load_tmac(tg_context* ctx, const char* path, tg_model** out);
+TG_API int tg_model_destroy(tg_model* m);
+TG_API int tg_model_count(tg_model* m, int* n_tensors);
+TG_API int tg_model_tensor_at(tg_model* m, int index, tg_tensor_info* out);
+/* get_tensor_info (tmac_gguf.cpp:417-422): the first tensor of that name;
+ * out->name == NULL (status TG_OK) when there is none. */
+TG_API int tg_model_find(tg_model* m, const char* name, tg_tensor_info* out);
+/* Copy the first `bytes` of tensor `index` to host memory. */
+TG_API int tg_model_read(tg_model* m, int index, void* dst, size_t bytes);
+/* One layer's attention weights, blk.<layer>.attn_{q,k,v}.weight, the fp32
+ * biases blk.<layer>.attn_{q,k,v}.bias (NULL when absent) and
+ * blk.<layer>.attn_output.weight (*w_o NULL and *o_type -1 when absent),
+ * ready for tg_decode_layer_x / tg_attention_block. */
+TG_API int tg_model_layer_attention(tg_model* m, int layer, tg_qkv_weights* w,
+                                    const void** w_o, int* o_type);
+
 /* ------------------------------------------------- device KV caches */
 
 /* A device-resident cache replacing the static g_k_cache / g_v_cache

@@ -135,6 +135,14 @@ def ref():
             C.c_int, _u8p, C.c_int, _u8p, C.c_int, _u8p, C.c_void_p, C.c_void_p,
             C.c_void_p, C.c_int, _u8p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
             _f32p, _f32p, _f32p, C.c_int]
+        R.tgref_load_tmac.restype = C.c_int
+        R.tgref_load_tmac.argtypes = [C.c_char_p]
+        R.tgref_tmac_count.restype = C.c_int
+        R.tgref_tmac_tensor.restype = C.c_int
+        R.tgref_tmac_tensor.argtypes = [C.c_int, C.c_char_p, C.POINTER(C.c_uint64),
+                                        C.POINTER(C.c_uint64), C.POINTER(C.c_uint32),
+                                        C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
+        R.tgref_tmac_ddr.restype = C.c_void_p
         R.tgref_qkv_layer.restype = C.c_int
         R.tgref_qkv_layer.argtypes = [C.c_int, _u8p, C.c_int, _u8p, C.c_int, _u8p,
                                       C.c_void_p, C.c_void_p, C.c_void_p, _f32p,
@@ -418,3 +426,22 @@ def ref_attention_block(wq, wk, wv, bq, bk, bv, wo, x, original_hidden, k_cache,
     if rc != 0:
         raise RuntimeError("tgref_attention_block failed")
     return hid, q, k, v, ctx
+
+
+def ref_load_tmac(path: str):
+    """The reference's load_tmac (tmac_gguf.cpp:1372-1425): returns its
+    status and the table it built, a list of (name, rows, cols, type,
+    n_bytes, data bytes)."""
+    R = ref()
+    rc = R.tgref_load_tmac(path.encode())
+    table = []
+    ddr = R.tgref_tmac_ddr()
+    for i in range(R.tgref_tmac_count() if rc == 0 else 0):
+        name = C.create_string_buffer(128)
+        rows, cols, nb, off = C.c_uint64(), C.c_uint64(), C.c_uint64(), C.c_uint64()
+        typ = C.c_uint32()
+        R.tgref_tmac_tensor(i, name, C.byref(rows), C.byref(cols), C.byref(typ), C.byref(nb),
+                            C.byref(off))
+        data = C.string_at(ddr + off.value, nb.value)
+        table.append((name.value.decode(), rows.value, cols.value, typ.value, nb.value, data))
+    return rc, table

@@ -81,6 +81,11 @@ class tg_qkv_weights(C.Structure):
                 ("b_v", C.c_void_p)]
 
 
+class tg_tensor_info(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("rows", C.c_uint64), ("cols", C.c_uint64),
+                ("n_bytes", C.c_uint64), ("type", C.c_uint32), ("data", C.c_void_p)]
+
+
 _vp = C.c_void_p
 _SIGS = {
     "tg_status_string": (C.c_char_p, [C.c_int]),
@@ -153,6 +158,14 @@ _SIGS = {
     "tg_decode_layer_splitkv_x": (C.c_int, [_vp, _vp, C.c_int, C.c_int,
                                             C.POINTER(tg_qkv_weights), _vp, _vp, _vp]),
     "tg_attn_output": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp]),
+    "tg_model_load_tmac": (C.c_int, [_vp, C.c_char_p, C.POINTER(_vp)]),
+    "tg_model_destroy": (C.c_int, [_vp]),
+    "tg_model_count": (C.c_int, [_vp, C.POINTER(C.c_int)]),
+    "tg_model_tensor_at": (C.c_int, [_vp, C.c_int, C.POINTER(tg_tensor_info)]),
+    "tg_model_find": (C.c_int, [_vp, C.c_char_p, C.POINTER(tg_tensor_info)]),
+    "tg_model_read": (C.c_int, [_vp, C.c_int, _vp, C.c_size_t]),
+    "tg_model_layer_attention": (C.c_int, [_vp, C.c_int, C.POINTER(tg_qkv_weights),
+                                           C.POINTER(_vp), C.POINTER(C.c_int)]),
     "tg_attention_block": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.POINTER(tg_qkv_weights),
                                      C.c_int, _vp, _vp, _vp, _vp]),
     "tg_attention_block_splitkv": (C.c_int, [_vp, _vp, C.c_int, C.c_int,
@@ -601,3 +614,67 @@ class QKVWeights:
         self._keep = (w_q, w_k, w_v, b_q, b_k, b_v)
         self.desc = tg_qkv_weights(q_type, k_type, v_type, cols, _ptr(w_q), _ptr(w_k),
                                    _ptr(w_v), _ptr(b_q), _ptr(b_k), _ptr(b_v))
+
+
+class Model:
+    """A TMAC model file in device memory (tg_model_load_tmac: load_tmac,
+    tmac_gguf.cpp:1372-1425)."""
+
+    def __init__(self, backend: CudaBackend, path: str):
+        self.backend = backend
+        h = C.c_void_p()
+        _check(lib().tg_model_load_tmac(backend.handle, os.fsencode(path), C.byref(h)))
+        self._h = h
+
+    def __len__(self) -> int:
+        n = C.c_int()
+        _check(lib().tg_model_count(self._h, C.byref(n)))
+        return n.value
+
+    @staticmethod
+    def _info(t: tg_tensor_info):
+        if not t.name:
+            return None
+        return {"name": t.name.decode(errors="replace"), "rows": t.rows, "cols": t.cols,
+                "n_bytes": t.n_bytes, "type": t.type, "data": t.data}
+
+    def tensor(self, index: int):
+        t = tg_tensor_info()
+        _check(lib().tg_model_tensor_at(self._h, index, C.byref(t)))
+        return self._info(t)
+
+    def find(self, name: str):
+        """get_tensor_info (tmac_gguf.cpp:417-422); None when absent."""
+        t = tg_tensor_info()
+        _check(lib().tg_model_find(self._h, name.encode(), C.byref(t)))
+        return self._info(t)
+
+    def read(self, index: int) -> bytes:
+        info = self.tensor(index)
+        buf = C.create_string_buffer(max(int(info["n_bytes"]), 1))
+        _check(lib().tg_model_read(self._h, index, buf, int(info["n_bytes"])))
+        return buf.raw[:int(info["n_bytes"])]
+
+    def layer_attention(self, layer: int):
+        """(QKVWeights, w_o device address or None, o_type) of one layer."""
+        d = tg_qkv_weights()
+        wo = C.c_void_p()
+        ot = C.c_int()
+        _check(lib().tg_model_layer_attention(self._h, layer, C.byref(d), C.byref(wo),
+                                              C.byref(ot)))
+        w = QKVWeights.__new__(QKVWeights)
+        w._keep = (self,)
+        w.desc = d
+        return w, wo.value, ot.value
+
+    def destroy(self) -> None:
+        if self._h:
+            _check(lib().tg_model_destroy(self._h))
+        self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            if getattr(self, "_h", None):
+                lib().tg_model_destroy(self._h)
+        except Exception:
+            pass

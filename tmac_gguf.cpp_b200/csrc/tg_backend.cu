@@ -2392,4 +2392,10 @@ int set_last_error(int code, const char* msg) {
   t_err = msg;
   return code;
 }
+
+int context_device(tg_context* ctx, int* device) {
+  if (!ctx || !device) return fail(TG_ERR_INVALID_ARG, "null context");
+  *device = ctx->device;
+  return TG_OK;
+}
 }  // namespace tg
