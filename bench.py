@@ -791,7 +791,8 @@ def main():
                                     + ("qkv_gemm_kernel" if B >= 9 else "qkv_kernel"))
                          if qkv else
                          ("decode_fused_kernel" if kv.uses_tensor_cores()
-                          else "decode_generic_kernel"),
+                          else ("decode_small_kernel" if kv.max_ctx <= 1024 and
+                                shard_start == 0 and not split else "decode_generic_kernel")),
                          "bytes_per_launch": k_bytes, "launch_ms": k_avg_ms,
                          "traffic": ncu_traffic(args.workload,
                                                 shard_len / wl["ctx"] if wl["split"] else 1.0),

@@ -502,6 +502,93 @@ def test_errors_are_reported(tg, backend, cases):
                         np.zeros((2, 128), np.float32), np.array([0, 0], np.int32), out)
 
 
+@pytest.mark.parametrize("bf16", [False, True], ids=["f32", "bf16"])
+def test_short_cache_kernel_other_group(tg, backend, O, bf16):
+    """Caches of at most 1024 positions take the one-CTA-per-(sequence, KV
+    head) kernel; 12 query heads over 3 KV heads keep a bf16 cache off the
+    tensor-core kernel too.  Ragged positions up to the capacity."""
+    n_head, n_kv, hd, cap = 12, 3, 64, 1024
+    positions = [0, 1, 31, 32, 255, 1023, 700]
+    B = len(positions)
+    kv = tg.KVCache(backend, 1, B, cap, n_head=n_head, n_kv_head=n_kv, head_dim=hd,
+                    dtype=tg.DTYPE_BF16 if bf16 else tg.DTYPE_F32)
+    gen = O.normal_bf16 if bf16 else O.normal
+    Q = np.stack([O.normal(50 + i, n_head * hd) for i in range(B)])
+    out = np.zeros_like(Q)
+    ks, vs = [], []
+    for i, pos in enumerate(positions):
+        kc = gen(60 + i, (pos + 1) * n_kv * hd).reshape(pos + 1, -1)
+        vc = gen(70 + i, (pos + 1) * n_kv * hd).reshape(pos + 1, -1)
+        kv.write_rows(0, i, 0, kc, vc)
+        ks.append(kc)
+        vs.append(vc)
+    kv.attention(0, Q, np.array(positions, np.int32), out)
+    tol = BF16_TOL if bf16 else F32_TOL
+    for i, pos in enumerate(positions):
+        ref = O.attention(Q[i], ks[i], vs[i], pos, n_head, n_kv, hd)
+        assert maxabs(out[i], ref) <= tol, (i, pos)
+    kv.destroy()
+
+
+@pytest.mark.parametrize("bf16", [False, True], ids=["f32", "bf16"])
+def test_short_cache_decode_step_other_group(tg, backend, O, bf16):
+    """The one-launch decode step of short caches (RoPE, new-row write and
+    attention in the short-cache kernel) with 12 query / 3 KV heads:
+    rotated q and k bit-exact, cache rows as stored, output within the bar."""
+    n_head, n_kv, hd, cap = 12, 3, 64, 300
+    positions = [0, 5, 299, 130]
+    B = len(positions)
+    kv = tg.KVCache(backend, 1, B, cap, n_head=n_head, n_kv_head=n_kv, head_dim=hd,
+                    dtype=tg.DTYPE_BF16 if bf16 else tg.DTYPE_F32)
+    gen = O.normal_bf16 if bf16 else O.normal
+    Q = np.stack([O.normal(80 + i, n_head * hd) for i in range(B)])
+    K = np.stack([O.normal(90 + i, n_kv * hd) for i in range(B)])
+    V = np.stack([gen(100 + i, n_kv * hd) for i in range(B)])
+    caches = []
+    for i, pos in enumerate(positions):
+        kc = np.zeros((pos + 1, n_kv * hd), np.float32)
+        vc = np.zeros_like(kc)
+        if pos > 0:
+            kc[:pos] = gen(110 + i, pos * n_kv * hd).reshape(pos, -1)
+            vc[:pos] = gen(120 + i, pos * n_kv * hd).reshape(pos, -1)
+            kv.write_rows(0, i, 0, kc[:pos], vc[:pos])
+        caches.append((kc, vc))
+    Qg, Kg = Q.copy(), K.copy()
+    out = np.zeros_like(Q)
+    kv.decode_layer(0, Qg, Kg, V, np.array(positions, np.int32), out)
+    tol = BF16_TOL if bf16 else F32_TOL
+    for i, pos in enumerate(positions):
+        q = O.rope_heads(Q[i], n_head, hd, pos)
+        k = O.rope_heads(K[i], n_kv, hd, pos)
+        assert np.array_equal(bits(Qg[i]), bits(q)) and np.array_equal(bits(Kg[i]), bits(k))
+        kc, vc = caches[i]
+        kc[pos] = O.round_bf16(k) if bf16 else k
+        vc[pos] = V[i]
+        kr, vr = kv.read_rows(0, i, pos, 1)
+        if bf16:
+            assert np.array_equal(kr[0], O.pack_bf16(kc[pos]))
+            assert np.array_equal(vr[0], O.pack_bf16(vc[pos]))
+        else:
+            assert np.array_equal(bits(kr[0]), bits(kc[pos]))
+            assert np.array_equal(bits(vr[0]), bits(vc[pos]))
+        ref = O.attention(q, kc, vc, pos, n_head, n_kv, hd)
+        assert maxabs(out[i], ref) <= tol, (i, pos)
+    kv.destroy()
+
+
+def test_short_cache_kernel_reports_bad_positions(tg, backend, cases):
+    import torch
+    kv = tg.KVCache(backend, 1, 2, 64, dtype=tg.DTYPE_F32)
+    q = np.zeros((2, 896), np.float32)
+    out = np.zeros_like(q)
+    bad = torch.tensor([3, 500], dtype=torch.int32, device="cuda")
+    with pytest.raises(tg.TGError) as e:
+        kv.attention(0, q, bad, out)                            # device-side check
+    assert e.value.status == tg.TG_ERR_DEVICE
+    kv.attention(0, q, np.array([3, 5], np.int32), out)         # context recovers
+    kv.destroy()
+
+
 def test_outputs_leave_neighbours_untouched(tg, backend, cases):
     import torch
     positions = [10, 3000]

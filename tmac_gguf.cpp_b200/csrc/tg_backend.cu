@@ -760,6 +760,15 @@ int prof_end(tg_context* ctx, cudaEvent_t ev_stop) {
   return TG_OK;
 }
 
+// Caches the one-CTA-per-(sequence, KV head) kernel takes: capacity at most
+// kSmallMaxRows, head_dim 64, at most 8 query heads per KV head, whole cache.
+bool small_eligible(const tg_kv_cache* kv) {
+  const tg_kv_desc& d = kv->d;
+  const int group = d.n_head / d.n_kv_head;
+  return d.head_dim == 64 && group <= 8 && d.max_ctx <= tg::kSmallMaxRows &&
+         d.shard_start == 0 && tg::decode_small_smem(group, d.max_ctx) <= 227 * 1024;
+}
+
 // Core decode launch on device pointers.  mode 0 writes `out`; mode 1
 // writes per-sequence records to ctx->records.
 int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const float* q,
@@ -792,6 +801,17 @@ int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const f
                     ? 1
                     : 0;
 
+  // Short caches: one CTA per (sequence, KV head) does the whole attention
+  // (no split, no merge launch).  The cache capacity decides, so the choice
+  // holds for any positions, also inside a graph capture.
+  if (mode == 0 && small_eligible(kv)) {
+    cudaEvent_t ev_small = nullptr;
+    TG_TRY(prof_begin(ctx, TG_PROFILE_ATTENTION, &ev_small));
+    cudaError_t e = tg::launch_decode_small(p, d.dtype, ctx->stream);
+    if (e != cudaSuccess) return fail(TG_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
+    ctx->launches++;
+    return prof_end(ctx, ev_small);
+  }
   const bool mma = mma_eligible(kv);
   int grid;
   size_t smem;
@@ -833,6 +853,53 @@ int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const f
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "merge launch: %s", cudaGetErrorString(e));
   ctx->launches++;
   return TG_OK;
+}
+
+// Short caches: RoPE of q and k, the new row's cache-write and attention in
+// one launch of the short-cache kernel (q and k rotated in place).
+int run_small_step(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, float* q, float* k,
+                   const float* v, const int* pos_dev, float* out) {
+  TG_TRY(commit_inputs(ctx));
+  const tg_kv_desc& d = kv->d;
+  TG_TRY(check_align8(q, "q"));
+  TG_TRY(check_align8(k, "k_new"));
+  TG_TRY(check_align8(out, "out"));
+  RopeTable* t = nullptr;
+  TG_TRY(get_table(ctx, d.rope_base, d.head_dim, kv->global_ctx, &t));
+  tg::DecodeParams p{};
+  p.q = q;
+  p.out = out;
+  p.past_len = pos_dev;
+  p.k = static_cast<const char*>(kv->k) + (size_t)layer * kv->layer_elems * kv->esize;
+  p.v = static_cast<const char*>(kv->v) + (size_t)layer * kv->layer_elems * kv->esize;
+  p.B = B;
+  p.n_head = d.n_head;
+  p.n_kv = d.n_kv_head;
+  p.head_dim = d.head_dim;
+  p.group = d.n_head / d.n_kv_head;
+  p.max_ctx = d.max_ctx;
+  p.shard_start = 0;
+  p.scale_log2 = kLog2e / sqrtf((float)d.head_dim);
+  p.mode = 0;
+  p.err = ctx->d_err;
+  p.aligned16 = ((reinterpret_cast<uintptr_t>(p.k) | reinterpret_cast<uintptr_t>(p.v)) % 16 == 0 &&
+                 (kv->row_elems * kv->esize) % 16 == 0)
+                    ? 1
+                    : 0;
+  p.rope = 1;
+  p.q_io = q;
+  p.k_io = k;
+  p.v_new = v;
+  p.cs = t->d;
+  p.table_len = kv->global_ctx;
+  p.k_cache = const_cast<void*>(p.k);
+  p.v_cache = const_cast<void*>(p.v);
+  cudaEvent_t ev = nullptr;
+  TG_TRY(prof_begin(ctx, TG_PROFILE_ATTENTION, &ev));
+  cudaError_t e = tg::launch_decode_small(p, d.dtype, ctx->stream);
+  if (e != cudaSuccess) return fail(TG_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
+  ctx->launches++;
+  return prof_end(ctx, ev);
 }
 
 int run_rope(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, float* q, float* k,
@@ -1737,6 +1804,12 @@ int tg_decode_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, flo
                      static_cast<float*>(dq), const_cast<float*>(static_cast<const float*>(dk_in)),
                      static_cast<const float*>(dv), static_cast<const int*>(dp),
                      static_cast<float*>(dout), nullptr, 0, true, true, static_cast<float*>(dk)));
+    return finish_call(ctx);
+  }
+  if (small_eligible(kv)) {
+    TG_TRY(run_small_step(ctx, kv, layer, n_seqs, static_cast<float*>(dq), static_cast<float*>(dk),
+                          static_cast<const float*>(dv), static_cast<const int*>(dp),
+                          static_cast<float*>(dout)));
     return finish_call(ctx);
   }
   TG_TRY(run_rope(ctx, kv, layer, n_seqs, static_cast<float*>(dq), static_cast<float*>(dk),

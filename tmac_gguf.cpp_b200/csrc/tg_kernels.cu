@@ -10,6 +10,9 @@
 //                             (tmac_gguf.cpp:1093-1128, kernel_attn.metal).
 //   decode_generic_kernel<T>  the same contract on CUDA cores for fp32 (and
 //                             any shape the tensor-core kernel does not take).
+//   decode_small_kernel<T>    caches of at most kSmallMaxRows positions
+//                             (head_dim 64): one CTA per (sequence, KV head),
+//                             no split, no merge.
 //   merge_kernel              combines the partial records of sequences that
 //                             were split across CTAs.
 //   gather_merge_kernel       combines per-GPU records after the all-gather.
@@ -701,6 +704,299 @@ __global__ void __launch_bounds__(GEN_THREADS, 4) decode_generic_kernel(const De
   }
 }
 
+// ========================================================== short caches
+
+// One CTA per (sequence, KV head) for caches of at most kSmallMaxRows
+// positions and head_dim 64 (configs 1-2 and the compatible attention_op):
+// the whole attention of the KV head's query group happens in one CTA, so
+// there is no split and no merge launch.  With p.rope the CTA also rotates
+// its query heads and its part of the new k row at the sequence's position
+// (tmac_gguf.cpp:990-1016, one rounding per product and sum), writes them
+// back, writes the new k / v row into the cache (:1090-1091) and attends
+// with its own copy of that row: one launch per layer.  Phase 1: one thread per cache row
+// loads the row's 64 keys (all loads issued together) and forms the scores
+// of the group's heads (q broadcast from shared memory).  Phase 2: warp g
+// takes head g's softmax (max, 2^(s - max), sum).  Phase 3: warp w takes
+// rows [w n / 8, (w+1) n / 8), lane l dimensions 2l and 2l+1, accumulating
+// every head of the group; the 8 partial outputs are summed through shared
+// memory and divided by the head's sum.
+constexpr int SMALL_THREADS = 256;
+constexpr int SMALL_WARPS = SMALL_THREADS / 32;
+
+template <typename Elem>
+__device__ __forceinline__ void load_row64(const Elem* src, bool vec, float (&kr)[64]);
+template <>
+__device__ __forceinline__ void load_row64<float>(const float* src, bool vec, float (&kr)[64]) {
+  if (vec) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(src) + i);
+      kr[4 * i] = f.x;
+      kr[4 * i + 1] = f.y;
+      kr[4 * i + 2] = f.z;
+      kr[4 * i + 3] = f.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) kr[i] = __ldg(src + i);
+  }
+}
+template <>
+__device__ __forceinline__ void load_row64<__nv_bfloat16>(const __nv_bfloat16* src, bool vec,
+                                                          float (&kr)[64]) {
+  if (vec) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(src) + i);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        kr[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
+        kr[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) kr[i] = __bfloat162float(src[i]);
+  }
+}
+
+template <typename Elem>
+__device__ __forceinline__ float2 load_pair(const Elem* src);
+template <>
+__device__ __forceinline__ float2 load_pair<float>(const float* src) {
+  return make_float2(__ldg(src), __ldg(src + 1));
+}
+template <>
+__device__ __forceinline__ float2 load_pair<__nv_bfloat16>(const __nv_bfloat16* src) {
+  const uint32_t w = __ldg(reinterpret_cast<const unsigned int*>(src));
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+// Score rows are padded to a multiple of 4 floats so that the partial
+// outputs after them stay 16-byte aligned (they are stored as float2).
+__host__ __device__ inline int small_row_stride(int max_ctx) { return (max_ctx + 3) & ~3; }
+
+size_t decode_small_smem(int group, int max_ctx) {
+  return (size_t)(group * 64 + (size_t)group * small_row_stride(max_ctx) +
+                  SMALL_WARPS * group * 64 + 2 * group + 2 * 64) *
+         4;
+}
+
+template <typename Elem>
+__device__ __forceinline__ void store_elem(Elem* dst, float v);
+template <>
+__device__ __forceinline__ void store_elem<float>(float* dst, float v) {
+  *dst = v;
+}
+template <>
+__device__ __forceinline__ void store_elem<__nv_bfloat16>(__nv_bfloat16* dst, float v) {
+  *dst = __float2bfloat16_rn(v);
+}
+// The value a cache element of type Elem holds after store_elem.
+template <typename Elem>
+__device__ __forceinline__ float as_stored(float v);
+template <>
+__device__ __forceinline__ float as_stored<float>(float v) {
+  return v;
+}
+template <>
+__device__ __forceinline__ float as_stored<__nv_bfloat16>(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+template <typename Elem>
+__global__ void __launch_bounds__(SMALL_THREADS) decode_small_kernel(const DecodeParams p) {
+  extern __shared__ float ssm[];
+  griddep_launch_dependents();
+  constexpr int HD = 64;
+  const int G = p.group, cap = small_row_stride(p.max_ctx);  // score row stride
+  const int seq = blockIdx.x / p.n_kv, kvh = blockIdx.x - seq * p.n_kv;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float* q_s = ssm;                           // [G][64]
+  float* s_s = q_s + G * HD;                  // [G][cap] scores, then 2^(s - max)
+  float* o_s = s_s + (size_t)G * cap;         // [8][G][64] partial outputs
+  float* l_s = o_s + SMALL_WARPS * G * HD;    // [G] sums
+  float* kn_s = l_s + 2 * G;                  // new k row (this KV head), rope mode
+  float* vn_s = kn_s + HD;                    // new v row
+
+  griddep_wait();
+  const int pl = past_of(p, seq);
+  if (pl < 0 || pl >= p.max_ctx) {
+    if (tid == 0) record_error(p.err, kDevErrBadPos);
+    return;
+  }
+  const int n = pl + 1;
+  const int kdim = p.n_kv * HD;
+  const size_t seq_rows = (size_t)seq * p.max_ctx;
+  const Elem* kb = static_cast<const Elem*>(p.k) + seq_rows * kdim + kvh * HD;
+  const Elem* vb = static_cast<const Elem*>(p.v) + seq_rows * kdim + kvh * HD;
+  const bool vec = p.aligned16 != 0;
+  // The thread's first key row is requested before q is staged, so the two
+  // loads overlap (the new row, in rope mode, comes from shared memory).
+  const bool fuse = p.rope != 0;
+  float kr[64];
+  if (tid < n && !(fuse && tid == pl)) load_row64<Elem>(kb + (size_t)tid * kdim, vec, kr);
+  const size_t qoff = (size_t)seq * p.n_head * HD + (size_t)kvh * G * HD;
+  if (!fuse) {
+    const float* qsrc = p.q + qoff;
+    for (int i = tid; i < G * HD; i += SMALL_THREADS) q_s[i] = qsrc[i];
+  } else {
+    if (pl >= p.table_len) {
+      if (tid == 0) record_error(p.err, kDevErrBadPos);
+      return;
+    }
+    // RoPE of the group's query heads and of this KV head's part of the new
+    // k row: pairs (2j, 2j+1), x0*c - x1*s and x0*s + x1*c; rotated values
+    // go back to q_io / k_io and into the cache row pl.
+    const float* cs = p.cs + (size_t)pl * HD;
+    float* qio = p.q_io + qoff;
+    const size_t koff = (size_t)seq * kdim + kvh * HD;
+    const size_t crow = (seq_rows + pl) * kdim + kvh * HD;
+    for (int i = tid; i < (G + 1) * (HD / 2); i += SMALL_THREADS) {
+      const int g = i / (HD / 2), j = i - g * (HD / 2);
+      float* src = g < G ? qio + g * HD + 2 * j : p.k_io + koff + 2 * j;
+      const float2 x = *reinterpret_cast<const float2*>(src);
+      const float2 c = *reinterpret_cast<const float2*>(cs + 2 * j);
+      const float y0 = __fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(x.y, c.y));
+      const float y1 = __fadd_rn(__fmul_rn(x.x, c.y), __fmul_rn(x.y, c.x));
+      *reinterpret_cast<float2*>(src) = make_float2(y0, y1);
+      if (g < G) {
+        q_s[g * HD + 2 * j] = y0;
+        q_s[g * HD + 2 * j + 1] = y1;
+      } else {
+        // The cache holds the row rounded to its type; attention reads it so.
+        Elem* kc = static_cast<Elem*>(p.k_cache) + crow + 2 * j;
+        store_elem<Elem>(kc, y0);
+        store_elem<Elem>(kc + 1, y1);
+        kn_s[2 * j] = as_stored<Elem>(y0);
+        kn_s[2 * j + 1] = as_stored<Elem>(y1);
+      }
+    }
+    for (int i = tid; i < HD; i += SMALL_THREADS) {
+      const float v = p.v_new[koff + i];
+      store_elem<Elem>(static_cast<Elem*>(p.v_cache) + crow + i, v);
+      vn_s[i] = as_stored<Elem>(v);
+    }
+  }
+  __syncthreads();
+  if (fuse && tid == pl) {
+#pragma unroll
+    for (int d = 0; d < HD; ++d) kr[d] = kn_s[d];
+  }
+
+  // 1. Scores, one thread per row.
+  for (int r = tid; r < n; r += SMALL_THREADS) {
+    if (r != tid) {
+      if (fuse && r == pl) {
+#pragma unroll
+        for (int d = 0; d < HD; ++d) kr[d] = kn_s[d];
+      } else {
+        load_row64<Elem>(kb + (size_t)r * kdim, vec, kr);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      if (g < G) {
+        const float* qg = q_s + g * HD;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+        for (int d = 0; d < HD; d += 4) {
+          const float4 q4 = *reinterpret_cast<const float4*>(qg + d);
+          a0 = fmaf(q4.x, kr[d], a0);
+          a1 = fmaf(q4.y, kr[d + 1], a1);
+          a2 = fmaf(q4.z, kr[d + 2], a2);
+          a3 = fmaf(q4.w, kr[d + 3], a3);
+        }
+        s_s[(size_t)g * cap + r] = ((a0 + a1) + (a2 + a3)) * p.scale_log2;
+      }
+    }
+  }
+  __syncthreads();
+  // 2. Softmax of head g on warp g.
+  if (warp < G) {
+    float* sg = s_s + (size_t)warp * cap;
+    float mx = -INFINITY;
+    for (int r = lane; r < n; r += 32) mx = fmaxf(mx, sg[r]);
+    mx = warp_max(mx);
+    float sum = 0.f;
+    for (int r = lane; r < n; r += 32) {
+      const float e = ex2(sg[r] - mx);
+      sg[r] = e;
+      sum += e;
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) l_s[warp] = sum;
+  }
+  __syncthreads();
+  // 3. P.V over this warp's rows, every head of the group.
+  float acc[8][2];
+#pragma unroll
+  for (int g = 0; g < 8; ++g) acc[g][0] = acc[g][1] = 0.f;
+  const int r0 = (warp * n) / SMALL_WARPS, r1 = ((warp + 1) * n) / SMALL_WARPS;
+  const Elem* vcol = vb + 2 * lane;
+  int r = r0;
+  // 16 rows of V requested at a time: one memory latency per 16 rows.
+  for (; r + 15 < r1; r += 16) {
+    float2 v[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u)
+      v[u] = (fuse && r + u == pl) ? make_float2(vn_s[2 * lane], vn_s[2 * lane + 1])
+                                   : load_pair<Elem>(vcol + (size_t)(r + u) * kdim);
+#pragma unroll
+    for (int u = 0; u < 16; ++u)
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        if (g < G) {
+          const float pr = s_s[(size_t)g * cap + r + u];
+          acc[g][0] = fmaf(pr, v[u].x, acc[g][0]);
+          acc[g][1] = fmaf(pr, v[u].y, acc[g][1]);
+        }
+  }
+  for (; r + 3 < r1; r += 4) {
+    float2 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      v[u] = (fuse && r + u == pl) ? make_float2(vn_s[2 * lane], vn_s[2 * lane + 1])
+                                   : load_pair<Elem>(vcol + (size_t)(r + u) * kdim);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        if (g < G) {
+          const float pr = s_s[(size_t)g * cap + r + u];
+          acc[g][0] = fmaf(pr, v[u].x, acc[g][0]);
+          acc[g][1] = fmaf(pr, v[u].y, acc[g][1]);
+        }
+  }
+  for (; r < r1; ++r) {
+    const float2 v = (fuse && r == pl) ? make_float2(vn_s[2 * lane], vn_s[2 * lane + 1])
+                                       : load_pair<Elem>(vcol + (size_t)r * kdim);
+#pragma unroll
+    for (int g = 0; g < 8; ++g)
+      if (g < G) {
+        const float pr = s_s[(size_t)g * cap + r];
+        acc[g][0] = fmaf(pr, v.x, acc[g][0]);
+        acc[g][1] = fmaf(pr, v.y, acc[g][1]);
+      }
+  }
+#pragma unroll
+  for (int g = 0; g < 8; ++g)
+    if (g < G)
+      *reinterpret_cast<float2*>(o_s + (warp * G + g) * HD + 2 * lane) =
+          make_float2(acc[g][0], acc[g][1]);
+  __syncthreads();
+  // 4. Sum the warps' partial outputs, normalise, write.
+  float* out = p.out + (size_t)seq * p.n_head * HD + (size_t)kvh * G * HD;
+  for (int i = tid; i < G * HD; i += SMALL_THREADS) {
+    const int g = i / HD;
+    float o = 0.f;
+#pragma unroll
+    for (int w = 0; w < SMALL_WARPS; ++w) o += o_s[w * G * HD + i];
+    out[i] = o / l_s[g];
+  }
+}
+
 // ================================================================== merges
 
 // One CTA per (sequence, head); thread d owns output dimension d.  The
@@ -942,6 +1238,22 @@ cudaError_t launch_decode_mma(const CUtensorMap& tk, const CUtensorMap& tv,
     case 4: return launch_mma_nkv<4>(tk, tv, p, grid, st);
     default: return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t launch_decode_small(const DecodeParams& p, int dtype, cudaStream_t st) {
+  if (p.B <= 0) return cudaSuccess;
+  const size_t smem = decode_small_smem(p.group, p.max_ctx);
+  static size_t configured_f32[64] = {}, configured_bf16[64] = {};
+  cudaError_t e;
+  const dim3 grid((unsigned)(p.B * p.n_kv));
+  if (dtype == 0) {
+    e = ensure_smem(decode_small_kernel<float>, smem, configured_f32);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(decode_small_kernel<float>, grid, dim3(SMALL_THREADS), smem, st, p);
+  }
+  e = ensure_smem(decode_small_kernel<__nv_bfloat16>, smem, configured_bf16);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(decode_small_kernel<__nv_bfloat16>, grid, dim3(SMALL_THREADS), smem, st, p);
 }
 
 cudaError_t launch_decode_generic(const DecodeParams& p, int dtype, int grid,

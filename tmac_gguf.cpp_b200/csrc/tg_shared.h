@@ -85,6 +85,16 @@ struct DecodeParams {
   int mode;              // 0: normalised output, 1: records (split-KV)
   int past_len_scalar;   // used for every sequence when past_len == null
   int aligned16;         // k and v rows start on 16-byte boundaries
+  // Short-cache kernel only (rope != 0): RoPE of q and of the new k row at
+  // the sequence's position and the new row's cache-write, fused in.
+  int rope;
+  float* q_io;           // [B][n_head*head_dim] raw q in, rotated q out
+  float* k_io;           // [B][n_kv*head_dim] raw k in, rotated k out
+  const float* v_new;    // [B][n_kv*head_dim]
+  const float* cs;       // RoPE table [table_len][head_dim] (cos, sin pairs)
+  int table_len;
+  void* k_cache;         // layer base of the caches (writable views of k / v)
+  void* v_cache;
 };
 
 TG_HD int past_of(const DecodeParams& p, int s) {
