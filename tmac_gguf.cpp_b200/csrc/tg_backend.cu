@@ -766,7 +766,17 @@ bool small_eligible(const tg_kv_cache* kv) {
   const tg_kv_desc& d = kv->d;
   const int group = d.n_head / d.n_kv_head;
   return d.head_dim == 64 && group <= 8 && d.max_ctx <= tg::kSmallMaxRows &&
-         d.shard_start == 0 && tg::decode_small_smem(group, d.max_ctx) <= 227 * 1024;
+         d.shard_start == 0 && tg::decode_small_smem(group, d.max_ctx, 1) <= 227 * 1024;
+}
+
+// CTAs per (sequence, KV head) of the short-cache kernel: the largest of 8,
+// 4, 2, 1 that keeps the launch within two CTAs per SM and gives every CTA
+// at least 16 rows of a full cache.
+int small_split(const tg_context* ctx, const tg_kv_cache* kv, int B) {
+  const long long items = (long long)B * kv->d.n_kv_head;
+  int c = 8;
+  while (c > 1 && (items * c > 2LL * ctx->num_sms || kv->d.max_ctx < 16 * c)) c >>= 1;
+  return c;
 }
 
 // Core decode launch on device pointers.  mode 0 writes `out`; mode 1
@@ -805,6 +815,7 @@ int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const f
   // (no split, no merge launch).  The cache capacity decides, so the choice
   // holds for any positions, also inside a graph capture.
   if (mode == 0 && small_eligible(kv)) {
+    p.split = small_split(ctx, kv, B);
     cudaEvent_t ev_small = nullptr;
     TG_TRY(prof_begin(ctx, TG_PROFILE_ATTENTION, &ev_small));
     cudaError_t e = tg::launch_decode_small(p, d.dtype, ctx->stream);
@@ -894,6 +905,7 @@ int run_small_step(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, flo
   p.table_len = kv->global_ctx;
   p.k_cache = const_cast<void*>(p.k);
   p.v_cache = const_cast<void*>(p.v);
+  p.split = small_split(ctx, kv, B);
   cudaEvent_t ev = nullptr;
   TG_TRY(prof_begin(ctx, TG_PROFILE_ATTENTION, &ev));
   cudaError_t e = tg::launch_decode_small(p, d.dtype, ctx->stream);

@@ -22,6 +22,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cooperative_groups.h>
+
 #include <utility>
 
 #include "tg_device.cuh"
@@ -706,20 +708,22 @@ __global__ void __launch_bounds__(GEN_THREADS, 4) decode_generic_kernel(const De
 
 // ========================================================== short caches
 
-// One CTA per (sequence, KV head) for caches of at most kSmallMaxRows
-// positions and head_dim 64 (configs 1-2 and the compatible attention_op):
-// the whole attention of the KV head's query group happens in one CTA, so
-// there is no split and no merge launch.  With p.rope the CTA also rotates
-// its query heads and its part of the new k row at the sequence's position
-// (tmac_gguf.cpp:990-1016, one rounding per product and sum), writes them
-// back, writes the new k / v row into the cache (:1090-1091) and attends
-// with its own copy of that row: one launch per layer.  Phase 1: one thread per cache row
-// loads the row's 64 keys (all loads issued together) and forms the scores
-// of the group's heads (q broadcast from shared memory).  Phase 2: warp g
-// takes head g's softmax (max, 2^(s - max), sum).  Phase 3: warp w takes
-// rows [w n / 8, (w+1) n / 8), lane l dimensions 2l and 2l+1, accumulating
-// every head of the group; the 8 partial outputs are summed through shared
-// memory and divided by the head's sum.
+// A cluster of p.split CTAs (1, 2, 4 or 8) per (sequence, KV head) for
+// caches of at most kSmallMaxRows positions and head_dim 64 (configs 1-2
+// and the compatible attention_op): CTA c of the cluster attends rows
+// [c n / C, (c+1) n / C) for the KV head's whole query group, and the
+// cluster merges its softmax states through distributed shared memory, so
+// there is no merge launch.  With p.rope the CTAs also rotate the query
+// heads and the KV head's part of the new k row at the sequence's position
+// (tmac_gguf.cpp:990-1016, one rounding per product and sum) and attend
+// with their own copy of the new row; rank 0 writes the rotated q / k back
+// and the new k / v row into the cache (:1090-1091): one launch per layer.
+// Phase 1: one thread per row of the CTA's share loads the row's 64 keys
+// (all loads issued together) and forms the scores of the group's heads (q
+// broadcast from shared memory).  Phase 2: warp g takes head g's maximum and
+// sum.  Phase 3: the 8 warps split the share's rows for P.V, lane l holding
+// dimensions 2l and 2l+1 of every head, 16 rows of V requested at a time.
+// Phase 4: rank c merges heads c, c + C, ... over the cluster.
 constexpr int SMALL_THREADS = 256;
 constexpr int SMALL_WARPS = SMALL_THREADS / 32;
 
@@ -775,11 +779,15 @@ __device__ __forceinline__ float2 load_pair<__nv_bfloat16>(const __nv_bfloat16* 
 
 // Score rows are padded to a multiple of 4 floats so that the partial
 // outputs after them stay 16-byte aligned (they are stored as float2).
-__host__ __device__ inline int small_row_stride(int max_ctx) { return (max_ctx + 3) & ~3; }
+__host__ __device__ inline int small_row_stride(int rows) { return (rows + 3) & ~3; }
+// Rows a CTA of a cluster of `split` takes at most.
+__host__ __device__ inline int small_chunk_rows(int max_ctx, int split) {
+  return (max_ctx + split - 1) / split;
+}
 
-size_t decode_small_smem(int group, int max_ctx) {
-  return (size_t)(group * 64 + (size_t)group * small_row_stride(max_ctx) +
-                  SMALL_WARPS * group * 64 + 2 * group + 2 * 64) *
+size_t decode_small_smem(int group, int max_ctx, int split) {
+  return (size_t)(group * 64 + (size_t)group * small_row_stride(small_chunk_rows(max_ctx, split)) +
+                  SMALL_WARPS * group * 64 + group * 64 + 2 * group + 2 * 64) *
          4;
 }
 
@@ -809,24 +817,37 @@ template <typename Elem>
 __global__ void __launch_bounds__(SMALL_THREADS) decode_small_kernel(const DecodeParams p) {
   extern __shared__ float ssm[];
   griddep_launch_dependents();
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
   constexpr int HD = 64;
-  const int G = p.group, cap = small_row_stride(p.max_ctx);  // score row stride
-  const int seq = blockIdx.x / p.n_kv, kvh = blockIdx.x - seq * p.n_kv;
+  const int C = p.split;                       // CTAs per (sequence, KV head)
+  const int crank = (int)cluster.block_rank();
+  const int item = blockIdx.x / C;
+  const int G = p.group;
+  const int cap = small_row_stride(small_chunk_rows(p.max_ctx, C));  // score row stride
+  const int seq = item / p.n_kv, kvh = item - seq * p.n_kv;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float* q_s = ssm;                           // [G][64]
-  float* s_s = q_s + G * HD;                  // [G][cap] scores, then 2^(s - max)
-  float* o_s = s_s + (size_t)G * cap;         // [8][G][64] partial outputs
-  float* l_s = o_s + SMALL_WARPS * G * HD;    // [G] sums
-  float* kn_s = l_s + 2 * G;                  // new k row (this KV head), rope mode
+  float* s_s = q_s + G * HD;                  // [G][cap] scores, then 2^(s - m)
+  float* o_s = s_s + (size_t)G * cap;         // [8][G][64] per-warp partial outputs
+  float* oc_s = o_s + SMALL_WARPS * G * HD;   // [G][64] this CTA's output sums
+  float* m_s = oc_s + G * HD;                 // [G] this CTA's maxima
+  float* l_s = m_s + G;                       // [G] this CTA's sums
+  float* kn_s = l_s + G;                      // new k row (this KV head), rope mode
   float* vn_s = kn_s + HD;                    // new v row
 
   griddep_wait();
+  // Every CTA of a cluster has the same sequence: the checks below end the
+  // whole cluster or none of it.
   const int pl = past_of(p, seq);
-  if (pl < 0 || pl >= p.max_ctx) {
+  const bool fuse = p.rope != 0;
+  if (pl < 0 || pl >= p.max_ctx || (fuse && pl >= p.table_len)) {
     if (tid == 0) record_error(p.err, kDevErrBadPos);
     return;
   }
   const int n = pl + 1;
+  const int lo = (int)((long long)crank * n / C), hi = (int)((long long)(crank + 1) * n / C);
+  const int nloc = hi - lo;
   const int kdim = p.n_kv * HD;
   const size_t seq_rows = (size_t)seq * p.max_ctx;
   const Elem* kb = static_cast<const Elem*>(p.k) + seq_rows * kdim + kvh * HD;
@@ -834,63 +855,47 @@ __global__ void __launch_bounds__(SMALL_THREADS) decode_small_kernel(const Decod
   const bool vec = p.aligned16 != 0;
   // The thread's first key row is requested before q is staged, so the two
   // loads overlap (the new row, in rope mode, comes from shared memory).
-  const bool fuse = p.rope != 0;
   float kr[64];
-  if (tid < n && !(fuse && tid == pl)) load_row64<Elem>(kb + (size_t)tid * kdim, vec, kr);
+  if (tid < nloc && !(fuse && lo + tid == pl)) load_row64<Elem>(kb + (size_t)(lo + tid) * kdim, vec, kr);
   const size_t qoff = (size_t)seq * p.n_head * HD + (size_t)kvh * G * HD;
+  const size_t koff = (size_t)seq * kdim + kvh * HD;
   if (!fuse) {
     const float* qsrc = p.q + qoff;
     for (int i = tid; i < G * HD; i += SMALL_THREADS) q_s[i] = qsrc[i];
   } else {
-    if (pl >= p.table_len) {
-      if (tid == 0) record_error(p.err, kDevErrBadPos);
-      return;
-    }
     // RoPE of the group's query heads and of this KV head's part of the new
-    // k row: pairs (2j, 2j+1), x0*c - x1*s and x0*s + x1*c; rotated values
-    // go back to q_io / k_io and into the cache row pl.
+    // k row: pairs (2j, 2j+1), x0*c - x1*s and x0*s + x1*c.  Every CTA of
+    // the cluster rotates for itself; rank 0 writes the results back after
+    // the cluster barrier, when no CTA reads the raw values any more.
     const float* cs = p.cs + (size_t)pl * HD;
-    float* qio = p.q_io + qoff;
-    const size_t koff = (size_t)seq * kdim + kvh * HD;
-    const size_t crow = (seq_rows + pl) * kdim + kvh * HD;
     for (int i = tid; i < (G + 1) * (HD / 2); i += SMALL_THREADS) {
       const int g = i / (HD / 2), j = i - g * (HD / 2);
-      float* src = g < G ? qio + g * HD + 2 * j : p.k_io + koff + 2 * j;
+      const float* src = g < G ? p.q_io + qoff + g * HD + 2 * j : p.k_io + koff + 2 * j;
       const float2 x = *reinterpret_cast<const float2*>(src);
       const float2 c = *reinterpret_cast<const float2*>(cs + 2 * j);
       const float y0 = __fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(x.y, c.y));
       const float y1 = __fadd_rn(__fmul_rn(x.x, c.y), __fmul_rn(x.y, c.x));
-      *reinterpret_cast<float2*>(src) = make_float2(y0, y1);
-      if (g < G) {
-        q_s[g * HD + 2 * j] = y0;
-        q_s[g * HD + 2 * j + 1] = y1;
-      } else {
-        // The cache holds the row rounded to its type; attention reads it so.
-        Elem* kc = static_cast<Elem*>(p.k_cache) + crow + 2 * j;
-        store_elem<Elem>(kc, y0);
-        store_elem<Elem>(kc + 1, y1);
-        kn_s[2 * j] = as_stored<Elem>(y0);
-        kn_s[2 * j + 1] = as_stored<Elem>(y1);
-      }
+      float* dst = g < G ? q_s + g * HD + 2 * j : kn_s + 2 * j;
+      dst[0] = y0;
+      dst[1] = y1;
     }
-    for (int i = tid; i < HD; i += SMALL_THREADS) {
-      const float v = p.v_new[koff + i];
-      store_elem<Elem>(static_cast<Elem*>(p.v_cache) + crow + i, v);
-      vn_s[i] = as_stored<Elem>(v);
-    }
+    for (int i = tid; i < HD; i += SMALL_THREADS) vn_s[i] = p.v_new[koff + i];
   }
   __syncthreads();
-  if (fuse && tid == pl) {
+  // The new row as the cache stores it (rounded to the cache type).
+  const auto new_k = [&](int d) { return as_stored<Elem>(kn_s[d]); };
+  if (fuse && tid < nloc && lo + tid == pl) {
 #pragma unroll
-    for (int d = 0; d < HD; ++d) kr[d] = kn_s[d];
+    for (int d = 0; d < HD; ++d) kr[d] = new_k(d);
   }
 
-  // 1. Scores, one thread per row.
-  for (int r = tid; r < n; r += SMALL_THREADS) {
-    if (r != tid) {
+  // 1. Scores of this CTA's rows, one thread per row.
+  for (int t = tid; t < nloc; t += SMALL_THREADS) {
+    const int r = lo + t;
+    if (t != tid) {
       if (fuse && r == pl) {
 #pragma unroll
-        for (int d = 0; d < HD; ++d) kr[d] = kn_s[d];
+        for (int d = 0; d < HD; ++d) kr[d] = new_k(d);
       } else {
         load_row64<Elem>(kb + (size_t)r * kdim, vec, kr);
       }
@@ -908,74 +913,60 @@ __global__ void __launch_bounds__(SMALL_THREADS) decode_small_kernel(const Decod
           a2 = fmaf(q4.z, kr[d + 2], a2);
           a3 = fmaf(q4.w, kr[d + 3], a3);
         }
-        s_s[(size_t)g * cap + r] = ((a0 + a1) + (a2 + a3)) * p.scale_log2;
+        s_s[(size_t)g * cap + t] = ((a0 + a1) + (a2 + a3)) * p.scale_log2;
       }
     }
   }
   __syncthreads();
-  // 2. Softmax of head g on warp g.
+  // 2. This CTA's softmax state of head g on warp g: maximum and sum.
   if (warp < G) {
     float* sg = s_s + (size_t)warp * cap;
     float mx = -INFINITY;
-    for (int r = lane; r < n; r += 32) mx = fmaxf(mx, sg[r]);
+    for (int t = lane; t < nloc; t += 32) mx = fmaxf(mx, sg[t]);
     mx = warp_max(mx);
     float sum = 0.f;
-    for (int r = lane; r < n; r += 32) {
-      const float e = ex2(sg[r] - mx);
-      sg[r] = e;
+    for (int t = lane; t < nloc; t += 32) {
+      const float e = ex2(sg[t] - mx);
+      sg[t] = e;
       sum += e;
     }
     sum = warp_sum(sum);
-    if (lane == 0) l_s[warp] = sum;
+    if (lane == 0) {
+      m_s[warp] = mx;
+      l_s[warp] = sum;
+    }
   }
   __syncthreads();
-  // 3. P.V over this warp's rows, every head of the group.
+  // 3. P.V over this warp's share of the CTA's rows, every head of the group.
   float acc[8][2];
 #pragma unroll
   for (int g = 0; g < 8; ++g) acc[g][0] = acc[g][1] = 0.f;
-  const int r0 = (warp * n) / SMALL_WARPS, r1 = ((warp + 1) * n) / SMALL_WARPS;
+  const int t0 = (warp * nloc) / SMALL_WARPS, t1 = ((warp + 1) * nloc) / SMALL_WARPS;
   const Elem* vcol = vb + 2 * lane;
-  int r = r0;
+  const float2 vnew = make_float2(as_stored<Elem>(vn_s[2 * lane]), as_stored<Elem>(vn_s[2 * lane + 1]));
+  int t = t0;
   // 16 rows of V requested at a time: one memory latency per 16 rows.
-  for (; r + 15 < r1; r += 16) {
+  for (; t + 15 < t1; t += 16) {
     float2 v[16];
 #pragma unroll
     for (int u = 0; u < 16; ++u)
-      v[u] = (fuse && r + u == pl) ? make_float2(vn_s[2 * lane], vn_s[2 * lane + 1])
-                                   : load_pair<Elem>(vcol + (size_t)(r + u) * kdim);
+      v[u] = (fuse && lo + t + u == pl) ? vnew : load_pair<Elem>(vcol + (size_t)(lo + t + u) * kdim);
 #pragma unroll
     for (int u = 0; u < 16; ++u)
 #pragma unroll
       for (int g = 0; g < 8; ++g)
         if (g < G) {
-          const float pr = s_s[(size_t)g * cap + r + u];
+          const float pr = s_s[(size_t)g * cap + t + u];
           acc[g][0] = fmaf(pr, v[u].x, acc[g][0]);
           acc[g][1] = fmaf(pr, v[u].y, acc[g][1]);
         }
   }
-  for (; r + 3 < r1; r += 4) {
-    float2 v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u)
-      v[u] = (fuse && r + u == pl) ? make_float2(vn_s[2 * lane], vn_s[2 * lane + 1])
-                                   : load_pair<Elem>(vcol + (size_t)(r + u) * kdim);
-#pragma unroll
-    for (int u = 0; u < 4; ++u)
-#pragma unroll
-      for (int g = 0; g < 8; ++g)
-        if (g < G) {
-          const float pr = s_s[(size_t)g * cap + r + u];
-          acc[g][0] = fmaf(pr, v[u].x, acc[g][0]);
-          acc[g][1] = fmaf(pr, v[u].y, acc[g][1]);
-        }
-  }
-  for (; r < r1; ++r) {
-    const float2 v = (fuse && r == pl) ? make_float2(vn_s[2 * lane], vn_s[2 * lane + 1])
-                                       : load_pair<Elem>(vcol + (size_t)r * kdim);
+  for (; t < t1; ++t) {
+    const float2 v = (fuse && lo + t == pl) ? vnew : load_pair<Elem>(vcol + (size_t)(lo + t) * kdim);
 #pragma unroll
     for (int g = 0; g < 8; ++g)
       if (g < G) {
-        const float pr = s_s[(size_t)g * cap + r];
+        const float pr = s_s[(size_t)g * cap + t];
         acc[g][0] = fmaf(pr, v.x, acc[g][0]);
         acc[g][1] = fmaf(pr, v.y, acc[g][1]);
       }
@@ -986,15 +977,41 @@ __global__ void __launch_bounds__(SMALL_THREADS) decode_small_kernel(const Decod
       *reinterpret_cast<float2*>(o_s + (warp * G + g) * HD + 2 * lane) =
           make_float2(acc[g][0], acc[g][1]);
   __syncthreads();
-  // 4. Sum the warps' partial outputs, normalise, write.
-  float* out = p.out + (size_t)seq * p.n_head * HD + (size_t)kvh * G * HD;
   for (int i = tid; i < G * HD; i += SMALL_THREADS) {
-    const int g = i / HD;
     float o = 0.f;
 #pragma unroll
     for (int w = 0; w < SMALL_WARPS; ++w) o += o_s[w * G * HD + i];
-    out[i] = o / l_s[g];
+    oc_s[i] = o;
   }
+  // 4. Merge the cluster's states: rank c finishes heads c, c + C, ...,
+  //    reading every rank's (m, l, o) through distributed shared memory.
+  cluster.sync();
+  float* out = p.out + qoff;
+  for (int g = crank; g < G; g += C) {
+    for (int d = tid; d < HD; d += SMALL_THREADS) {
+      float M = -INFINITY;
+      for (int c = 0; c < C; ++c) M = fmaxf(M, cluster.map_shared_rank(m_s, c)[g]);
+      float L = 0.f, O = 0.f;
+      for (int c = 0; c < C; ++c) {
+        const float w = ex2(cluster.map_shared_rank(m_s, c)[g] - M);
+        L = fmaf(w, cluster.map_shared_rank(l_s, c)[g], L);
+        O = fmaf(w, cluster.map_shared_rank(oc_s, c)[g * HD + d], O);
+      }
+      out[g * HD + d] = O / L;
+    }
+  }
+  // 5. Rank 0 writes the rotated q / k back and the new row into the cache.
+  if (fuse && crank == 0) {
+    for (int i = tid; i < G * HD; i += SMALL_THREADS) p.q_io[qoff + i] = q_s[i];
+    const size_t crow = (seq_rows + pl) * kdim + kvh * HD;
+    for (int i = tid; i < HD; i += SMALL_THREADS) {
+      p.k_io[koff + i] = kn_s[i];
+      store_elem<Elem>(static_cast<Elem*>(p.k_cache) + crow + i, kn_s[i]);
+      store_elem<Elem>(static_cast<Elem*>(p.v_cache) + crow + i, vn_s[i]);
+    }
+  }
+  // Shared memory stays alive until every rank has read it.
+  cluster.sync();
 }
 
 // ================================================================== merges
@@ -1242,18 +1259,28 @@ cudaError_t launch_decode_mma(const CUtensorMap& tk, const CUtensorMap& tv,
 
 cudaError_t launch_decode_small(const DecodeParams& p, int dtype, cudaStream_t st) {
   if (p.B <= 0) return cudaSuccess;
-  const size_t smem = decode_small_smem(p.group, p.max_ctx);
+  const size_t smem = decode_small_smem(p.group, p.max_ctx, p.split);
   static size_t configured_f32[64] = {}, configured_bf16[64] = {};
-  cudaError_t e;
-  const dim3 grid((unsigned)(p.B * p.n_kv));
-  if (dtype == 0) {
-    e = ensure_smem(decode_small_kernel<float>, smem, configured_f32);
-    if (e != cudaSuccess) return e;
-    return launch_pdl(decode_small_kernel<float>, grid, dim3(SMALL_THREADS), smem, st, p);
-  }
-  e = ensure_smem(decode_small_kernel<__nv_bfloat16>, smem, configured_bf16);
+  void (*fn)(const DecodeParams) =
+      dtype == 0 ? decode_small_kernel<float> : decode_small_kernel<__nv_bfloat16>;
+  cudaError_t e = dtype == 0 ? ensure_smem(decode_small_kernel<float>, smem, configured_f32)
+                             : ensure_smem(decode_small_kernel<__nv_bfloat16>, smem, configured_bf16);
   if (e != cudaSuccess) return e;
-  return launch_pdl(decode_small_kernel<__nv_bfloat16>, grid, dim3(SMALL_THREADS), smem, st, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.B * p.n_kv * p.split));
+  cfg.blockDim = dim3(SMALL_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)p.split;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, fn, p);
 }
 
 cudaError_t launch_decode_generic(const DecodeParams& p, int dtype, int grid,

@@ -28,11 +28,11 @@ size_t decode_generic_smem(int B, int n_head, int n_kv, int hd);
 int decode_generic_blocks_per_sm(int dtype, size_t smem);
 
 // Caches of at most kSmallMaxRows positions, head_dim 64, at most 8 query
-// heads per KV head, mode 0 only: one CTA per (sequence, KV head), writes
-// p.out directly (no merge launch).
+// heads per KV head, mode 0 only: a cluster of p.split (1, 2, 4 or 8) CTAs
+// per (sequence, KV head), writes p.out directly (no merge launch).
 constexpr int kSmallMaxRows = 1024;
 cudaError_t launch_decode_small(const DecodeParams& p, int dtype, cudaStream_t st);
-size_t decode_small_smem(int group, int max_ctx);
+size_t decode_small_smem(int group, int max_ctx, int split);
 
 cudaError_t launch_merge(const MergeParams& p, cudaStream_t st);
 cudaError_t launch_gather_merge(const GatherMergeParams& p, cudaStream_t st);

@@ -95,6 +95,7 @@ struct DecodeParams {
   int table_len;
   void* k_cache;         // layer base of the caches (writable views of k / v)
   void* v_cache;
+  int split;             // short-cache kernel: CTAs (a cluster) per (sequence, KV head)
 };
 
 TG_HD int past_of(const DecodeParams& p, int s) {
