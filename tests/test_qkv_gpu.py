@@ -287,19 +287,23 @@ def test_decode_layer_x_matches_oracle(tg, backend, O, cases, bf16):
     kv2.destroy()
 
 
-@pytest.mark.parametrize("B,ot", [(1, 6), (1, 8), (20, 6)])
-def test_attn_output_matches_oracle(tg, backend, O, cases, B, ot):
+@pytest.mark.parametrize("B,ot,rows,cols", [(1, 6, 896, 896), (1, 8, 896, 896),
+                                            (20, 6, 896, 896), (70, 8, 200, 896),
+                                            (20, 6, 96, 1056)])
+def test_attn_output_matches_oracle(tg, backend, O, cases, B, ot, rows, cols):
     """hidden += W_o context (tmac_gguf.cpp:1129-1140): the product within
-    the summation-order bound, then one rounding of the add.  B = 20 takes
-    the batched kernel."""
-    wo = cases.attn_output_weight(801 + B, ot)
-    ctx = O.normal(802, B * cases.QD).reshape(B, cases.QD)
-    h0 = cases.residual_in(803, B)
+    the summation-order bound, then one rounding of the add.  B >= 9 takes
+    the tensor-core kernel (3xTF32; 200 rows leave a partial 128-row tile,
+    70 sequences a partial group), or past its column limit (1056) the
+    CUDA-core batched kernel."""
+    wo = O.qblocks(ot, 801 + B, rows, cols, cases.D_SCALE[ot])
+    ctx = O.normal(802, B * cols).reshape(B, cols)
+    h0 = O.normal(803, B * rows).reshape(B, rows)
     hid = h0.copy()
-    backend.attn_output(ot, wo, cases.QD, cases.QD, ctx, hid, n_seqs=B)
-    Wf = dequant_np(O, ot, wo, cases.QD, cases.QD)
+    backend.attn_output(ot, wo, rows, cols, ctx, hid, n_seqs=B)
+    Wf = dequant_np(O, ot, wo, rows, cols)
     for s in range(B):
-        ref = O.attn_output(ot, wo, ctx[s], h0[s])
+        ref = h0[s] + O.matmul_q(ot, wo, ctx[s], rows, cols)
         check_within(hid[s], ref, sum_bound(Wf, ctx[s]) + ulp(ref), f"seq {s}")
 
 

@@ -1184,7 +1184,7 @@ int weight_ptr(tg_context* ctx, const void* p, size_t bytes, const void** dev) {
 
 int run_qkv(tg_context* ctx, tg::QkvParams& p) {
   TG_TRY(commit_inputs(ctx));
-  const int per = tg::qkv_use_gemm(p.B, p.cols) ? tg::kQkvGemmRows : tg::kQkvRows;
+  const int per = tg::qkv_rows_per_cta(p.B, p.cols);
   for (int m = 0; m < 3; ++m) p.tiles[m] = (p.rows[m] + per - 1) / per;
   p.err = ctx->d_err;
   cudaEvent_t ev_stop = nullptr;

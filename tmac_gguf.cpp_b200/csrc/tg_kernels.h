@@ -72,5 +72,11 @@ size_t qkv_smem(int cols);
 int qkv_max_cols();
 int qkv_gemm_max_cols();
 bool qkv_use_gemm(int B, int cols);
+// Rows per CTA of the kernel launch_qkv picks for (B, cols): the tensor-core
+// kernel (128) for batches of kQkvGemmMinB+ with cols up to
+// qkv_tc_max_cols(), else the CUDA-core batched kernel or the GEMV.
+int qkv_tc_max_cols();
+bool qkv_use_tc(int B, int cols);
+int qkv_rows_per_cta(int B, int cols);
 
 }  // namespace tg

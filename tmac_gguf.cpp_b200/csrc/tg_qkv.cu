@@ -51,6 +51,7 @@
 #include <utility>
 
 #include "tg_device.cuh"
+#include "tg_tc.cuh"
 #include "tg_kernels.h"
 #include "tg_shared.h"
 
@@ -140,6 +141,33 @@ __device__ __forceinline__ float dot32(const float (&w)[32], const float (&v)[32
     a3 = fmaf(w[k + 3], v[k + 3], a3);
   }
   return (a0 + a1) + (a2 + a3);
+}
+
+// Elements 16h..16h+15 of one block (h = 0 or 1), decoded as decode_block.
+__device__ __forceinline__ void decode_half(const uint8_t* blk, int type, int h, float (&w)[16]) {
+  const uint16_t* hw = reinterpret_cast<const uint16_t*>(blk);
+  const float d = f16_scale(hw[0]);
+  if (type == kWTypeQ5_0) {
+    const uint32_t qh = ((uint32_t)hw[1] | ((uint32_t)hw[2] << 16)) >> (16 * h);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t two = hw[3 + k];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int j = 2 * k + t;
+        const uint32_t byte = (two >> (8 * t)) & 0xffu;
+        const uint32_t lo = h ? (byte >> 4) : (byte & 0xfu);
+        w[j] = d * (float)((int)((((qh >> j) & 1u) << 4) | lo) - 16);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t two = hw[1 + 8 * h + k];
+      w[2 * k] = (float)(int8_t)(two & 0xffu) * d;
+      w[2 * k + 1] = (float)(int8_t)(two >> 8) * d;
+    }
+  }
 }
 
 // Cache element write: fp32, or bf16 rounded to nearest even.
@@ -565,6 +593,385 @@ __global__ void __launch_bounds__(QG_THREADS) qkv_gemm_kernel(const QkvParams p)
   }
 }
 
+// ------------------------------------------------------------ tensor cores
+
+namespace {
+
+constexpr int TC_M = 128;                  // weight rows per CTA (TMEM lanes)
+constexpr int TC_N = kQkvSeqs;             // sequences per CTA (TMEM columns)
+constexpr int TC_KC = 32;                  // columns per chunk: one weight block
+constexpr int TC_STAGES = 2;
+constexpr int TC_A_BYTES = TC_M * TC_KC * 4;  // 16 KB
+constexpr int TC_B_BYTES = TC_N * TC_KC * 4;  // 8 KB
+constexpr int TC_STAGE_BYTES = 2 * TC_A_BYTES + 2 * TC_B_BYTES;  // hi and lo of A and B
+constexpr int TC_THREADS = 288;  // warps 0-7 producers (0-3 also the epilogue), 8 TMEM + MMA
+constexpr uint32_t TC_TMEM_COLS = 64;
+
+struct TcSmem {
+  int raw_off;   // the CTA's raw weight rows
+  int bar_off;   // full[TC_STAGES], empty[TC_STAGES], done
+  int misc_off;  // TMEM base address, abort flag
+  int total;     // bytes to request (with 1 KB for the alignment of the base)
+};
+
+__host__ __device__ inline TcSmem qkv_tc_layout(int cols) {
+  TcSmem L;
+  L.raw_off = TC_STAGES * TC_STAGE_BYTES;
+  L.bar_off = L.raw_off + (((TC_M * (cols / 32) * 34) + 15) & ~15);
+  L.misc_off = L.bar_off + (2 * TC_STAGES + 1) * 8;
+  L.total = 1024 + L.misc_off + 16;
+  return L;
+}
+
+// Instruction descriptor of kind::tf32: fp32 accumulator, tf32 A and B,
+// both K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::tf32.
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Nearest tf32 (10 stored mantissa bits), as a float with the low 13 bits 0.
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t y;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(y) : "f"(x));
+  return __uint_as_float(y);
+}
+
+// Byte offset of element (row r, k) in a K-major tile of 32 four-byte
+// elements per row, 128-byte swizzle (8-row atoms of 1024 bytes).
+__device__ __forceinline__ uint32_t sw128_off(int r, int k) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((((k >> 2) ^ r) & 7) << 4) + ((k & 3) << 2));
+}
+
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err,
+                                        volatile int* abort_flag) {
+  if (*abort_flag) return false;
+  if (mbar_wait(bar, parity, err, kDevErrWaitFull)) return true;
+  *abort_flag = 1;
+  return false;
+}
+
+}  // namespace
+
+// The batched projection on the tensor cores, 3xTF32: a decoded weight (an
+// fp16 scale times a small integer, at most 19 significant bits) is exactly
+// w_hi + w_lo with both parts tf32; x is split into x_hi = tf32(x) and
+// x_lo = x - x_hi; D = w_hi x_hi + w_hi x_lo + w_lo x_hi accumulates in fp32
+// in TMEM (the dropped w_lo x_lo and x_lo's own tf32 rounding are below
+// 2^-21 of |w x|).  CTA (c, g) computes 128 weight rows x 64 sequences:
+//   warps 0-7  producers: per 32-column chunk thread t decodes half of weight
+//              row t % 128's block from the raw rows staged in shared memory
+//              (before the grid-dependency wait) and writes its hi / lo
+//              parts into the stage's A tiles (K-major, 128-byte swizzle),
+//              and splits 8 inputs of sequence t / 4, loaded one chunk
+//              ahead, into the B tiles;
+//   warp 8     allocates the 64 TMEM columns; one thread issues per chunk
+//              12 tcgen05.mma (4 K-steps x 3 products, M128 N64 K8) and
+//              commits the stage back to the producers;
+//   epilogue   warps 0-3 stage the sequences' positions and cos/sin rows in
+//              shared memory, read their rows' 64 sums with tcgen05.ld and
+//              apply mode 0 / 1 / 2 exactly as qkv_kernel does (a RoPE
+//              partner row is the neighbouring lane).
+// Every mbarrier wait is bounded; a failed wait raises the CTA's abort
+// flag, all roles leave their loops, the issued MMAs are drained and TMEM
+// is freed.
+__global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p) {
+  extern __shared__ uint8_t tsm_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) &
+                                           ~uintptr_t(1023));
+  griddep_launch_dependents();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int cols = p.cols, nchunks = cols / TC_KC;
+  const TcSmem L = qkv_tc_layout(cols);
+  uint8_t* raw = sm + L.raw_off;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + L.bar_off);  // 256 producer arrivals
+  uint64_t* empty = full + TC_STAGES;                              // MMA commit
+  uint64_t* done = empty + TC_STAGES;                              // all MMAs complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L.misc_off);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L.misc_off + 4);
+
+  int b = blockIdx.x, m = 0;
+  while (m < 2 && b >= p.tiles[m]) {
+    b -= p.tiles[m];
+    ++m;
+  }
+  const int rows = p.rows[m], r0 = b * TC_M, nr = min(TC_M, rows - r0);
+  const int type = p.wtype[m], bs = wtype_block_bytes(type);
+  const size_t row_bytes = (size_t)(cols >> 5) * bs;
+  const uint8_t* src = p.w[m] + (size_t)r0 * row_bytes;
+  const size_t bytes = (size_t)nr * row_bytes;
+  const int s_begin = blockIdx.y * TC_N, ns = min(TC_N, p.B - s_begin);
+
+  if (tid == 0) {
+    for (int i = 0; i < TC_STAGES; ++i) {
+      mbar_init(&full[i], 256);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TC_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // Raw weight rows into shared memory (constants: before the wait).
+  if (((reinterpret_cast<uintptr_t>(src) | bytes) & 15) == 0) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    uint4* d4 = reinterpret_cast<uint4*>(raw);
+    const int n4 = (int)(bytes >> 4);
+    for (int i0 = 0; i0 < n4; i0 += 4 * TC_THREADS) {
+      uint4 r[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * TC_THREADS + tid;
+        if (i < n4) r[u] = __ldg(s4 + i);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * TC_THREADS + tid;
+        if (i < n4) d4[i] = r[u];
+      }
+    }
+  } else {
+    const uint16_t* s2 = reinterpret_cast<const uint16_t*>(src);
+    uint16_t* d2 = reinterpret_cast<uint16_t*>(raw);
+    const int n2 = (int)(bytes >> 1);
+    for (int i = tid; i < n2; i += TC_THREADS) d2[i] = __ldg(s2 + i);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_wait();
+
+  if (warp < 8) {
+    // ------------------------------------------------------------ producers
+    // Thread t: elements 16h..16h+15 (h = t / 128) of weight row t % 128's
+    // block, and 8 inputs (columns 8u..8u+7, u = t % 4) of sequence t / 4.
+    const int r = tid & (TC_M - 1), h = tid >> 7;
+    const uint8_t* rowp = raw + (size_t)min(r, nr - 1) * row_bytes;
+    const int sq = tid >> 2, u = tid & 3;
+    const bool vec = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
+    const float* xrow = p.x + (size_t)(s_begin + min(sq, ns - 1)) * cols + u * 8;
+    float4 cur[2], nxt[2];
+    auto load = [&](int c, float4 (&d)[2]) {
+      if (sq < ns) {
+        const float* xp = xrow + c * TC_KC;
+        if (vec) {
+          d[0] = __ldg(reinterpret_cast<const float4*>(xp));
+          d[1] = __ldg(reinterpret_cast<const float4*>(xp) + 1);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 2; ++q)
+            d[q] = make_float4(__ldg(xp + 4 * q), __ldg(xp + 4 * q + 1), __ldg(xp + 4 * q + 2),
+                               __ldg(xp + 4 * q + 3));
+        }
+      } else {
+        d[0] = d[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    };
+    load(0, cur);
+    for (int c = 0; c < nchunks; ++c) {
+      if (c + 1 < nchunks) load(c + 1, nxt);
+      const int st = c % TC_STAGES;
+      if (c >= TC_STAGES &&
+          !tc_wait(&empty[st], (uint32_t)(((c / TC_STAGES) & 1) ^ 1), p.err, abort_flag))
+        break;
+      float w[16];
+      if (r < nr) {
+        decode_half(rowp + (size_t)c * bs, type, h, w);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) w[k] = 0.f;
+      }
+      uint8_t* ahi = sm + st * TC_STAGE_BYTES;
+      uint8_t* alo = ahi + TC_A_BYTES;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float4 hi, lo;
+        hi.x = tf32_round(w[4 * j]);
+        hi.y = tf32_round(w[4 * j + 1]);
+        hi.z = tf32_round(w[4 * j + 2]);
+        hi.w = tf32_round(w[4 * j + 3]);
+        lo.x = w[4 * j] - hi.x;
+        lo.y = w[4 * j + 1] - hi.y;
+        lo.z = w[4 * j + 2] - hi.z;
+        lo.w = w[4 * j + 3] - hi.w;
+        const uint32_t off = sw128_off(r, 16 * h + 4 * j);
+        *reinterpret_cast<float4*>(ahi + off) = hi;
+        *reinterpret_cast<float4*>(alo + off) = lo;
+      }
+      uint8_t* bhi = sm + st * TC_STAGE_BYTES + 2 * TC_A_BYTES;
+      uint8_t* blo = bhi + TC_B_BYTES;
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        float4 hi, lo;
+        hi.x = tf32_round(cur[q].x);
+        hi.y = tf32_round(cur[q].y);
+        hi.z = tf32_round(cur[q].z);
+        hi.w = tf32_round(cur[q].w);
+        lo.x = cur[q].x - hi.x;
+        lo.y = cur[q].y - hi.y;
+        lo.z = cur[q].z - hi.z;
+        lo.w = cur[q].w - hi.w;
+        const uint32_t off = sw128_off(sq, 8 * u + 4 * q);
+        *reinterpret_cast<float4*>(bhi + off) = hi;
+        *reinterpret_cast<float4*>(blo + off) = lo;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&full[st]);
+      cur[0] = nxt[0];
+      cur[1] = nxt[1];
+    }
+  } else if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t IDESC = idesc_tf32(TC_M, TC_N);
+    const uint32_t base = smem_u32(sm);
+    bool issued = false;
+    for (int c = 0; c < nchunks; ++c) {
+      const int st = c % TC_STAGES;
+      if (!tc_wait(&full[st], (uint32_t)((c / TC_STAGES) & 1), p.err, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t sa = base + st * TC_STAGE_BYTES;
+      const uint64_t ahi = smem_desc_sw128(sa, 16, 1024);
+      const uint64_t alo = smem_desc_sw128(sa + TC_A_BYTES, 16, 1024);
+      const uint64_t bhi = smem_desc_sw128(sa + 2 * TC_A_BYTES, 16, 1024);
+      const uint64_t blo = smem_desc_sw128(sa + 2 * TC_A_BYTES + TC_B_BYTES, 16, 1024);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {  // 8 tf32 = 32 bytes along K per step: +2
+        umma_tf32(tmem, ahi + 2 * kk, bhi + 2 * kk, IDESC, (c > 0 || kk > 0) ? 1u : 0u);
+        umma_tf32(tmem, ahi + 2 * kk, blo + 2 * kk, IDESC, 1u);
+        umma_tf32(tmem, alo + 2 * kk, bhi + 2 * kk, IDESC, 1u);
+      }
+      umma_commit(&empty[st]);
+      issued = true;
+    }
+    // done completes when every issued MMA has; wait for it (bounded) so
+    // that TMEM is not freed under them.
+    umma_commit(done);
+    if (issued) mbar_wait(done, 0u, p.err, kDevErrWaitFull);
+    if (!issued || *abort_flag) *abort_flag = 1;
+  }
+
+  if (warp < 4) {
+    // ------------------------------------------------------------ epilogue
+    const bool ok = tc_wait(done, 0u, p.err, abort_flag);
+    // Positions and their cos/sin rows of the CTA's sequences, staged once in
+    // the stage buffers (free now that every MMA has completed): the
+    // per-sequence loop below then reads shared memory only.
+    int* pos_s = reinterpret_cast<int*>(sm);
+    float* cs_s = reinterpret_cast<float*>(sm + 256);  // [TC_N][head_dim]
+    const bool pairs_m = p.mode == 1 && m < 2;
+    if (p.mode == 1) {
+      if (tid < ns) pos_s[tid] = p.pos[s_begin + tid];
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (pairs_m) {
+        const int hd = p.head_dim;
+        for (int i = tid; i < ns * hd; i += 128) {
+          const int j = i / hd, d = i - j * hd;
+          const int pos = pos_s[j];
+          cs_s[i] = (pos >= 0 && pos < p.table_len) ? p.cs[(size_t)pos * hd + d] : 0.f;
+        }
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    }
+    if (__all_sync(0xffffffffu, ok)) {
+      tc_fence_after();
+      const int lr = warp * 32 + lane, r = r0 + lr;
+      const bool row_ok = lr < nr;
+      const float* bias = p.bias[m];
+      const float b_own = (bias && row_ok) ? bias[r] : 0.f;
+      const bool pairs = p.mode == 1 && m < 2;
+      const float b_par = __shfl_xor_sync(0xffffffffu, b_own, 1);
+      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
+      // Eight sequences (TMEM columns) per trip: a small loop body that stays
+      // in the instruction cache (a fully unrolled 64-sequence epilogue ran
+      // once per warp from cold instruction memory).
+#pragma unroll 1
+      for (int j0 = 0; j0 < ns; j0 += 8) {
+        uint32_t v[8];
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+            "tcgen05.wait::ld.sync.aligned;"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+              "=r"(v[7])
+            : "r"(taddr + (uint32_t)j0));
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const int j = j0 + t;
+          if (j >= ns) continue;  // warp-uniform
+          const int seq = s_begin + j;
+          float y = __uint_as_float(v[t]);
+          if (pairs) {
+            const float other = __shfl_xor_sync(0xffffffffu, y, 1);
+            if (!row_ok) continue;
+            const bool even = (lr & 1) == 0;
+            float x0 = even ? y : other, x1 = even ? other : y;
+            if (bias) {
+              x0 = __fadd_rn(x0, even ? b_own : b_par);
+              x1 = __fadd_rn(x1, even ? b_par : b_own);
+            }
+            const int pos = pos_s[j];
+            if (pos < 0 || pos >= p.table_len) {
+              record_error(p.err, kDevErrBadPos);
+              continue;
+            }
+            const int re = r & ~1;
+            const float2 cs =
+                *reinterpret_cast<const float2*>(cs_s + j * p.head_dim + re % p.head_dim);
+            const float out = even ? __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y))
+                                   : __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+            const size_t o = (size_t)seq * rows + r;
+            if (m == 0) {
+              p.q_out[o] = out;
+            } else {
+              if (p.k_out) p.k_out[o] = out;
+              const int local = pos - p.shard_start;
+              if (local >= 0 && local < p.max_ctx)
+                cache_store(p.k_cache, ((size_t)seq * p.max_ctx + local) * rows + r, p.dtype,
+                            out);
+            }
+          } else if (row_ok) {
+            if (bias) y = __fadd_rn(y, b_own);
+            if (p.mode != 1) {
+              float* dst = p.y[m] + (size_t)seq * rows + r;
+              *dst = p.mode == 2 ? __fadd_rn(*dst, y) : y;
+            } else {
+              if (p.v_out) p.v_out[(size_t)seq * rows + r] = y;
+              const int local = pos_s[j] - p.shard_start;
+              if (local >= 0 && local < p.max_ctx)
+                cache_store(p.v_cache, ((size_t)seq * p.max_ctx + local) * rows + r, p.dtype, y);
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 8) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(TC_TMEM_COLS)
+                 : "memory");
+  }
+}
+
 size_t qkv_smem(int cols) { return (size_t)qkv_smem_layout(cols).total; }
 
 int qkv_gemm_max_cols() {
@@ -574,6 +981,18 @@ int qkv_gemm_max_cols() {
 }
 
 bool qkv_use_gemm(int B, int cols) { return B >= kQkvGemmMinB && cols <= qkv_gemm_max_cols(); }
+
+int qkv_tc_max_cols() {
+  int c = 32;
+  while (qkv_tc_layout(c + 32).total <= 227 * 1024) c += 32;
+  return c;
+}
+
+bool qkv_use_tc(int B, int cols) { return B >= kQkvGemmMinB && cols <= qkv_tc_max_cols(); }
+
+int qkv_rows_per_cta(int B, int cols) {
+  return qkv_use_tc(B, cols) ? TC_M : (qkv_use_gemm(B, cols) ? kQkvGemmRows : kQkvRows);
+}
 
 int qkv_max_cols() {
   // Largest multiple of 32 whose layout fits the 227 KB opt-in limit.
@@ -585,8 +1004,32 @@ int qkv_max_cols() {
 cudaError_t launch_qkv(const QkvParams& p, cudaStream_t st) {
   const int grid = p.tiles[0] + p.tiles[1] + p.tiles[2];
   if (grid <= 0 || p.B <= 0) return cudaSuccess;
-  const bool gemm = qkv_use_gemm(p.B, p.cols);
   const int groups = (p.B + kQkvSeqs - 1) / kQkvSeqs;
+  if (qkv_use_tc(p.B, p.cols)) {
+    const size_t smem = (size_t)qkv_tc_layout(p.cols).total;
+    static size_t configured_tc[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (smem > configured_tc[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(qkv_tc_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      configured_tc[dev] = smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, groups);
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, qkv_tc_kernel, p);
+  }
+  const bool gemm = qkv_use_gemm(p.B, p.cols);
   const size_t smem = gemm ? (size_t)qkv_gemm_layout(p.cols).total : qkv_smem(p.cols);
   void (*fn)(const QkvParams) = gemm ? qkv_gemm_kernel : qkv_kernel;
   static size_t configured[2][64] = {};
