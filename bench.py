@@ -788,7 +788,7 @@ def main():
                          "unit": "GB/s", "frac": achieved / hbm_peak,
                          "peak_kind": peak_kind,
                          "kernel": ("projection kernels (q/k/v + attn_output), "
-                                    + ("qkv_gemm_kernel" if B >= 9 else "qkv_kernel"))
+                                    + ("qkv_tc_kernel" if B >= 9 else "qkv_kernel"))
                          if qkv else
                          ("decode_fused_kernel" if kv.uses_tensor_cores()
                           else ("decode_small_kernel" if kv.max_ctx <= 1024 and
