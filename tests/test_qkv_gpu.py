@@ -260,6 +260,90 @@ def test_qkv_batched_path_matches_oracle(tg, backend, O, cases, bf16, B):
     kv.destroy()
 
 
+@pytest.mark.parametrize("split", [1, 2, 4, 8])
+def test_qkv_batched_every_cluster_width(tg, backend, O, cases, split):
+    """The tensor-core projection at each cluster width (the CTAs of a
+    cluster split the columns and sum their partials in rank order): RoPE
+    pairs, bias and bf16 cache rows of 70 sequences (a partial second
+    group; rank k finishes sequences 64k/S.. of each group)."""
+    B = 70
+    rng = np.random.default_rng(900 + split)
+    positions = [int(v) for v in rng.integers(0, 300, size=B)]
+    kv, W, X, refs, bounds = _layer_case(tg, backend, O, cases, positions, True, 8, True,
+                                         910 + split)
+    q_out = np.zeros((B, cases.QD), np.float32)
+    tg.set_projection_split(split)
+    try:
+        kv.qkv_rope_cache_write(0, W, X, positions, q_out)
+        backend.synchronize()
+    finally:
+        tg.set_projection_split(0)
+    for i, pos in enumerate(positions):
+        q, k, v = refs[i]
+        bq, bk, bv = bounds[i]
+        check_within(q_out[i], q, bq, f"q seq {i}")
+        kr, vr = kv.read_rows(0, i, pos, 1)
+        check_within(as_f32(kr).reshape(-1), k, bk + np.abs(k) * 2.0 ** -8, f"k row seq {i}")
+        check_within(as_f32(vr).reshape(-1), v, bv + np.abs(v) * 2.0 ** -8, f"v row seq {i}")
+    kv.destroy()
+
+
+@pytest.mark.parametrize("split", [1, 2, 4, 8])
+@pytest.mark.parametrize("B,ot,rows,cols", [(70, 8, 200, 896), (20, 6, 256, 224),
+                                            (12, 8, 130, 32)])
+def test_attn_output_every_cluster_width(tg, backend, O, cases, split, B, ot, rows, cols):
+    """attn_output on the tensor cores at each cluster width: 7 chunks over
+    4 or 8 ranks leave ranks of 1 and 2 chunks, a single chunk clamps the
+    width to 1; the residual add happens once per value."""
+    wo = O.qblocks(ot, 811 + B + split, rows, cols, cases.D_SCALE[ot])
+    ctx = O.normal(812 + split, B * cols).reshape(B, cols)
+    h0 = O.normal(813 + split, B * rows).reshape(B, rows)
+    hid = h0.copy()
+    tg.set_projection_split(split)
+    try:
+        backend.attn_output(ot, wo, rows, cols, ctx, hid, n_seqs=B)
+    finally:
+        tg.set_projection_split(0)
+    Wf = dequant_np(O, ot, wo, rows, cols)
+    for s in range(B):
+        ref = h0[s] + O.matmul_q(ot, wo, ctx[s], rows, cols)
+        check_within(hid[s], ref, sum_bound(Wf, ctx[s]) + ulp(ref), f"seq {s}")
+
+
+def test_fixed_cluster_width_on_the_first_launch():
+    """A fixed width on a process's first tensor-core launch (nothing before
+    it has opted the kernel in to its shared-memory request)."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = (
+        "import sys, numpy as np\n"
+        f"sys.path[:0] = [{root!r}, {os.path.join(root, 'tests')!r}, {os.path.join(root, 'oracle')!r}]\n"
+        "from conftest import load_package\n"
+        "import oracle as O\n"
+        "tg = load_package()\n"
+        "tg.set_projection_split(4)\n"
+        "be = tg.CudaBackend(0)\n"
+        "rows, cols, B = 128, 256, 16\n"
+        "w = O.qblocks(8, 5, rows, cols, 0.01)\n"
+        "x = O.normal(6, B * cols).reshape(B, cols)\n"
+        "h = np.zeros((B, rows), np.float32)\n"
+        "be.attn_output(8, w, rows, cols, x, h, n_seqs=B)\n"
+        "ref = np.stack([O.matmul_q(8, w, x[s], rows, cols) for s in range(B)])\n"
+        "assert np.allclose(h, ref, rtol=1e-5, atol=1e-5), float(np.max(np.abs(h - ref)))\n"
+        "print('ok')\n")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+def test_projection_split_rejects_other_widths(tg):
+    for bad in (3, -1, 16):
+        with pytest.raises(tg.TGError):
+            tg.set_projection_split(bad)
+    tg.set_projection_split(0)
+
+
 @pytest.mark.parametrize("bf16", [False, True], ids=["f32", "bf16"])
 def test_decode_layer_x_matches_oracle(tg, backend, O, cases, bf16):
     """x -> attention output in one call; attention checked on the kernel's
@@ -289,13 +373,13 @@ def test_decode_layer_x_matches_oracle(tg, backend, O, cases, bf16):
 
 @pytest.mark.parametrize("B,ot,rows,cols", [(1, 6, 896, 896), (1, 8, 896, 896),
                                             (20, 6, 896, 896), (70, 8, 200, 896),
-                                            (20, 6, 96, 1056)])
+                                            (20, 6, 96, 1312), (20, 6, 96, 1344)])
 def test_attn_output_matches_oracle(tg, backend, O, cases, B, ot, rows, cols):
     """hidden += W_o context (tmac_gguf.cpp:1129-1140): the product within
     the summation-order bound, then one rounding of the add.  B >= 9 takes
     the tensor-core kernel (3xTF32; 200 rows leave a partial 128-row tile,
-    70 sequences a partial group), or past its column limit (1056) the
-    CUDA-core batched kernel."""
+    70 sequences a partial group; 1312 columns are its limit), or past it
+    (1344) the CUDA-core batched kernel."""
     wo = O.qblocks(ot, 801 + B, rows, cols, cases.D_SCALE[ot])
     ctx = O.normal(802, B * cols).reshape(B, cols)
     h0 = O.normal(803, B * rows).reshape(B, rows)

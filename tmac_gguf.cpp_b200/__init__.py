@@ -158,6 +158,7 @@ _SIGS = {
     "tg_decode_layer_splitkv_x": (C.c_int, [_vp, _vp, C.c_int, C.c_int,
                                             C.POINTER(tg_qkv_weights), _vp, _vp, _vp]),
     "tg_attn_output": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp]),
+    "tg_set_projection_split": (C.c_int, [C.c_int]),
     "tg_model_load_tmac": (C.c_int, [_vp, C.c_char_p, C.POINTER(_vp)]),
     "tg_model_destroy": (C.c_int, [_vp]),
     "tg_model_count": (C.c_int, [_vp, C.POINTER(C.c_int)]),
@@ -218,6 +219,12 @@ def _ptr(x) -> Optional[int]:
             raise ValueError("tensors must be contiguous")
         return x.data_ptr()
     raise TypeError(f"cannot take the address of {type(x).__name__}")
+
+
+def set_projection_split(split: int) -> None:
+    """Cluster width of the tensor-core projections (tg_set_projection_split):
+    1, 2, 4 or 8 CTAs splitting the columns, or 0 for the automatic choice."""
+    _check(lib().tg_set_projection_split(int(split)))
 
 
 def shard_range(global_ctx: int, world: int, rank: int):

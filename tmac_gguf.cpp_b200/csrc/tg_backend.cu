@@ -1876,6 +1876,12 @@ int tg_attn_output(tg_context* ctx, int n_seqs, int wtype, const void* w_o, int 
   return finish_call(ctx);
 }
 
+int tg_set_projection_split(int split) {
+  if (tg::set_qkv_tc_split(split) != 0)
+    return fail(TG_ERR_INVALID_ARG, "projection split %d: 0, 1, 2, 4 or 8", split);
+  return TG_OK;
+}
+
 int tg_fused_qkv_op(tg_context* ctx, const uint8_t* W_q, const uint8_t* W_k, const uint8_t* W_v,
                     const float* x, float* y_q, float* y_k, float* y_v, int q_rows, int k_rows,
                     int v_rows, int cols, int v_is_q8) {

@@ -45,6 +45,7 @@
 // touched only after the wait.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -56,6 +57,8 @@
 #include "tg_shared.h"
 
 namespace tg {
+
+namespace cg = cooperative_groups;
 
 namespace {
 
@@ -600,24 +603,43 @@ namespace {
 constexpr int TC_M = 128;                  // weight rows per CTA (TMEM lanes)
 constexpr int TC_N = kQkvSeqs;             // sequences per CTA (TMEM columns)
 constexpr int TC_KC = 32;                  // columns per chunk: one weight block
-constexpr int TC_STAGES = 2;
-constexpr int TC_A_BYTES = TC_M * TC_KC * 4;  // 16 KB
-constexpr int TC_B_BYTES = TC_N * TC_KC * 4;  // 8 KB
-constexpr int TC_STAGE_BYTES = 2 * TC_A_BYTES + 2 * TC_B_BYTES;  // hi and lo of A and B
-constexpr int TC_THREADS = 288;  // warps 0-7 producers (0-3 also the epilogue), 8 TMEM + MMA
-constexpr uint32_t TC_TMEM_COLS = 64;
+constexpr int TC_STAGES = 3;
+constexpr int TC_B_BYTES = TC_N * TC_KC * 4;     // 8 KB
+constexpr int TC_STAGE_BYTES = 2 * TC_B_BYTES;   // hi and lo of the inputs (B)
+constexpr int TC_THREADS = 288;  // warps 0-7 producers and epilogue, 8 TMEM + MMA
+// TMEM: the accumulator in columns [0, 64); the weights' (A) hi / lo parts of
+// stage s in columns 64 + 64 s + [0, 32) / [32, 64), one tf32 per column.
+constexpr uint32_t TC_A_COL0 = 64;
+constexpr uint32_t TC_TMEM_COLS = 256;
+static_assert(TC_A_COL0 + TC_STAGES * 64 <= TC_TMEM_COLS, "A stages fit the allocation");
+
+constexpr int TC_MAX_SPLIT = 8;  // CTAs per cluster along the columns
+// After the last MMA the stage buffers hold the CTA's partial sums
+// [TC_N][TC_M] fp32, then the positions and cos/sin rows of the sequences
+// the CTA finishes.
+constexpr int TC_PART_BYTES = TC_N * TC_M * 4;  // 32 KB
+// Partials, positions and cos/sin rows (head_dim <= 128): they overlay the
+// stages and raw rows, which are dead once every MMA has completed.
+constexpr int TC_EPI_BYTES = TC_PART_BYTES + 256 + TC_N * 128 * 4;
 
 struct TcSmem {
-  int raw_off;   // the CTA's raw weight rows
+  int raw_off;   // the CTA's raw weight rows (its chunks only)
   int bar_off;   // full[TC_STAGES], empty[TC_STAGES], done
   int misc_off;  // TMEM base address, abort flag
   int total;     // bytes to request (with 1 KB for the alignment of the base)
 };
 
-__host__ __device__ inline TcSmem qkv_tc_layout(int cols) {
+// Chunks of 32 columns that a CTA of a `split`-wide cluster takes at most;
+// rank k takes chunks [k n / split, (k + 1) n / split).
+__host__ __device__ inline int tc_chunks_per_cta(int cols, int split) {
+  return (cols / TC_KC + split - 1) / split;
+}
+
+__host__ __device__ inline TcSmem qkv_tc_layout(int cols, int split) {
   TcSmem L;
   L.raw_off = TC_STAGES * TC_STAGE_BYTES;
-  L.bar_off = L.raw_off + (((TC_M * (cols / 32) * 34) + 15) & ~15);
+  const int raw_end = L.raw_off + (((TC_M * tc_chunks_per_cta(cols, split) * 34) + 15) & ~15);
+  L.bar_off = raw_end > TC_EPI_BYTES ? raw_end : TC_EPI_BYTES;
   L.misc_off = L.bar_off + (2 * TC_STAGES + 1) * 8;
   L.total = 1024 + L.misc_off + 16;
   return L;
@@ -630,14 +652,26 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
          ((uint32_t)(M >> 4) << 24);
 }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc], kind::tf32.
-__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                          uint32_t idesc, uint32_t accumulate) {
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::tf32 (A: lane = row, one
+// tf32 per column along K).
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 16 columns of this warp's 32 TMEM lanes from 16 registers per thread (no
+// wait).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
       : "memory");
 }
 
@@ -669,37 +703,48 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err
 // w_hi + w_lo with both parts tf32; x is split into x_hi = tf32(x) and
 // x_lo = x - x_hi; D = w_hi x_hi + w_hi x_lo + w_lo x_hi accumulates in fp32
 // in TMEM (the dropped w_lo x_lo and x_lo's own tf32 rounding are below
-// 2^-21 of |w x|).  CTA (c, g) computes 128 weight rows x 64 sequences:
-//   warps 0-7  producers: per 32-column chunk thread t decodes half of weight
-//              row t % 128's block from the raw rows staged in shared memory
-//              (before the grid-dependency wait) and writes its hi / lo
-//              parts into the stage's A tiles (K-major, 128-byte swizzle),
-//              and splits 8 inputs of sequence t / 4, loaded one chunk
-//              ahead, into the B tiles;
-//   warp 8     allocates the 64 TMEM columns; one thread issues per chunk
-//              12 tcgen05.mma (4 K-steps x 3 products, M128 N64 K8) and
-//              commits the stage back to the producers;
-//   epilogue   warps 0-3 stage the sequences' positions and cos/sin rows in
-//              shared memory, read their rows' 64 sums with tcgen05.ld and
-//              apply mode 0 / 1 / 2 exactly as qkv_kernel does (a RoPE
-//              partner row is the neighbouring lane).
+// 2^-21 of |w x|).  A cluster of S = gridDim.z CTAs (1, 2, 4 or 8) computes
+// 128 weight rows x 64 sequences; rank k takes the columns of chunks
+// [k n / S, (k + 1) n / S) of the n 32-column chunks:
+//   warps 0-7  producers: per chunk thread t decodes half of weight row
+//              t % 128's block from the raw rows staged in shared memory
+//              (before the grid-dependency wait) and stores its hi / lo
+//              parts into the stage's A columns of TMEM (lane = row: no
+//              shared-memory traffic for the weights), and splits 8 inputs
+//              of sequence t / 4, loaded two chunks ahead, into the stage's
+//              B tiles in shared memory (K-major, 128-byte swizzle);
+//   warp 8     allocates 256 TMEM columns; one thread issues per chunk 12
+//              tcgen05.mma (4 K-steps x 3 products, M128 N64 K8, A from
+//              TMEM) and commits the stage back to the producers;
+//   reduction  warps 0-7 copy the CTA's 128 x 64 partial sums from TMEM to
+//              shared memory; after a cluster barrier rank k sums sequences
+//              [64 k / S, 64 (k + 1) / S) over the cluster's ranks in rank
+//              order (distributed shared memory) and applies mode 0 / 1 / 2
+//              exactly as qkv_kernel does (a RoPE partner row is the
+//              neighbouring lane); a second cluster barrier keeps every
+//              CTA's partials alive until its peers have read them.
 // Every mbarrier wait is bounded; a failed wait raises the CTA's abort
-// flag, all roles leave their loops, the issued MMAs are drained and TMEM
-// is freed.
+// flag, all roles leave their loops, the issued MMAs are drained, every
+// thread still takes both cluster barriers, the cluster stores nothing if
+// any rank aborted, and TMEM is freed.
 __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p) {
   extern __shared__ uint8_t tsm_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) &
                                            ~uintptr_t(1023));
   griddep_launch_dependents();
+  cg::cluster_group cluster = cg::this_cluster();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int cols = p.cols, nchunks = cols / TC_KC;
-  const TcSmem L = qkv_tc_layout(cols);
+  const int split = (int)gridDim.z, rank = (int)blockIdx.z;
+  const int c_begin = rank * nchunks / split, nck = (rank + 1) * nchunks / split - c_begin;
+  const TcSmem L = qkv_tc_layout(cols, split);
   uint8_t* raw = sm + L.raw_off;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + L.bar_off);  // 256 producer arrivals
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + L.bar_off);  // one arrival per producer warp
   uint64_t* empty = full + TC_STAGES;                              // MMA commit
   uint64_t* done = empty + TC_STAGES;                              // all MMAs complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L.misc_off);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L.misc_off + 4);
+  int* abort_ptr = reinterpret_cast<int*>(sm + L.misc_off + 4);
+  volatile int* abort_flag = abort_ptr;
 
   int b = blockIdx.x, m = 0;
   while (m < 2 && b >= p.tiles[m]) {
@@ -708,14 +753,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
   }
   const int rows = p.rows[m], r0 = b * TC_M, nr = min(TC_M, rows - r0);
   const int type = p.wtype[m], bs = wtype_block_bytes(type);
-  const size_t row_bytes = (size_t)(cols >> 5) * bs;
-  const uint8_t* src = p.w[m] + (size_t)r0 * row_bytes;
-  const size_t bytes = (size_t)nr * row_bytes;
+  const size_t row_bytes = (size_t)nchunks * bs;
+  const int seg = nck * bs;  // bytes of each row in this CTA's chunks
+  const uint8_t* src = p.w[m] + (size_t)r0 * row_bytes + (size_t)c_begin * bs;
   const int s_begin = blockIdx.y * TC_N, ns = min(TC_N, p.B - s_begin);
 
   if (tid == 0) {
     for (int i = 0; i < TC_STAGES; ++i) {
-      mbar_init(&full[i], 256);
+      mbar_init(&full[i], 8);
       mbar_init(&empty[i], 1);
     }
     mbar_init(done, 1);
@@ -729,8 +774,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // Raw weight rows into shared memory (constants: before the wait).
-  if (((reinterpret_cast<uintptr_t>(src) | bytes) & 15) == 0) {
+  // Raw weight rows of the CTA's chunks into shared memory, row after row
+  // (constants: before the wait).  One contiguous range when the CTA takes
+  // whole rows, else 2-byte units of nr row segments.
+  const size_t bytes = (size_t)nr * seg;
+  if (nck == nchunks && ((reinterpret_cast<uintptr_t>(src) | bytes) & 15) == 0) {
     const uint4* s4 = reinterpret_cast<const uint4*>(src);
     uint4* d4 = reinterpret_cast<uint4*>(raw);
     const int n4 = (int)(bytes >> 4);
@@ -750,8 +798,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
   } else {
     const uint16_t* s2 = reinterpret_cast<const uint16_t*>(src);
     uint16_t* d2 = reinterpret_cast<uint16_t*>(raw);
-    const int n2 = (int)(bytes >> 1);
-    for (int i = tid; i < n2; i += TC_THREADS) d2[i] = __ldg(s2 + i);
+    const int upr = seg >> 1, stride = (int)(row_bytes >> 1), n2 = nr * upr;
+    for (int i0 = 0; i0 < n2; i0 += 16 * TC_THREADS) {
+      uint16_t r[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int i = i0 + u * TC_THREADS + tid;
+        if (i < n2) {
+          const int row = i / upr;
+          r[u] = __ldg(s2 + (size_t)row * stride + (i - row * upr));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int i = i0 + u * TC_THREADS + tid;
+        if (i < n2) d2[i] = r[u];
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -764,11 +827,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
     // Thread t: elements 16h..16h+15 (h = t / 128) of weight row t % 128's
     // block, and 8 inputs (columns 8u..8u+7, u = t % 4) of sequence t / 4.
     const int r = tid & (TC_M - 1), h = tid >> 7;
-    const uint8_t* rowp = raw + (size_t)min(r, nr - 1) * row_bytes;
+    const uint8_t* rowp = raw + (size_t)min(r, nr - 1) * seg;
     const int sq = tid >> 2, u = tid & 3;
     const bool vec = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
-    const float* xrow = p.x + (size_t)(s_begin + min(sq, ns - 1)) * cols + u * 8;
-    float4 cur[2], nxt[2];
+    const float* xrow =
+        p.x + (size_t)(s_begin + min(sq, ns - 1)) * cols + (size_t)c_begin * TC_KC + u * 8;
+    const uint32_t a_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16) + TC_A_COL0 + 16 * h;
+    float4 cur[2], nxt[2], nxt2[2];
     auto load = [&](int c, float4 (&d)[2]) {
       if (sq < ns) {
         const float* xp = xrow + c * TC_KC;
@@ -786,12 +851,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
       }
     };
     load(0, cur);
-    for (int c = 0; c < nchunks; ++c) {
-      if (c + 1 < nchunks) load(c + 1, nxt);
+    if (nck > 1) load(1, nxt);
+    for (int c = 0; c < nck; ++c) {
+      if (c + 2 < nck) load(c + 2, nxt2);
       const int st = c % TC_STAGES;
-      if (c >= TC_STAGES &&
-          !tc_wait(&empty[st], (uint32_t)(((c / TC_STAGES) & 1) ^ 1), p.err, abort_flag))
-        break;
+      // Lane 0 waits for the stage; the exit is warp-uniform (the TMEM
+      // stores below are warp-collective).
+      if (c >= TC_STAGES) {
+        bool ok = true;
+        if (lane == 0)
+          ok = tc_wait(&empty[st], (uint32_t)(((c / TC_STAGES) & 1) ^ 1), p.err, abort_flag);
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      }
       float w[16];
       if (r < nr) {
         decode_half(rowp + (size_t)c * bs, type, h, w);
@@ -799,24 +870,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
 #pragma unroll
         for (int k = 0; k < 16; ++k) w[k] = 0.f;
       }
-      uint8_t* ahi = sm + st * TC_STAGE_BYTES;
-      uint8_t* alo = ahi + TC_A_BYTES;
+      uint32_t whi[16], wlo[16];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float4 hi, lo;
-        hi.x = tf32_round(w[4 * j]);
-        hi.y = tf32_round(w[4 * j + 1]);
-        hi.z = tf32_round(w[4 * j + 2]);
-        hi.w = tf32_round(w[4 * j + 3]);
-        lo.x = w[4 * j] - hi.x;
-        lo.y = w[4 * j + 1] - hi.y;
-        lo.z = w[4 * j + 2] - hi.z;
-        lo.w = w[4 * j + 3] - hi.w;
-        const uint32_t off = sw128_off(r, 16 * h + 4 * j);
-        *reinterpret_cast<float4*>(ahi + off) = hi;
-        *reinterpret_cast<float4*>(alo + off) = lo;
+      for (int k = 0; k < 16; ++k) {
+        const float hi = tf32_round(w[k]);
+        whi[k] = __float_as_uint(hi);
+        wlo[k] = __float_as_uint(w[k] - hi);
       }
-      uint8_t* bhi = sm + st * TC_STAGE_BYTES + 2 * TC_A_BYTES;
+      const uint32_t ta = a_lane + (uint32_t)(st * 64);
+      tmem_st16(ta, whi);
+      tmem_st16(ta + 32, wlo);
+      uint8_t* bhi = sm + st * TC_STAGE_BYTES;
       uint8_t* blo = bhi + TC_B_BYTES;
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
@@ -833,30 +897,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
         *reinterpret_cast<float4*>(bhi + off) = hi;
         *reinterpret_cast<float4*>(blo + off) = lo;
       }
+      // Each thread orders its own B stores (async proxy) and TMEM stores;
+      // after the warp barrier one arrival publishes the warp's share.
       fence_proxy_async_smem();
-      mbar_arrive(&full[st]);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[st]);
       cur[0] = nxt[0];
       cur[1] = nxt[1];
+      nxt[0] = nxt2[0];
+      nxt[1] = nxt2[1];
     }
   } else if (lane == 0) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t IDESC = idesc_tf32(TC_M, TC_N);
     const uint32_t base = smem_u32(sm);
     bool issued = false;
-    for (int c = 0; c < nchunks; ++c) {
+    for (int c = 0; c < nck; ++c) {
       const int st = c % TC_STAGES;
       if (!tc_wait(&full[st], (uint32_t)((c / TC_STAGES) & 1), p.err, abort_flag)) break;
       tc_fence_after();
-      const uint32_t sa = base + st * TC_STAGE_BYTES;
-      const uint64_t ahi = smem_desc_sw128(sa, 16, 1024);
-      const uint64_t alo = smem_desc_sw128(sa + TC_A_BYTES, 16, 1024);
-      const uint64_t bhi = smem_desc_sw128(sa + 2 * TC_A_BYTES, 16, 1024);
-      const uint64_t blo = smem_desc_sw128(sa + 2 * TC_A_BYTES + TC_B_BYTES, 16, 1024);
+      const uint32_t sb = base + st * TC_STAGE_BYTES;
+      const uint64_t bhi = smem_desc_sw128(sb, 16, 1024);
+      const uint64_t blo = smem_desc_sw128(sb + TC_B_BYTES, 16, 1024);
+      const uint32_t ahi = tmem + TC_A_COL0 + (uint32_t)(st * 64), alo = ahi + 32;
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {  // 8 tf32 = 32 bytes along K per step: +2
-        umma_tf32(tmem, ahi + 2 * kk, bhi + 2 * kk, IDESC, (c > 0 || kk > 0) ? 1u : 0u);
-        umma_tf32(tmem, ahi + 2 * kk, blo + 2 * kk, IDESC, 1u);
-        umma_tf32(tmem, alo + 2 * kk, bhi + 2 * kk, IDESC, 1u);
+      for (int kk = 0; kk < 4; ++kk) {  // K-step: 8 TMEM columns of A, 32 bytes of B (+2)
+        umma_tf32_ts(tmem, ahi + 8 * kk, bhi + 2 * kk, IDESC, (c > 0 || kk > 0) ? 1u : 0u);
+        umma_tf32_ts(tmem, ahi + 8 * kk, blo + 2 * kk, IDESC, 1u);
+        umma_tf32_ts(tmem, alo + 8 * kk, bhi + 2 * kk, IDESC, 1u);
       }
       umma_commit(&empty[st]);
       issued = true;
@@ -868,42 +938,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
     if (!issued || *abort_flag) *abort_flag = 1;
   }
 
-  if (warp < 4) {
-    // ------------------------------------------------------------ epilogue
+  // Sequences this rank finishes, and their staging (stage buffers, free
+  // once every MMA has completed).
+  const int per = TC_N / split, jb = rank * per, je = min(jb + per, ns);
+  float* part = reinterpret_cast<float*>(sm);  // [TC_N][TC_M]
+  int* pos_s = reinterpret_cast<int*>(sm + TC_PART_BYTES);
+  float* cs_s = reinterpret_cast<float*>(sm + TC_PART_BYTES + 256);  // [per][head_dim]
+  const bool pairs = p.mode == 1 && m < 2;
+  if (warp < 8) {
+    // ------------------------------------------------------------ partials
+    // Warp w reads TMEM lanes 32 (w % 4).. and columns 32 (w / 4)..
     const bool ok = tc_wait(done, 0u, p.err, abort_flag);
-    // Positions and their cos/sin rows of the CTA's sequences, staged once in
-    // the stage buffers (free now that every MMA has completed): the
-    // per-sequence loop below then reads shared memory only.
-    int* pos_s = reinterpret_cast<int*>(sm);
-    float* cs_s = reinterpret_cast<float*>(sm + 256);  // [TC_N][head_dim]
-    const bool pairs_m = p.mode == 1 && m < 2;
-    if (p.mode == 1) {
-      if (tid < ns) pos_s[tid] = p.pos[s_begin + tid];
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (pairs_m) {
-        const int hd = p.head_dim;
-        for (int i = tid; i < ns * hd; i += 128) {
-          const int j = i / hd, d = i - j * hd;
-          const int pos = pos_s[j];
-          cs_s[i] = (pos >= 0 && pos < p.table_len) ? p.cs[(size_t)pos * hd + d] : 0.f;
-        }
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-    }
     if (__all_sync(0xffffffffu, ok)) {
       tc_fence_after();
-      const int lr = warp * 32 + lane, r = r0 + lr;
-      const bool row_ok = lr < nr;
-      const float* bias = p.bias[m];
-      const float b_own = (bias && row_ok) ? bias[r] : 0.f;
-      const bool pairs = p.mode == 1 && m < 2;
-      const float b_par = __shfl_xor_sync(0xffffffffu, b_own, 1);
-      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-      // Eight sequences (TMEM columns) per trip: a small loop body that stays
-      // in the instruction cache (a fully unrolled 64-sequence epilogue ran
-      // once per warp from cold instruction memory).
+      const int lr = (warp & 3) * 32 + lane, cb = (warp >> 2) * 32;
+      const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)cb;
 #pragma unroll 1
-      for (int j0 = 0; j0 < ns; j0 += 8) {
+      for (int j0 = 0; j0 < 32; j0 += 8) {
         uint32_t v[8];
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
@@ -912,58 +963,96 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
               "=r"(v[7])
             : "r"(taddr + (uint32_t)j0));
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const int j = j0 + t;
-          if (j >= ns) continue;  // warp-uniform
-          const int seq = s_begin + j;
-          float y = __uint_as_float(v[t]);
-          if (pairs) {
-            const float other = __shfl_xor_sync(0xffffffffu, y, 1);
-            if (!row_ok) continue;
-            const bool even = (lr & 1) == 0;
-            float x0 = even ? y : other, x1 = even ? other : y;
-            if (bias) {
-              x0 = __fadd_rn(x0, even ? b_own : b_par);
-              x1 = __fadd_rn(x1, even ? b_par : b_own);
-            }
-            const int pos = pos_s[j];
-            if (pos < 0 || pos >= p.table_len) {
-              record_error(p.err, kDevErrBadPos);
-              continue;
-            }
-            const int re = r & ~1;
-            const float2 cs =
-                *reinterpret_cast<const float2*>(cs_s + j * p.head_dim + re % p.head_dim);
-            const float out = even ? __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y))
-                                   : __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-            const size_t o = (size_t)seq * rows + r;
-            if (m == 0) {
-              p.q_out[o] = out;
-            } else {
-              if (p.k_out) p.k_out[o] = out;
-              const int local = pos - p.shard_start;
-              if (local >= 0 && local < p.max_ctx)
-                cache_store(p.k_cache, ((size_t)seq * p.max_ctx + local) * rows + r, p.dtype,
-                            out);
-            }
-          } else if (row_ok) {
-            if (bias) y = __fadd_rn(y, b_own);
-            if (p.mode != 1) {
-              float* dst = p.y[m] + (size_t)seq * rows + r;
-              *dst = p.mode == 2 ? __fadd_rn(*dst, y) : y;
-            } else {
-              if (p.v_out) p.v_out[(size_t)seq * rows + r] = y;
-              const int local = pos_s[j] - p.shard_start;
-              if (local >= 0 && local < p.max_ctx)
-                cache_store(p.v_cache, ((size_t)seq * p.max_ctx + local) * rows + r, p.dtype, y);
-            }
+        for (int t = 0; t < 8; ++t) part[(cb + j0 + t) * TC_M + lr] = __uint_as_float(v[t]);
+      }
+    }
+    if (p.mode == 1) {
+      if (tid < je - jb) pos_s[tid] = p.pos[s_begin + jb + tid];
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (pairs) {
+        const int hd = p.head_dim;
+        for (int i = tid; i < (je - jb) * hd; i += 256) {
+          const int j = i / hd, d = i - j * hd;
+          const int pos = pos_s[j];
+          cs_s[i] = (pos >= 0 && pos < p.table_len) ? p.cs[(size_t)pos * hd + d] : 0.f;
+        }
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster.sync();
+
+  if (warp < 8) {
+    // ------------------------------------------------------------ epilogue
+    bool bad = false;
+    const float* peer[TC_MAX_SPLIT];
+#pragma unroll
+    for (int q = 0; q < TC_MAX_SPLIT; ++q) {
+      if (q < split) {
+        bad |= *cluster.map_shared_rank(abort_ptr, q) != 0;
+        peer[q] = cluster.map_shared_rank(part, q);
+      }
+    }
+    if (!bad) {
+      const int lr = tid & (TC_M - 1), r = r0 + lr;
+      const bool row_ok = lr < nr;
+      const float* bias = p.bias[m];
+      const float b_own = (bias && row_ok) ? bias[r] : 0.f;
+      const float b_par = __shfl_xor_sync(0xffffffffu, b_own, 1);
+#pragma unroll 1
+      for (int j = jb + (tid >> 7); j < je; j += 2) {  // warp-uniform
+        const int seq = s_begin + j;
+        float y = peer[0][j * TC_M + lr];
+#pragma unroll
+        for (int q = 1; q < TC_MAX_SPLIT; ++q)
+          if (q < split) y += peer[q][j * TC_M + lr];
+        if (pairs) {
+          const float other = __shfl_xor_sync(0xffffffffu, y, 1);
+          if (!row_ok) continue;
+          const bool even = (lr & 1) == 0;
+          float x0 = even ? y : other, x1 = even ? other : y;
+          if (bias) {
+            x0 = __fadd_rn(x0, even ? b_own : b_par);
+            x1 = __fadd_rn(x1, even ? b_par : b_own);
+          }
+          const int pos = pos_s[j - jb];
+          if (pos < 0 || pos >= p.table_len) {
+            record_error(p.err, kDevErrBadPos);
+            continue;
+          }
+          const int re = r & ~1;
+          const float2 cs = *reinterpret_cast<const float2*>(cs_s + (j - jb) * p.head_dim +
+                                                             re % p.head_dim);
+          const float out = even ? __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y))
+                                 : __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+          const size_t o = (size_t)seq * rows + r;
+          if (m == 0) {
+            p.q_out[o] = out;
+          } else {
+            if (p.k_out) p.k_out[o] = out;
+            const int local = pos - p.shard_start;
+            if (local >= 0 && local < p.max_ctx)
+              cache_store(p.k_cache, ((size_t)seq * p.max_ctx + local) * rows + r, p.dtype, out);
+          }
+        } else if (row_ok) {
+          if (bias) y = __fadd_rn(y, b_own);
+          if (p.mode != 1) {
+            float* dst = p.y[m] + (size_t)seq * rows + r;
+            *dst = p.mode == 2 ? __fadd_rn(*dst, y) : y;
+          } else {
+            if (p.v_out) p.v_out[(size_t)seq * rows + r] = y;
+            const int local = pos_s[j - jb] - p.shard_start;
+            if (local >= 0 && local < p.max_ctx)
+              cache_store(p.v_cache, ((size_t)seq * p.max_ctx + local) * rows + r, p.dtype, y);
           }
         }
       }
     }
   }
-  tc_fence_before();
-  __syncthreads();
+  // Peers read this CTA's partials until they pass this barrier.
+  __syncwarp();
+  cluster.sync();
   tc_fence_after();
   if (warp == 8) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
@@ -984,7 +1073,7 @@ bool qkv_use_gemm(int B, int cols) { return B >= kQkvGemmMinB && cols <= qkv_gem
 
 int qkv_tc_max_cols() {
   int c = 32;
-  while (qkv_tc_layout(c + 32).total <= 227 * 1024) c += 32;
+  while (qkv_tc_layout(c + 32, 1).total <= 227 * 1024) c += 32;
   return c;
 }
 
@@ -1001,32 +1090,104 @@ int qkv_max_cols() {
   return c;
 }
 
+// Clusters of `split` tensor-core CTAs that the device keeps resident at
+// once (cached per device, column count and split).
+static int tc_resident_clusters(int dev, int cols, int split) {
+  struct Entry {
+    int dev, cols, split, n;
+  };
+  static Entry cache[64];
+  static int used = 0;
+  for (int i = 0; i < used; ++i)
+    if (cache[i].dev == dev && cache[i].cols == cols && cache[i].split == split) return cache[i].n;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(split, 1, split);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = (size_t)qkv_tc_layout(cols, split).total;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = (unsigned)split;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, qkv_tc_kernel, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  if (used < 64) cache[used++] = {dev, cols, split, n};
+  return n;
+}
+
+static int g_tc_split_override = 0;
+
+int set_qkv_tc_split(int split) {
+  if (split != 0 && split != 1 && split != 2 && split != 4 && split != 8) return -1;
+  g_tc_split_override = split;
+  return 0;
+}
+
+int qkv_tc_split(int tiles, int cols, int dev) {
+  const int nchunks = cols / TC_KC;
+  if (g_tc_split_override > 0) {
+    int split = g_tc_split_override;
+    while (split > nchunks) split >>= 1;
+    return split;
+  }
+  // Cost in chunk times: waves x (chunks per CTA + ~3 chunks of fixed work:
+  // TMEM allocation, staging, reduction and epilogue); ties keep the
+  // narrower cluster.
+  int best = 0;
+  long best_cost = 0;
+  for (int split = 1; split <= TC_MAX_SPLIT && split <= nchunks; split *= 2) {
+    const int resident = tc_resident_clusters(dev, cols, split);
+    if (resident <= 0) continue;
+    const long waves = (tiles + resident - 1) / resident;
+    const long cost = waves * (tc_chunks_per_cta(cols, split) + 3);
+    if (best == 0 || cost < best_cost) {
+      best = split;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
 cudaError_t launch_qkv(const QkvParams& p, cudaStream_t st) {
   const int grid = p.tiles[0] + p.tiles[1] + p.tiles[2];
   if (grid <= 0 || p.B <= 0) return cudaSuccess;
   const int groups = (p.B + kQkvSeqs - 1) / kQkvSeqs;
   if (qkv_use_tc(p.B, p.cols)) {
-    const size_t smem = (size_t)qkv_tc_layout(p.cols).total;
-    static size_t configured_tc[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (smem > configured_tc[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(qkv_tc_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // Opt in once per device to the largest request the kernel makes (the
+    // whole tensor-core column range at split 1); the occupancy queries of
+    // the split choice need it too.
+    static bool opted_in[64] = {};
+    if (!opted_in[dev]) {
+      cudaError_t e =
+          cudaFuncSetAttribute(qkv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               qkv_tc_layout(qkv_tc_max_cols(), 1).total);
       if (e != cudaSuccess) return e;
-      configured_tc[dev] = smem;
+      opted_in[dev] = true;
     }
+    const int split = qkv_tc_split(grid * groups, p.cols, dev);
+    if (split <= 0) return cudaErrorInvalidConfiguration;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid, groups);
+    cfg.gridDim = dim3(grid, groups, split);
     cfg.blockDim = dim3(TC_THREADS);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = (size_t)qkv_tc_layout(p.cols, split).total;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = (unsigned)split;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, qkv_tc_kernel, p);
   }
   const bool gemm = qkv_use_gemm(p.B, p.cols);
