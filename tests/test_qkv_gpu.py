@@ -373,13 +373,13 @@ def test_decode_layer_x_matches_oracle(tg, backend, O, cases, bf16):
 
 @pytest.mark.parametrize("B,ot,rows,cols", [(1, 6, 896, 896), (1, 8, 896, 896),
                                             (20, 6, 896, 896), (70, 8, 200, 896),
-                                            (20, 6, 96, 1312), (20, 6, 96, 1344)])
+                                            (20, 6, 96, 1088), (20, 6, 96, 1120)])
 def test_attn_output_matches_oracle(tg, backend, O, cases, B, ot, rows, cols):
     """hidden += W_o context (tmac_gguf.cpp:1129-1140): the product within
     the summation-order bound, then one rounding of the add.  B >= 9 takes
     the tensor-core kernel (3xTF32; 200 rows leave a partial 128-row tile,
-    70 sequences a partial group; 1312 columns are its limit), or past it
-    (1344) the CUDA-core batched kernel."""
+    70 sequences a partial group; 1088 columns are its limit), or past it
+    (1120) the CUDA-core batched kernel."""
     wo = O.qblocks(ot, 801 + B, rows, cols, cases.D_SCALE[ot])
     ctx = O.normal(802, B * cols).reshape(B, cols)
     h0 = O.normal(803, B * rows).reshape(B, rows)

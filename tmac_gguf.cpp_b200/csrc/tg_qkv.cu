@@ -617,14 +617,19 @@ constexpr int TC_MAX_SPLIT = 8;  // CTAs per cluster along the columns
 // After the last MMA the stage buffers hold the CTA's partial sums
 // [TC_N][TC_M] fp32, then the positions and cos/sin rows of the sequences
 // the CTA finishes.
-constexpr int TC_PART_BYTES = TC_N * TC_M * 4;  // 32 KB
-// Partials, positions and cos/sin rows (head_dim <= 128): they overlay the
-// stages and raw rows, which are dead once every MMA has completed.
-constexpr int TC_EPI_BYTES = TC_PART_BYTES + 256 + TC_N * 128 * 4;
+// Partial sums received from the cluster's ranks: [split][64 / split][128]
+// fp32 (a region of its own: peers store into it while this CTA may still
+// be in its main loop).
+constexpr int TC_RECV_BYTES = TC_N * TC_M * 4;  // 32 KB
+// Positions and cos/sin rows (head_dim <= 128) overlay the stages, dead once
+// every MMA has completed.
+static_assert(256 + TC_N * 128 * 4 <= TC_STAGES * TC_STAGE_BYTES, "positions fit the stages");
 
 struct TcSmem {
-  int raw_off;   // the CTA's raw weight rows (its chunks only)
-  int bar_off;   // full[TC_STAGES], empty[TC_STAGES], done
+  int raw_off;    // the CTA's raw weight rows (its chunks only)
+  int recv_off;   // partial sums received from the cluster
+  int flags_off;  // abort flags received from the cluster [TC_MAX_SPLIT]
+  int bar_off;    // full[TC_STAGES], empty[TC_STAGES], done
   int misc_off;  // TMEM base address, abort flag
   int total;     // bytes to request (with 1 KB for the alignment of the base)
 };
@@ -635,11 +640,18 @@ __host__ __device__ inline int tc_chunks_per_cta(int cols, int split) {
   return (cols / TC_KC + split - 1) / split;
 }
 
+// Shared-memory slot of one staged row segment of `seg` bytes: the segment
+// keeps its global address's 2-byte phase within 4 bytes (it starts at
+// offset (address & 2)), so that whole 4-byte words line up on both sides.
+__host__ __device__ inline int tc_row_slot(int seg) { return (seg + 2 + 3) & ~3; }
+
 __host__ __device__ inline TcSmem qkv_tc_layout(int cols, int split) {
   TcSmem L;
   L.raw_off = TC_STAGES * TC_STAGE_BYTES;
-  const int raw_end = L.raw_off + (((TC_M * tc_chunks_per_cta(cols, split) * 34) + 15) & ~15);
-  L.bar_off = raw_end > TC_EPI_BYTES ? raw_end : TC_EPI_BYTES;
+  const int raw_end = L.raw_off + TC_M * tc_row_slot(tc_chunks_per_cta(cols, split) * 34);
+  L.recv_off = (raw_end + 15) & ~15;
+  L.flags_off = L.recv_off + TC_RECV_BYTES;
+  L.bar_off = L.flags_off + TC_MAX_SPLIT * 4;
   L.misc_off = L.bar_off + (2 * TC_STAGES + 1) * 8;
   L.total = 1024 + L.misc_off + 16;
   return L;
@@ -688,6 +700,41 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int k) {
   return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((((k >> 2) ^ r) & 7) << 4) + ((k & 3) << 2));
 }
 
+// Stages nr row segments of `seg` bytes (global rows row_bytes apart, every
+// address 2-byte aligned) into slots of tc_row_slot(seg) bytes: warp w takes
+// rows w, w + nwarps, ...; the 4-byte words inside a segment move by
+// cp.async (many in flight, no registers), a 2-byte piece at either end by a
+// plain load and store.  Reads stay inside the segments.  The caller waits
+// with cp.async.wait_all and a barrier.
+__device__ __forceinline__ void tc_stage_rows(uint8_t* raw, const uint8_t* src, size_t row_bytes,
+                                              int seg, int nr, int warp, int lane, int nwarps) {
+  const int slot = tc_row_slot(seg);
+  for (int r = warp; r < nr; r += nwarps) {
+    const uint8_t* a = src + (size_t)r * row_bytes;
+    const int head = (int)(reinterpret_cast<uintptr_t>(a) & 2);  // 0 or 2
+    uint8_t* d = raw + (size_t)r * slot + head;                     // d = a (mod 4)
+    const int words = (seg - head) >> 2;
+    const int tail = seg - head - 4 * words;  // 0 or 2
+    const uint32_t d0 = smem_u32(d + head);
+    for (int k = lane; k < words; k += 32)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d0 + 4u * k),
+                   "l"(a + head + 4 * k)
+                   : "memory");
+    if (lane == 0 && head)
+      *reinterpret_cast<uint16_t*>(d) = __ldg(reinterpret_cast<const uint16_t*>(a));
+    if (lane == 1 && tail)
+      *reinterpret_cast<uint16_t*>(d + head + 4 * words) =
+          __ldg(reinterpret_cast<const uint16_t*>(a + head + 4 * words));
+  }
+}
+
+// Where tc_stage_rows put row r's segment.
+__device__ __forceinline__ const uint8_t* tc_staged_row(const uint8_t* raw, const uint8_t* src,
+                                                        size_t row_bytes, int seg, int r) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(src + (size_t)r * row_bytes);
+  return raw + (size_t)r * tc_row_slot(seg) + (a & 2);
+}
+
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err,
                                         volatile int* abort_flag) {
   if (*abort_flag) return false;
@@ -716,17 +763,19 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err
 //   warp 8     allocates 256 TMEM columns; one thread issues per chunk 12
 //              tcgen05.mma (4 K-steps x 3 products, M128 N64 K8, A from
 //              TMEM) and commits the stage back to the producers;
-//   reduction  warps 0-7 copy the CTA's 128 x 64 partial sums from TMEM to
-//              shared memory; after a cluster barrier rank k sums sequences
-//              [64 k / S, 64 (k + 1) / S) over the cluster's ranks in rank
-//              order (distributed shared memory) and applies mode 0 / 1 / 2
-//              exactly as qkv_kernel does (a RoPE partner row is the
-//              neighbouring lane); a second cluster barrier keeps every
-//              CTA's partials alive until its peers have read them.
+//   reduction  rank k finishes sequences [64 k / S, 64 (k + 1) / S): warps
+//              0-7 read the CTA's 128 x 64 partial sums from TMEM and store
+//              each sequence's into its finishing rank's receive buffer
+//              (distributed shared memory stores: no round trip), every
+//              rank its abort flag likewise; after one cluster barrier rank
+//              k sums its sequences' S partials in rank order from its own
+//              shared memory and applies mode 0 / 1 / 2 exactly as
+//              qkv_kernel does (a RoPE partner row is the neighbouring
+//              lane).
 // Every mbarrier wait is bounded; a failed wait raises the CTA's abort
 // flag, all roles leave their loops, the issued MMAs are drained, every
-// thread still takes both cluster barriers, the cluster stores nothing if
-// any rank aborted, and TMEM is freed.
+// thread still takes the cluster barrier, the cluster stores nothing if any
+// rank aborted, and TMEM is freed.
 __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p) {
   extern __shared__ uint8_t tsm_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) &
@@ -774,48 +823,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // Raw weight rows of the CTA's chunks into shared memory, row after row
-  // (constants: before the wait).  One contiguous range when the CTA takes
-  // whole rows, else 2-byte units of nr row segments.
-  const size_t bytes = (size_t)nr * seg;
-  if (nck == nchunks && ((reinterpret_cast<uintptr_t>(src) | bytes) & 15) == 0) {
-    const uint4* s4 = reinterpret_cast<const uint4*>(src);
-    uint4* d4 = reinterpret_cast<uint4*>(raw);
-    const int n4 = (int)(bytes >> 4);
-    for (int i0 = 0; i0 < n4; i0 += 4 * TC_THREADS) {
-      uint4 r[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int i = i0 + u * TC_THREADS + tid;
-        if (i < n4) r[u] = __ldg(s4 + i);
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int i = i0 + u * TC_THREADS + tid;
-        if (i < n4) d4[i] = r[u];
-      }
-    }
-  } else {
-    const uint16_t* s2 = reinterpret_cast<const uint16_t*>(src);
-    uint16_t* d2 = reinterpret_cast<uint16_t*>(raw);
-    const int upr = seg >> 1, stride = (int)(row_bytes >> 1), n2 = nr * upr;
-    for (int i0 = 0; i0 < n2; i0 += 16 * TC_THREADS) {
-      uint16_t r[16];
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const int i = i0 + u * TC_THREADS + tid;
-        if (i < n2) {
-          const int row = i / upr;
-          r[u] = __ldg(s2 + (size_t)row * stride + (i - row * upr));
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const int i = i0 + u * TC_THREADS + tid;
-        if (i < n2) d2[i] = r[u];
-      }
-    }
-  }
+  // Raw weight rows of the CTA's chunks into shared memory (constants:
+  // before the wait).
+  tc_stage_rows(raw, src, row_bytes, seg, nr, warp, lane, TC_THREADS / 32);
+  asm volatile("cp.async.wait_all;" ::: "memory");
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -827,7 +838,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
     // Thread t: elements 16h..16h+15 (h = t / 128) of weight row t % 128's
     // block, and 8 inputs (columns 8u..8u+7, u = t % 4) of sequence t / 4.
     const int r = tid & (TC_M - 1), h = tid >> 7;
-    const uint8_t* rowp = raw + (size_t)min(r, nr - 1) * seg;
+    const uint8_t* rowp = tc_staged_row(raw, src, row_bytes, seg, min(r, nr - 1));
     const int sq = tid >> 2, u = tid & 3;
     const bool vec = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
     const float* xrow =
@@ -938,20 +949,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
     if (!issued || *abort_flag) *abort_flag = 1;
   }
 
-  // Sequences this rank finishes, and their staging (stage buffers, free
-  // once every MMA has completed).
+  // Sequences this rank finishes; positions and cos/sin rows staged in the
+  // stage buffers (free once every MMA has completed).
   const int per = TC_N / split, jb = rank * per, je = min(jb + per, ns);
-  float* part = reinterpret_cast<float*>(sm);  // [TC_N][TC_M]
-  int* pos_s = reinterpret_cast<int*>(sm + TC_PART_BYTES);
-  float* cs_s = reinterpret_cast<float*>(sm + TC_PART_BYTES + 256);  // [per][head_dim]
+  float* recv = reinterpret_cast<float*>(sm + L.recv_off);  // [split][per][TC_M]
+  int* flags = reinterpret_cast<int*>(sm + L.flags_off);
+  int* pos_s = reinterpret_cast<int*>(sm);
+  float* cs_s = reinterpret_cast<float*>(sm + 256);  // [per][head_dim]
   const bool pairs = p.mode == 1 && m < 2;
+  const int lr = tid & (TC_M - 1), r = r0 + lr;  // epilogue row (warps 0-7)
+  const bool row_ok = lr < nr;
+  const float* bias = p.bias[m];
+  float b_own = 0.f;
   if (warp < 8) {
     // ------------------------------------------------------------ partials
-    // Warp w reads TMEM lanes 32 (w % 4).. and columns 32 (w / 4)..
     const bool ok = tc_wait(done, 0u, p.err, abort_flag);
+    if (bias && row_ok) b_own = __ldg(bias + r);  // in flight during the stores
     if (__all_sync(0xffffffffu, ok)) {
+      // Warp w reads TMEM lanes 32 (w % 4).. and columns 32 (w / 4)..; the
+      // sums of column j go to rank j / per, slot [rank][j % per].
       tc_fence_after();
-      const int lr = (warp & 3) * 32 + lane, cb = (warp >> 2) * 32;
+      const int cb = (warp >> 2) * 32;
       const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)cb;
 #pragma unroll 1
       for (int j0 = 0; j0 < 32; j0 += 8) {
@@ -962,8 +980,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
             : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
               "=r"(v[7])
             : "r"(taddr + (uint32_t)j0));
+        const int owner = (cb + j0) / per;  // the 8 columns share one owner (per >= 8)
+        float* dst = owner == rank ? recv : cluster.map_shared_rank(recv, owner);
+        dst += (rank * per + (cb + j0 - owner * per)) * TC_M + lr;
 #pragma unroll
-        for (int t = 0; t < 8; ++t) part[(cb + j0 + t) * TC_M + lr] = __uint_as_float(v[t]);
+        for (int t = 0; t < 8; ++t) dst[t * TC_M] = __uint_as_float(v[t]);
       }
     }
     if (p.mode == 1) {
@@ -981,79 +1002,94 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
   }
   __syncwarp();
   tc_fence_before();
+  __syncthreads();  // every role has finished: this CTA's abort flag is final
+  if (tid < split)
+    (tid == rank ? flags : cluster.map_shared_rank(flags, tid))[rank] = *abort_flag;
+  // The cluster's partial sums and flags are in this CTA's shared memory
+  // after this barrier; no CTA touches another's shared memory after it.
   cluster.sync();
+  tc_fence_after();
 
   if (warp < 8) {
     // ------------------------------------------------------------ epilogue
     bool bad = false;
-    const float* peer[TC_MAX_SPLIT];
 #pragma unroll
-    for (int q = 0; q < TC_MAX_SPLIT; ++q) {
-      if (q < split) {
-        bad |= *cluster.map_shared_rank(abort_ptr, q) != 0;
-        peer[q] = cluster.map_shared_rank(part, q);
-      }
-    }
+    for (int q = 0; q < TC_MAX_SPLIT; ++q)
+      if (q < split) bad |= flags[q] != 0;
     if (!bad) {
-      const int lr = tid & (TC_M - 1), r = r0 + lr;
-      const bool row_ok = lr < nr;
-      const float* bias = p.bias[m];
-      const float b_own = (bias && row_ok) ? bias[r] : 0.f;
       const float b_par = __shfl_xor_sync(0xffffffffu, b_own, 1);
+      // Eight sequences per trip: every residual load (mode 2) of the trip
+      // is issued before the first is used.
+      constexpr int EU = 8;
 #pragma unroll 1
-      for (int j = jb + (tid >> 7); j < je; j += 2) {  // warp-uniform
-        const int seq = s_begin + j;
-        float y = peer[0][j * TC_M + lr];
+      for (int j0 = jb + (tid >> 7); j0 < je; j0 += 2 * EU) {  // warp-uniform
+        float yv[EU], hv[EU];
 #pragma unroll
-        for (int q = 1; q < TC_MAX_SPLIT; ++q)
-          if (q < split) y += peer[q][j * TC_M + lr];
-        if (pairs) {
-          const float other = __shfl_xor_sync(0xffffffffu, y, 1);
-          if (!row_ok) continue;
-          const bool even = (lr & 1) == 0;
-          float x0 = even ? y : other, x1 = even ? other : y;
-          if (bias) {
-            x0 = __fadd_rn(x0, even ? b_own : b_par);
-            x1 = __fadd_rn(x1, even ? b_par : b_own);
+        for (int u = 0; u < EU; ++u) {
+          const int j = j0 + 2 * u;
+          yv[u] = 0.f;
+          hv[u] = 0.f;
+          if (j < je) {
+            const float* rp = recv + (j - jb) * TC_M + lr;
+            float y = rp[0];
+#pragma unroll
+            for (int q = 1; q < TC_MAX_SPLIT; ++q)
+              if (q < split) y += rp[q * per * TC_M];  // rank order
+            yv[u] = y;
+            if (p.mode == 2 && row_ok) hv[u] = p.y[m][(size_t)(s_begin + j) * rows + r];
           }
-          const int pos = pos_s[j - jb];
-          if (pos < 0 || pos >= p.table_len) {
-            record_error(p.err, kDevErrBadPos);
-            continue;
-          }
-          const int re = r & ~1;
-          const float2 cs = *reinterpret_cast<const float2*>(cs_s + (j - jb) * p.head_dim +
-                                                             re % p.head_dim);
-          const float out = even ? __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y))
-                                 : __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-          const size_t o = (size_t)seq * rows + r;
-          if (m == 0) {
-            p.q_out[o] = out;
-          } else {
-            if (p.k_out) p.k_out[o] = out;
-            const int local = pos - p.shard_start;
-            if (local >= 0 && local < p.max_ctx)
-              cache_store(p.k_cache, ((size_t)seq * p.max_ctx + local) * rows + r, p.dtype, out);
-          }
-        } else if (row_ok) {
-          if (bias) y = __fadd_rn(y, b_own);
-          if (p.mode != 1) {
-            float* dst = p.y[m] + (size_t)seq * rows + r;
-            *dst = p.mode == 2 ? __fadd_rn(*dst, y) : y;
-          } else {
-            if (p.v_out) p.v_out[(size_t)seq * rows + r] = y;
-            const int local = pos_s[j - jb] - p.shard_start;
-            if (local >= 0 && local < p.max_ctx)
-              cache_store(p.v_cache, ((size_t)seq * p.max_ctx + local) * rows + r, p.dtype, y);
+        }
+#pragma unroll
+        for (int u = 0; u < EU; ++u) {
+          const int j = j0 + 2 * u;
+          if (j >= je) break;  // warp-uniform
+          const int seq = s_begin + j;
+          float y = yv[u];
+          if (pairs) {
+            const float other = __shfl_xor_sync(0xffffffffu, y, 1);
+            if (!row_ok) continue;
+            const bool even = (lr & 1) == 0;
+            float x0 = even ? y : other, x1 = even ? other : y;
+            if (bias) {
+              x0 = __fadd_rn(x0, even ? b_own : b_par);
+              x1 = __fadd_rn(x1, even ? b_par : b_own);
+            }
+            const int pos = pos_s[j - jb];
+            if (pos < 0 || pos >= p.table_len) {
+              record_error(p.err, kDevErrBadPos);
+              continue;
+            }
+            const int re = r & ~1;
+            const float2 cs = *reinterpret_cast<const float2*>(cs_s + (j - jb) * p.head_dim +
+                                                               re % p.head_dim);
+            const float out = even ? __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y))
+                                   : __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+            const size_t o = (size_t)seq * rows + r;
+            if (m == 0) {
+              p.q_out[o] = out;
+            } else {
+              if (p.k_out) p.k_out[o] = out;
+              const int local = pos - p.shard_start;
+              if (local >= 0 && local < p.max_ctx)
+                cache_store(p.k_cache, ((size_t)seq * p.max_ctx + local) * rows + r, p.dtype,
+                            out);
+            }
+          } else if (row_ok) {
+            if (bias) y = __fadd_rn(y, b_own);
+            if (p.mode != 1) {
+              p.y[m][(size_t)seq * rows + r] = p.mode == 2 ? __fadd_rn(hv[u], y) : y;
+            } else {
+              if (p.v_out) p.v_out[(size_t)seq * rows + r] = y;
+              const int local = pos_s[j - jb] - p.shard_start;
+              if (local >= 0 && local < p.max_ctx)
+                cache_store(p.v_cache, ((size_t)seq * p.max_ctx + local) * rows + r, p.dtype,
+                            y);
+            }
           }
         }
       }
     }
   }
-  // Peers read this CTA's partials until they pass this barrier.
-  __syncwarp();
-  cluster.sync();
-  tc_fence_after();
   if (warp == 8) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(TC_TMEM_COLS)
