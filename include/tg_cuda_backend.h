@@ -190,11 +190,11 @@ TG_API int tg_attn_output(tg_context* ctx, int n_seqs, int wtype, const void* w_
                           int cols, const float* context, float* hidden);
 
 /* Tuning: projections of 9+ sequences run on the tensor cores in clusters
- * of 1, 2, 4 or 8 CTAs that split the columns (chosen per launch from the
- * device's resident-cluster count).  split 1 / 2 / 4 / 8 fixes the width
- * for later launches of every context (clamped to cols / 32), 0 restores
- * the automatic choice; other values give TG_ERR_INVALID_ARG.  Results
- * differ between widths only by the order of the fp32 partial sums. */
+ * of 1 to 8 CTAs that split the columns (chosen per launch from the
+ * device's resident-cluster count).  split 1-8 fixes the width for later
+ * launches of every context (clamped to cols / 32), 0 restores the
+ * automatic choice; other values give TG_ERR_INVALID_ARG.  Results differ
+ * between widths only by the order of the fp32 partial sums. */
 TG_API int tg_set_projection_split(int split);
 
 /* One layer's projection weights: W_q has n_head*head_dim rows, W_k and

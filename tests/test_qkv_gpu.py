@@ -260,7 +260,7 @@ def test_qkv_batched_path_matches_oracle(tg, backend, O, cases, bf16, B):
     kv.destroy()
 
 
-@pytest.mark.parametrize("split", [1, 2, 4, 8])
+@pytest.mark.parametrize("split", [1, 2, 3, 4, 7, 8])
 def test_qkv_batched_every_cluster_width(tg, backend, O, cases, split):
     """The tensor-core projection at each cluster width (the CTAs of a
     cluster split the columns and sum their partials in rank order): RoPE
@@ -288,13 +288,14 @@ def test_qkv_batched_every_cluster_width(tg, backend, O, cases, split):
     kv.destroy()
 
 
-@pytest.mark.parametrize("split", [1, 2, 4, 8])
+@pytest.mark.parametrize("split", [1, 2, 3, 4, 5, 6, 7, 8])
 @pytest.mark.parametrize("B,ot,rows,cols", [(70, 8, 200, 896), (20, 6, 256, 224),
                                             (12, 8, 130, 32)])
 def test_attn_output_every_cluster_width(tg, backend, O, cases, split, B, ot, rows, cols):
     """attn_output on the tensor cores at each cluster width: 7 chunks over
     4 or 8 ranks leave ranks of 1 and 2 chunks, a single chunk clamps the
-    width to 1; the residual add happens once per value."""
+    width to 1, widths 3, 5, 6 and 7 split the 64 sequence columns of a
+    group unevenly; the residual add happens once per value."""
     wo = O.qblocks(ot, 811 + B + split, rows, cols, cases.D_SCALE[ot])
     ctx = O.normal(812 + split, B * cols).reshape(B, cols)
     h0 = O.normal(813 + split, B * rows).reshape(B, rows)
@@ -338,7 +339,7 @@ def test_fixed_cluster_width_on_the_first_launch():
 
 
 def test_projection_split_rejects_other_widths(tg):
-    for bad in (3, -1, 16):
+    for bad in (9, -1, 16):
         with pytest.raises(tg.TGError):
             tg.set_projection_split(bad)
     tg.set_projection_split(0)
@@ -373,13 +374,13 @@ def test_decode_layer_x_matches_oracle(tg, backend, O, cases, bf16):
 
 @pytest.mark.parametrize("B,ot,rows,cols", [(1, 6, 896, 896), (1, 8, 896, 896),
                                             (20, 6, 896, 896), (70, 8, 200, 896),
-                                            (20, 6, 96, 1088), (20, 6, 96, 1120)])
+                                            (20, 6, 96, 1056), (20, 6, 96, 1088)])
 def test_attn_output_matches_oracle(tg, backend, O, cases, B, ot, rows, cols):
     """hidden += W_o context (tmac_gguf.cpp:1129-1140): the product within
     the summation-order bound, then one rounding of the add.  B >= 9 takes
     the tensor-core kernel (3xTF32; 200 rows leave a partial 128-row tile,
-    70 sequences a partial group; 1088 columns are its limit), or past it
-    (1120) the CUDA-core batched kernel."""
+    70 sequences a partial group; 1056 columns are its limit), or past it
+    (1088) the CUDA-core batched kernel."""
     wo = O.qblocks(ot, 801 + B, rows, cols, cases.D_SCALE[ot])
     ctx = O.normal(802, B * cols).reshape(B, cols)
     h0 = O.normal(803, B * rows).reshape(B, rows)

@@ -223,7 +223,7 @@ def _ptr(x) -> Optional[int]:
 
 def set_projection_split(split: int) -> None:
     """Cluster width of the tensor-core projections (tg_set_projection_split):
-    1, 2, 4 or 8 CTAs splitting the columns, or 0 for the automatic choice."""
+    1 to 8 CTAs splitting the columns, or 0 for the automatic choice."""
     _check(lib().tg_set_projection_split(int(split)))
 
 

@@ -1878,7 +1878,7 @@ int tg_attn_output(tg_context* ctx, int n_seqs, int wtype, const void* w_o, int 
 
 int tg_set_projection_split(int split) {
   if (tg::set_qkv_tc_split(split) != 0)
-    return fail(TG_ERR_INVALID_ARG, "projection split %d: 0, 1, 2, 4 or 8", split);
+    return fail(TG_ERR_INVALID_ARG, "projection split %d: 0 to 8", split);
   return TG_OK;
 }
 

@@ -76,12 +76,12 @@ bool qkv_use_gemm(int B, int cols);
 // kernel (128) for batches of kQkvGemmMinB+ with cols up to
 // qkv_tc_max_cols(), else the CUDA-core batched kernel or the GEMV.
 int qkv_tc_max_cols();
-// Cluster width (1, 2, 4 or 8 CTAs splitting the columns) of a tensor-core
+// Cluster width (1 to 8 CTAs splitting the columns) of a tensor-core
 // projection launch of `tiles` row tiles x sequence groups on device dev,
 // from the device's resident-cluster count; 0 if none fits.
 int qkv_tc_split(int tiles, int cols, int dev);
-// Fixes the cluster width of later launches (1, 2, 4 or 8, clamped to the
-// chunk count) or restores the automatic choice (0); -1 for other values.
+// Fixes the cluster width of later launches (1 to 8, clamped to the chunk
+// count) or restores the automatic choice (0); -1 for other values.
 int set_qkv_tc_split(int split);
 bool qkv_use_tc(int B, int cols);
 int qkv_rows_per_cta(int B, int cols);

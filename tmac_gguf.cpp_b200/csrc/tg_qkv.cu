@@ -617,10 +617,16 @@ constexpr int TC_MAX_SPLIT = 8;  // CTAs per cluster along the columns
 // After the last MMA the stage buffers hold the CTA's partial sums
 // [TC_N][TC_M] fp32, then the positions and cos/sin rows of the sequences
 // the CTA finishes.
-// Partial sums received from the cluster's ranks: [split][64 / split][128]
-// fp32 (a region of its own: peers store into it while this CTA may still
-// be in its main loop).
-constexpr int TC_RECV_BYTES = TC_N * TC_M * 4;  // 32 KB
+// Rank k of a cluster of S finishes sequence columns [64 k / S, 64 (k + 1) / S)
+// of its group, at most tc_per(S) of them.
+__host__ __device__ constexpr int tc_per(int split) { return (TC_N + split - 1) / split; }
+// Partial sums received from the cluster's ranks: [split][tc_per][128] fp32
+// (a region of its own: peers store into it while this CTA may still be in
+// its main loop); the largest over widths 1-8 (7 x 10 columns).
+constexpr int TC_RECV_BYTES = 70 * TC_M * 4;  // 35 KB
+static_assert(7 * tc_per(7) <= 70 && 6 * tc_per(6) <= 70 && 5 * tc_per(5) <= 70 &&
+                  3 * tc_per(3) <= 70 && 8 * tc_per(8) <= 70,
+              "receive buffer holds every width");
 // Positions and cos/sin rows (head_dim <= 128) overlay the stages, dead once
 // every MMA has completed.
 static_assert(256 + TC_N * 128 * 4 <= TC_STAGES * TC_STAGE_BYTES, "positions fit the stages");
@@ -750,7 +756,7 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err
 // w_hi + w_lo with both parts tf32; x is split into x_hi = tf32(x) and
 // x_lo = x - x_hi; D = w_hi x_hi + w_hi x_lo + w_lo x_hi accumulates in fp32
 // in TMEM (the dropped w_lo x_lo and x_lo's own tf32 rounding are below
-// 2^-21 of |w x|).  A cluster of S = gridDim.z CTAs (1, 2, 4 or 8) computes
+// 2^-21 of |w x|).  A cluster of S = gridDim.z CTAs (1 to 8) computes
 // 128 weight rows x 64 sequences; rank k takes the columns of chunks
 // [k n / S, (k + 1) n / S) of the n 32-column chunks:
 //   warps 0-7  producers: per chunk thread t decodes half of weight row
@@ -951,7 +957,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
 
   // Sequences this rank finishes; positions and cos/sin rows staged in the
   // stage buffers (free once every MMA has completed).
-  const int per = TC_N / split, jb = rank * per, je = min(jb + per, ns);
+  const int per = tc_per(split), jb = rank * TC_N / split;
+  const int je = min((rank + 1) * TC_N / split, ns);
   float* recv = reinterpret_cast<float*>(sm + L.recv_off);  // [split][per][TC_M]
   int* flags = reinterpret_cast<int*>(sm + L.flags_off);
   int* pos_s = reinterpret_cast<int*>(sm);
@@ -967,10 +974,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
     if (bias && row_ok) b_own = __ldg(bias + r);  // in flight during the stores
     if (__all_sync(0xffffffffu, ok)) {
       // Warp w reads TMEM lanes 32 (w % 4).. and columns 32 (w / 4)..; the
-      // sums of column j go to rank j / per, slot [rank][j % per].
+      // sums of column j go to the rank k that finishes it, slot
+      // [rank][j - 64 k / S].
       tc_fence_after();
       const int cb = (warp >> 2) * 32;
       const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)cb;
+      // Owner of the current column and its column range [b_lo, b_hi);
+      // owners only grow with the column, by at most one per 8 columns.
+      int owner = 0, b_lo = 0, b_hi = TC_N / split;
+      while (cb >= b_hi) {
+        ++owner;
+        b_lo = b_hi;
+        b_hi = (owner + 1) * TC_N / split;
+      }
+      auto slot_base = [&]() {
+        return (owner == rank ? recv : cluster.map_shared_rank(recv, owner)) +
+               (rank * per - b_lo) * TC_M + lr;
+      };
+      float* base = slot_base();  // column j of the owner: base[j * TC_M]
 #pragma unroll 1
       for (int j0 = 0; j0 < 32; j0 += 8) {
         uint32_t v[8];
@@ -980,11 +1001,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qkv_tc_kernel(const QkvParams p
             : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
               "=r"(v[7])
             : "r"(taddr + (uint32_t)j0));
-        const int owner = (cb + j0) / per;  // the 8 columns share one owner (per >= 8)
-        float* dst = owner == rank ? recv : cluster.map_shared_rank(recv, owner);
-        dst += (rank * per + (cb + j0 - owner * per)) * TC_M + lr;
 #pragma unroll
-        for (int t = 0; t < 8; ++t) dst[t * TC_M] = __uint_as_float(v[t]);
+        for (int t = 0; t < 8; ++t) {
+          const int j = cb + j0 + t;
+          if (j >= b_hi) {  // warp-uniform
+            ++owner;
+            b_lo = b_hi;
+            b_hi = (owner + 1) * TC_N / split;
+            base = slot_base();
+          }
+          base[j * TC_M] = __uint_as_float(v[t]);
+        }
       }
     }
     if (p.mode == 1) {
@@ -1159,7 +1186,7 @@ static int tc_resident_clusters(int dev, int cols, int split) {
 static int g_tc_split_override = 0;
 
 int set_qkv_tc_split(int split) {
-  if (split != 0 && split != 1 && split != 2 && split != 4 && split != 8) return -1;
+  if (split < 0 || split > TC_MAX_SPLIT) return -1;
   g_tc_split_override = split;
   return 0;
 }
@@ -1167,16 +1194,14 @@ int set_qkv_tc_split(int split) {
 int qkv_tc_split(int tiles, int cols, int dev) {
   const int nchunks = cols / TC_KC;
   if (g_tc_split_override > 0) {
-    int split = g_tc_split_override;
-    while (split > nchunks) split >>= 1;
-    return split;
+    return g_tc_split_override < nchunks ? g_tc_split_override : nchunks;
   }
   // Cost in chunk times: waves x (chunks per CTA + ~3 chunks of fixed work:
   // TMEM allocation, staging, reduction and epilogue); ties keep the
   // narrower cluster.
   int best = 0;
   long best_cost = 0;
-  for (int split = 1; split <= TC_MAX_SPLIT && split <= nchunks; split *= 2) {
+  for (int split = 1; split <= TC_MAX_SPLIT && split <= nchunks; ++split) {
     const int resident = tc_resident_clusters(dev, cols, split);
     if (resident <= 0) continue;
     const long waves = (tiles + resident - 1) / resident;
