@@ -38,6 +38,47 @@ def test_prefill_matches_token_by_token_oracle(tg, backend, O, cases, S):
         assert np.array_equal(vrow, O.pack_bf16(vb))
 
 
+@pytest.mark.parametrize("S", [1, 127])
+def test_prefill_odd_row_count(tg, backend, O, cases, S):
+    """One sequence of odd length (the other cases run two sequences): the
+    rotated k rows and the v rows in the cache are bit-exact."""
+    kv, out = run_prefill(tg, backend, cases, S, B=1, seed=17)
+    qb, kb, vb = cases.prefill_inputs(17, S, seq=0)
+    assert float(np.abs(out[0] - O.prefill_causal(qb, kb, vb)).max()) <= TOL
+    krow, vrow = kv.read_rows(0, 0, 0, S)
+    assert np.array_equal(krow, O.pack_bf16(kb))
+    assert np.array_equal(vrow, O.pack_bf16(vb))
+
+
+def test_prefill_unaligned_device_inputs(tg, backend, cases):
+    """q / k / v device buffers 4 bytes off a 16-byte boundary take the
+    RoPE kernel's per-pair path; aligned ones its 16-byte row path.  Both
+    must give the same cache rows and the same output, bit for bit."""
+    import torch
+    S, B = 129, 2
+    raw = [cases.prefill_raw(23, S, seq=i) for i in range(B)]
+    host = [np.ascontiguousarray(np.stack([r[j] for r in raw])) for j in range(3)]
+    results = []
+    for shift in (0, 1):
+        dev = []
+        for a in host:
+            flat = torch.zeros(a.size + 4, dtype=torch.float32, device="cuda")
+            view = flat[shift:shift + a.size].view(a.shape)
+            view.copy_(torch.from_numpy(a))
+            dev.append(view)
+        assert all((t.data_ptr() % 16 == 0) == (shift == 0) for t in dev)
+        kv = tg.KVCache(backend, 1, B, S, dtype=tg.DTYPE_BF16)
+        out = torch.zeros(B, S, cases.QD, device="cuda")
+        kv.prefill(0, B, S, dev[0], dev[1], dev[2], out)
+        backend.synchronize()
+        rows = [kv.read_rows(0, i, 0, S) for i in range(B)]
+        results.append((out.cpu().numpy(), rows))
+        kv.destroy()
+    assert np.array_equal(results[0][0], results[1][0])
+    for (k0, v0), (k1, v1) in zip(results[0][1], results[1][1]):
+        assert np.array_equal(k0, k1) and np.array_equal(v0, v1)
+
+
 def test_prefill_golden_from_reference(tg, backend, golden, cases):
     S = int(golden["prefill_S"])
     kv, out = run_prefill(tg, backend, cases, S, B=1, seed=int(golden["seed"]))

@@ -109,6 +109,82 @@ __global__ void __launch_bounds__(128) prefill_rope_kernel(const PrefillRopePara
   }
 }
 
+// The same work, one warp per (sequence, position) row and 8 rows per CTA,
+// for head_dim 64 and inputs 16-byte aligned: each lane issues all its
+// 16-byte loads of the row (q in batches of 8, k, v, and the one cos/sin
+// float4 its columns share) before it uses the first, so the kernel keeps
+// enough bytes in flight to stream at the copy rate.  Arithmetic per element
+// as prefill_rope_kernel's.
+__device__ __forceinline__ uint2 rope4_bf16(float4 x, float4 c) {
+  const __nv_bfloat162 a =
+      __floats2bfloat162_rn(__fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(x.y, c.y)),
+                            __fadd_rn(__fmul_rn(x.x, c.y), __fmul_rn(x.y, c.x)));
+  const __nv_bfloat162 b =
+      __floats2bfloat162_rn(__fsub_rn(__fmul_rn(x.z, c.z), __fmul_rn(x.w, c.w)),
+                            __fadd_rn(__fmul_rn(x.z, c.w), __fmul_rn(x.w, c.z)));
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+}
+
+__global__ void __launch_bounds__(256) prefill_rope_rows_kernel(const PrefillRopeParams p) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);  // (sequence, position)
+  if (row >= p.B * p.S) return;
+  const int s = row / p.S, t = row - s * p.S;
+  // float4 i of a row holds pairs 2m, 2m + 1 of its head, m = i % 16, whose
+  // (cos, sin) are float4 m of the table row; a lane's i are all = lane (16).
+  const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cs + (size_t)t * 64) + (lane & 15));
+  const int nq = p.n_head * 16, nk = p.n_kv * 16;  // float4 per row
+  const float4* __restrict__ q = reinterpret_cast<const float4*>(p.q) + (size_t)row * nq;
+  uint2* __restrict__ qo = reinterpret_cast<uint2*>(p.q_bf16) + (size_t)row * nq;
+  for (int i0 = 0; i0 < nq; i0 += 8 * 32) {
+    float4 x[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * 32 + lane;
+      if (i < nq) x[u] = __ldg(q + i);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * 32 + lane;
+      if (i < nq) qo[i] = rope4_bf16(x[u], c4);
+    }
+  }
+  const float4* __restrict__ k = reinterpret_cast<const float4*>(p.k) + (size_t)row * nk;
+  const float4* __restrict__ v = reinterpret_cast<const float4*>(p.v) + (size_t)row * nk;
+  const size_t crow = ((size_t)s * p.max_ctx + t) * nk;
+  uint2* __restrict__ kc = reinterpret_cast<uint2*>(p.k_cache) + crow;
+  uint2* __restrict__ vc = reinterpret_cast<uint2*>(p.v_cache) + crow;
+  uint2* __restrict__ vh = reinterpret_cast<uint2*>(p.v_f16) + (size_t)row * nk;
+  for (int i0 = 0; i0 < nk; i0 += 4 * 32) {
+    float4 xk[4], xv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * 32 + lane;
+      if (i < nk) {
+        xk[u] = __ldg(k + i);
+        xv[u] = __ldg(v + i);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * 32 + lane;
+      if (i < nk) {
+        kc[i] = rope4_bf16(xk[u], c4);
+        // v: bf16 into the cache, and fp16 of the same bf16 value (exact) as
+        // the operand of the attention's P.V products.
+        const __nv_bfloat162 b0 = __floats2bfloat162_rn(xv[u].x, xv[u].y);
+        const __nv_bfloat162 b1 = __floats2bfloat162_rn(xv[u].z, xv[u].w);
+        vc[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&b0),
+                           *reinterpret_cast<const uint32_t*>(&b1));
+        const __half2 h0 = __floats2half2_rn(__low2float(b0), __high2float(b0));
+        const __half2 h1 = __floats2half2_rn(__low2float(b1), __high2float(b1));
+        vh[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&h0),
+                           *reinterpret_cast<const uint32_t*>(&h1));
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------ attention
 
 constexpr int PF_M = 128;          // query rows per tile (TMEM lanes)
@@ -549,7 +625,17 @@ size_t prefill_attn_smem() { return PF_SMEM; }
 
 cudaError_t launch_prefill_rope(const PrefillRopeParams& p, cudaStream_t st) {
   if (p.B <= 0 || p.S <= 0) return cudaSuccess;
-  prefill_rope_kernel<<<p.B * p.S, 128, 0, st>>>(p);
+  const bool rows16 =
+      p.head_dim == 64 &&
+      ((reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.k) |
+        reinterpret_cast<uintptr_t>(p.v) | reinterpret_cast<uintptr_t>(p.cs) |
+        reinterpret_cast<uintptr_t>(p.q_bf16) | reinterpret_cast<uintptr_t>(p.k_cache) |
+        reinterpret_cast<uintptr_t>(p.v_cache) | reinterpret_cast<uintptr_t>(p.v_f16)) &
+       15) == 0;
+  if (rows16)
+    prefill_rope_rows_kernel<<<(p.B * p.S + 7) / 8, 256, 0, st>>>(p);
+  else
+    prefill_rope_kernel<<<p.B * p.S, 128, 0, st>>>(p);
   return cudaGetLastError();
 }
 
