@@ -723,7 +723,9 @@ __global__ void __launch_bounds__(GEN_THREADS, 4) decode_generic_kernel(const De
 // broadcast from shared memory).  Phase 2: warp g takes head g's maximum and
 // sum.  Phase 3: the 8 warps split the share's rows for P.V, lane l holding
 // dimensions 2l and 2l+1 of every head, 16 rows of V requested at a time.
-// Phase 4: rank c merges heads c, c + C, ... over the cluster.
+// Phase 4: every rank stores its state of head g into the shared memory of
+// rank g % C (distributed shared memory stores: no round trip), and after one
+// cluster barrier rank c merges heads c, c + C, ... from its own memory.
 constexpr int SMALL_THREADS = 256;
 constexpr int SMALL_WARPS = SMALL_THREADS / 32;
 
@@ -787,7 +789,7 @@ __host__ __device__ inline int small_chunk_rows(int max_ctx, int split) {
 
 size_t decode_small_smem(int group, int max_ctx, int split) {
   return (size_t)(group * 64 + (size_t)group * small_row_stride(small_chunk_rows(max_ctx, split)) +
-                  SMALL_WARPS * group * 64 + group * 64 + 2 * group + 2 * 64) *
+                  SMALL_WARPS * group * 64 + 2 * group + 2 * 64 + (size_t)split * group * 66) *
          4;
 }
 
@@ -830,11 +832,13 @@ __global__ void __launch_bounds__(SMALL_THREADS) decode_small_kernel(const Decod
   float* q_s = ssm;                           // [G][64]
   float* s_s = q_s + G * HD;                  // [G][cap] scores, then 2^(s - m)
   float* o_s = s_s + (size_t)G * cap;         // [8][G][64] per-warp partial outputs
-  float* oc_s = o_s + SMALL_WARPS * G * HD;   // [G][64] this CTA's output sums
-  float* m_s = oc_s + G * HD;                 // [G] this CTA's maxima
+  float* m_s = o_s + SMALL_WARPS * G * HD;    // [G] this CTA's maxima
   float* l_s = m_s + G;                       // [G] this CTA's sums
   float* kn_s = l_s + G;                      // new k row (this KV head), rope mode
   float* vn_s = kn_s + HD;                    // new v row
+  float* r_m = vn_s + HD;                     // [C][G] maxima received from rank c
+  float* r_l = r_m + C * G;                   // [C][G] sums received
+  float* r_o = r_l + C * G;                   // [C][G][64] output sums received
 
   griddep_wait();
   // Every CTA of a cluster has the same sequence: the checks below end the
@@ -977,25 +981,33 @@ __global__ void __launch_bounds__(SMALL_THREADS) decode_small_kernel(const Decod
       *reinterpret_cast<float2*>(o_s + (warp * G + g) * HD + 2 * lane) =
           make_float2(acc[g][0], acc[g][1]);
   __syncthreads();
+  // 4. Merge the cluster's states: rank c finishes heads c, c + C, ....
+  //    This CTA's (m, l, o) of head g go to rank g % C's receive buffers
+  //    (slot crank); the cluster barrier makes them visible there.
   for (int i = tid; i < G * HD; i += SMALL_THREADS) {
     float o = 0.f;
 #pragma unroll
     for (int w = 0; w < SMALL_WARPS; ++w) o += o_s[w * G * HD + i];
-    oc_s[i] = o;
+    const int g = i / HD, owner = g % C;
+    (owner == crank ? r_o : cluster.map_shared_rank(r_o, owner))[(crank * G + g) * HD + i - g * HD] = o;
   }
-  // 4. Merge the cluster's states: rank c finishes heads c, c + C, ...,
-  //    reading every rank's (m, l, o) through distributed shared memory.
+  if (tid < G) {
+    const int owner = tid % C;
+    (owner == crank ? r_m : cluster.map_shared_rank(r_m, owner))[crank * G + tid] = m_s[tid];
+    (owner == crank ? r_l : cluster.map_shared_rank(r_l, owner))[crank * G + tid] = l_s[tid];
+  }
+  // No CTA touches another's shared memory after this barrier.
   cluster.sync();
   float* out = p.out + qoff;
   for (int g = crank; g < G; g += C) {
     for (int d = tid; d < HD; d += SMALL_THREADS) {
       float M = -INFINITY;
-      for (int c = 0; c < C; ++c) M = fmaxf(M, cluster.map_shared_rank(m_s, c)[g]);
+      for (int c = 0; c < C; ++c) M = fmaxf(M, r_m[c * G + g]);
       float L = 0.f, O = 0.f;
       for (int c = 0; c < C; ++c) {
-        const float w = ex2(cluster.map_shared_rank(m_s, c)[g] - M);
-        L = fmaf(w, cluster.map_shared_rank(l_s, c)[g], L);
-        O = fmaf(w, cluster.map_shared_rank(oc_s, c)[g * HD + d], O);
+        const float w = ex2(r_m[c * G + g] - M);
+        L = fmaf(w, r_l[c * G + g], L);
+        O = fmaf(w, r_o[(c * G + g) * HD + d], O);
       }
       out[g * HD + d] = O / L;
     }
@@ -1010,8 +1022,6 @@ __global__ void __launch_bounds__(SMALL_THREADS) decode_small_kernel(const Decod
       store_elem<Elem>(static_cast<Elem*>(p.v_cache) + crow + i, vn_s[i]);
     }
   }
-  // Shared memory stays alive until every rank has read it.
-  cluster.sync();
 }
 
 // ================================================================== merges
