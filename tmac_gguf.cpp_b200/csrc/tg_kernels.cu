@@ -722,7 +722,10 @@ __global__ void __launch_bounds__(GEN_THREADS, 4) decode_generic_kernel(const De
 // (all loads issued together) and forms the scores of the group's heads (q
 // broadcast from shared memory).  Phase 2: warp g takes head g's maximum and
 // sum.  Phase 3: the 8 warps split the share's rows for P.V, lane l holding
-// dimensions 2l and 2l+1 of every head, 16 rows of V requested at a time.
+// dimensions 2l and 2l+1 of every head.  With p.stage_v the CTA's V rows
+// were copied to shared memory (cp.async) right after its K rows were
+// requested, so the two memory round trips overlap; otherwise 16 rows of V
+// are requested at a time in phase 3.
 // Phase 4: every rank stores its state of head g into the shared memory of
 // rank g % C (distributed shared memory stores: no round trip), and after one
 // cluster barrier rank c merges heads c, c + C, ... from its own memory.
@@ -779,6 +782,19 @@ __device__ __forceinline__ float2 load_pair<__nv_bfloat16>(const __nv_bfloat16* 
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
 }
 
+// Two consecutive elements of a V row staged in shared memory, widened.
+template <typename Elem>
+__device__ __forceinline__ float2 smem_pair(const Elem* src);
+template <>
+__device__ __forceinline__ float2 smem_pair<float>(const float* src) {
+  return *reinterpret_cast<const float2*>(src);
+}
+template <>
+__device__ __forceinline__ float2 smem_pair<__nv_bfloat16>(const __nv_bfloat16* src) {
+  const uint32_t w = *reinterpret_cast<const uint32_t*>(src);
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
 // Score rows are padded to a multiple of 4 floats so that the partial
 // outputs after them stay 16-byte aligned (they are stored as float2).
 __host__ __device__ inline int small_row_stride(int rows) { return (rows + 3) & ~3; }
@@ -787,10 +803,17 @@ __host__ __device__ inline int small_chunk_rows(int max_ctx, int split) {
   return (max_ctx + split - 1) / split;
 }
 
+// Floats of the short-cache kernel's shared memory before its V rows (a
+// multiple of 4, so that the 16-byte copies of the rows land aligned).
+__host__ __device__ inline size_t small_vstage_offset(int group, int max_ctx, int split) {
+  const size_t f = (size_t)group * 64 +
+                   (size_t)group * small_row_stride(small_chunk_rows(max_ctx, split)) +
+                   SMALL_WARPS * group * 64 + 2 * group + 2 * 64 + (size_t)split * group * 66;
+  return (f + 3) & ~size_t(3);
+}
+
 size_t decode_small_smem(int group, int max_ctx, int split) {
-  return (size_t)(group * 64 + (size_t)group * small_row_stride(small_chunk_rows(max_ctx, split)) +
-                  SMALL_WARPS * group * 64 + 2 * group + 2 * 64 + (size_t)split * group * 66) *
-         4;
+  return small_vstage_offset(group, max_ctx, split) * 4;
 }
 
 template <typename Elem>
@@ -839,6 +862,7 @@ __global__ void __launch_bounds__(SMALL_THREADS) decode_small_kernel(const Decod
   float* r_m = vn_s + HD;                     // [C][G] maxima received from rank c
   float* r_l = r_m + C * G;                   // [C][G] sums received
   float* r_o = r_l + C * G;                   // [C][G][64] output sums received
+  Elem* v_s = reinterpret_cast<Elem*>(ssm + small_vstage_offset(G, p.max_ctx, C));  // [rows][64]
 
   griddep_wait();
   // Every CTA of a cluster has the same sequence: the checks below end the
@@ -861,6 +885,20 @@ __global__ void __launch_bounds__(SMALL_THREADS) decode_small_kernel(const Decod
   // loads overlap (the new row, in rope mode, comes from shared memory).
   float kr[64];
   if (tid < nloc && !(fuse && lo + tid == pl)) load_row64<Elem>(kb + (size_t)(lo + tid) * kdim, vec, kr);
+  if (p.stage_v) {
+    // The V rows of this CTA's share, 16 bytes per copy (the new row in
+    // rope mode comes from shared memory instead).
+    constexpr int CH = HD * (int)sizeof(Elem) / 16;
+    constexpr int EPC = 16 / (int)sizeof(Elem);
+    for (int i = tid; i < nloc * CH; i += SMALL_THREADS) {
+      const int t = i / CH, c = i - t * CH;
+      if (fuse && lo + t == pl) continue;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                       smem_u32(v_s + (size_t)t * HD + c * EPC)),
+                   "l"(vb + (size_t)(lo + t) * kdim + c * EPC)
+                   : "memory");
+    }
+  }
   const size_t qoff = (size_t)seq * p.n_head * HD + (size_t)kvh * G * HD;
   const size_t koff = (size_t)seq * kdim + kvh * HD;
   if (!fuse) {
@@ -940,6 +978,7 @@ __global__ void __launch_bounds__(SMALL_THREADS) decode_small_kernel(const Decod
       l_s[warp] = sum;
     }
   }
+  if (p.stage_v) asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
   // 3. P.V over this warp's share of the CTA's rows, every head of the group.
   float acc[8][2];
@@ -954,7 +993,9 @@ __global__ void __launch_bounds__(SMALL_THREADS) decode_small_kernel(const Decod
     float2 v[16];
 #pragma unroll
     for (int u = 0; u < 16; ++u)
-      v[u] = (fuse && lo + t + u == pl) ? vnew : load_pair<Elem>(vcol + (size_t)(lo + t + u) * kdim);
+      v[u] = (fuse && lo + t + u == pl) ? vnew
+             : p.stage_v ? smem_pair<Elem>(v_s + (size_t)(t + u) * HD + 2 * lane)
+                         : load_pair<Elem>(vcol + (size_t)(lo + t + u) * kdim);
 #pragma unroll
     for (int u = 0; u < 16; ++u)
 #pragma unroll
@@ -966,7 +1007,9 @@ __global__ void __launch_bounds__(SMALL_THREADS) decode_small_kernel(const Decod
         }
   }
   for (; t < t1; ++t) {
-    const float2 v = (fuse && lo + t == pl) ? vnew : load_pair<Elem>(vcol + (size_t)(lo + t) * kdim);
+    const float2 v = (fuse && lo + t == pl) ? vnew
+                     : p.stage_v ? smem_pair<Elem>(v_s + (size_t)t * HD + 2 * lane)
+                                 : load_pair<Elem>(vcol + (size_t)(lo + t) * kdim);
 #pragma unroll
     for (int g = 0; g < 8; ++g)
       if (g < G) {
@@ -1267,9 +1310,16 @@ cudaError_t launch_decode_mma(const CUtensorMap& tk, const CUtensorMap& tv,
   }
 }
 
-cudaError_t launch_decode_small(const DecodeParams& p, int dtype, cudaStream_t st) {
-  if (p.B <= 0) return cudaSuccess;
-  const size_t smem = decode_small_smem(p.group, p.max_ctx, p.split);
+// V rows staged in shared memory when the caches are 16-byte aligned and a
+// CTA's share takes at most this many bytes (two CTAs per SM stay resident).
+constexpr size_t kSmallVStageMax = 32 * 1024;
+
+cudaError_t launch_decode_small(const DecodeParams& p_in, int dtype, cudaStream_t st) {
+  if (p_in.B <= 0) return cudaSuccess;
+  DecodeParams p = p_in;
+  const size_t vbytes = (size_t)small_chunk_rows(p.max_ctx, p.split) * 64 * (dtype == 0 ? 4 : 2);
+  p.stage_v = (p.aligned16 && vbytes <= kSmallVStageMax) ? 1 : 0;
+  const size_t smem = decode_small_smem(p.group, p.max_ctx, p.split) + (p.stage_v ? vbytes : 0);
   static size_t configured_f32[64] = {}, configured_bf16[64] = {};
   void (*fn)(const DecodeParams) =
       dtype == 0 ? decode_small_kernel<float> : decode_small_kernel<__nv_bfloat16>;

@@ -96,6 +96,7 @@ struct DecodeParams {
   void* k_cache;         // layer base of the caches (writable views of k / v)
   void* v_cache;
   int split;             // short-cache kernel: CTAs (a cluster) per (sequence, KV head)
+  int stage_v;           // short-cache kernel: V rows copied to shared memory with the K loads
 };
 
 TG_HD int past_of(const DecodeParams& p, int s) {
