@@ -151,6 +151,10 @@ struct tg_context {
   int num_sms = 0;
   cudaStream_t stream = nullptr;
   bool own_stream = false;
+  // Inside a batch, host inputs move on this stream and `stream` waits for
+  // them through copy_done (created at the first batched call).
+  cudaStream_t copy_stream = nullptr;
+  cudaEvent_t copy_done = nullptr;
   int* d_err = nullptr;
 
   float* part = nullptr;     size_t part_cap = 0;    // floats
@@ -394,10 +398,23 @@ int pack_input(tg_context* ctx, const void* p, size_t bytes, void** dev) {
 // Moves the current call's host inputs to their arena slots: packed into
 // page-locked staging on the CPU and moved by one copy-engine transfer per
 // run of consecutive slots (measured faster end to end than a kernel that
-// reads page-locked inputs over the host link, which would spare the copy
-// node between kernels).
+// reads page-locked inputs over the host link).  Inside a batch the
+// transfers run on a side stream that the compute stream waits for through
+// an event, so no copy node sits between two kernels of the compute stream:
+// a copy between kernels makes the next kernel wait for the previous one to
+// end and for the copy, and loses its programmatic (PDL) overlap.  Arena
+// slots are fresh within a batch and the stream is drained before they are
+// reused, so the early copies overwrite nothing still in use.
 int commit_inputs(tg_context* ctx) {
   if (ctx->pack.empty()) return TG_OK;
+  cudaStream_t cs = ctx->stream;
+  if (ctx->in_batch) {
+    if (!ctx->copy_stream) {
+      TG_CUDA(cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking));
+      TG_CUDA(cudaEventCreateWithFlags(&ctx->copy_done, cudaEventDisableTiming));
+    }
+    cs = ctx->copy_stream;
+  }
   std::vector<char*> stage(ctx->pack.size());
   for (size_t i = 0; i < ctx->pack.size(); ++i) {
     TG_TRY(hpin_alloc(ctx, ctx->pack[i].bytes, &stage[i]));
@@ -413,10 +430,14 @@ int commit_inputs(tg_context* ctx) {
       run += (ctx->pack[j].bytes + 255) & ~size_t(255);
     }
     const size_t bytes = (size_t)(ctx->pack[j - 1].dev - d0) + ctx->pack[j - 1].bytes;
-    TG_CUDA(cudaMemcpyAsync(d0, h0, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    TG_CUDA(cudaMemcpyAsync(d0, h0, bytes, cudaMemcpyHostToDevice, cs));
     i = j;
   }
   ctx->pack.clear();
+  if (cs != ctx->stream) {
+    TG_CUDA(cudaEventRecord(ctx->copy_done, cs));
+    TG_CUDA(cudaStreamWaitEvent(ctx->stream, ctx->copy_done, 0));
+  }
   return TG_OK;
 }
 
@@ -1354,6 +1375,11 @@ int tg_shutdown(tg_context* ctx) {
   cudaFree(ctx->qx);
   cudaFree(ctx->cx);
   cudaFree(ctx->d_err);
+  if (ctx->copy_stream) {
+    cudaStreamSynchronize(ctx->copy_stream);
+    cudaStreamDestroy(ctx->copy_stream);
+  }
+  if (ctx->copy_done) cudaEventDestroy(ctx->copy_done);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
   return TG_OK;
