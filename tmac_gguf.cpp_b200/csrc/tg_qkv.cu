@@ -1,4 +1,5 @@
-// tg_qkv.cu -- the Q/K/V projection of a decode step (sm_100a, CUDA cores).
+// tg_qkv.cu -- the Q/K/V projection of a decode step (sm_100a: CUDA cores for
+// small batches and very wide rows, tcgen05 tensor cores for batches).
 //
 //   qkv_kernel   y_m = W_m x for the layer's three projection matrices and B
 //                input vectors, weights in the model file's 32-element
@@ -26,8 +27,15 @@
 // than 32 blocks loop over groups of 32 blocks and decode per sequence.  The
 // epilogue runs over (sequence, row pair).
 //
-//   qkv_gemm_kernel  the same contract for batches of kQkvGemmMinB or more
-//                sequences: a CTA covers kQkvGemmRows = 16 rows x 64
+//   qkv_tc_kernel  the same contract for batches of kQkvGemmMinB or more
+//                sequences with rows of up to qkv_tc_max_cols() inputs, on
+//                the tensor cores (3xTF32 products accumulated in TMEM,
+//                clusters of 1-8 CTAs splitting the columns; described at
+//                the kernel).
+//
+//   qkv_gemm_kernel  the same contract for such batches whose rows are
+//                wider than the tensor-core kernel takes: a CTA covers
+//                kQkvGemmRows = 16 rows x 64
 //                sequences.  The rows are decoded once into a K-major fp32
 //                tile in shared memory, x is staged transposed 32 columns
 //                at a time (double-buffered through registers), and every
