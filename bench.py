@@ -114,6 +114,86 @@ def load_oracle():
     return oracle
 
 
+def stamp_summary(st, n_sms):
+    """In-step timing of the bf16 decode steps from their %globaltimer
+    stamps, uint64 [step][row][4] in ns (decode CTA c in row c: start,
+    dependency released, tiles done, end; merge CTA m in row n_sms + m:
+    start, decode data available, -, end):
+      launch_us  decode dependency released (earliest CTA) -> the step's last
+                 CTA ended (decode and merge kernel: one layer in the step)
+      tiles_us   released -> the last decode CTA finished its tiles
+      tail_us    last tile finished -> step end (merge of split sequences
+                 and, across GPUs, the record exchange)
+      period_us  between consecutive steps' ends (one layer)
+      early_us   how long before the release the first decode CTA started
+                 (its pre-wait prologue and tile loads)"""
+    st = st.astype(np.int64)
+    dec, mrg = st[:, :n_sms, :], st[:, n_sms:, :]
+    big = np.iinfo(np.int64).max
+    rel = np.where(dec[:, :, 1] > 0, dec[:, :, 1], big).min(axis=1)
+    start = np.where(dec[:, :, 0] > 0, dec[:, :, 0], big).min(axis=1)
+    tiles = dec[:, :, 2].max(axis=1)
+    end = np.maximum(dec[:, :, 3].max(axis=1), mrg[:, :, 3].max(axis=1))
+    out = {"steps": int(st.shape[0]),
+           "launch_us": float(np.mean(end - rel)) / 1e3,
+           "tiles_us": float(np.mean(tiles - rel)) / 1e3,
+           "tail_us": float(np.mean(end - tiles)) / 1e3,
+           "early_us": float(np.mean(rel - start)) / 1e3}
+    if st.shape[0] > 1:
+        out["period_us"] = float(np.mean(np.diff(end))) / 1e3
+    return out
+
+
+def torch_reference_check(kv, layer, q_rot, out, pos, world, tol, dist=None):
+    """Independent check of one layer's output: attention of the rotated q
+    (the kernels write it back) over this rank's cache rows in float64 torch
+    on the GPU, every rank's softmax record combined, compared with the
+    library's output (tmac_gguf.cpp:1093-1128 semantics: scale 1/sqrt(64),
+    causal window 0..pos, query head h on KV head h / 7)."""
+    import torch
+    B = len(pos)
+    g = N_HEAD // N_KV
+    kvh = torch.arange(N_HEAD, device="cuda") // g
+    ms, ls, os_ = [], [], []
+    for s in range(B):
+        n_loc = int(min(max(int(pos[s]) + 1 - kv.shard_start, 0), kv.max_ctx))
+        if n_loc == 0:
+            ms.append(torch.full((N_HEAD,), -1e300, dtype=torch.float64, device="cuda"))
+            ls.append(torch.zeros(N_HEAD, dtype=torch.float64, device="cuda"))
+            os_.append(torch.zeros(N_HEAD, HD, dtype=torch.float64, device="cuda"))
+            continue
+        kr, vr = kv.read_rows(layer, s, 0, n_loc)
+        to32 = lambda a: torch.from_numpy(
+            (np.ascontiguousarray(a).view(np.uint16).astype(np.uint32) << 16).view(np.float32))
+        K = to32(kr).cuda().double().reshape(n_loc, N_KV, HD)[:, kvh, :]
+        V = to32(vr).cuda().double().reshape(n_loc, N_KV, HD)[:, kvh, :]
+        q = q_rot[s].double().reshape(N_HEAD, HD)
+        sc = torch.einsum("hd,nhd->hn", q, K) / 8.0
+        m = sc.max(dim=1).values
+        w = torch.exp(sc - m[:, None])
+        ms.append(m)
+        ls.append(w.sum(dim=1))
+        os_.append(torch.einsum("hn,nhd->hd", w, V))
+    m, l, o = torch.stack(ms), torch.stack(ls), torch.stack(os_)
+    if world > 1:
+        gm = [torch.zeros_like(m) for _ in range(world)]
+        gl = [torch.zeros_like(l) for _ in range(world)]
+        go = [torch.zeros_like(o) for _ in range(world)]
+        dist.all_gather(gm, m)
+        dist.all_gather(gl, l)
+        dist.all_gather(go, o)
+        M = torch.stack(gm).max(dim=0).values
+        wt = [torch.exp(mi - M) for mi in gm]
+        l = sum(li * wi for li, wi in zip(gl, wt))
+        o = sum(oi * wi[..., None] for oi, wi in zip(go, wt))
+    ref = (o / l[..., None]).reshape(B, QD)
+    err = float((out.double() - ref).abs().max())
+    return {"max_abs": err, "tol": tol, "ok": bool(err <= tol), "layer": layer,
+            "sequences": B,
+            "against": "float64 torch attention over the same bf16 cache rows and rotated q, "
+                       "every rank's softmax record combined"}
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -518,6 +598,12 @@ def main():
     ap.add_argument("--ctx", type=int, default=0,
                     help="override the workload's context length (small cases for "
                          "profiler captures; the reported config says so)")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the independent check of layer 0's output")
+    ap.add_argument("--ring", type=int, default=0, choices=[0, 128, 192],
+                    help="decode K/V ring per CTA in KB (tg_set_decode_tuning; 0 automatic)")
+    ap.add_argument("--preload", type=int, default=1, choices=[0, 1],
+                    help="tile loads before the grid-dependency wait when safe (1) or never")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layers per step (small profiling cases)")
     args = ap.parse_args()
@@ -543,6 +629,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
     tg = load_package()
+    tg.set_decode_tuning(args.ring, args.preload)
     be = tg.CudaBackend(local)
     if wl.get("prefill"):
         def barrier_p():
@@ -716,6 +803,35 @@ def main():
     achieved_min = max_over_ranks(-achieved)  # slowest rank's kernel
     achieved = -achieved_min if world > 1 else achieved
 
+    # ---- in-step timing of the bf16 decode steps (globaltimer stamps) ------
+    instep = None
+    fused = kv.uses_tensor_cores() and not qkv
+    if fused:
+        be.profile_enable(tg.PROFILE_STAMPS)
+        be.graph_begin()
+        step(q, kn, vn, pos_d, out)
+        gst = be.graph_end()
+        be.profile_enable(False)
+        sums = []
+        for _ in range(max(3, min(args.steps, 20))):
+            l2_flush()
+            gst.launch()
+            sums.append(stamp_summary(be.profile_read_stamps(), be.num_sms()))
+        gst.destroy()
+        instep = {k: float(np.mean([x[k] for x in sums])) for k in sums[0]}
+        for k in ("launch_us", "tiles_us", "tail_us", "period_us"):  # slowest rank
+            if k in instep:
+                instep[k] = max_over_ranks(instep[k])
+        k_in_ms = instep["launch_us"] / 1e3
+        achieved_in = k_bytes / (k_in_ms * 1e-3) / 1e9
+
+    # ---- parity of one layer against an independent reference -----------
+    parity = None
+    if fused and not args.no_parity:
+        be.synchronize()
+        parity = torch_reference_check(kv, 0, q[0], out[0], pos, world, 2e-3,
+                                       dist if world > 1 else None)
+
     # ---- end to end through the C ABI with pinned host buffers ---------------
     qh = torch.randn(L, B, QD).pin_memory()
     kh = torch.randn(L, B, KD).pin_memory()
@@ -784,21 +900,31 @@ def main():
             "seq_steps_per_s": seqs_step / (ms_step * 1e-3),
             "hbm_frac_of_measured": value / (hbm_peak * world),
             "gpu_launches": launches,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak,
-                         "unit": "GB/s", "frac": achieved / hbm_peak,
+            "roofline": {"bound": "hbm",
+                         "achieved": achieved_in if fused else achieved, "peak": hbm_peak,
+                         "unit": "GB/s", "frac": (achieved_in if fused else achieved) / hbm_peak,
                          "peak_kind": peak_kind,
+                         "timing": ("in-step: %globaltimer stamps of every CTA, decode "
+                                    "dependency released -> last decode / merge CTA ended, "
+                                    "mean over the step's layers (the decode + merge pair)"
+                                    if fused else "CUDA events around each launch"),
                          "kernel": ("projection kernels (q/k/v + attn_output), "
                                     + ("qkv_tc_kernel" if B >= 9 else "qkv_kernel"))
                          if qkv else
                          ("decode_fused_kernel" if kv.uses_tensor_cores()
                           else ("decode_small_kernel" if kv.max_ctx <= 1024 and
                                 shard_start == 0 and not split else "decode_generic_kernel")),
-                         "bytes_per_launch": k_bytes, "launch_ms": k_avg_ms,
+                         "bytes_per_launch": k_bytes,
+                         "launch_ms": k_in_ms if fused else k_avg_ms,
+                         "launch_ms_alone": k_avg_ms, "achieved_alone": achieved,
                          "traffic": ncu_traffic(args.workload,
                                                 shard_len / wl["ctx"] if wl["split"] else 1.0),
                          "traffic_unit": "bytes per launch (ncu dram__bytes_read + write)"},
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
+            "instep_us": instep,
+            "merge_exchange_us_per_layer": instep["tail_us"] if instep else None,
+            "parity": parity,
             "clocks": clocks,
             "cpu_baseline": cpu,
         }

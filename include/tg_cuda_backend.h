@@ -197,6 +197,17 @@ TG_API int tg_attn_output(tg_context* ctx, int n_seqs, int wtype, const void* w_
  * between widths only by the order of the fp32 partial sums. */
 TG_API int tg_set_projection_split(int split);
 
+/* Tuning of the bf16 decode kernel (no reference counterpart: the
+ * reference's attention_op, metal_backend.hpp:413-453, has no knobs).
+ * ring_kb: K/V ring per CTA, 128 or 192 KB (0: 192 for short shards of at
+ * most 16 tiles of 64 rows per SM when its shared memory fits, else 128).
+ * preload: 1 (default) lets the kernel load its first tiles before its
+ * grid-dependency wait when the library knows that no kernel still running
+ * writes those cache rows; 0 never.  Applies to later launches of every
+ * context; results do not depend on either.  Other values give
+ * TG_ERR_INVALID_ARG. */
+TG_API int tg_set_decode_tuning(int ring_kb, int preload);
+
 /* One layer's projection weights: W_q has n_head*head_dim rows, W_k and
  * W_v n_kv_head*head_dim rows of `cols` inputs.  Device pointers or
  * registered host arrays; a NULL bias is a bias the model does not have. */
@@ -361,8 +372,16 @@ TG_API int tg_comm_destroy(tg_context* ctx);
 
 /* How the ranks exchange their softmax records in the split-KV calls. */
 #define TG_EXCHANGE_AUTO 0  /* peer memory when every GPU maps every other's, else NCCL */
-#define TG_EXCHANGE_PEER 1  /* NVLink peer stores + flags inside the merge kernel */
+#define TG_EXCHANGE_PEER 1  /* NVLink peer stores of epoch-tagged words inside the merge kernel */
 #define TG_EXCHANGE_NCCL 2  /* ncclAllGather of the records, then a merge kernel */
+/* Bound, in milliseconds (default 5000), of the waits inside the split-KV
+ * kernels: for another GPU's softmax records in the peer exchange and for
+ * the decode CTAs of the same GPU.  A wait that runs out ends the kernel
+ * with device error 0x105 (peer record) or 0x106 (decode CTAs), reported as
+ * TG_ERR_DEVICE at the next synchronisation; after either, destroy and
+ * create the communicator again (the ranks' exchange epochs may differ).
+ * No counterpart in the reference (metal_backend.cpp:23-27 only prints). */
+TG_API int tg_comm_set_wait_limit_ms(tg_context* ctx, int ms);
 /* Choose the exchange (collective: every rank passes the same value before
  * its next split-KV call).  TG_EXCHANGE_PEER fails with TG_ERR_UNSUPPORTED
  * at the next call if peer memory cannot be set up on some rank. */
@@ -422,11 +441,14 @@ TG_API int tg_attention_block_splitkv(tg_context* ctx, tg_kv_cache* shard, int l
  * allocate device memory when they run it: code recording a CUDA graph in
  * global capture mode (allocation calls are refused there), runtimes that
  * own a fixed memory pool and forbid the driver allocator after start-up,
- * or an allocator hook that must not re-enter itself.  It creates no
- * context and calls no cudaMalloc / cudaFree: the split-KV scratch (partial
- * softmax records, tile schedule, error word) is one fixed device array of
+ * or an allocator hook that must not re-enter itself.  It calls no
+ * cudaMalloc / cudaFree: the split-KV scratch (partial softmax records, tile
+ * schedule, error word) is one fixed device array of
  * TG_NOALLOC_SCRATCH_BYTES inside the library, held by every GPU that loads
- * the library until the process exits.
+ * the library until the process exits.  It works on the calling thread's
+ * current device; if that device's primary context is not yet set up, the
+ * first call sets it up (as any CUDA runtime call does), so make the first
+ * call before any stream capture.
  *
  * Same work as tg_attention_batched on one layer: sequence s attends rows
  * 0..past_len[s] of its cache rows [s][max_ctx][n_kv_head*head_dim] of
@@ -438,10 +460,12 @@ TG_API int tg_attention_block_splitkv(tg_context* ctx, tg_kv_cache* shard, int l
  * copied there once the work has run.
  *
  * The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress) with that device current; make it before any
- * stream capture.  All calls share the array and it keeps the last call's
- * contents, so calls whose GPU work overlaps (other streams or threads)
- * race: serialise them. */
+ * (cudaGetSymbolAddress) with that device current and raises the
+ * shared-memory limit of every kernel variant it can launch; make it before
+ * any stream capture.  bf16 caches with head_dim 64 take the tensor-core
+ * kernel when both caches are 16-byte aligned, else the CUDA-core kernel.
+ * All calls share the array and it keeps the last call's contents, so calls
+ * whose GPU work overlaps (other streams or threads) race: serialise them. */
 #define TG_NOALLOC_MAX_SEQS 4096
 #define TG_NOALLOC_SCRATCH_BYTES ((4u << 20) + 16896u)
 TG_API int tg_attention_noalloc(void* cuda_stream, const float* q, const void* k_cache,
@@ -464,8 +488,23 @@ TG_API int tg_launch_count(tg_context* ctx, long long* out);
  * number. */
 #define TG_PROFILE_ATTENTION 1
 #define TG_PROFILE_PROJECTION 2
+/* TG_PROFILE_STAMPS: the CTAs of each bf16 decode step record %globaltimer
+ * values (ns) -- decode CTAs: start, grid dependency released, tile loop
+ * done, end; merge CTAs: start, decode data available, (unused), end.
+ * Unlike events this keeps the launches' programmatic overlap, so it times
+ * the kernels as they run inside a step.  Up to TG_STAMP_LAUNCHES decode
+ * steps are recorded after enabling (also into a graph being captured;
+ * each replay rewrites them). */
+#define TG_PROFILE_STAMPS 4
+#define TG_STAMP_LAUNCHES 1024
 TG_API int tg_profile_enable(tg_context* ctx, int on);
 TG_API int tg_profile_read(tg_context* ctx, double* total_ms, long long* launches);
+/* Waits for the stream and copies the stamps into out (at most cap_words
+ * values): [step][row][4], steps in enqueue order, rows = 3 x the SM count
+ * (*rows): decode CTA c in row c, merge CTA m in row SMs + m, absent CTAs
+ * 0.  *n_launches: the recorded steps. */
+TG_API int tg_profile_read_stamps(tg_context* ctx, unsigned long long* out, size_t cap_words,
+                                  int* n_launches, int* rows);
 /* 1 if the next batched decode on `kv` uses the tensor-core kernel. */
 TG_API int tg_kv_uses_tensor_cores(tg_kv_cache* kv, int* out);
 

@@ -103,6 +103,47 @@ def main() -> int:
             print(f"rank {rank}: outputs differ across ranks")
             ok = False
         kv.destroy()
+    # BASELINE config 4 at full size: 4 sequences at position 131071 (131072
+    # rows each, bf16), the rows sharded over the world, one layer, three
+    # steps per exchange and decode ring, against the oracle's decode step
+    # (tmac_gguf.cpp:990-1016 / :1090-1128 restated) on the same values.
+    ctx4, B4 = 131072, 4
+    pos4 = np.full(B4, ctx4 - 1, np.int32)
+    start, length = tg.shard_range(ctx4, world, rank)
+    kv = tg.KVCache(be, 1, B4, length, shard_start=start, global_ctx=ctx4, dtype=tg.DTYPE_BF16)
+    Q = np.zeros((B4, cases.QD), np.float32)
+    K = np.zeros((B4, cases.KD), np.float32)
+    V = np.zeros((B4, cases.KD), np.float32)
+    ref4 = []
+    for i in range(B4):
+        qr, kr, _, kc, vc, ctx = cases.oracle_decode(91, ctx4 - 1, True, seq=i)
+        q, k_new, v_new, _, _ = cases.decode_inputs(91, ctx4 - 1, True, seq=i)
+        hi = min(start + length, ctx4 - 1)
+        if hi > start:
+            kv.write_rows(0, i, 0, kc[start:hi], vc[start:hi])
+        Q[i], K[i], V[i] = q, k_new, v_new
+        ref4.append((qr, ctx))
+        del kc, vc
+    for ex in (tg.EXCHANGE_AUTO, tg.EXCHANGE_NCCL):
+        be.set_exchange(ex)
+        for ring, pre in ((0, 1), (128, 1), (192, 0)):
+            tg.set_decode_tuning(ring, pre)
+            for it in range(3):
+                Qi, Ki = Q.copy(), K.copy()
+                out = np.zeros((B4, cases.QD), np.float32)
+                kv.decode_layer_splitkv(0, Qi, Ki, V, pos4, out)
+                for i in range(B4):
+                    err = float(np.abs(out[i] - ref4[i][1]).max())
+                    same_q = np.array_equal(Qi[i].view(np.uint32), ref4[i][0].view(np.uint32))
+                    if err > 2e-3 or not same_q:
+                        print(f"rank {rank}: config 4 exchange {ex} ring {ring} preload {pre} "
+                              f"step {it} seq {i} err={err} rope_ok={same_q}")
+                        ok = False
+        if rank == 0:
+            print(f"config 4 x{world}: exchange requested {ex} used {be.exchange}, "
+                  f"max err {max(float(np.abs(out[i] - ref4[i][1]).max()) for i in range(B4)):.2e}")
+    tg.set_decode_tuning(0, 1)
+    kv.destroy()
     # The layer from the normed hidden state x (projection + split-KV
     # attention) against the same layer on this GPU over the whole cache:
     # the owner's new k / v row is bit-identical, the output agrees to the
@@ -164,6 +205,77 @@ def main() -> int:
             print(f"x path bf16={bf16} exchange {be.exchange} block err {err:.2e}")
         kv.destroy()
         full.destroy()
+    # Failure detection: with a 1 s wait limit, rank 1 skips one layer's
+    # call (it stays alive, its memory stays mapped, nothing of it is in
+    # flight).  Every other rank's merge kernel stops waiting for rank 1's
+    # records and the call reports TG_ERR_DEVICE (device error 0x105) at its
+    # synchronisation.  All ranks then destroy and re-create the
+    # communicator, and the next step matches the oracle again.
+    be.set_exchange(tg.EXCHANGE_AUTO)
+    be.set_wait_limit_ms(1000)
+    positions = [5000, 77, world * 64 + 3]
+    B = len(positions)
+    gctx = max(positions) + 1
+    start, length = tg.shard_range(gctx, world, rank)
+    kv = tg.KVCache(be, 1, B, max(length, 1), shard_start=start, global_ctx=gctx,
+                    dtype=tg.DTYPE_BF16)
+    Q = np.zeros((B, cases.QD), np.float32)
+    K = np.zeros((B, cases.KD), np.float32)
+    V = np.zeros((B, cases.KD), np.float32)
+    refs = []
+    for i, p in enumerate(positions):
+        q, k_new, v_new, kc, vc = cases.decode_inputs(55, p, True, seq=i)
+        hi = min(start + length, p)
+        if hi > start:
+            kv.write_rows(0, i, 0, kc[start:hi], vc[start:hi])
+        Q[i], K[i], V[i] = q, k_new, v_new
+        refs.append(cases.oracle_decode(55, p, True, seq=i)[5])
+
+    def run_step():
+        out = np.zeros((B, cases.QD), np.float32)
+        kv.decode_layer_splitkv(0, Q.copy(), K.copy(), V, np.array(positions, np.int32), out)
+        return max(float(np.abs(out[i] - refs[i]).max()) for i in range(B))
+
+    err0 = run_step()                      # all ranks: a good step first
+    if err0 > 2e-3:
+        print(f"rank {rank}: pre-failure step err={err0}")
+        ok = False
+    dist.barrier()
+    import time
+    if rank != 1:
+        t0 = time.perf_counter()
+        try:
+            run_step()
+            print(f"rank {rank}: a step without rank 1 did not fail")
+            ok = False
+        except tg.TGError as e:
+            dt = time.perf_counter() - t0
+            if e.status != tg.TG_ERR_DEVICE or "0x105" not in e.message or dt > 30:
+                print(f"rank {rank}: unexpected failure {e.status} {e.message} after {dt:.1f} s")
+                ok = False
+            elif rank == 0:
+                print(f"failure detected in {dt:.2f} s: {e.message}")
+    dist.barrier()                         # rank 1 waited here, idle, memory mapped
+    be.comm_destroy()
+    uid = [tg.comm_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    be.comm_init(uid[0], rank, world, timeout_ms=60000)
+    be.set_wait_limit_ms(5000)
+    kv.destroy()
+    kv = tg.KVCache(be, 1, B, max(length, 1), shard_start=start, global_ctx=gctx,
+                    dtype=tg.DTYPE_BF16)
+    for i, p in enumerate(positions):
+        _, _, _, kc, vc = cases.decode_inputs(55, p, True, seq=i)
+        hi = min(start + length, p)
+        if hi > start:
+            kv.write_rows(0, i, 0, kc[start:hi], vc[start:hi])
+    err1 = run_step()
+    if err1 > 2e-3 or be.exchange != tg.EXCHANGE_PEER:
+        print(f"rank {rank}: after recovery err={err1} exchange={be.exchange}")
+        ok = False
+    elif rank == 0:
+        print(f"recovered: step err {err1:.2e} over the re-created communicator")
+    kv.destroy()
     be.comm_destroy()
     be.shutdown()
     flag = torch.tensor([1 if ok else 0])

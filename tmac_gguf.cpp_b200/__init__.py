@@ -41,7 +41,7 @@ TG_ERR_STATE = 8
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 WTYPE_Q5_0, WTYPE_Q8_0 = 6, 8  # GGML block types (TG_WTYPE_*)
-PROFILE_ATTENTION, PROFILE_PROJECTION = 1, 2  # tg_profile_enable masks
+PROFILE_ATTENTION, PROFILE_PROJECTION, PROFILE_STAMPS = 1, 2, 4  # tg_profile_enable masks
 
 # split-KV record exchange (tg_comm_set_exchange)
 EXCHANGE_AUTO, EXCHANGE_PEER, EXCHANGE_NCCL = 0, 1, 2
@@ -159,6 +159,10 @@ _SIGS = {
                                             C.POINTER(tg_qkv_weights), _vp, _vp, _vp]),
     "tg_attn_output": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp]),
     "tg_set_projection_split": (C.c_int, [C.c_int]),
+    "tg_set_decode_tuning": (C.c_int, [C.c_int, C.c_int]),
+    "tg_comm_set_wait_limit_ms": (C.c_int, [_vp, C.c_int]),
+    "tg_profile_read_stamps": (C.c_int, [_vp, _vp, C.c_size_t, C.POINTER(C.c_int),
+                                         C.POINTER(C.c_int)]),
     "tg_model_load_tmac": (C.c_int, [_vp, C.c_char_p, C.POINTER(_vp)]),
     "tg_model_destroy": (C.c_int, [_vp]),
     "tg_model_count": (C.c_int, [_vp, C.POINTER(C.c_int)]),
@@ -225,6 +229,13 @@ def set_projection_split(split: int) -> None:
     """Cluster width of the tensor-core projections (tg_set_projection_split):
     1 to 8 CTAs splitting the columns, or 0 for the automatic choice."""
     _check(lib().tg_set_projection_split(int(split)))
+
+
+def set_decode_tuning(ring_kb: int = 0, preload: int = 1) -> None:
+    """Tuning of the bf16 decode kernel (tg_set_decode_tuning): K/V ring per
+    CTA (0 automatic, 128 or 192 KB) and whether tiles may be loaded before
+    the grid-dependency wait when that is safe."""
+    _check(lib().tg_set_decode_tuning(int(ring_kb), int(preload)))
 
 
 def shard_range(global_ctx: int, world: int, rank: int):
@@ -343,6 +354,17 @@ class CudaBackend:
         _check(lib().tg_profile_read(self._h, C.byref(ms), C.byref(n)))
         return ms.value, n.value
 
+    def profile_read_stamps(self) -> np.ndarray:
+        """%globaltimer stamps of the recorded bf16 decode steps
+        (PROFILE_STAMPS): uint64 [step][row][4] in ns; decode CTA c in row
+        c, merge CTA m in row num_sms() + m, absent CTAs 0."""
+        n, rows = C.c_int(), C.c_int()
+        cap = 1024 * 3 * self.num_sms() * 4
+        buf = np.zeros(cap, np.uint64)
+        _check(lib().tg_profile_read_stamps(self._h, buf.ctypes.data, cap, C.byref(n),
+                                            C.byref(rows)))
+        return buf[: n.value * rows.value * 4].reshape(n.value, rows.value, 4)
+
     # -- host-array mirrors (wrap_buffer) -----------------------------------
     def register_host(self, arr, flags: int = REGION_MIRROR) -> None:
         _check(lib().tg_register_host(self._h, _ptr(arr), arr.nbytes, flags))
@@ -396,6 +418,12 @@ class CudaBackend:
                   timeout_ms: int = 60000) -> None:
         buf = C.create_string_buffer(uid, 128)
         _check(lib().tg_comm_init(self._h, buf, rank, world, timeout_ms))
+
+    def set_wait_limit_ms(self, ms: int) -> None:
+        """Bound of the split-KV kernels' in-kernel waits
+        (tg_comm_set_wait_limit_ms); on expiry the next synchronisation
+        raises TGError with TG_ERR_DEVICE."""
+        _check(lib().tg_comm_set_wait_limit_ms(self._h, int(ms)))
 
     def set_exchange(self, exchange: int) -> None:
         """EXCHANGE_AUTO / EXCHANGE_PEER / EXCHANGE_NCCL (collective: the same

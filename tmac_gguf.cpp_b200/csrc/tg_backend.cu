@@ -13,6 +13,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <atomic>
 #include <chrono>
 #include <cmath>
 #include <cstdarg>
@@ -119,6 +120,12 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Fused decode tuning (tg_set_decode_tuning): the K/V ring per CTA in KB
+// (0 = automatic) and whether tiles may be loaded before the
+// grid-dependency wait when that is safe (1) or never (0).
+std::atomic<int> g_decode_ring{0};
+std::atomic<int> g_decode_preload{1};
+
 }  // namespace
 
 // ================================================================ context
@@ -199,7 +206,7 @@ struct tg_context {
   int exchange_used = TG_EXCHANGE_AUTO;  // last split-KV call
   int p2p_bcap = 0, p2p_rf = 0, p2p_heads = 0;
   unsigned long long* xchg_local = nullptr;  // peer-exchange receive words
-  unsigned* xchg_ctl = nullptr;              // exchange epoch word (this GPU only)
+  unsigned* xchg_ctl = nullptr;              // exchange control words (FusedParams::xctl)
   unsigned long long* xchg_peer[tg::kMaxPeers] = {};
   unsigned char* nccl_stage = nullptr;  // small device staging for handle exchange
 
@@ -209,6 +216,22 @@ struct tg_context {
   int prof_on = 0;  // TG_PROFILE_* mask
   std::vector<cudaEvent_t> prof_ev;  // start/stop pairs
   size_t prof_used = 0;              // events recorded since the last read
+  // Optional %globaltimer stamps of bf16 decode steps (TG_PROFILE_STAMPS):
+  // one record of kStampRowsPerSm * num_sms rows per decode launch.
+  unsigned long long* stamps = nullptr;
+  int stamp_cap = 0, stamp_used = 0;
+
+  long long wait_ns = 5000000000LL;  // bound of in-kernel waits (tg_comm_set_wait_limit_ms)
+
+  // (cache, layer) pairs whose rows a kernel that lets its successor start
+  // early (programmatic dependent launch) has written since the stream was
+  // last known idle; layer -1 = every layer.  Such rows may still be in
+  // flight when a later kernel starts, so the bf16 decode does not load
+  // them before its grid-dependency wait.  pdl_unknown: work of unknown
+  // extent (a graph launch) may still run.
+  std::vector<std::pair<const tg_kv_cache*, int>> pdl_writes;
+  std::vector<std::pair<const tg_kv_cache*, int>> pdl_saved;  // live set during a capture
+  bool pdl_unknown = false, pdl_unknown_saved = false;
 };
 
 struct tg_graph {
@@ -285,7 +308,9 @@ int check_device_error(tg_context* ctx) {
                        : h == tg::kDevErrWaitFull     ? "bounded wait for a K/V tile expired"
                        : h == tg::kDevErrWaitEmpty    ? "bounded wait for a free stage expired"
                        : h == tg::kDevErrPeerTimeout  ? "another GPU's softmax record did not arrive"
-                                                      : "device error";
+                       : h == tg::kDevErrDecodeTimeout
+                           ? "the merge kernel's wait for the decode CTAs expired"
+                           : "device error";
     return fail(TG_ERR_DEVICE, "kernel reported 0x%x: %s", h, what);
   }
   return TG_OK;
@@ -293,15 +318,44 @@ int check_device_error(tg_context* ctx) {
 
 // Waits for the stream; with a communicator, polls NCCL's async error and
 // aborts the communicator once the timeout passes.
+// The stream has no work in flight: nothing written earlier can still be
+// changing.
+void stream_idle(tg_context* ctx) {
+  if (ctx->capturing) return;
+  ctx->pdl_writes.clear();
+  ctx->pdl_unknown = false;
+}
+
+// Rows of (kv, layer) written by a kernel that may still be running when
+// the next kernel starts (see tg_context::pdl_writes).
+void note_pdl_write(tg_context* ctx, const tg_kv_cache* kv, int layer) {
+  for (const auto& w : ctx->pdl_writes)
+    if (w.first == kv && (w.second == layer || w.second == -1)) return;
+  ctx->pdl_writes.emplace_back(kv, layer);
+}
+
+// True when no kernel that may still be running writes rows of (kv, layer),
+// so the bf16 decode may load them before its grid-dependency wait.
+bool preload_allowed(const tg_context* ctx, const tg_kv_cache* kv, int layer) {
+  if (ctx->pdl_unknown || g_decode_preload == 0) return false;
+  for (const auto& w : ctx->pdl_writes)
+    if (w.first == kv && (w.second == layer || w.second == -1)) return false;
+  return true;
+}
+
 int wait_stream(tg_context* ctx) {
   if (!ctx->comm) {
     TG_CUDA(cudaStreamSynchronize(ctx->stream));
+    stream_idle(ctx);
     return TG_OK;
   }
   const auto t0 = std::chrono::steady_clock::now();
   for (;;) {
     cudaError_t q = cudaStreamQuery(ctx->stream);
-    if (q == cudaSuccess) return TG_OK;
+    if (q == cudaSuccess) {
+      stream_idle(ctx);
+      return TG_OK;
+    }
     if (q != cudaErrorNotReady)
       return fail(TG_ERR_CUDA, "stream failed: %s", cudaGetErrorString(q));
     ncclResult_t ae = ncclSuccess;
@@ -856,7 +910,9 @@ int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const f
     grid = generic_grid(ctx, d.dtype, smem);
   }
   if (smem > 227 * 1024)
-    return fail(TG_ERR_INVALID_ARG, "batch of %d sequences exceeds the shared-memory schedule", B);
+    return fail(TG_ERR_INVALID_ARG,
+                "%d sequences of shape %d/%d/%d need %zu KB of shared memory (at most 227)", B,
+                d.n_head, d.n_kv_head, d.head_dim, (smem + 1023) / 1024);
   TG_TRY(ensure_buf(ctx, &ctx->part, &ctx->part_cap, (size_t)2 * grid * rf));
   TG_TRY(ensure_buf(ctx, &ctx->sched, &ctx->sched_cap, (size_t)B + 1));
   if (mode == 1) TG_TRY(ensure_buf(ctx, &ctx->records, &ctx->rec_cap, (size_t)B * rf));
@@ -933,6 +989,7 @@ int run_small_step(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, flo
   cudaError_t e = tg::launch_decode_small(p, d.dtype, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
   ctx->launches++;
+  note_pdl_write(ctx, kv, layer);
   return prof_end(ctx, ev);
 }
 
@@ -964,6 +1021,7 @@ int run_rope(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, float* q,
   cudaError_t e = tg::launch_rope(rp, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "rope launch: %s", cudaGetErrorString(e));
   ctx->launches++;
+  note_pdl_write(ctx, kv, layer);
   return TG_OK;
 }
 
@@ -1065,13 +1123,35 @@ int ensure_p2p(tg_context* ctx, int B, int n_head, int rf) {
   return TG_OK;
 }
 
+// A short shard: at most 16 tiles of 64 rows per SM on average, so that a
+// CTA can load a good part of its tiles before its grid-dependency wait.
+bool short_shard(const tg_context* ctx, const tg_kv_cache* kv, int B) {
+  return (long long)B * ((kv->d.max_ctx + 63) / 64) <= 16LL * ctx->num_sms;
+}
+
+// K/V ring per CTA of the bf16 decode: the deep ring for short shards when
+// its shared memory fits, otherwise 128 KB (measured faster on long shards:
+// 4 x 131072 rows on one GPU, 46.2 vs 47.4 us per layer).  Fixed by
+// tg_set_decode_tuning.
+int fused_ring(const tg_context* ctx, const tg_kv_cache* kv, int B) {
+  const int nkv = kv->d.n_kv_head;
+  if (g_decode_ring != 0) return g_decode_ring;
+  if (short_shard(ctx, kv, B) &&
+      tg::decode_fused_smem(nkv, tg::kFusedRingDeep, B) <= 227 * 1024)
+    return tg::kFusedRingDeep;
+  return tg::kFusedRing;
+}
+
 // The decode step on the tensor-core path (bf16 cache): the decode kernel
 // and, PDL-chained behind it, the merge kernel.  mode 0: normalised output;
 // 1: per-sequence records to `records`; 2: exchange with the other GPUs of
 // the communicator (peer memory, set up by ensure_p2p) and output.
+// preload: the caller checked with preload_allowed (before any launch of its
+// own that writes the new rows) that the cache rows may be loaded before
+// the decode kernel's grid-dependency wait.
 int run_fused(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const float* q_in,
               float* q_out, float* k_io, const float* v_new, const int* pos, float* out,
-              float* records, int mode, bool rope, bool new_row, float* k_out = nullptr) {
+              float* records, int mode, bool rope, bool new_row, float* k_out, bool preload) {
   TG_TRY(commit_inputs(ctx));
   const tg_kv_desc& d = kv->d;
   TG_TRY(check_align8(q_in, "q"));
@@ -1083,9 +1163,11 @@ int run_fused(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const fl
   RopeTable* t = nullptr;
   TG_TRY(get_table(ctx, d.rope_base, d.head_dim, kv->global_ctx, &t));
   const int grid = ctx->num_sms;
-  const size_t smem = tg::decode_fused_smem(d.n_kv_head, B);
+  const int ring = fused_ring(ctx, kv, B);
+  const size_t smem = tg::decode_fused_smem(d.n_kv_head, ring, B);
   if (smem > 227 * 1024)
     return fail(TG_ERR_INVALID_ARG, "batch of %d sequences exceeds the shared-memory schedule", B);
+  TG_TRY(check_align8(records, "records"));
   TG_TRY(ensure_buf(ctx, &ctx->part, &ctx->part_cap, (size_t)2 * grid * rf));
   TG_TRY(ensure_buf(ctx, &ctx->sched, &ctx->sched_cap, (size_t)B + 1));
   if (mode == 2) {  // records of sequences finished inside one CTA
@@ -1134,19 +1216,31 @@ int run_fused(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const fl
   // to prefetch its first tiles into L2 before its wait returns (measured:
   // -0.8 us per layer at 4 x 16384..131072 rows, +4 us at 256 x 4096).
   p.prefetch = mgroups == tg::kMergeGroupsWide ? 1 : 0;
+  // Tile loads before the wait pay off on short shards, where they cover a
+  // good part of a CTA's tiles; on long ones they only compete with the
+  // previous layer's merge for memory (measured +1.2 us per layer at
+  // 4 x 131072 rows on one GPU).
+  p.preload = (preload && short_shard(ctx, kv, B)) ? 1 : 0;
+  p.wait_ns = ctx->wait_ns;
   if (mode == 2) {
     p.world = ctx->world;
     p.rank = ctx->rank;
     p.b_cap = ctx->p2p_bcap;
     p.xchg_local = ctx->xchg_local;
     for (int r = 0; r < ctx->world; ++r) p.xchg_peer[r] = ctx->xchg_peer[r];
-    p.epoch = ctx->xchg_ctl;
+    p.xctl = ctx->xchg_ctl;
+  }
+  if ((ctx->prof_on & TG_PROFILE_STAMPS) && ctx->stamps && ctx->stamp_used < ctx->stamp_cap) {
+    p.stamps = ctx->stamps +
+               (size_t)ctx->stamp_used * tg::kStampRowsPerSm * ctx->num_sms * tg::kStampsPerCta;
+    ctx->stamp_used++;
   }
   cudaEvent_t ev_stop = nullptr;
   TG_TRY(prof_begin(ctx, TG_PROFILE_ATTENTION, &ev_stop));
-  cudaError_t e = tg::launch_decode_fused(kv->tmk, kv->tmv, p, grid, ctx->stream);
+  cudaError_t e = tg::launch_decode_fused(kv->tmk, kv->tmv, p, ring, grid, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "fused decode launch: %s", cudaGetErrorString(e));
   ctx->launches++;
+  if (new_row) note_pdl_write(ctx, kv, layer);
   TG_TRY(prof_end(ctx, ev_stop));
   e = tg::launch_merge_exchange(p, mgrid, mgroups, ctx->stream);
   if (e != cudaSuccess) return fail(TG_ERR_CUDA, "merge launch: %s", cudaGetErrorString(e));
@@ -1266,7 +1360,9 @@ int qkv_layer_core(tg_context* ctx, const tg_kv_cache* kv, int layer, int n,
   p.dtype = d.dtype;
   p.max_ctx = d.max_ctx;
   p.shard_start = d.shard_start;
-  return run_qkv(ctx, p);
+  TG_TRY(run_qkv(ctx, p));
+  note_pdl_write(ctx, kv, layer);
+  return TG_OK;
 }
 
 int check_kv_call(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs) {
@@ -1365,6 +1461,7 @@ int tg_shutdown(tg_context* ctx) {
   for (RopeTable& t : ctx->tables) cudaFree(t.d);
   for (cudaEvent_t ev : ctx->prof_ev) cudaEventDestroy(ev);
   cudaFree(ctx->part);
+  cudaFree(ctx->stamps);
   cudaFree(ctx->sched);
   cudaFree(ctx->records);
   cudaFree(ctx->recv);
@@ -1442,6 +1539,12 @@ int tg_graph_begin(tg_context* ctx) {
   TG_CUDA(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
   ctx->capturing = true;
   ctx->capture_launches0 = ctx->launches;
+  // A graph starts once the work before its launch has finished: inside it
+  // only its own kernels can be in flight.
+  ctx->pdl_saved.swap(ctx->pdl_writes);
+  ctx->pdl_writes.clear();
+  ctx->pdl_unknown_saved = ctx->pdl_unknown;
+  ctx->pdl_unknown = false;
   return TG_OK;
 }
 
@@ -1450,6 +1553,9 @@ int tg_graph_end(tg_context* ctx, tg_graph** out) {
   if (!ctx->capturing) return fail(TG_ERR_STATE, "tg_graph_end without tg_graph_begin");
   if (!out) return fail(TG_ERR_INVALID_ARG, "null output pointer");
   ctx->capturing = false;
+  ctx->pdl_writes.swap(ctx->pdl_saved);  // nothing captured has run
+  ctx->pdl_saved.clear();
+  ctx->pdl_unknown = ctx->pdl_unknown_saved;
   cudaGraph_t g = nullptr;
   TG_CUDA(cudaStreamEndCapture(ctx->stream, &g));
   cudaGraphExec_t ex = nullptr;
@@ -1473,6 +1579,7 @@ int tg_graph_launch(tg_context* ctx, tg_graph* g) {
   if (!g || g->ctx != ctx) return fail(TG_ERR_INVALID_ARG, "graph of another context");
   TG_CUDA(cudaGraphLaunch(g->exec, ctx->stream));
   ctx->launches += g->kernels;
+  ctx->pdl_unknown = true;  // its kernels' writes are not tracked here
   return TG_OK;
 }
 
@@ -1683,7 +1790,7 @@ int tg_kv_create(tg_context* ctx, const tg_kv_desc* desc, tg_kv_cache** out) {
 int tg_kv_destroy(tg_kv_cache* kv) {
   if (!kv) return TG_OK;
   cudaSetDevice(kv->ctx->device);
-  cudaStreamSynchronize(kv->ctx->stream);
+  if (cudaStreamSynchronize(kv->ctx->stream) == cudaSuccess) stream_idle(kv->ctx);
   auto& cs = kv->ctx->caches;
   for (size_t i = 0; i < cs.size(); ++i)
     if (cs[i] == kv) {
@@ -1812,7 +1919,7 @@ int tg_attention_batched(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs
   if (mma_eligible(kv))
     TG_TRY(run_fused(ctx, kv, layer, n_seqs, static_cast<const float*>(dq), nullptr, nullptr,
                      nullptr, static_cast<const int*>(dp), static_cast<float*>(dout), nullptr,
-                     0, false, false));
+                     0, false, false, nullptr, preload_allowed(ctx, kv, layer)));
   else
     TG_TRY(run_decode(ctx, kv, layer, n_seqs, static_cast<const float*>(dq),
                       static_cast<const int*>(dp), 0, static_cast<float*>(dout), 0));
@@ -1842,7 +1949,8 @@ int tg_decode_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, flo
     TG_TRY(run_fused(ctx, kv, layer, n_seqs, static_cast<const float*>(dq_in),
                      static_cast<float*>(dq), const_cast<float*>(static_cast<const float*>(dk_in)),
                      static_cast<const float*>(dv), static_cast<const int*>(dp),
-                     static_cast<float*>(dout), nullptr, 0, true, true, static_cast<float*>(dk)));
+                     static_cast<float*>(dout), nullptr, 0, true, true, static_cast<float*>(dk),
+                     preload_allowed(ctx, kv, layer)));
     return finish_call(ctx);
   }
   if (small_eligible(kv)) {
@@ -1900,6 +2008,16 @@ int tg_attn_output(tg_context* ctx, int n_seqs, int wtype, const void* w_o, int 
   TG_TRY(attn_output_core(ctx, n_seqs, wtype, w_o, rows, cols, static_cast<const float*>(dc),
                           static_cast<float*>(dh)));
   return finish_call(ctx);
+}
+
+int tg_set_decode_tuning(int ring_kb, int preload) {
+  if ((ring_kb != 0 && ring_kb != tg::kFusedRing && ring_kb != tg::kFusedRingDeep) ||
+      (preload != 0 && preload != 1))
+    return fail(TG_ERR_INVALID_ARG, "decode tuning: ring_kb %d (0, 128, 192), preload %d (0, 1)",
+                ring_kb, preload);
+  g_decode_ring = ring_kb;
+  g_decode_preload = preload;
+  return TG_OK;
 }
 
 int tg_set_projection_split(int split) {
@@ -2017,12 +2135,15 @@ int tg_decode_layer_x(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs,
   TG_TRY(stage_in(ctx, pos, (size_t)n_seqs * 4, &dp));
   TG_TRY(stage_out(ctx, out, qb, false, &dout));
   TG_TRY(ensure_buf(ctx, &ctx->qx, &ctx->qx_cap, qb / 4));
+  // Checked before the projection, which writes only the new rows (the
+  // decode kernel loads the tiles holding them after its wait).
+  const bool pre = preload_allowed(ctx, kv, layer);
   TG_TRY(qkv_layer_core(ctx, kv, layer, n_seqs, w, static_cast<const float*>(dx),
                         static_cast<const int*>(dp), ctx->qx));
   if (mma_eligible(kv))
     TG_TRY(run_fused(ctx, kv, layer, n_seqs, ctx->qx, nullptr, nullptr, nullptr,
                      static_cast<const int*>(dp), static_cast<float*>(dout), nullptr, 0, false,
-                     false));
+                     false, nullptr, pre));
   else
     TG_TRY(run_decode(ctx, kv, layer, n_seqs, ctx->qx, static_cast<const int*>(dp), 0,
                       static_cast<float*>(dout), 0));
@@ -2085,6 +2206,13 @@ int tg_comm_set_exchange(tg_context* ctx, int exchange) {
   return TG_OK;
 }
 
+int tg_comm_set_wait_limit_ms(tg_context* ctx, int ms) {
+  if (!ctx) return fail(TG_ERR_INVALID_ARG, "null context");
+  if (ms <= 0) return fail(TG_ERR_INVALID_ARG, "wait limit %d ms must be positive", ms);
+  ctx->wait_ns = (long long)ms * 1000000LL;
+  return TG_OK;
+}
+
 int tg_comm_exchange(tg_context* ctx, int* exchange) {
   if (!ctx || !exchange) return fail(TG_ERR_INVALID_ARG, "null argument");
   *exchange = ctx->exchange_used;
@@ -2111,7 +2239,7 @@ namespace {
 // only the tensor-core path does).
 int splitkv_core(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, float* dq,
                  float* dk, const float* dv, const int* dp, float* dout, bool rope_new,
-                 float* dq_out = nullptr, float* dk_out = nullptr) {
+                 bool preload, float* dq_out = nullptr, float* dk_out = nullptr) {
   TG_TRY(commit_inputs(ctx));
   if (!dq_out) dq_out = dq;
   if (!dk_out) dk_out = dk;
@@ -2121,14 +2249,14 @@ int splitkv_core(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, float*
   if (fused && ctx->world == 1)  // one GPU: no exchange at all
     return run_fused(ctx, kv, layer, n_seqs, dq, rope_new ? dq_out : nullptr,
                      rope_new ? dk : nullptr, dv, dp, dout, nullptr, 0, rope_new, rope_new,
-                     rope_new ? dk_out : nullptr);
+                     rope_new ? dk_out : nullptr, preload);
   if (ctx->world > 1 && ctx->exchange_pref != TG_EXCHANGE_NCCL) {
     const int rc = fused ? ensure_p2p(ctx, n_seqs, d.n_head, rf) : TG_ERR_UNSUPPORTED;
     if (rc == TG_OK) {
       ctx->exchange_used = TG_EXCHANGE_PEER;
       return run_fused(ctx, kv, layer, n_seqs, dq, rope_new ? dq_out : nullptr,
                        rope_new ? dk : nullptr, dv, dp, dout, nullptr, 2, rope_new, rope_new,
-                       rope_new ? dk_out : nullptr);
+                       rope_new ? dk_out : nullptr, preload);
     }
     if (rc != TG_ERR_UNSUPPORTED) return rc;
     if (ctx->exchange_pref == TG_EXCHANGE_PEER)
@@ -2143,7 +2271,7 @@ int splitkv_core(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, float*
   if (fused) {
     TG_TRY(run_fused(ctx, kv, layer, n_seqs, dq, rope_new ? dq_out : nullptr,
                      rope_new ? dk : nullptr, dv, dp, nullptr, ctx->records, 1, rope_new,
-                     rope_new, rope_new ? dk_out : nullptr));
+                     rope_new, rope_new ? dk_out : nullptr, preload));
   } else {
     if (dq_out != dq || dk_out != dk)
       return fail(TG_ERR_STATE, "separate q / k outputs need the tensor-core path");
@@ -2205,7 +2333,7 @@ int tg_attention_splitkv(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs
   TG_TRY(stage_out(ctx, out, qb, false, &dout));
   TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, const_cast<float*>(static_cast<const float*>(dq)),
                       nullptr, nullptr, static_cast<const int*>(dp), static_cast<float*>(dout),
-                      false));
+                      false, preload_allowed(ctx, kv, layer)));
   return finish_call(ctx);
 }
 
@@ -2225,7 +2353,7 @@ int tg_attention_records(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs
   if (mma_eligible(kv)) {
     TG_TRY(run_fused(ctx, kv, layer, n_seqs, static_cast<const float*>(dq), nullptr, nullptr,
                      nullptr, static_cast<const int*>(dp), nullptr, static_cast<float*>(drec), 1,
-                     false, false));
+                     false, false, nullptr, preload_allowed(ctx, kv, layer)));
     return finish_call(ctx);
   }
   TG_TRY(ensure_buf(ctx, &ctx->records, &ctx->rec_cap, (size_t)n_seqs * rf));
@@ -2288,8 +2416,8 @@ int tg_decode_layer_splitkv(tg_context* ctx, tg_kv_cache* kv, int layer, int n_s
   TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, const_cast<float*>(static_cast<const float*>(dq_in)),
                       const_cast<float*>(static_cast<const float*>(dk_in)),
                       static_cast<const float*>(dv), static_cast<const int*>(dp),
-                      static_cast<float*>(dout), true, static_cast<float*>(dq),
-                      static_cast<float*>(dk)));
+                      static_cast<float*>(dout), true, preload_allowed(ctx, kv, layer),
+                      static_cast<float*>(dq), static_cast<float*>(dk)));
   return finish_call(ctx);
 }
 
@@ -2309,12 +2437,13 @@ int tg_decode_layer_splitkv_x(tg_context* ctx, tg_kv_cache* kv, int layer, int n
   TG_TRY(stage_in(ctx, pos, (size_t)n_seqs * 4, &dp));
   TG_TRY(stage_out(ctx, out, qb, false, &dout));
   TG_TRY(ensure_buf(ctx, &ctx->qx, &ctx->qx_cap, qb / 4));
+  const bool pre = preload_allowed(ctx, kv, layer);
   // Every rank projects q (replicated); only the shard holding pos[s]
   // writes the k / v row.
   TG_TRY(qkv_layer_core(ctx, kv, layer, n_seqs, w, static_cast<const float*>(dx),
                         static_cast<const int*>(dp), ctx->qx));
   TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, ctx->qx, nullptr, nullptr,
-                      static_cast<const int*>(dp), static_cast<float*>(dout), false));
+                      static_cast<const int*>(dp), static_cast<float*>(dout), false, pre));
   return finish_call(ctx);
 }
 
@@ -2338,14 +2467,15 @@ int attention_block(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs,
   TG_TRY(stage_out(ctx, hidden, qb, true, &dh));
   TG_TRY(ensure_buf(ctx, &ctx->qx, &ctx->qx_cap, qb / 4));
   TG_TRY(ensure_buf(ctx, &ctx->cx, &ctx->cx_cap, qb / 4));
+  const bool pre = preload_allowed(ctx, kv, layer);
   TG_TRY(qkv_layer_core(ctx, kv, layer, n_seqs, w, static_cast<const float*>(dx),
                         static_cast<const int*>(dp), ctx->qx));
   if (split) {
     TG_TRY(splitkv_core(ctx, kv, layer, n_seqs, ctx->qx, nullptr, nullptr,
-                        static_cast<const int*>(dp), ctx->cx, false));
+                        static_cast<const int*>(dp), ctx->cx, false, pre));
   } else if (mma_eligible(kv)) {
     TG_TRY(run_fused(ctx, kv, layer, n_seqs, ctx->qx, nullptr, nullptr, nullptr,
-                     static_cast<const int*>(dp), ctx->cx, nullptr, 0, false, false));
+                     static_cast<const int*>(dp), ctx->cx, nullptr, 0, false, false, nullptr, pre));
   } else {
     TG_TRY(run_decode(ctx, kv, layer, n_seqs, ctx->qx, static_cast<const int*>(dp), 0, ctx->cx,
                       0));
@@ -2473,10 +2603,36 @@ int tg_launch_count(tg_context* ctx, long long* out) {
 
 int tg_profile_enable(tg_context* ctx, int on) {
   TG_TRY(set_device(ctx));
-  if (on < 0 || on > (TG_PROFILE_ATTENTION | TG_PROFILE_PROJECTION))
+  if (on < 0 || on > (TG_PROFILE_ATTENTION | TG_PROFILE_PROJECTION | TG_PROFILE_STAMPS))
     return fail(TG_ERR_INVALID_ARG, "profile_enable: unknown mask %d", on);
+  if ((on & TG_PROFILE_STAMPS) && !ctx->stamps) {
+    if (ctx->capturing) return fail(TG_ERR_STATE, "enable stamps before graph capture");
+    const size_t words =
+        (size_t)TG_STAMP_LAUNCHES * tg::kStampRowsPerSm * ctx->num_sms * tg::kStampsPerCta;
+    TG_CUDA(cudaMalloc(&ctx->stamps, words * sizeof(unsigned long long)));
+    TG_CUDA(cudaMemsetAsync(ctx->stamps, 0, words * sizeof(unsigned long long), ctx->stream));
+    ctx->stamp_cap = TG_STAMP_LAUNCHES;
+  }
   ctx->prof_on = on;
-  if (on) ctx->prof_used = 0;  // disabling keeps the record (a graph may replay it)
+  if (on) {  // disabling keeps the record (a graph may replay it)
+    ctx->prof_used = 0;
+    if (on & TG_PROFILE_STAMPS) ctx->stamp_used = 0;
+  }
+  return TG_OK;
+}
+
+int tg_profile_read_stamps(tg_context* ctx, unsigned long long* out, size_t cap_words,
+                           int* n_launches, int* rows) {
+  TG_TRY(set_device(ctx));
+  if (!out || !n_launches || !rows) return fail(TG_ERR_INVALID_ARG, "null argument");
+  TG_CUDA(cudaStreamSynchronize(ctx->stream));
+  *n_launches = ctx->stamp_used;
+  *rows = tg::kStampRowsPerSm * ctx->num_sms;
+  size_t words = (size_t)ctx->stamp_used * (*rows) * tg::kStampsPerCta;
+  if (words > cap_words) words = cap_words;
+  if (words)
+    TG_CUDA(cudaMemcpy(out, ctx->stamps, words * sizeof(unsigned long long),
+                       cudaMemcpyDeviceToHost));
   return TG_OK;
 }
 

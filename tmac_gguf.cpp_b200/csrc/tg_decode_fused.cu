@@ -39,12 +39,13 @@
 
 namespace tg {
 
-template <int NKV>
+template <int NKV, int RING_KB>
 struct FusedCfg {
   static constexpr int TILE = 64;
-  // 128 KB ring: enough K/V in flight per SM to cover loaded HBM latency
-  // (a pure TMA stream of this tiling reaches the copy peak with it).
-  static constexpr int STAGES = (128 * 1024) / (2 * NKV * TILE * 128);
+  // RING_KB of K/V per CTA: 128 covers loaded HBM latency (a pure TMA stream
+  // of this tiling reaches the copy peak with it); 192 lets a small shard
+  // load more of its tiles before the grid-dependency wait.
+  static constexpr int STAGES = (RING_KB * 1024) / (2 * NKV * TILE * 128);
   // Consumer warps per KV head: each takes RW rows of every tile.  Four (16
   // rows) give every SM sub-partition two or more warps to interleave; with
   // four KV heads, two (32 rows) keep the CTA within the register file.
@@ -65,10 +66,20 @@ struct FusedCfg {
   static constexpr size_t smem_bytes(int B) { return 1024 + (size_t)OFF_PREFIX + (size_t)(B + 1) * 4; }
 };
 
-// Bound of a wait for another GPU's record: about 5 s of SM clock, long
-// enough for host-side launch skew between ranks.
-constexpr long long kPeerWaitCycles = 10000000000LL;
-constexpr long long kPeerWaitPolls = 1LL << 28;
+// Iteration cap of every poll loop; the time bound is FusedParams::wait_ns.
+constexpr long long kPollCap = 1LL << 28;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ void cons_sync(int n) {
   asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory");
@@ -143,11 +154,11 @@ __device__ void fused_prefix(const FusedParams& p, int* prefix, int* warp_tot) {
   __syncthreads();
 }
 
-template <int NKV>
-__global__ void __launch_bounds__(FusedCfg<NKV>::THREADS, 1)
+template <int NKV, int RING_KB>
+__global__ void __launch_bounds__(FusedCfg<NKV, RING_KB>::THREADS, 1)
     decode_fused_kernel(const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv, const FusedParams p) {
-  using Cfg = FusedCfg<NKV>;
+  using Cfg = FusedCfg<NKV, RING_KB>;
   constexpr int TILE = Cfg::TILE, STAGES = Cfg::STAGES, NCT = Cfg::CTHREADS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -161,14 +172,27 @@ __global__ void __launch_bounds__(FusedCfg<NKV>::THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qdim = p.n_head * 64;
   const int rf = record_floats(p.n_head, 64);
+  unsigned long long* stamp = p.stamps ? p.stamps + (size_t)blockIdx.x * kStampsPerCta : nullptr;
 
-  griddep_launch_dependents();
-  // Before the wait for the previous kernel: the schedule (positions only)
-  // and, when the host expects that wait to be long (p.prefetch), an L2
-  // prefetch of this CTA's first tiles, so the ring fills from L2 once the
-  // wait returns.  A prefetch never returns stale data: the loads after the
-  // wait read through L2.  When the wait is short the loads follow the
-  // prefetches while they are still in flight and the step gets slower.
+  // Modes 0 / 1: the merge kernel may launch at once (it waits for this
+  // grid's completion).  Mode 2: only once every CTA of this grid has passed
+  // its grid-dependency wait (below), so that the merge kernel starts after
+  // the previous exchange launch has finished and reads its epoch.
+  if (p.mode != 2) griddep_launch_dependents();
+  if (stamp && threadIdx.x == 0) stamp[0] = global_ns();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], Cfg::CWARPS);
+    }
+    fence_mbar_init();
+  }
+  // Before the wait for the previous kernel: the schedule (positions only;
+  // its barriers also publish the mbarrier initialisation), the TMA
+  // descriptors, the first ring stages when the host allows it (p.preload),
+  // and an L2 prefetch of the following tiles (p.prefetch: when the host
+  // expects the wait to be long).  A prefetch never returns stale data (the
+  // loads after the wait read through L2).
   fused_prefix(p, prefix, warp_tot);
   const long long T = prefix[p.B];
   const int G = (int)min((long long)gridDim.x, T), cta = blockIdx.x;
@@ -178,79 +202,81 @@ __global__ void __launch_bounds__(FusedCfg<NKV>::THREADS, 1)
     t_lo = cta_tile_lo(cta, G, T);
     t_hi = cta_tile_lo(cta + 1, G, T);
   }
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], Cfg::CWARPS);
-    }
-    fence_mbar_init();
-  }
-  if (active && warp == Cfg::CWARPS && lane == 0) {
-    tma_prefetch_desc(&tmk);
-    tma_prefetch_desc(&tmv);
-  }
-  if (p.prefetch && active && warp == Cfg::CWARPS && lane == 0) {
-    int s = 0;
-    const int t_pf = (int)min(t_hi, t_lo + STAGES);
-    for (int t = (int)t_lo; t < t_pf; ++t) {
-      while (prefix[s + 1] <= t) ++s;
-      const int y = (int)(p.row0 + (long long)s * p.max_ctx) + (t - prefix[s]) * TILE;
+  // Producer state, carried from the pre-wait loads into the main loop.
+  int pt = (int)t_lo, ps = 0, pst = 0, pissued = 0;
+  uint32_t pph = 0;
+  bool pok = true;
+  const bool producer = active && warp == Cfg::CWARPS && lane == 0;
+  // Issues the loads of tiles [pt, t_stop); with `guard`, stops before the
+  // first tile holding a sequence's new-token row (a row the previous
+  // kernel may write).  TMA row of tile t: row0 + s*max_ctx +
+  // (t - prefix[s])*TILE (< 2^31, checked when the cache is created).
+  auto produce = [&](int t_stop, bool guard) {
+    while (pt < t_stop && pok) {
+      while (prefix[ps + 1] <= pt) ++ps;
+      const int j = pt - prefix[ps];
+      if (guard) {
+        const int local_new = p.pos[ps] - p.shard_start;
+        if (local_new >= j * TILE && local_new < (j + 1) * TILE) break;
+      }
+      if (!mbar_wait(&empty[pst], pph ^ 1u, p.err, kDevErrWaitEmpty)) {
+        pok = false;
+        break;
+      }
+      uint8_t* stage = smem + pst * Cfg::STAGE_BYTES;
+      mbar_arrive_expect_tx(&full[pst], Cfg::STAGE_BYTES);
+      const int y = (int)(p.row0 + (long long)ps * p.max_ctx) + j * TILE;
 #pragma unroll
       for (int g = 0; g < NKV; ++g) {
-        tma_prefetch_l2_2d(&tmk, 64 * g, y);
-        tma_prefetch_l2_2d(&tmv, 64 * g, y);
+        tma_load_2d(stage + g * Cfg::BOX, &tmk, &full[pst], 64 * g, y);
+        tma_load_2d(stage + (NKV + g) * Cfg::BOX, &tmv, &full[pst], 64 * g, y);
+      }
+      ++pissued;
+      ++pt;
+      if (++pst == STAGES) {
+        pst = 0;
+        pph ^= 1u;
+      }
+    }
+  };
+  if (producer) {
+    tma_prefetch_desc(&tmk);
+    tma_prefetch_desc(&tmv);
+    if (p.preload) produce((int)min(t_hi, t_lo + STAGES), !p.new_row);
+    if (p.prefetch) {
+      int s = ps;
+      const int t_pf = (int)min(t_hi, (long long)pt + STAGES);
+      for (int t = pt; t < t_pf; ++t) {
+        while (prefix[s + 1] <= t) ++s;
+        const int y = (int)(p.row0 + (long long)s * p.max_ctx) + (t - prefix[s]) * TILE;
+#pragma unroll
+        for (int g = 0; g < NKV; ++g) {
+          tma_prefetch_l2_2d(&tmk, 64 * g, y);
+          tma_prefetch_l2_2d(&tmv, 64 * g, y);
+        }
       }
     }
   }
   griddep_wait();
+  if (stamp && threadIdx.x == 0) stamp[1] = global_ns();
   // The previous launch's merge kernel has finished: it read the schedule
-  // buffer and, in mode 2, the exchange epoch, which advances here once per
-  // launch (the merge kernel of this launch reads it after its own wait).
+  // buffer and, in mode 2, the decode-done count of the other parity, which
+  // block 0 clears here for the next launch.
+  const unsigned xpar = p.mode == 2 ? ((*reinterpret_cast<volatile unsigned*>(p.xctl + kXcEpoch) + 1u) & 1u) : 0u;
   if (blockIdx.x == 0) {
     for (int i = threadIdx.x; i <= p.B; i += blockDim.x) p.sched[i] = prefix[i];
-    if (p.mode == 2 && threadIdx.x == 0) *p.epoch += 1u;
+    if (p.mode == 2 && threadIdx.x == 0) p.xctl[kXcDecDone + (xpar ^ 1u)] = 0u;
   }
+  if (p.mode == 2) griddep_launch_dependents();
   __syncthreads();
 
-  if (active && warp == Cfg::CWARPS) {
+  if (producer) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      const int tlo = (int)t_lo, thi = (int)t_hi;
-      int issued = 0, st = 0, s = 0;
-      uint32_t ph = 0;
-      bool ok = true;
-      for (int t = tlo; t < thi && ok; ++s) {
-        while (prefix[s + 1] <= t) ++s;
-        const int s_end = min(thi, prefix[s + 1]);
-        // TMA row of tile t: row0 + s*max_ctx + (t - prefix[s])*TILE (< 2^31,
-        // checked when the cache is created).
-        const int y0 = (int)(p.row0 + (long long)s * p.max_ctx) - prefix[s] * TILE;
-        for (; t < s_end; ++t) {
-          if (!mbar_wait(&empty[st], ph ^ 1u, p.err, kDevErrWaitEmpty)) {
-            ok = false;
-            break;
-          }
-          uint8_t* stage = smem + st * Cfg::STAGE_BYTES;
-          mbar_arrive_expect_tx(&full[st], Cfg::STAGE_BYTES);
-          const int y = y0 + t * TILE;
-#pragma unroll
-          for (int g = 0; g < NKV; ++g) {
-            tma_load_2d(stage + g * Cfg::BOX, &tmk, &full[st], 64 * g, y);
-            tma_load_2d(stage + (NKV + g) * Cfg::BOX, &tmv, &full[st], 64 * g, y);
-          }
-          ++issued;
-          if (++st == STAGES) {
-            st = 0;
-            ph ^= 1u;
-          }
-        }
-      }
-      // Drain: every issued load lands before the CTA exits.
-      for (int k2 = max(0, issued - STAGES); k2 < issued; ++k2)
-        mbar_wait(&full[k2 % STAGES], (uint32_t)((k2 / STAGES) & 1), p.err, kDevErrWaitFull);
-    }
-    __syncwarp();
-  } else if (active) {
+    produce((int)t_hi, false);
+    // Drain: every issued load lands before the CTA exits.
+    for (int k2 = max(0, pissued - STAGES); k2 < pissued; ++k2)
+      mbar_wait(&full[k2 % STAGES], (uint32_t)((k2 / STAGES) & 1), p.err, kDevErrWaitFull);
+  } else if (active && warp < Cfg::CWARPS) {
     // ------------------------------------------------------------ consumers
     constexpr int WPH = Cfg::WPH, RW = Cfg::RW, NT = Cfg::NT, KP = Cfg::KP;
     const int g = warp / WPH, hf = warp % WPH;
@@ -498,6 +524,17 @@ __global__ void __launch_bounds__(FusedCfg<NKV>::THREADS, 1)
       }
     }
   }
+  if (stamp && threadIdx.x == 0) stamp[2] = global_ns();
+  if (p.mode == 2) {
+    // Everything this CTA wrote (records, partial records, rotated q / k, the
+    // new cache row, the schedule) is published to the merge kernel through
+    // the decode-done count, which it waits for instead of this grid's
+    // completion: every thread fences its own stores, then one arrival.
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) atomicAdd(p.xctl + kXcDecDone + xpar, 1u);
+  }
+  if (stamp && threadIdx.x == 0) stamp[3] = global_ns();
 }
 
 
@@ -506,10 +543,11 @@ __global__ void __launch_bounds__(FusedCfg<NKV>::THREADS, 1)
 constexpr int kMaxMergeGroups = 4;
 constexpr int kPartBatch = 16;  // parts per group per load round
 
-// One item per (sequence s, head h) and 64 * GROUPS threads: thread d of
-// group grp handles dimension d of parts grp, grp + GROUPS, ...  Every part's
-// m, l and o are loaded in the same round (kPartBatch per group) and merged
-// online, then the groups are combined through shared memory.
+// One item per (sequence s, head h) and 64 * GROUPS threads; parts are
+// merged in rounds of up to GROUPS * kPartBatch: every part's m and l go to
+// shared memory (one load each), thread d of group grp loads dimension d of
+// o for parts grp, grp + GROUPS, ...  -- all in one round -- and every thread
+// applies the same running maximum, so the groups' sums just add up.
 //   1. this GPU's record slice of (s, h): the merge of the partial records of
 //      a split sequence, the complete record the decode kernel wrote, or a
 //      neutral record when this shard holds no row of s;
@@ -523,25 +561,31 @@ constexpr int kPartBatch = 16;  // parts per group per load round
 // increasing order on every GPU, and the grid is small enough to be
 // resident, so a CTA waiting for another GPU's item i only ever waits for a
 // CTA that processes i next.
+// At most 64 registers per thread, so that a merge CTA fits on an SM beside a
+// decode CTA (168 registers x 288 threads): the next layer's decode CTAs then
+// land on every SM as soon as this layer's decode CTAs exit and load their
+// first tiles while this kernel runs.  (The per-thread m / l / o version
+// needed 123 registers; capped at 64 it spilled and took two load rounds.)
 template <int GROUPS>
-__global__ void __launch_bounds__(64 * GROUPS) merge_exchange_kernel(const FusedParams p) {
+__global__ void __launch_bounds__(64 * GROUPS, 16 / GROUPS) merge_exchange_kernel(const FusedParams p) {
+  constexpr int NT = 64 * GROUPS, MAXP = GROUPS * kPartBatch;
+  __shared__ float m_s[MAXP], l_s[MAXP];  // this round's parts; m_s then holds weights
+  __shared__ float mb_s, lsum_s;
   __shared__ float o_grp[GROUPS][64];
-  __shared__ float ml_grp[GROUPS][2];
+  __shared__ float xm[kMaxPeers], xl[kMaxPeers];
   __shared__ int pre[64 * GROUPS + 1];
   __shared__ int wsum[2 * GROUPS];
+  __shared__ int x_bad;
   const int tid = threadIdx.x, d = tid & 63, grp = tid >> 6;
   griddep_launch_dependents();
+  unsigned long long* stamp = (p.stamps && (int)blockIdx.x < 2 * p.grid)
+                                  ? p.stamps + (size_t)(p.grid + blockIdx.x) * kStampsPerCta
+                                  : nullptr;
+  if (stamp && tid == 0) stamp[0] = global_ns();
   // With at most one sequence per thread, the tile prefix is rebuilt from the
   // positions before the wait (as the decode kernel does); otherwise the
   // decode kernel's copy is read after it.
   const bool local_sched = p.B <= 64 * GROUPS;
-  // The RoPE row of this CTA's first item (the table is written only when
-  // it is created).
-  const int s_first = blockIdx.x / p.n_head;
-  const int pos_first = s_first < p.B ? p.pos[s_first] : -1;
-  float2 cs_first = make_float2(0.f, 0.f);
-  if (p.rope && pos_first >= 0 && pos_first < p.table_len)
-    cs_first = reinterpret_cast<const float2*>(p.cs + (size_t)pos_first * 64)[d >> 1];
   if (local_sched) {
     const int lane = tid & 31, w = tid >> 5;
     const int tiles = tid < p.B ? max(seq_tiles(p, p.pos[tid]), 0) : 0;
@@ -559,22 +603,49 @@ __global__ void __launch_bounds__(64 * GROUPS) merge_exchange_kernel(const Fused
     if (tid == 0) pre[0] = 0;
     __syncthreads();
   }
-  griddep_wait();
-  const int* sched = local_sched ? pre : p.sched;
+  uint32_t epoch = 0u;
+  if (p.mode == 2) {
+    // This kernel starts only once every CTA of its decode launch has passed
+    // its grid-dependency wait, i.e. after the previous exchange launch has
+    // finished: the epoch word holds that launch's tag.  Instead of waiting
+    // for the decode grid's completion, wait (bounded) until all its CTAs
+    // have counted themselves done; their stores are fenced before that.
+    epoch = *reinterpret_cast<volatile unsigned*>(p.xctl + kXcEpoch) + 1u;
+    if (tid == 0) {
+      const unsigned* done = p.xctl + kXcDecDone + (epoch & 1u);
+      const unsigned long long t_end = global_ns() + (unsigned long long)p.wait_ns;
+      bool ok = false;
+      for (long long n = 0; n < kPollCap; ++n) {
+        if ((int)ld_acquire_gpu_u32(done) >= p.grid) {
+          ok = true;
+          break;
+        }
+        if (global_ns() > t_end) break;
+        __nanosleep(64);
+      }
+      if (!ok) record_error(p.err, kDevErrDecodeTimeout);
+    }
+    __syncthreads();
+  } else {
+    griddep_wait();
+  }
+  if (stamp && tid == 0) stamp[1] = global_ns();
+  // Data of the decode launch is read past L1 (in mode 2 this kernel may
+  // have started before it was written).
+  auto sch = [&](int i) { return local_sched ? pre[i] : __ldcg(p.sched + i); };
   const int H = p.n_head, qdim = H * 64, rf = record_floats(H, 64);
-  const uint32_t epoch = (p.mode == 2) ? *reinterpret_cast<volatile unsigned*>(p.epoch) : 0u;
-  const int T = sched[p.B];
+  const int T = sch(p.B);
   const int G = min(p.grid, T);
   const int items = p.B * H;
+  if (tid == 0) x_bad = 0;  // first read after several barriers below
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
     const int s = it / H, h = it - s * H;
-    const int t0 = sched[s], t1 = sched[s + 1];
+    const int t0 = sch(s), t1 = sch(s + 1);
     const int c1 = t1 > t0 ? cta_of_tile(t0, G, T) : 0;
     const int c2 = t1 > t0 ? cta_of_tile(t1 - 1, G, T) : 0;
     const bool split = t1 > t0 && c1 != c2;
     if (p.mode == 0 && !split) continue;  // finished by the decode kernel
-    const bool first = it == (int)blockIdx.x;
-    const int pos_s = first ? pos_first : p.pos[s];
+    const int pos_s = p.pos[s];
     const bool rope = p.rope && (split || t1 == t0) && grp == 0 && pos_s >= 0 &&
                       pos_s < p.table_len;
     const bool has_k = rope && p.k_io && h < p.n_kv;
@@ -583,87 +654,82 @@ __global__ void __launch_bounds__(64 * GROUPS) merge_exchange_kernel(const Fused
     if (rope) {
       const float* qi = p.q_in + (size_t)s * qdim + h * 64;
       xq = make_float2(qi[d & ~1], qi[d | 1]);
-      cs = first ? cs_first : reinterpret_cast<const float2*>(p.cs + (size_t)pos_s * 64)[d >> 1];
+      cs = reinterpret_cast<const float2*>(p.cs + (size_t)pos_s * 64)[d >> 1];
       if (has_k) {
         const float* kk = p.k_io + (size_t)s * p.n_kv * 64 + h * 64;
         xk = make_float2(kk[d & ~1], kk[d | 1]);
       }
     }
-    float o = 0.f, m = kNegBig, l = 0.f;  // this GPU's record slice (group 0)
-    if (split) {
-      const int first_slot = 2 * c1 + (cta_tile_lo(c1, G, T) == t0 ? 0 : 1);
-      const int n_parts = 1 + (c2 - c1);
-      float mg = kNegBig, lg = 0.f, og = 0.f;
-      for (int k0 = grp; k0 < n_parts; k0 += GROUPS * kPartBatch) {
-        float mv[kPartBatch], lv[kPartBatch], ov[kPartBatch];
+    // Parts of (s, h) on this GPU: the partial records of a split sequence,
+    // the record of a sequence finished in one CTA (modes 1 and 2), none for
+    // a sequence without rows on this shard.
+    const int n_parts = split ? 1 + (c2 - c1) : (t1 > t0 ? 1 : 0);
+    const int first_slot = split ? 2 * c1 + (cta_tile_lo(c1, G, T) == t0 ? 0 : 1) : 0;
+    float o = 0.f, M = kNegBig, L = 0.f;  // running merge, same M in every thread
+    for (int k0 = 0; k0 < n_parts; k0 += MAXP) {
+      const int cnt = min(MAXP, n_parts - k0);
+      auto rec = [&](int k) {
+        return split ? p.part + (size_t)(k == 0 ? first_slot : 2 * (c1 + k)) * rf
+                     : p.records + (size_t)s * rf;
+      };
+      float ml = 0.f;
+      if (tid < 2 * cnt) ml = __ldcg(rec(k0 + (tid >> 1)) + qdim + (tid & 1) * H + h);
+      float ov[kPartBatch];
 #pragma unroll
-        for (int u = 0; u < kPartBatch; ++u) {
-          const int kk = k0 + u * GROUPS;
-          mv[u] = kNegBig;
-          lv[u] = 0.f;
-          ov[u] = 0.f;
-          if (kk < n_parts) {
-            const float* r = p.part + (size_t)(kk == 0 ? first_slot : 2 * (c1 + kk)) * rf;
-            mv[u] = r[qdim + h];
-            lv[u] = r[qdim + H + h];
-            ov[u] = r[h * 64 + d];
-          }
-        }
-        float Mb = mg;
-#pragma unroll
-        for (int u = 0; u < kPartBatch; ++u) Mb = fmaxf(Mb, mv[u]);
-        const float a = ex2(mg - Mb);
-        og *= a;
-        lg *= a;
-#pragma unroll
-        for (int u = 0; u < kPartBatch; ++u) {
-          const float w = ex2(mv[u] - Mb);
-          og = fmaf(ov[u], w, og);
-          lg = fmaf(lv[u], w, lg);
-        }
-        mg = Mb;
+      for (int u = 0; u < kPartBatch; ++u) {
+        const int k = grp + u * GROUPS;
+        ov[u] = k < cnt ? __ldcg(rec(k0 + k) + h * 64 + d) : 0.f;
       }
-      if (GROUPS > 1) {
-        o_grp[grp][d] = og;
-        if (d == 0) {
-          ml_grp[grp][0] = mg;
-          ml_grp[grp][1] = lg;
+      if (tid < 2 * cnt) ((tid & 1) ? l_s : m_s)[tid >> 1] = ml;
+      __syncthreads();
+      // Warp 0: the round's maximum, each part's weight (in place of its m)
+      // and the weighted sum of l, once for the whole CTA.
+      if (tid < 32) {
+        float mx = M;
+        for (int k = tid; k < cnt; k += 32) mx = fmaxf(mx, m_s[k]);
+        mx = warp_max(mx);
+        float ls = 0.f;
+        for (int k = tid; k < cnt; k += 32) {
+          const float w = ex2(m_s[k] - mx);
+          m_s[k] = w;
+          ls = fmaf(l_s[k], w, ls);
         }
-        __syncthreads();
-        if (grp == 0) {
-          float M = kNegBig;
-#pragma unroll
-          for (int g2 = 0; g2 < GROUPS; ++g2) M = fmaxf(M, ml_grp[g2][0]);
-          o = 0.f;
-          l = 0.f;
-#pragma unroll
-          for (int g2 = 0; g2 < GROUPS; ++g2) {
-            const float w = ex2(ml_grp[g2][0] - M);
-            o = fmaf(o_grp[g2][d], w, o);
-            l = fmaf(ml_grp[g2][1], w, l);
-          }
-          m = M;
+        ls = warp_sum(ls);
+        if (tid == 0) {
+          mb_s = mx;
+          lsum_s = ls;
         }
-      } else {
-        o = og;
-        m = mg;
-        l = lg;
       }
-    } else if (t1 > t0 && p.mode != 0 && grp == 0) {
-      const float* rec = p.records + (size_t)s * rf;
-      o = rec[h * 64 + d];
-      m = rec[qdim + h];
-      l = rec[qdim + H + h];
+      __syncthreads();
+      const float Mb = mb_s;
+      const float a = ex2(M - Mb);
+      o *= a;
+#pragma unroll
+      for (int u = 0; u < kPartBatch; ++u) {
+        const int k = grp + u * GROUPS;
+        if (k < cnt) o = fmaf(ov[u], m_s[k], o);
+      }
+      L = fmaf(L, a, lsum_s);
+      M = Mb;
+      __syncthreads();
+    }
+    if (GROUPS > 1) {
+      o_grp[grp][d] = o;
+      __syncthreads();
+      if (grp == 0) {
+#pragma unroll
+        for (int g2 = 1; g2 < GROUPS; ++g2) o += o_grp[g2][d];
+      }
     }
     if (p.mode == 0) {
-      if (grp == 0) p.out[(size_t)s * qdim + h * 64 + d] = o / l;
+      if (grp == 0) p.out[(size_t)s * qdim + h * 64 + d] = o / L;
     } else if (p.mode == 1) {
-      if ((split || t1 == t0) && grp == 0) {
-        float* rec = p.records + (size_t)s * rf;
-        rec[h * 64 + d] = o;
+      if (grp == 0 && (split || t1 == t0)) {
+        float* r = p.records + (size_t)s * rf;
+        r[h * 64 + d] = o;
         if (d == 0) {
-          rec[qdim + h] = m;
-          rec[qdim + H + h] = l;
+          r[qdim + h] = M;
+          r[qdim + H + h] = L;
         }
       }
     } else {
@@ -675,64 +741,64 @@ __global__ void __launch_bounds__(64 * GROUPS) merge_exchange_kernel(const Fused
       const unsigned long long tag = (unsigned long long)epoch << 32;  // epoch >= 1
       const size_t item_words = (size_t)kXchgWords;
       const size_t mine = (((size_t)(par * p.world + p.rank) * p.b_cap + s) * H + h) * item_words;
+      const unsigned long long* base =
+          p.xchg_local + (((size_t)(par * p.world) * p.b_cap + s) * H + h) * item_words;
+      const size_t stride = (size_t)p.b_cap * H * item_words;
+      float orv[kMaxPeers];
       if (grp == 0) {
         const unsigned long long wo = tag | __float_as_uint(o);
-        const unsigned long long wm = tag | __float_as_uint(m);
-        const unsigned long long wl = tag | __float_as_uint(l);
         for (int r = 0; r < p.world; ++r) {
           unsigned long long* dst = (r == p.rank ? p.xchg_local : p.xchg_peer[r]) + mine;
           st_relaxed_sys_u64(dst + d, wo);
-          if (d == 0) {
-            st_relaxed_sys_u64(dst + 64, wm);
-            st_relaxed_sys_u64(dst + 65, wl);
-          }
+          if (d < 2) st_relaxed_sys_u64(dst + 64 + d, tag | __float_as_uint(d ? L : M));
         }
-        // Gather: this thread's dimension and every GPU's m and l.
-        const unsigned long long* base =
-            p.xchg_local + (((size_t)(par * p.world) * p.b_cap + s) * H + h) * item_words;
-        const size_t stride = (size_t)p.b_cap * H * item_words;
-        float mv[kMaxPeers], lv[kMaxPeers], ov[kMaxPeers];
+        // Gather: this thread's dimension of every GPU's slice, and (threads
+        // 0 .. 2*world-1) one GPU's m or l into shared memory.
         unsigned pending = (1u << p.world) - 1u;
-        const long long c0 = clock64();
-        for (long long n = 0; pending && n < kPeerWaitPolls; ++n) {
+        bool ml_pending = d < 2 * p.world;
+        const unsigned long long t_end = global_ns() + (unsigned long long)p.wait_ns;
+        for (long long n = 0; (pending || ml_pending) && n < kPollCap; ++n) {
 #pragma unroll
           for (int r = 0; r < kMaxPeers; ++r) {
             if (!(pending >> r & 1u)) continue;
-            const unsigned long long* rr = base + r * stride;
-            const unsigned long long x = ld_relaxed_sys_u64(rr + d);
-            const unsigned long long y = ld_relaxed_sys_u64(rr + 64);
-            const unsigned long long z = ld_relaxed_sys_u64(rr + 65);
-            if ((x >> 32) == (tag >> 32) && (y >> 32) == (tag >> 32) && (z >> 32) == (tag >> 32)) {
-              ov[r] = __uint_as_float((unsigned)x);
-              mv[r] = __uint_as_float((unsigned)y);
-              lv[r] = __uint_as_float((unsigned)z);
+            const unsigned long long x = ld_relaxed_sys_u64(base + r * stride + d);
+            if ((x >> 32) == (tag >> 32)) {
+              orv[r] = __uint_as_float((unsigned)x);
               pending &= ~(1u << r);
             }
           }
-          if (pending && clock64() - c0 > kPeerWaitCycles) break;
-        }
-        if (pending) {
-          record_error(p.err, kDevErrPeerTimeout);
-        } else {
-          float M = kNegBig;
-#pragma unroll
-          for (int r = 0; r < kMaxPeers; ++r)
-            if (r < p.world) M = fmaxf(M, mv[r]);
-          float O = 0.f, L = 0.f;
-#pragma unroll
-          for (int r = 0; r < kMaxPeers; ++r) {
-            if (r < p.world) {
-              const float w = ex2(mv[r] - M);
-              O = fmaf(ov[r], w, O);
-              L = fmaf(lv[r], w, L);
+          if (ml_pending) {
+            const unsigned long long y = ld_relaxed_sys_u64(base + (d >> 1) * stride + 64 + (d & 1));
+            if ((y >> 32) == (tag >> 32)) {
+              ((d & 1) ? xl : xm)[d >> 1] = __uint_as_float((unsigned)y);
+              ml_pending = false;
             }
           }
-          p.out[(size_t)s * qdim + h * 64 + d] = O / L;
+          if ((pending || ml_pending) && global_ns() > t_end) break;
         }
+        if (pending || ml_pending) {
+          record_error(p.err, kDevErrPeerTimeout);
+          x_bad = 1;
+        }
+      }
+      __syncthreads();
+      if (grp == 0 && !x_bad) {
+        float Mx = kNegBig;
+        for (int r = 0; r < p.world; ++r) Mx = fmaxf(Mx, xm[r]);
+        float O = 0.f, Lx = 0.f;
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r) {
+          if (r < p.world) {
+            const float w = ex2(xm[r] - Mx);
+            O = fmaf(orv[r], w, O);
+            Lx = fmaf(xl[r], w, Lx);
+          }
+        }
+        p.out[(size_t)s * qdim + h * 64 + d] = O / Lx;
       }
     }
     if (rope) {
-      // All readers of the raw q / k of s have finished (previous kernel);
+      // All readers of the raw q / k of s have finished (the decode kernel);
       // each thread writes only the element of the pair it owns.
       const float2 rq = rot(xq, cs);
       p.q_out[(size_t)s * qdim + h * 64 + d] = (d & 1) ? rq.y : rq.x;
@@ -741,8 +807,22 @@ __global__ void __launch_bounds__(64 * GROUPS) merge_exchange_kernel(const Fused
         p.k_out[(size_t)s * p.n_kv * 64 + h * 64 + d] = (d & 1) ? rk.y : rk.x;
       }
     }
-    if (GROUPS > 1) __syncthreads();
+    __syncthreads();
+    if (tid == 0) x_bad = 0;  // read above, before the barrier
   }
+  if (p.mode == 2) {
+    // The last CTA to finish publishes this launch's tag (every CTA read the
+    // previous one above).
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      if (atomicAdd(p.xctl + kXcMergeDone, 1u) == gridDim.x - 1) {
+        p.xctl[kXcMergeDone] = 0u;
+        p.xctl[kXcEpoch] = epoch;
+      }
+    }
+  }
+  if (stamp && tid == 0) stamp[3] = global_ns();
 }
 
 // ---------------------------------------------------------------- launch
@@ -763,29 +843,31 @@ static cudaError_t launch_pdl_f(void (*fn)(KArgs...), dim3 grid, dim3 block, siz
   return cudaLaunchKernelEx(&cfg, fn, std::forward<Args>(args)...);
 }
 
-template <int NKV>
-static cudaError_t launch_fused_nkv(const CUtensorMap& tk, const CUtensorMap& tv,
+template <int NKV, int RING_KB>
+static cudaError_t launch_fused_cfg(const CUtensorMap& tk, const CUtensorMap& tv,
                                     const FusedParams& p, int grid, cudaStream_t st) {
+  using Cfg = FusedCfg<NKV, RING_KB>;
   static size_t configured[64] = {};
-  const size_t smem = FusedCfg<NKV>::smem_bytes(p.B);
+  const size_t smem = Cfg::smem_bytes(p.B);
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (smem > configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(decode_fused_kernel<NKV>,
+    cudaError_t e = cudaFuncSetAttribute(decode_fused_kernel<NKV, RING_KB>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     configured[dev] = smem;
   }
-  return launch_pdl_f(decode_fused_kernel<NKV>, dim3(grid), dim3(FusedCfg<NKV>::THREADS), smem,
+  return launch_pdl_f(decode_fused_kernel<NKV, RING_KB>, dim3(grid), dim3(Cfg::THREADS), smem,
                       st, tk, tv, p);
 }
 
-size_t decode_fused_smem(int nkv, int B) {
+size_t decode_fused_smem(int nkv, int ring_kb, int B) {
+  const bool deep = ring_kb == kFusedRingDeep;
   switch (nkv) {
-    case 1: return FusedCfg<1>::smem_bytes(B);
-    case 2: return FusedCfg<2>::smem_bytes(B);
-    case 4: return FusedCfg<4>::smem_bytes(B);
+    case 1: return deep ? FusedCfg<1, kFusedRingDeep>::smem_bytes(B) : FusedCfg<1, kFusedRing>::smem_bytes(B);
+    case 2: return deep ? FusedCfg<2, kFusedRingDeep>::smem_bytes(B) : FusedCfg<2, kFusedRing>::smem_bytes(B);
+    case 4: return deep ? FusedCfg<4, kFusedRingDeep>::smem_bytes(B) : FusedCfg<4, kFusedRing>::smem_bytes(B);
     default: return 0;
   }
 }
@@ -800,11 +882,16 @@ cudaError_t launch_merge_exchange(const FusedParams& p, int grid, int groups, cu
 }
 
 cudaError_t launch_decode_fused(const CUtensorMap& tk, const CUtensorMap& tv,
-                                const FusedParams& p, int grid, cudaStream_t st) {
+                                const FusedParams& p, int ring_kb, int grid, cudaStream_t st) {
+  const bool deep = ring_kb == kFusedRingDeep;
+  if (!deep && ring_kb != kFusedRing) return cudaErrorInvalidValue;
   switch (p.n_kv) {
-    case 1: return launch_fused_nkv<1>(tk, tv, p, grid, st);
-    case 2: return launch_fused_nkv<2>(tk, tv, p, grid, st);
-    case 4: return launch_fused_nkv<4>(tk, tv, p, grid, st);
+    case 1: return deep ? launch_fused_cfg<1, kFusedRingDeep>(tk, tv, p, grid, st)
+                        : launch_fused_cfg<1, kFusedRing>(tk, tv, p, grid, st);
+    case 2: return deep ? launch_fused_cfg<2, kFusedRingDeep>(tk, tv, p, grid, st)
+                        : launch_fused_cfg<2, kFusedRing>(tk, tv, p, grid, st);
+    case 4: return deep ? launch_fused_cfg<4, kFusedRingDeep>(tk, tv, p, grid, st)
+                        : launch_fused_cfg<4, kFusedRing>(tk, tv, p, grid, st);
     default: return cudaErrorInvalidValue;
   }
 }

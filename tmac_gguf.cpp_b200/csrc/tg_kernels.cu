@@ -24,6 +24,8 @@
 
 #include <cooperative_groups.h>
 
+#include <mutex>
+
 #include <utility>
 
 #include "tg_device.cuh"
@@ -1267,25 +1269,37 @@ cudaError_t launch_rope(const RopeParams& p, cudaStream_t st) {
   return launch_pdl(rope_cache_write_kernel, dim3(p.B), dim3(128), 0, st, p);
 }
 
-// Raises a kernel's dynamic shared-memory limit once per device and size.
+// Dynamic shared-memory limits set on the CUDA-core decode kernel, per device.
+static size_t g_generic_cfg_f32[64] = {}, g_generic_cfg_bf16[64] = {};
+
+// Raises a kernel's dynamic shared-memory limit once per device and size
+// (never lowers it); callers on several threads share the caches.
+static std::mutex g_attr_mu;
 template <typename F>
 static cudaError_t ensure_smem(F* fn, size_t smem, size_t* cache) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_attr_mu);
   if (smem <= cache[dev]) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e == cudaSuccess) cache[dev] = smem;
   return e;
 }
 
+// Dynamic shared-memory limits set on decode_mma_kernel<NKV>, per device.
+template <int NKV>
+static size_t* mma_configured() {
+  static size_t configured[64] = {};
+  return configured;
+}
+
 template <int NKV>
 static cudaError_t launch_mma_nkv(const CUtensorMap& tk, const CUtensorMap& tv,
                                   const DecodeParams& p, int grid,
                                   cudaStream_t st) {
-  static size_t configured[64] = {};
   const size_t smem = MmaCfg<NKV>::smem_bytes(p.B);
-  cudaError_t e = ensure_smem(decode_mma_kernel<NKV>, smem, configured);
+  cudaError_t e = ensure_smem(decode_mma_kernel<NKV>, smem, mma_configured<NKV>());
   if (e != cudaSuccess) return e;
   return launch_pdl(decode_mma_kernel<NKV>, dim3(grid), dim3(MmaCfg<NKV>::THREADS), smem, st,
                     tk, tv, p);
@@ -1298,6 +1312,23 @@ size_t decode_mma_smem(int nkv, int B) {
     case 4: return MmaCfg<4>::smem_bytes(B);
     default: return 0;
   }
+}
+
+cudaError_t prepare_decode_kernels(int max_seqs) {
+  const size_t cap = 227 * 1024;
+  auto lim = [&](size_t x) { return x < cap ? x : cap; };
+  cudaError_t e = ensure_smem(decode_mma_kernel<1>, lim(MmaCfg<1>::smem_bytes(max_seqs)),
+                              mma_configured<1>());
+  if (e == cudaSuccess)
+    e = ensure_smem(decode_mma_kernel<2>, lim(MmaCfg<2>::smem_bytes(max_seqs)),
+                    mma_configured<2>());
+  if (e == cudaSuccess)
+    e = ensure_smem(decode_mma_kernel<4>, lim(MmaCfg<4>::smem_bytes(max_seqs)),
+                    mma_configured<4>());
+  if (e == cudaSuccess) e = ensure_smem(decode_generic_kernel<float>, cap, g_generic_cfg_f32);
+  if (e == cudaSuccess)
+    e = ensure_smem(decode_generic_kernel<__nv_bfloat16>, cap, g_generic_cfg_bf16);
+  return e;
 }
 
 cudaError_t launch_decode_mma(const CUtensorMap& tk, const CUtensorMap& tv,
@@ -1345,7 +1376,8 @@ cudaError_t launch_decode_small(const DecodeParams& p_in, int dtype, cudaStream_
 
 cudaError_t launch_decode_generic(const DecodeParams& p, int dtype, int grid,
                                   cudaStream_t st) {
-  static size_t configured_f32[64] = {}, configured_bf16[64] = {};
+  size_t* configured_f32 = g_generic_cfg_f32;
+  size_t* configured_bf16 = g_generic_cfg_bf16;
   const size_t smem = decode_generic_smem(p.B, p.n_head, p.n_kv, p.head_dim);
   cudaError_t e;
   if (dtype == 0) {
@@ -1361,26 +1393,35 @@ cudaError_t launch_decode_generic(const DecodeParams& p, int dtype, int grid,
 }
 
 int decode_generic_blocks_per_sm(int dtype, size_t smem) {
-  static size_t last_smem[2] = {0, 0};
-  static int last_n[2] = {0, 0};
+  // Resident CTAs per SM for a dynamic shared-memory size, cached per device
+  // and dtype; the limit is raised through the launcher's cache so that a
+  // query never lowers what a launch relies on.
+  static std::mutex mu;
+  static size_t last_smem[64][2] = {};
+  static int last_n[64][2] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return 1;
+  }
   const int di = dtype == 0 ? 0 : 1;
-  if (last_n[di] && last_smem[di] == smem) return last_n[di];
+  std::lock_guard<std::mutex> lock(mu);
+  if (last_n[dev][di] && last_smem[dev][di] == smem) return last_n[dev][di];
   int n = 0;
   if (dtype == 0) {
-    cudaFuncSetAttribute(decode_generic_kernel<float>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_generic_kernel<float>,
-                                                  GEN_THREADS, smem);
+    if (ensure_smem(decode_generic_kernel<float>, smem, g_generic_cfg_f32) == cudaSuccess)
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_generic_kernel<float>,
+                                                    GEN_THREADS, smem);
   } else {
-    cudaFuncSetAttribute(decode_generic_kernel<__nv_bfloat16>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_generic_kernel<__nv_bfloat16>,
-                                                  GEN_THREADS, smem);
+    if (ensure_smem(decode_generic_kernel<__nv_bfloat16>, smem, g_generic_cfg_bf16) ==
+        cudaSuccess)
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_generic_kernel<__nv_bfloat16>,
+                                                    GEN_THREADS, smem);
   }
   cudaGetLastError();
   n = n < 1 ? 1 : n;
-  last_smem[di] = smem;
-  last_n[di] = n;
+  last_smem[dev][di] = smem;
+  last_n[dev][di] = n;
   return n;
 }
 

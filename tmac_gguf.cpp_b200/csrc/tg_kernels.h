@@ -35,6 +35,10 @@ cudaError_t launch_decode_small(const DecodeParams& p, int dtype, cudaStream_t s
 size_t decode_small_smem(int group, int max_ctx, int split);
 
 cudaError_t launch_merge(const MergeParams& p, cudaStream_t st);
+// Raises the shared-memory limit of the tensor-core decode (n_kv 1, 2, 4) and
+// the CUDA-core decode (fp32, bf16) on the current device to what max_seqs
+// sequences can need, so that later launches change no kernel attribute.
+cudaError_t prepare_decode_kernels(int max_seqs);
 cudaError_t launch_gather_merge(const GatherMergeParams& p, cudaStream_t st);
 cudaError_t launch_elem(int op, float* data, const float* aux, int dim,
                         cudaStream_t st);
@@ -45,13 +49,16 @@ cudaError_t launch_convert_rows(void* dst, const float* src, size_t n,
 
 // Fused decode step (tg_decode_fused.cu): bf16 cache, head_dim 64,
 // n_kv in {1, 2, 4}, at most 8 query heads per KV head.
+// ring_kb: K/V ring per CTA, kFusedRing or kFusedRingDeep.
+constexpr int kFusedRing = 128;
+constexpr int kFusedRingDeep = 192;
 cudaError_t launch_decode_fused(const CUtensorMap& tk, const CUtensorMap& tv,
-                                const FusedParams& p, int grid, cudaStream_t st);
+                                const FusedParams& p, int ring_kb, int grid, cudaStream_t st);
 // groups: 1 (64 threads per item, many items) or 4 (256 threads, few items or
 // the persistent peer-exchange grid).
 constexpr int kMergeGroupsWide = 4;
 cudaError_t launch_merge_exchange(const FusedParams& p, int grid, int groups, cudaStream_t st);
-size_t decode_fused_smem(int nkv, int B);
+size_t decode_fused_smem(int nkv, int ring_kb, int B);
 
 // Prefill (tg_prefill.cu).  The attention kernel needs a bf16 cache with
 // head_dim 64 and S a positive length; tq is a 3-D map of the rotated bf16 q

@@ -60,7 +60,10 @@ int err(int code, const char* fmt, ...) {
 }
 
 // Once per device, with that device current: the array's device address
-// (host code must not use the symbol itself) and the SM count.
+// (host code must not use the symbol itself), the SM count, and the
+// shared-memory limits of every kernel variant this entry point can launch,
+// raised to what TG_NOALLOC_MAX_SEQS sequences need, so that a later call
+// with another dtype, shape or batch changes no kernel attribute.
 int setup(int dev, unsigned char** scratch, int* sms) {
   std::lock_guard<std::mutex> lock(g_setup_mu);
   if (!g_scratch_addr[dev]) {
@@ -73,6 +76,9 @@ int setup(int dev, unsigned char** scratch, int* sms) {
     e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess)
       return err(TG_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
+    e = tg::prepare_decode_kernels(kMaxSeqs);
+    if (e != cudaSuccess)
+      return err(TG_ERR_CUDA, "tg_attention_noalloc: kernel set-up: %s", cudaGetErrorString(e));
     g_sms[dev] = n;
     g_scratch_addr[dev] = static_cast<unsigned char*>(p);
   }
@@ -163,11 +169,11 @@ extern "C" TG_API int tg_attention_noalloc(void* cuda_stream, const float* q, co
                     ? 1
                     : 0;
 
-  const bool mma = dtype == TG_DTYPE_BF16 && head_dim == 64 &&
-                   (n_kv_head == 1 || n_kv_head == 2 || n_kv_head == 4) &&
-                   n_head / n_kv_head <= 8 && encoder() != nullptr;
-  int grid;
-  size_t smem;
+  bool mma = dtype == TG_DTYPE_BF16 && head_dim == 64 &&
+             (n_kv_head == 1 || n_kv_head == 2 || n_kv_head == 4) &&
+             n_head / n_kv_head <= 8 && encoder() != nullptr;
+  int grid = 0;
+  size_t smem = 0;
   alignas(64) CUtensorMap tk, tv;
   if (mma) {
     const cuuint64_t gdim[2] = {(cuuint64_t)n_kv_head * 64, (cuuint64_t)n_seqs * max_ctx};
@@ -182,9 +188,11 @@ extern "C" TG_API int tg_attention_noalloc(void* cuda_stream, const float* q, co
                             gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS)
-      return err(TG_ERR_INVALID_ARG,
-                 "tg_attention_noalloc: TMA descriptor rejected (caches must be 16-byte aligned)");
+    // Caches that are not 16-byte aligned have no TMA descriptor: the
+    // CUDA-core kernel takes them.
+    if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS) mma = false;
+  }
+  if (mma) {
     smem = tg::decode_mma_smem(n_kv_head, n_seqs);
     grid = sms;
   } else {
@@ -194,8 +202,10 @@ extern "C" TG_API int tg_attention_noalloc(void* cuda_stream, const float* q, co
     grid = sms * per_sm;
   }
   if (smem > 227 * 1024)
-    return err(TG_ERR_INVALID_ARG, "tg_attention_noalloc: %d sequences exceed shared memory",
-               n_seqs);
+    return err(TG_ERR_INVALID_ARG,
+               "tg_attention_noalloc: %d sequences of shape %d/%d/%d need %zu KB of shared "
+               "memory (at most 227)",
+               n_seqs, n_head, n_kv_head, head_dim, (smem + 1023) / 1024);
   if (grid > max_grid) grid = max_grid;
 
   e = cudaMemsetAsync(dev_err, 0, sizeof(int), st);
