@@ -81,19 +81,19 @@ WORKLOADS = {
 }
 
 
-# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
-# capture on a B200 at N = 1 (the committed summary named beside each).  For a
-# KV shard of 1/N of the context the launch streams 1/N of the rows, so the
-# figure is scaled by the shard's share of the rows.
+# DRAM bytes (read, write) per launch of the dominant kernel, from one ncu
+# capture of that kernel on a B200 at N = 1 (dram__bytes_read.sum and
+# dram__bytes_write.sum).  For a KV shard of 1/N of the context the launch
+# streams 1/N of the rows, so the figure is scaled by the shard's share.
 NCU_TRAFFIC = {
-    "longctx": (268508928 + 3666176, "profiles/decode_fused_longctx.md"),
-    "prefill": (75751936 + 67844352, "profiles/prefill_attn_config5.md"),
+    "longctx": (268508928, 3666176),
+    "prefill": (75751936, 67844352),
 }
 
 
 def ncu_traffic(workload, share=1.0):
     t = NCU_TRAFFIC.get(workload)
-    return None if t is None else t[0] * share
+    return None if t is None else (t[0] + t[1]) * share
 
 
 def load_package():
@@ -602,7 +602,7 @@ def main():
                     help="skip the independent check of layer 0's output")
     ap.add_argument("--ring", type=int, default=0, choices=[0, 128, 192],
                     help="decode K/V ring per CTA in KB (tg_set_decode_tuning; 0 automatic)")
-    ap.add_argument("--preload", type=int, default=1, choices=[0, 1],
+    ap.add_argument("--preload", type=int, default=0, choices=[0, 1],
                     help="tile loads before the grid-dependency wait when safe (1) or never")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layers per step (small profiling cases)")

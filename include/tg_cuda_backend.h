@@ -199,13 +199,14 @@ TG_API int tg_set_projection_split(int split);
 
 /* Tuning of the bf16 decode kernel (no reference counterpart: the
  * reference's attention_op, metal_backend.hpp:413-453, has no knobs).
- * ring_kb: K/V ring per CTA, 128 or 192 KB (0: 192 for short shards of at
- * most 16 tiles of 64 rows per SM when its shared memory fits, else 128).
- * preload: 1 (default) lets the kernel load its first tiles before its
- * grid-dependency wait when the library knows that no kernel still running
- * writes those cache rows; 0 never.  Applies to later launches of every
- * context; results do not depend on either.  Other values give
- * TG_ERR_INVALID_ARG. */
+ * ring_kb: K/V ring per CTA, 128 or 192 KB (0, the default: 128).
+ * preload: 1 lets the kernel load its first tiles before its
+ * grid-dependency wait on short shards (at most 16 tiles of 64 rows per SM)
+ * when the library knows that no kernel still running writes those cache
+ * rows; 0 (the default) never.  Both measured slower on B200 at 4 x 131072
+ * rows on 1 and 8 GPUs and are kept as tuning knobs.  Applies to later
+ * launches of every context; results do not depend on either.  Other
+ * values give TG_ERR_INVALID_ARG. */
 TG_API int tg_set_decode_tuning(int ring_kb, int preload);
 
 /* One layer's projection weights: W_q has n_head*head_dim rows, W_k and
@@ -372,15 +373,14 @@ TG_API int tg_comm_destroy(tg_context* ctx);
 
 /* How the ranks exchange their softmax records in the split-KV calls. */
 #define TG_EXCHANGE_AUTO 0  /* peer memory when every GPU maps every other's, else NCCL */
-#define TG_EXCHANGE_PEER 1  /* NVLink peer stores of epoch-tagged words inside the merge kernel */
+#define TG_EXCHANGE_PEER 1  /* NVLink peer stores of epoch-tagged words in the merge kernel */
 #define TG_EXCHANGE_NCCL 2  /* ncclAllGather of the records, then a merge kernel */
-/* Bound, in milliseconds (default 5000), of the waits inside the split-KV
- * kernels: for another GPU's softmax records in the peer exchange and for
- * the decode CTAs of the same GPU.  A wait that runs out ends the kernel
- * with device error 0x105 (peer record) or 0x106 (decode CTAs), reported as
- * TG_ERR_DEVICE at the next synchronisation; after either, destroy and
- * create the communicator again (the ranks' exchange epochs may differ).
- * No counterpart in the reference (metal_backend.cpp:23-27 only prints). */
+/* Bound, in milliseconds (default 5000), of the merge kernel's wait for the
+ * other GPUs' softmax records in the peer exchange.  A wait that runs out
+ * ends the kernel with device error 0x105, reported as TG_ERR_DEVICE at the
+ * next synchronisation; then destroy and create the communicator again (the
+ * ranks' exchange epochs may differ).  No counterpart in the reference
+ * (metal_backend.cpp:23-27 only prints). */
 TG_API int tg_comm_set_wait_limit_ms(tg_context* ctx, int ms);
 /* Choose the exchange (collective: every rank passes the same value before
  * its next split-KV call).  TG_EXCHANGE_PEER fails with TG_ERR_UNSUPPORTED
@@ -490,7 +490,8 @@ TG_API int tg_launch_count(tg_context* ctx, long long* out);
 #define TG_PROFILE_PROJECTION 2
 /* TG_PROFILE_STAMPS: the CTAs of each bf16 decode step record %globaltimer
  * values (ns) -- decode CTAs: start, grid dependency released, tile loop
- * done, end; merge CTAs: start, decode data available, (unused), end.
+ * done, end; merge CTAs: start, grid dependency released, first record
+ * slice stored to the peers (split-KV), end.
  * Unlike events this keeps the launches' programmatic overlap, so it times
  * the kernels as they run inside a step.  Up to TG_STAMP_LAUNCHES decode
  * steps are recorded after enabling (also into a graph being captured;

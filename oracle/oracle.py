@@ -114,8 +114,8 @@ def ref():
     if _ref is None:
         if not os.path.exists(REF_SO):
             raise FileNotFoundError(
-                f"{REF_SO} is missing: build it with `make -C oracle ref` "
-                "where the reference tree is mounted")
+                f"{REF_SO} is missing: build it with `make -C oracle ref "
+                "REF_DIR=<checkout of the reference>`")
         R = C.CDLL(REF_SO)
         R.tgref_max_ctx.restype = C.c_int
         R.tgref_apply_rope.argtypes = [_f32p, _f32p, C.c_int]

@@ -126,7 +126,7 @@ def main() -> int:
         del kc, vc
     for ex in (tg.EXCHANGE_AUTO, tg.EXCHANGE_NCCL):
         be.set_exchange(ex)
-        for ring, pre in ((0, 1), (128, 1), (192, 0)):
+        for ring, pre in ((0, 0), (128, 1), (192, 1)):
             tg.set_decode_tuning(ring, pre)
             for it in range(3):
                 Qi, Ki = Q.copy(), K.copy()
@@ -142,7 +142,7 @@ def main() -> int:
         if rank == 0:
             print(f"config 4 x{world}: exchange requested {ex} used {be.exchange}, "
                   f"max err {max(float(np.abs(out[i] - ref4[i][1]).max()) for i in range(B4)):.2e}")
-    tg.set_decode_tuning(0, 1)
+    tg.set_decode_tuning(0, 0)
     kv.destroy()
     # The layer from the normed hidden state x (projection + split-KV
     # attention) against the same layer on this GPU over the whole cache:

@@ -231,7 +231,7 @@ def set_projection_split(split: int) -> None:
     _check(lib().tg_set_projection_split(int(split)))
 
 
-def set_decode_tuning(ring_kb: int = 0, preload: int = 1) -> None:
+def set_decode_tuning(ring_kb: int = 0, preload: int = 0) -> None:
     """Tuning of the bf16 decode kernel (tg_set_decode_tuning): K/V ring per
     CTA (0 automatic, 128 or 192 KB) and whether tiles may be loaded before
     the grid-dependency wait when that is safe."""

@@ -124,7 +124,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 // (0 = automatic) and whether tiles may be loaded before the
 // grid-dependency wait when that is safe (1) or never (0).
 std::atomic<int> g_decode_ring{0};
-std::atomic<int> g_decode_preload{1};
+std::atomic<int> g_decode_preload{0};
 
 }  // namespace
 
@@ -206,7 +206,7 @@ struct tg_context {
   int exchange_used = TG_EXCHANGE_AUTO;  // last split-KV call
   int p2p_bcap = 0, p2p_rf = 0, p2p_heads = 0;
   unsigned long long* xchg_local = nullptr;  // peer-exchange receive words
-  unsigned* xchg_ctl = nullptr;              // exchange control words (FusedParams::xctl)
+  unsigned* xchg_ctl = nullptr;              // exchange epoch word (this GPU only)
   unsigned long long* xchg_peer[tg::kMaxPeers] = {};
   unsigned char* nccl_stage = nullptr;  // small device staging for handle exchange
 
@@ -308,8 +308,6 @@ int check_device_error(tg_context* ctx) {
                        : h == tg::kDevErrWaitFull     ? "bounded wait for a K/V tile expired"
                        : h == tg::kDevErrWaitEmpty    ? "bounded wait for a free stage expired"
                        : h == tg::kDevErrPeerTimeout  ? "another GPU's softmax record did not arrive"
-                       : h == tg::kDevErrDecodeTimeout
-                           ? "the merge kernel's wait for the decode CTAs expired"
                            : "device error";
     return fail(TG_ERR_DEVICE, "kernel reported 0x%x: %s", h, what);
   }
@@ -1129,15 +1127,14 @@ bool short_shard(const tg_context* ctx, const tg_kv_cache* kv, int B) {
   return (long long)B * ((kv->d.max_ctx + 63) / 64) <= 16LL * ctx->num_sms;
 }
 
-// K/V ring per CTA of the bf16 decode: the deep ring for short shards when
-// its shared memory fits, otherwise 128 KB (measured faster on long shards:
-// 4 x 131072 rows on one GPU, 46.2 vs 47.4 us per layer).  Fixed by
-// tg_set_decode_tuning.
+// K/V ring per CTA of the bf16 decode: 128 KB unless tg_set_decode_tuning
+// asks for the deep one (192 KB, when its shared memory fits).  Measured on
+// B200s at 4 x 131072 rows: on one GPU 46.2 us per layer with 128 KB against
+// 47.4 with 192; split over 8 GPUs 192 KB was 1-4 % slower too.
 int fused_ring(const tg_context* ctx, const tg_kv_cache* kv, int B) {
-  const int nkv = kv->d.n_kv_head;
-  if (g_decode_ring != 0) return g_decode_ring;
-  if (short_shard(ctx, kv, B) &&
-      tg::decode_fused_smem(nkv, tg::kFusedRingDeep, B) <= 227 * 1024)
+  (void)ctx;
+  if (g_decode_ring == tg::kFusedRingDeep &&
+      tg::decode_fused_smem(kv->d.n_kv_head, tg::kFusedRingDeep, B) <= 227 * 1024)
     return tg::kFusedRingDeep;
   return tg::kFusedRing;
 }
@@ -1216,10 +1213,11 @@ int run_fused(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const fl
   // to prefetch its first tiles into L2 before its wait returns (measured:
   // -0.8 us per layer at 4 x 16384..131072 rows, +4 us at 256 x 4096).
   p.prefetch = mgroups == tg::kMergeGroupsWide ? 1 : 0;
-  // Tile loads before the wait pay off on short shards, where they cover a
-  // good part of a CTA's tiles; on long ones they only compete with the
-  // previous layer's merge for memory (measured +1.2 us per layer at
-  // 4 x 131072 rows on one GPU).
+  // Tile loads before the wait, when tg_set_decode_tuning allows them, on
+  // short shards only: on long ones they only compete with the previous
+  // layer's merge for memory (+1.2 us per layer at 4 x 131072 rows on one
+  // GPU).  Off by default: measured 1-2 us per layer slower on the split
+  // 8-GPU shards too.
   p.preload = (preload && short_shard(ctx, kv, B)) ? 1 : 0;
   p.wait_ns = ctx->wait_ns;
   if (mode == 2) {
@@ -1228,7 +1226,7 @@ int run_fused(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const fl
     p.b_cap = ctx->p2p_bcap;
     p.xchg_local = ctx->xchg_local;
     for (int r = 0; r < ctx->world; ++r) p.xchg_peer[r] = ctx->xchg_peer[r];
-    p.xctl = ctx->xchg_ctl;
+    p.epoch = ctx->xchg_ctl;
   }
   if ((ctx->prof_on & TG_PROFILE_STAMPS) && ctx->stamps && ctx->stamp_used < ctx->stamp_cap) {
     p.stamps = ctx->stamps +

@@ -15,7 +15,9 @@
 //    no ordering between a writer kernel and the TMA loads is needed;
 //  * a sequence that lies within one CTA is finished there (output, or its
 //    record for the exchange); the pieces of a split sequence go to the
-//    CTA's two partial-record slots.
+//    CTA's two partial-record slots;
+//  * before its grid-dependency wait: the schedule, the TMA descriptors, an
+//    optional L2 prefetch and (tuning, off by default) the first ring stages.
 // Merge kernel: one item per (sequence, head), spread over many SMs so the
 // tail of the step is short; in mode 2 (split-KV across GPUs) it stores its
 // record slice into every GPU's receive words over NVLink, each 4-byte value
@@ -25,7 +27,8 @@
 // be at most one launch ahead of the others.
 //
 // Every wait is bounded (mbarriers, peer words); on expiry the error word is
-// set and the kernel still reaches its end.
+// set and the kernel still reaches its end.  With stamps on, every CTA of
+// both kernels records %globaltimer values (FusedParams::stamps).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -73,12 +76,6 @@ __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
-}
-
-__device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
 }
 
 __device__ __forceinline__ void cons_sync(int n) {
@@ -174,11 +171,7 @@ __global__ void __launch_bounds__(FusedCfg<NKV, RING_KB>::THREADS, 1)
   const int rf = record_floats(p.n_head, 64);
   unsigned long long* stamp = p.stamps ? p.stamps + (size_t)blockIdx.x * kStampsPerCta : nullptr;
 
-  // Modes 0 / 1: the merge kernel may launch at once (it waits for this
-  // grid's completion).  Mode 2: only once every CTA of this grid has passed
-  // its grid-dependency wait (below), so that the merge kernel starts after
-  // the previous exchange launch has finished and reads its epoch.
-  if (p.mode != 2) griddep_launch_dependents();
+  griddep_launch_dependents();
   if (stamp && threadIdx.x == 0) stamp[0] = global_ns();
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -262,12 +255,13 @@ __global__ void __launch_bounds__(FusedCfg<NKV, RING_KB>::THREADS, 1)
   // The previous launch's merge kernel has finished: it read the schedule
   // buffer and, in mode 2, the decode-done count of the other parity, which
   // block 0 clears here for the next launch.
-  const unsigned xpar = p.mode == 2 ? ((*reinterpret_cast<volatile unsigned*>(p.xctl + kXcEpoch) + 1u) & 1u) : 0u;
+  // The previous launch's merge kernel has finished: it read the schedule
+  // buffer and, in mode 2, the exchange epoch, which advances here once per
+  // launch (the merge kernel of this launch reads it after its own wait).
   if (blockIdx.x == 0) {
     for (int i = threadIdx.x; i <= p.B; i += blockDim.x) p.sched[i] = prefix[i];
-    if (p.mode == 2 && threadIdx.x == 0) p.xctl[kXcDecDone + (xpar ^ 1u)] = 0u;
+    if (p.mode == 2 && threadIdx.x == 0) *p.epoch += 1u;
   }
-  if (p.mode == 2) griddep_launch_dependents();
   __syncthreads();
 
   if (producer) {
@@ -525,15 +519,6 @@ __global__ void __launch_bounds__(FusedCfg<NKV, RING_KB>::THREADS, 1)
     }
   }
   if (stamp && threadIdx.x == 0) stamp[2] = global_ns();
-  if (p.mode == 2) {
-    // Everything this CTA wrote (records, partial records, rotated q / k, the
-    // new cache row, the schedule) is published to the merge kernel through
-    // the decode-done count, which it waits for instead of this grid's
-    // completion: every thread fences its own stores, then one arrival.
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) atomicAdd(p.xctl + kXcDecDone + xpar, 1u);
-  }
   if (stamp && threadIdx.x == 0) stamp[3] = global_ns();
 }
 
@@ -543,11 +528,10 @@ __global__ void __launch_bounds__(FusedCfg<NKV, RING_KB>::THREADS, 1)
 constexpr int kMaxMergeGroups = 4;
 constexpr int kPartBatch = 16;  // parts per group per load round
 
-// One item per (sequence s, head h) and 64 * GROUPS threads; parts are
-// merged in rounds of up to GROUPS * kPartBatch: every part's m and l go to
-// shared memory (one load each), thread d of group grp loads dimension d of
-// o for parts grp, grp + GROUPS, ...  -- all in one round -- and every thread
-// applies the same running maximum, so the groups' sums just add up.
+// One item per (sequence s, head h) and 64 * GROUPS threads: thread d of
+// group grp handles dimension d of parts grp, grp + GROUPS, ...  Every part's
+// m, l and o are loaded in the same round (kPartBatch per group) and merged
+// online, then the groups are combined through shared memory.
 //   1. this GPU's record slice of (s, h): the merge of the partial records of
 //      a split sequence, the complete record the decode kernel wrote, or a
 //      neutral record when this shard holds no row of s;
@@ -561,21 +545,12 @@ constexpr int kPartBatch = 16;  // parts per group per load round
 // increasing order on every GPU, and the grid is small enough to be
 // resident, so a CTA waiting for another GPU's item i only ever waits for a
 // CTA that processes i next.
-// At most 64 registers per thread, so that a merge CTA fits on an SM beside a
-// decode CTA (168 registers x 288 threads): the next layer's decode CTAs then
-// land on every SM as soon as this layer's decode CTAs exit and load their
-// first tiles while this kernel runs.  (The per-thread m / l / o version
-// needed 123 registers; capped at 64 it spilled and took two load rounds.)
 template <int GROUPS>
-__global__ void __launch_bounds__(64 * GROUPS, 16 / GROUPS) merge_exchange_kernel(const FusedParams p) {
-  constexpr int NT = 64 * GROUPS, MAXP = GROUPS * kPartBatch;
-  __shared__ float m_s[MAXP], l_s[MAXP];  // this round's parts; m_s then holds weights
-  __shared__ float mb_s, lsum_s;
+__global__ void __launch_bounds__(64 * GROUPS) merge_exchange_kernel(const FusedParams p) {
   __shared__ float o_grp[GROUPS][64];
-  __shared__ float xm[kMaxPeers], xl[kMaxPeers];
+  __shared__ float ml_grp[GROUPS][2];
   __shared__ int pre[64 * GROUPS + 1];
   __shared__ int wsum[2 * GROUPS];
-  __shared__ int x_bad;
   const int tid = threadIdx.x, d = tid & 63, grp = tid >> 6;
   griddep_launch_dependents();
   unsigned long long* stamp = (p.stamps && (int)blockIdx.x < 2 * p.grid)
@@ -586,6 +561,13 @@ __global__ void __launch_bounds__(64 * GROUPS, 16 / GROUPS) merge_exchange_kerne
   // positions before the wait (as the decode kernel does); otherwise the
   // decode kernel's copy is read after it.
   const bool local_sched = p.B <= 64 * GROUPS;
+  // The RoPE row of this CTA's first item (the table is written only when
+  // it is created).
+  const int s_first = blockIdx.x / p.n_head;
+  const int pos_first = s_first < p.B ? p.pos[s_first] : -1;
+  float2 cs_first = make_float2(0.f, 0.f);
+  if (p.rope && pos_first >= 0 && pos_first < p.table_len)
+    cs_first = reinterpret_cast<const float2*>(p.cs + (size_t)pos_first * 64)[d >> 1];
   if (local_sched) {
     const int lane = tid & 31, w = tid >> 5;
     const int tiles = tid < p.B ? max(seq_tiles(p, p.pos[tid]), 0) : 0;
@@ -603,49 +585,23 @@ __global__ void __launch_bounds__(64 * GROUPS, 16 / GROUPS) merge_exchange_kerne
     if (tid == 0) pre[0] = 0;
     __syncthreads();
   }
-  uint32_t epoch = 0u;
-  if (p.mode == 2) {
-    // This kernel starts only once every CTA of its decode launch has passed
-    // its grid-dependency wait, i.e. after the previous exchange launch has
-    // finished: the epoch word holds that launch's tag.  Instead of waiting
-    // for the decode grid's completion, wait (bounded) until all its CTAs
-    // have counted themselves done; their stores are fenced before that.
-    epoch = *reinterpret_cast<volatile unsigned*>(p.xctl + kXcEpoch) + 1u;
-    if (tid == 0) {
-      const unsigned* done = p.xctl + kXcDecDone + (epoch & 1u);
-      const unsigned long long t_end = global_ns() + (unsigned long long)p.wait_ns;
-      bool ok = false;
-      for (long long n = 0; n < kPollCap; ++n) {
-        if ((int)ld_acquire_gpu_u32(done) >= p.grid) {
-          ok = true;
-          break;
-        }
-        if (global_ns() > t_end) break;
-        __nanosleep(64);
-      }
-      if (!ok) record_error(p.err, kDevErrDecodeTimeout);
-    }
-    __syncthreads();
-  } else {
-    griddep_wait();
-  }
+  griddep_wait();
   if (stamp && tid == 0) stamp[1] = global_ns();
-  // Data of the decode launch is read past L1 (in mode 2 this kernel may
-  // have started before it was written).
-  auto sch = [&](int i) { return local_sched ? pre[i] : __ldcg(p.sched + i); };
+  const int* sched = local_sched ? pre : p.sched;
   const int H = p.n_head, qdim = H * 64, rf = record_floats(H, 64);
-  const int T = sch(p.B);
+  const uint32_t epoch = (p.mode == 2) ? *reinterpret_cast<volatile unsigned*>(p.epoch) : 0u;
+  const int T = sched[p.B];
   const int G = min(p.grid, T);
   const int items = p.B * H;
-  if (tid == 0) x_bad = 0;  // first read after several barriers below
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
     const int s = it / H, h = it - s * H;
-    const int t0 = sch(s), t1 = sch(s + 1);
+    const int t0 = sched[s], t1 = sched[s + 1];
     const int c1 = t1 > t0 ? cta_of_tile(t0, G, T) : 0;
     const int c2 = t1 > t0 ? cta_of_tile(t1 - 1, G, T) : 0;
     const bool split = t1 > t0 && c1 != c2;
     if (p.mode == 0 && !split) continue;  // finished by the decode kernel
-    const int pos_s = p.pos[s];
+    const bool first = it == (int)blockIdx.x;
+    const int pos_s = first ? pos_first : p.pos[s];
     const bool rope = p.rope && (split || t1 == t0) && grp == 0 && pos_s >= 0 &&
                       pos_s < p.table_len;
     const bool has_k = rope && p.k_io && h < p.n_kv;
@@ -654,82 +610,87 @@ __global__ void __launch_bounds__(64 * GROUPS, 16 / GROUPS) merge_exchange_kerne
     if (rope) {
       const float* qi = p.q_in + (size_t)s * qdim + h * 64;
       xq = make_float2(qi[d & ~1], qi[d | 1]);
-      cs = reinterpret_cast<const float2*>(p.cs + (size_t)pos_s * 64)[d >> 1];
+      cs = first ? cs_first : reinterpret_cast<const float2*>(p.cs + (size_t)pos_s * 64)[d >> 1];
       if (has_k) {
         const float* kk = p.k_io + (size_t)s * p.n_kv * 64 + h * 64;
         xk = make_float2(kk[d & ~1], kk[d | 1]);
       }
     }
-    // Parts of (s, h) on this GPU: the partial records of a split sequence,
-    // the record of a sequence finished in one CTA (modes 1 and 2), none for
-    // a sequence without rows on this shard.
-    const int n_parts = split ? 1 + (c2 - c1) : (t1 > t0 ? 1 : 0);
-    const int first_slot = split ? 2 * c1 + (cta_tile_lo(c1, G, T) == t0 ? 0 : 1) : 0;
-    float o = 0.f, M = kNegBig, L = 0.f;  // running merge, same M in every thread
-    for (int k0 = 0; k0 < n_parts; k0 += MAXP) {
-      const int cnt = min(MAXP, n_parts - k0);
-      auto rec = [&](int k) {
-        return split ? p.part + (size_t)(k == 0 ? first_slot : 2 * (c1 + k)) * rf
-                     : p.records + (size_t)s * rf;
-      };
-      float ml = 0.f;
-      if (tid < 2 * cnt) ml = __ldcg(rec(k0 + (tid >> 1)) + qdim + (tid & 1) * H + h);
-      float ov[kPartBatch];
+    float o = 0.f, m = kNegBig, l = 0.f;  // this GPU's record slice (group 0)
+    if (split) {
+      const int first_slot = 2 * c1 + (cta_tile_lo(c1, G, T) == t0 ? 0 : 1);
+      const int n_parts = 1 + (c2 - c1);
+      float mg = kNegBig, lg = 0.f, og = 0.f;
+      for (int k0 = grp; k0 < n_parts; k0 += GROUPS * kPartBatch) {
+        float mv[kPartBatch], lv[kPartBatch], ov[kPartBatch];
 #pragma unroll
-      for (int u = 0; u < kPartBatch; ++u) {
-        const int k = grp + u * GROUPS;
-        ov[u] = k < cnt ? __ldcg(rec(k0 + k) + h * 64 + d) : 0.f;
-      }
-      if (tid < 2 * cnt) ((tid & 1) ? l_s : m_s)[tid >> 1] = ml;
-      __syncthreads();
-      // Warp 0: the round's maximum, each part's weight (in place of its m)
-      // and the weighted sum of l, once for the whole CTA.
-      if (tid < 32) {
-        float mx = M;
-        for (int k = tid; k < cnt; k += 32) mx = fmaxf(mx, m_s[k]);
-        mx = warp_max(mx);
-        float ls = 0.f;
-        for (int k = tid; k < cnt; k += 32) {
-          const float w = ex2(m_s[k] - mx);
-          m_s[k] = w;
-          ls = fmaf(l_s[k], w, ls);
+        for (int u = 0; u < kPartBatch; ++u) {
+          const int kk = k0 + u * GROUPS;
+          mv[u] = kNegBig;
+          lv[u] = 0.f;
+          ov[u] = 0.f;
+          if (kk < n_parts) {
+            const float* r = p.part + (size_t)(kk == 0 ? first_slot : 2 * (c1 + kk)) * rf;
+            mv[u] = r[qdim + h];
+            lv[u] = r[qdim + H + h];
+            ov[u] = r[h * 64 + d];
+          }
         }
-        ls = warp_sum(ls);
-        if (tid == 0) {
-          mb_s = mx;
-          lsum_s = ls;
+        float Mb = mg;
+#pragma unroll
+        for (int u = 0; u < kPartBatch; ++u) Mb = fmaxf(Mb, mv[u]);
+        const float a = ex2(mg - Mb);
+        og *= a;
+        lg *= a;
+#pragma unroll
+        for (int u = 0; u < kPartBatch; ++u) {
+          const float w = ex2(mv[u] - Mb);
+          og = fmaf(ov[u], w, og);
+          lg = fmaf(lv[u], w, lg);
         }
+        mg = Mb;
       }
-      __syncthreads();
-      const float Mb = mb_s;
-      const float a = ex2(M - Mb);
-      o *= a;
+      if (GROUPS > 1) {
+        o_grp[grp][d] = og;
+        if (d == 0) {
+          ml_grp[grp][0] = mg;
+          ml_grp[grp][1] = lg;
+        }
+        __syncthreads();
+        if (grp == 0) {
+          float M = kNegBig;
 #pragma unroll
-      for (int u = 0; u < kPartBatch; ++u) {
-        const int k = grp + u * GROUPS;
-        if (k < cnt) o = fmaf(ov[u], m_s[k], o);
-      }
-      L = fmaf(L, a, lsum_s);
-      M = Mb;
-      __syncthreads();
-    }
-    if (GROUPS > 1) {
-      o_grp[grp][d] = o;
-      __syncthreads();
-      if (grp == 0) {
+          for (int g2 = 0; g2 < GROUPS; ++g2) M = fmaxf(M, ml_grp[g2][0]);
+          o = 0.f;
+          l = 0.f;
 #pragma unroll
-        for (int g2 = 1; g2 < GROUPS; ++g2) o += o_grp[g2][d];
+          for (int g2 = 0; g2 < GROUPS; ++g2) {
+            const float w = ex2(ml_grp[g2][0] - M);
+            o = fmaf(o_grp[g2][d], w, o);
+            l = fmaf(ml_grp[g2][1], w, l);
+          }
+          m = M;
+        }
+      } else {
+        o = og;
+        m = mg;
+        l = lg;
       }
+    } else if (t1 > t0 && p.mode != 0 && grp == 0) {
+      const float* rec = p.records + (size_t)s * rf;
+      o = rec[h * 64 + d];
+      m = rec[qdim + h];
+      l = rec[qdim + H + h];
     }
     if (p.mode == 0) {
-      if (grp == 0) p.out[(size_t)s * qdim + h * 64 + d] = o / L;
+      if (grp == 0) p.out[(size_t)s * qdim + h * 64 + d] = o / l;
     } else if (p.mode == 1) {
-      if (grp == 0 && (split || t1 == t0)) {
-        float* r = p.records + (size_t)s * rf;
-        r[h * 64 + d] = o;
+      if ((split || t1 == t0) && grp == 0) {
+        float* rec = p.records + (size_t)s * rf;
+        rec[h * 64 + d] = o;
         if (d == 0) {
-          r[qdim + h] = M;
-          r[qdim + H + h] = L;
+          rec[qdim + h] = m;
+          rec[qdim + H + h] = l;
         }
       }
     } else {
@@ -741,64 +702,65 @@ __global__ void __launch_bounds__(64 * GROUPS, 16 / GROUPS) merge_exchange_kerne
       const unsigned long long tag = (unsigned long long)epoch << 32;  // epoch >= 1
       const size_t item_words = (size_t)kXchgWords;
       const size_t mine = (((size_t)(par * p.world + p.rank) * p.b_cap + s) * H + h) * item_words;
-      const unsigned long long* base =
-          p.xchg_local + (((size_t)(par * p.world) * p.b_cap + s) * H + h) * item_words;
-      const size_t stride = (size_t)p.b_cap * H * item_words;
-      float orv[kMaxPeers];
       if (grp == 0) {
         const unsigned long long wo = tag | __float_as_uint(o);
+        const unsigned long long wm = tag | __float_as_uint(m);
+        const unsigned long long wl = tag | __float_as_uint(l);
         for (int r = 0; r < p.world; ++r) {
           unsigned long long* dst = (r == p.rank ? p.xchg_local : p.xchg_peer[r]) + mine;
           st_relaxed_sys_u64(dst + d, wo);
-          if (d < 2) st_relaxed_sys_u64(dst + 64 + d, tag | __float_as_uint(d ? L : M));
+          if (d == 0) {
+            st_relaxed_sys_u64(dst + 64, wm);
+            st_relaxed_sys_u64(dst + 65, wl);
+          }
         }
-        // Gather: this thread's dimension of every GPU's slice, and (threads
-        // 0 .. 2*world-1) one GPU's m or l into shared memory.
+        if (stamp && tid == 0 && it == (int)blockIdx.x) stamp[2] = global_ns();
+        // Gather: this thread's dimension and every GPU's m and l.
+        const unsigned long long* base =
+            p.xchg_local + (((size_t)(par * p.world) * p.b_cap + s) * H + h) * item_words;
+        const size_t stride = (size_t)p.b_cap * H * item_words;
+        float mv[kMaxPeers], lv[kMaxPeers], ov[kMaxPeers];
         unsigned pending = (1u << p.world) - 1u;
-        bool ml_pending = d < 2 * p.world;
         const unsigned long long t_end = global_ns() + (unsigned long long)p.wait_ns;
-        for (long long n = 0; (pending || ml_pending) && n < kPollCap; ++n) {
+        for (long long n = 0; pending && n < kPollCap; ++n) {
 #pragma unroll
           for (int r = 0; r < kMaxPeers; ++r) {
             if (!(pending >> r & 1u)) continue;
-            const unsigned long long x = ld_relaxed_sys_u64(base + r * stride + d);
-            if ((x >> 32) == (tag >> 32)) {
-              orv[r] = __uint_as_float((unsigned)x);
+            const unsigned long long* rr = base + r * stride;
+            const unsigned long long x = ld_relaxed_sys_u64(rr + d);
+            const unsigned long long y = ld_relaxed_sys_u64(rr + 64);
+            const unsigned long long z = ld_relaxed_sys_u64(rr + 65);
+            if ((x >> 32) == (tag >> 32) && (y >> 32) == (tag >> 32) && (z >> 32) == (tag >> 32)) {
+              ov[r] = __uint_as_float((unsigned)x);
+              mv[r] = __uint_as_float((unsigned)y);
+              lv[r] = __uint_as_float((unsigned)z);
               pending &= ~(1u << r);
             }
           }
-          if (ml_pending) {
-            const unsigned long long y = ld_relaxed_sys_u64(base + (d >> 1) * stride + 64 + (d & 1));
-            if ((y >> 32) == (tag >> 32)) {
-              ((d & 1) ? xl : xm)[d >> 1] = __uint_as_float((unsigned)y);
-              ml_pending = false;
+          if (pending && global_ns() > t_end) break;
+        }
+        if (pending) {
+          record_error(p.err, kDevErrPeerTimeout);
+        } else {
+          float M = kNegBig;
+#pragma unroll
+          for (int r = 0; r < kMaxPeers; ++r)
+            if (r < p.world) M = fmaxf(M, mv[r]);
+          float O = 0.f, L = 0.f;
+#pragma unroll
+          for (int r = 0; r < kMaxPeers; ++r) {
+            if (r < p.world) {
+              const float w = ex2(mv[r] - M);
+              O = fmaf(ov[r], w, O);
+              L = fmaf(lv[r], w, L);
             }
           }
-          if ((pending || ml_pending) && global_ns() > t_end) break;
+          p.out[(size_t)s * qdim + h * 64 + d] = O / L;
         }
-        if (pending || ml_pending) {
-          record_error(p.err, kDevErrPeerTimeout);
-          x_bad = 1;
-        }
-      }
-      __syncthreads();
-      if (grp == 0 && !x_bad) {
-        float Mx = kNegBig;
-        for (int r = 0; r < p.world; ++r) Mx = fmaxf(Mx, xm[r]);
-        float O = 0.f, Lx = 0.f;
-#pragma unroll
-        for (int r = 0; r < kMaxPeers; ++r) {
-          if (r < p.world) {
-            const float w = ex2(xm[r] - Mx);
-            O = fmaf(orv[r], w, O);
-            Lx = fmaf(xl[r], w, Lx);
-          }
-        }
-        p.out[(size_t)s * qdim + h * 64 + d] = O / Lx;
       }
     }
     if (rope) {
-      // All readers of the raw q / k of s have finished (the decode kernel);
+      // All readers of the raw q / k of s have finished (previous kernel);
       // each thread writes only the element of the pair it owns.
       const float2 rq = rot(xq, cs);
       p.q_out[(size_t)s * qdim + h * 64 + d] = (d & 1) ? rq.y : rq.x;
@@ -807,20 +769,7 @@ __global__ void __launch_bounds__(64 * GROUPS, 16 / GROUPS) merge_exchange_kerne
         p.k_out[(size_t)s * p.n_kv * 64 + h * 64 + d] = (d & 1) ? rk.y : rk.x;
       }
     }
-    __syncthreads();
-    if (tid == 0) x_bad = 0;  // read above, before the barrier
-  }
-  if (p.mode == 2) {
-    // The last CTA to finish publishes this launch's tag (every CTA read the
-    // previous one above).
-    __syncthreads();
-    if (tid == 0) {
-      __threadfence();
-      if (atomicAdd(p.xctl + kXcMergeDone, 1u) == gridDim.x - 1) {
-        p.xctl[kXcMergeDone] = 0u;
-        p.xctl[kXcEpoch] = epoch;
-      }
-    }
+    if (GROUPS > 1) __syncthreads();
   }
   if (stamp && tid == 0) stamp[3] = global_ns();
 }
@@ -855,6 +804,10 @@ static cudaError_t launch_fused_cfg(const CUtensorMap& tk, const CUtensorMap& tv
   if (smem > configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(decode_fused_kernel<NKV, RING_KB>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(decode_fused_kernel<NKV, RING_KB>,
+                               cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
     configured[dev] = smem;
   }
@@ -872,14 +825,6 @@ size_t decode_fused_smem(int nkv, int ring_kb, int B) {
   }
 }
 
-cudaError_t launch_merge_exchange(const FusedParams& p, int grid, int groups, cudaStream_t st) {
-  if (p.B <= 0) return cudaSuccess;
-  if (groups == kMaxMergeGroups)
-    return launch_pdl_f(merge_exchange_kernel<kMaxMergeGroups>, dim3(grid),
-                        dim3(64 * kMaxMergeGroups), 0, st, p);
-  if (groups == 1) return launch_pdl_f(merge_exchange_kernel<1>, dim3(grid), dim3(64), 0, st, p);
-  return cudaErrorInvalidValue;
-}
 
 cudaError_t launch_decode_fused(const CUtensorMap& tk, const CUtensorMap& tv,
                                 const FusedParams& p, int ring_kb, int grid, cudaStream_t st) {
@@ -894,6 +839,15 @@ cudaError_t launch_decode_fused(const CUtensorMap& tk, const CUtensorMap& tv,
                         : launch_fused_cfg<4, kFusedRing>(tk, tv, p, grid, st);
     default: return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t launch_merge_exchange(const FusedParams& p, int grid, int groups, cudaStream_t st) {
+  if (p.B <= 0) return cudaSuccess;
+  if (groups == kMaxMergeGroups)
+    return launch_pdl_f(merge_exchange_kernel<kMaxMergeGroups>, dim3(grid),
+                        dim3(64 * kMaxMergeGroups), 0, st, p);
+  if (groups == 1) return launch_pdl_f(merge_exchange_kernel<1>, dim3(grid), dim3(64), 0, st, p);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace tg

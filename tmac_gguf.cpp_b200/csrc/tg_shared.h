@@ -32,12 +32,12 @@ enum DeviceError : int {
   kDevErrBadPos = 0x103,     // position outside the RoPE table / cache
   kDevErrTooManySeqs = 0x104,
   kDevErrPeerTimeout = 0x105,  // a peer GPU's softmax record did not arrive in time
-  kDevErrDecodeTimeout = 0x106,  // the merge kernel's wait for the decode CTAs expired
 };
 
 // Per-CTA %globaltimer stamps (ns) of a profiled decode step: decode CTAs
 // {start, grid dependency released, tile loop done, end}, merge CTAs
-// {start, decode parts available, -, end}.  One record per decode launch:
+// {start, grid dependency released, first record slice stored to the peers
+// (mode 2), end}.  One record per decode launch:
 // kStampRowsPerSm * num_sms rows of kStampsPerCta (decode CTAs first, the
 // merge grid's CTAs from row num_sms on; rows of absent CTAs stay 0).
 constexpr int kStampsPerCta = 4;
@@ -196,7 +196,7 @@ struct FusedParams {
   // the new rows at pos[] when new_row == 0 (the tile holding such a row is
   // loaded after the wait).
   int preload;
-  long long wait_ns;       // bound of the in-kernel waits (peer words, decode-done count)
+  long long wait_ns;       // bound of the in-kernel waits for peer records
   unsigned long long* stamps;  // this launch's stamp record, or null
   // mode 2
   int world, rank, b_cap;  // receive buffers hold b_cap sequences
@@ -204,14 +204,8 @@ struct FusedParams {
   // mapped from every peer: each word = (epoch tag << 32) | float bits.
   unsigned long long* xchg_local;
   unsigned long long* xchg_peer[kMaxPeers];
-  // Exchange control words on this GPU (mode 2): ctl[kXcEpoch] = tag of the
-  // last finished exchange launch (written by its last merge CTA);
-  // ctl[kXcDecDone + parity] = decode CTAs of the current launch that have
-  // written everything (the merge kernel waits for all of them instead of
-  // for the decode grid's completion); ctl[kXcMergeDone] = merge CTAs done.
-  unsigned* xctl;
+  unsigned* epoch;         // exchange launches on this GPU (advanced by the decode kernel)
 };
-constexpr int kXcEpoch = 0, kXcDecDone = 1, kXcMergeDone = 3;
 
 
 // Q/K/V projection of one layer (tg_qkv.cu): y_m = W_m x (+ bias) for the
