@@ -28,6 +28,7 @@ For N > 1 launch with torch.distributed.run (one rank per GPU).
 from __future__ import annotations
 
 import argparse
+import ctypes as C
 import csv
 import datetime
 import importlib.util
@@ -844,15 +845,58 @@ def main():
         step(qh, kh, vh, ph, oh)
         be.metal_batch_end()
 
+    # Through the C ABI (include/tg_cuda_backend.h, the boundary the
+    # reference's C++ forward loop calls), arguments converted once per
+    # buffer: every step's host->device inputs and device->host outputs
+    # inside tg_batch_begin / tg_batch_end.  The same loop through the
+    # Python wrapper is reported beside it.
+    hb, kvb = be.handle, kv.handle
+    if qkv:
+        fn = tg.lib().tg_attention_block_splitkv if split else tg.lib().tg_attention_block
+        args_l = [(hb, kvb, l, B, C.byref(weights[l].desc), tg.WTYPE_Q5_0, w_out[l].data_ptr(),
+                   qh[l].data_ptr(), ph.data_ptr(), oh[l].data_ptr()) for l in range(L)]
+    else:
+        fn = tg.lib().tg_decode_layer_splitkv if split else tg.lib().tg_decode_layer
+        args_l = [(hb, kvb, l, B, qh[l].data_ptr(), kh[l].data_ptr(), vh[l].data_ptr(),
+                   ph.data_ptr(), oh[l].data_ptr()) for l in range(L)]
+
+    def c_step(timed=False):
+        t_call = 0
+        be.metal_batch_begin()
+        for a in args_l:
+            t0c = time.perf_counter_ns()
+            rc = fn(*a)
+            t_call += time.perf_counter_ns() - t0c
+            if rc != 0:
+                raise tg.TGError(rc, tg.lib().tg_last_error().decode())
+        be.metal_batch_end()
+        return t_call
+
     for _ in range(args.warmup):
-        e2e_step()
+        c_step()
     barrier()
     e2e_steps = max(3, args.steps // 2)
+    c_ns = 0
     t = time.perf_counter()
     for _ in range(e2e_steps):
-        e2e_step()
+        c_ns += c_step()
     e2e_s = max_over_ranks(time.perf_counter() - t)
     e2e_value = bytes_step * e2e_steps / e2e_s / 1e9
+    cabi_us_call = c_ns / (e2e_steps * L) / 1e3
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    host_s = 0.0
+    t = time.perf_counter()
+    for _ in range(e2e_steps):
+        be.metal_batch_begin()
+        th = time.perf_counter()
+        step(qh, kh, vh, ph, oh)
+        host_s += time.perf_counter() - th
+        be.metal_batch_end()
+    py_s = max_over_ranks(time.perf_counter() - t)
+    py_value = bytes_step * e2e_steps / py_s / 1e9
+    host_us_call = host_s / (e2e_steps * L) * 1e6
     if qkv:   # x and the hidden state in, hidden out; weights and caches stay
         h2d = L * B * QD * 4 * 2 + L * B * 4
         d2h = L * B * QD * 4
@@ -921,7 +965,13 @@ def main():
                                                 shard_len / wl["ctx"] if wl["split"] else 1.0),
                          "traffic_unit": "bytes per launch (ncu dram__bytes_read + write)"},
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+                    "d2h_bytes_per_step": d2h,
+                    "api": "C ABI (tg_decode_layer[_splitkv] / tg_attention_block[_splitkv]) "
+                           "called from ctypes with page-locked host buffers, one call per "
+                           "layer inside tg_batch_begin / tg_batch_end",
+                    "c_abi_us_per_layer_call": cabi_us_call,
+                    "python_api": {"value": py_value,
+                                   "host_us_per_layer_call": host_us_call}},
             "instep_us": instep,
             "merge_exchange_us_per_layer": instep["tail_us"] if instep else None,
             "parity": parity,

@@ -184,6 +184,7 @@ struct tg_context {
   std::vector<PackEntry> pack;
 
   char* hpin = nullptr;      size_t hpin_cap = 0, hpin_off = 0;
+  char* hpin_dev = nullptr;  // device address of the current pinned block
   std::vector<char*> hpin_old;  // outgrown pinned blocks, freed at the next sync
   std::vector<void*> graveyard;      // device buffers freed at the next sync
 
@@ -405,8 +406,14 @@ int hpin_alloc(tg_context* ctx, size_t bytes, char** out) {
     if (n < (size_t(1) << 20)) n = size_t(1) << 20;
     char* nb = nullptr;
     TG_CUDA(cudaHostAlloc(&nb, n, cudaHostAllocDefault));
+    void* nd = nullptr;
+    if (cudaHostGetDevicePointer(&nd, nb, 0) != cudaSuccess) {
+      cudaGetLastError();
+      nd = nullptr;  // no device address: inputs move by copies only
+    }
     if (ctx->hpin) ctx->hpin_old.push_back(ctx->hpin);
     ctx->hpin = nb;
+    ctx->hpin_dev = static_cast<char*>(nd);
     ctx->hpin_cap = n;
     ctx->hpin_off = 0;
   }
@@ -457,8 +464,74 @@ int pack_input(tg_context* ctx, const void* p, size_t bytes, void** dev) {
 // end and for the copy, and loses its programmatic (PDL) overlap.  Arena
 // slots are fresh within a batch and the stream is drained before they are
 // reused, so the early copies overwrite nothing still in use.
+// Inside a batch, small inputs (at most kStageKernelMax bytes in at most
+// tg::kStageMaxRuns runs of the current pinned block) move by a staging
+// kernel instead: copies on a side stream joined by an event still put the
+// event wait between two kernels of the compute stream (the next kernel
+// waits for the previous one to end), while a kernel keeps the chain
+// kernel-to-kernel with its programmatic overlap.
+constexpr size_t kStageKernelMax = 256 * 1024;
+
 int commit_inputs(tg_context* ctx) {
   if (ctx->pack.empty()) return TG_OK;
+  if (ctx->in_batch) {
+    size_t total = 0;
+    for (const auto& e : ctx->pack) total += (e.bytes + 255) & ~size_t(255);
+    if (total <= kStageKernelMax) {
+      std::vector<char*> stage(ctx->pack.size());
+      for (size_t i = 0; i < ctx->pack.size(); ++i) {
+        TG_TRY(hpin_alloc(ctx, ctx->pack[i].bytes, &stage[i]));
+        std::memcpy(stage[i], ctx->pack[i].host, ctx->pack[i].bytes);
+      }
+      tg::StageParams sp{};
+      bool ok = ctx->hpin_dev != nullptr;
+      int total16 = 0;
+      size_t i = 0;
+      while (ok && i < ctx->pack.size()) {
+        char* d0 = ctx->pack[i].dev;
+        char* h0 = stage[i];
+        size_t run = 0, j = i;
+        for (; j < ctx->pack.size(); ++j) {
+          if (ctx->pack[j].dev != d0 + run || stage[j] != h0 + run) break;
+          run += (ctx->pack[j].bytes + 255) & ~size_t(255);
+        }
+        const size_t bytes = (size_t)(ctx->pack[j - 1].dev - d0) + ctx->pack[j - 1].bytes;
+        if (sp.n_runs == tg::kStageMaxRuns || h0 < ctx->hpin ||
+            h0 + bytes > ctx->hpin + ctx->hpin_cap) {
+          ok = false;
+          break;
+        }
+        // Slots are 256-byte aligned and padded: 16-byte words cover them.
+        tg::StageRun& r = sp.run[sp.n_runs++];
+        r.src = reinterpret_cast<const uint4*>(ctx->hpin_dev + (h0 - ctx->hpin));
+        r.dst = reinterpret_cast<uint4*>(d0);
+        r.n16 = (int)((bytes + 15) / 16);
+        total16 += r.n16;
+        i = j;
+      }
+      if (ok) {
+        ctx->pack.clear();
+        cudaError_t e = tg::launch_stage_copy(sp, total16, ctx->stream);
+        if (e != cudaSuccess) return fail(TG_ERR_CUDA, "staging launch: %s", cudaGetErrorString(e));
+        ctx->launches++;
+        return TG_OK;
+      }
+      // Fall back to copies from the staging already filled.
+      cudaStream_t cs = ctx->stream;
+      if (!ctx->copy_stream) {
+        TG_CUDA(cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking));
+        TG_CUDA(cudaEventCreateWithFlags(&ctx->copy_done, cudaEventDisableTiming));
+      }
+      cs = ctx->copy_stream;
+      for (size_t k = 0; k < ctx->pack.size(); ++k)
+        TG_CUDA(cudaMemcpyAsync(ctx->pack[k].dev, stage[k], ctx->pack[k].bytes,
+                                cudaMemcpyHostToDevice, cs));
+      ctx->pack.clear();
+      TG_CUDA(cudaEventRecord(ctx->copy_done, cs));
+      TG_CUDA(cudaStreamWaitEvent(ctx->stream, ctx->copy_done, 0));
+      return TG_OK;
+    }
+  }
   cudaStream_t cs = ctx->stream;
   if (ctx->in_batch) {
     if (!ctx->copy_stream) {

@@ -1314,6 +1314,42 @@ size_t decode_mma_smem(int nkv, int B) {
   }
 }
 
+// One warp per CTA (so that CTAs fit beside a decode CTA, whose registers
+// leave room for single warps only), 4 x 16 bytes in flight per thread.
+// The copies run before the grid-dependency wait: the source is this call's
+// page-locked staging, written by the host before the launch, and the
+// destinations are slots no earlier kernel uses.  The wait comes after them
+// so that the next kernel's wait on this one also covers the previous
+// kernel.
+__global__ void __launch_bounds__(32) stage_copy_kernel(const StageParams p) {
+  griddep_launch_dependents();
+  const int stride = gridDim.x * 32;
+  for (int r = 0; r < p.n_runs; ++r) {
+    const StageRun c = p.run[r];
+    for (int i0 = blockIdx.x * 32 + threadIdx.x; i0 < c.n16; i0 += 4 * stride) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * stride;
+        if (i < c.n16) v[u] = c.src[i];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * stride;
+        if (i < c.n16) c.dst[i] = v[u];
+      }
+    }
+  }
+  griddep_wait();
+}
+
+cudaError_t launch_stage_copy(const StageParams& p, int total16, cudaStream_t st) {
+  int grid = (total16 + 4 * 32 - 1) / (4 * 32);
+  if (grid < 1) grid = 1;
+  if (grid > 64) grid = 64;
+  return launch_pdl(stage_copy_kernel, dim3(grid), dim3(32), 0, st, p);
+}
+
 cudaError_t prepare_decode_kernels(int max_seqs) {
   const size_t cap = 227 * 1024;
   auto lim = [&](size_t x) { return x < cap ? x : cap; };

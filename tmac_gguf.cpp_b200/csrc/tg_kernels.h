@@ -35,6 +35,22 @@ cudaError_t launch_decode_small(const DecodeParams& p, int dtype, cudaStream_t s
 size_t decode_small_smem(int group, int max_ctx, int split);
 
 cudaError_t launch_merge(const MergeParams& p, cudaStream_t st);
+
+// Copies of a call's packed host inputs from page-locked staging (through
+// its device address) into their device slots, issued by a kernel so that
+// the kernels of a batch follow one another with programmatic overlap (a
+// copy node or an event wait between two kernels removes it).
+constexpr int kStageMaxRuns = 8;
+struct StageRun {
+  const uint4* src;
+  uint4* dst;
+  int n16;  // 16-byte words
+};
+struct StageParams {
+  StageRun run[kStageMaxRuns];
+  int n_runs;
+};
+cudaError_t launch_stage_copy(const StageParams& p, int total16, cudaStream_t st);
 // Raises the shared-memory limit of the tensor-core decode (n_kv 1, 2, 4) and
 // the CUDA-core decode (fp32, bf16) on the current device to what max_seqs
 // sequences can need, so that later launches change no kernel attribute.
