@@ -343,6 +343,49 @@ def test_pinned_host_buffers_match_pageable(tg, backend, O, cases, splitkv):
     assert np.array_equal(bits(outp.numpy()), bits(res_a[0][2]))
 
 
+def test_pinned_host_buffers_short_cache(tg, backend, O, cases):
+    """The reference's own case -- an fp32 cache of at most 1024 positions
+    on the short-cache kernel -- with page-locked buffers inside a batch:
+    inputs move by the staging kernel, the rotated q / k and the output are
+    written through the buffers' device addresses (no device->host copies
+    between the kernels); bit-identical to pageable buffers, RoPE and the
+    cache row bit-exact, attention within the fp32 bar."""
+    import torch
+    positions = [0, 33, 255, 1000]
+    layers = 3
+    max_ctx = 1024
+    kv_a = tg.KVCache(backend, layers, len(positions), max_ctx, dtype=tg.DTYPE_F32)
+    kv_b = tg.KVCache(backend, layers, len(positions), max_ctx, dtype=tg.DTYPE_F32)
+    inputs, refs = _fill_same([kv_a, kv_b], cases, positions, False, 57, layers)
+    pos_np = np.array(positions, np.int32)
+    pos_pin = torch.from_numpy(pos_np.copy()).pin_memory()
+    res_a, res_b = [], []
+    backend.metal_batch_begin()
+    for layer in range(layers):
+        Q, K, V = (x.copy() for x in inputs[layer])
+        out = np.zeros_like(Q)
+        kv_a.decode_layer(layer, Q, K, V, pos_np, out)
+        res_a.append((Q, K, out))
+        Qp, Kp, Vp = (torch.from_numpy(x.copy()).pin_memory() for x in inputs[layer])
+        outp = torch.zeros(Qp.shape, dtype=torch.float32).pin_memory()
+        kv_b.decode_layer(layer, Qp, Kp, Vp, pos_pin, outp)
+        res_b.append((Qp, Kp, outp))
+    backend.metal_batch_end()
+    for layer in range(layers):
+        Q, K, out = res_a[layer]
+        Qp, Kp, outp = (t.numpy() for t in res_b[layer])
+        assert np.array_equal(bits(Qp), bits(Q)), layer
+        assert np.array_equal(bits(Kp), bits(K)), layer
+        assert np.array_equal(bits(outp), bits(out)), layer
+        for i, pos in enumerate(positions):
+            qr, kr, vr, kc, vc, ctx = refs[layer][i]
+            assert np.array_equal(bits(Qp[i]), bits(qr)), (layer, pos)
+            assert np.array_equal(bits(Kp[i]), bits(kr)), (layer, pos)
+            kb, vb = kv_b.read_rows(layer, i, pos, 1)
+            assert np.array_equal(bits(kb[0]), bits(kc[pos])), (layer, pos)
+            assert maxabs(outp[i], ctx) <= F32_TOL, (layer, pos)
+
+
 # ------------------------------------------------------ split-KV on one GPU
 
 def test_splitkv_world1_equals_batched(tg, backend, cases):

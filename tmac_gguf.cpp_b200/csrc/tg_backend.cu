@@ -1018,7 +1018,8 @@ int run_decode(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, const f
 // Short caches: RoPE of q and k, the new row's cache-write and attention in
 // one launch of the short-cache kernel (q and k rotated in place).
 int run_small_step(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, float* q, float* k,
-                   const float* v, const int* pos_dev, float* out) {
+                   const float* v, const int* pos_dev, float* out, float* q_wb = nullptr,
+                   float* k_wb = nullptr) {
   TG_TRY(commit_inputs(ctx));
   const tg_kv_desc& d = kv->d;
   TG_TRY(check_align8(q, "q"));
@@ -1049,6 +1050,8 @@ int run_small_step(tg_context* ctx, const tg_kv_cache* kv, int layer, int B, flo
   p.rope = 1;
   p.q_io = q;
   p.k_io = k;
+  p.q_wb = q_wb;
+  p.k_wb = k_wb;
   p.v_new = v;
   p.cs = t->d;
   p.table_len = kv->global_ctx;
@@ -2008,15 +2011,16 @@ int tg_decode_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, flo
   const size_t kb = (size_t)n_seqs * kv->row_elems * 4;
   void *dq = nullptr, *dk = nullptr, *dout = nullptr;
   const void *dv = nullptr, *dp = nullptr, *dq_in = nullptr, *dk_in = nullptr, *dout_in = nullptr;
-  // The tensor-core path reads staged copies and writes pinned host outputs
-  // directly; the CUDA-core path works in place.
-  const bool split_io = mma_eligible(kv);
+  // The tensor-core and short-cache paths read staged copies and write
+  // page-locked host outputs directly (no device->host copy between two
+  // kernels of a batch); the CUDA-core path works in place.
+  const bool split_io = mma_eligible(kv) || small_eligible(kv);
   TG_TRY(stage_out(ctx, q, qb, true, &dq, split_io ? &dq_in : nullptr));
   TG_TRY(stage_out(ctx, k_new, kb, true, &dk, split_io ? &dk_in : nullptr));
   TG_TRY(stage_in(ctx, v_new, kb, &dv));
   TG_TRY(stage_in(ctx, pos, (size_t)n_seqs * 4, &dp));
   TG_TRY(stage_out(ctx, out, qb, false, &dout, split_io ? &dout_in : nullptr));
-  if (split_io) {
+  if (split_io && mma_eligible(kv)) {
     TG_TRY(run_fused(ctx, kv, layer, n_seqs, static_cast<const float*>(dq_in),
                      static_cast<float*>(dq), const_cast<float*>(static_cast<const float*>(dk_in)),
                      static_cast<const float*>(dv), static_cast<const int*>(dp),
@@ -2025,9 +2029,11 @@ int tg_decode_layer(tg_context* ctx, tg_kv_cache* kv, int layer, int n_seqs, flo
     return finish_call(ctx);
   }
   if (small_eligible(kv)) {
-    TG_TRY(run_small_step(ctx, kv, layer, n_seqs, static_cast<float*>(dq), static_cast<float*>(dk),
+    TG_TRY(run_small_step(ctx, kv, layer, n_seqs, const_cast<float*>(static_cast<const float*>(dq_in)),
+                          const_cast<float*>(static_cast<const float*>(dk_in)),
                           static_cast<const float*>(dv), static_cast<const int*>(dp),
-                          static_cast<float*>(dout)));
+                          static_cast<float*>(dout), static_cast<float*>(dq),
+                          static_cast<float*>(dk)));
     return finish_call(ctx);
   }
   TG_TRY(run_rope(ctx, kv, layer, n_seqs, static_cast<float*>(dq), static_cast<float*>(dk),

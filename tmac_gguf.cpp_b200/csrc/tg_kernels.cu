@@ -1059,10 +1059,12 @@ __global__ void __launch_bounds__(SMALL_THREADS) decode_small_kernel(const Decod
   }
   // 5. Rank 0 writes the rotated q / k back and the new row into the cache.
   if (fuse && crank == 0) {
-    for (int i = tid; i < G * HD; i += SMALL_THREADS) p.q_io[qoff + i] = q_s[i];
+    float* qw = p.q_wb ? p.q_wb : p.q_io;
+    float* kw = p.k_wb ? p.k_wb : p.k_io;
+    for (int i = tid; i < G * HD; i += SMALL_THREADS) qw[qoff + i] = q_s[i];
     const size_t crow = (seq_rows + pl) * kdim + kvh * HD;
     for (int i = tid; i < HD; i += SMALL_THREADS) {
-      p.k_io[koff + i] = kn_s[i];
+      kw[koff + i] = kn_s[i];
       store_elem<Elem>(static_cast<Elem*>(p.k_cache) + crow + i, kn_s[i]);
       store_elem<Elem>(static_cast<Elem*>(p.v_cache) + crow + i, vn_s[i]);
     }

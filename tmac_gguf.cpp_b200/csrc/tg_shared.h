@@ -104,6 +104,8 @@ struct DecodeParams {
   int table_len;
   void* k_cache;         // layer base of the caches (writable views of k / v)
   void* v_cache;
+  float* q_wb;           // where the rotated q / k go (null: back into q_io / k_io)
+  float* k_wb;
   int split;             // short-cache kernel: CTAs (a cluster) per (sequence, KV head)
   int stage_v;           // short-cache kernel: V rows copied to shared memory with the K loads
 };
