@@ -88,6 +88,7 @@ WORKLOADS = {
 # streams 1/N of the rows, so the figure is scaled by the shard's share.
 NCU_TRAFFIC = {
     "longctx": (268508928, 3666176),
+    "batched": (538675200, 5082112),
     "prefill": (75751936, 67844352),
 }
 

@@ -96,3 +96,42 @@ def test_shard_ranges_cover_context(built):
                 if n:
                     assert s == pos
                 pos += n
+
+
+def test_tuning_and_wait_limit_validate_arguments(built):
+    L = built.lib()
+    assert L.tg_set_decode_tuning(0, 0) == built.TG_OK
+    assert L.tg_set_decode_tuning(128, 1) == built.TG_OK
+    assert L.tg_set_decode_tuning(192, 0) == built.TG_OK
+    assert L.tg_set_decode_tuning(64, 0) == built.TG_ERR_INVALID_ARG
+    assert L.tg_set_decode_tuning(0, 2) == built.TG_ERR_INVALID_ARG
+    assert L.tg_set_decode_tuning(0, 0) == built.TG_OK   # back to the defaults
+    assert L.tg_comm_set_wait_limit_ms(None, 1000) == built.TG_ERR_INVALID_ARG
+    n = C.c_int()
+    assert L.tg_profile_read_stamps(None, None, 0, C.byref(n), C.byref(n)) == \
+        built.TG_ERR_INVALID_ARG
+
+
+def test_stamp_summary_reads_the_record_layout():
+    """bench.py's in-step timing from per-CTA stamps: decode rows first,
+    merge rows after the SM count, absent CTAs zero."""
+    import numpy as np
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    n_sms, steps = 4, 3
+    st = np.zeros((steps, 3 * n_sms, 4), np.uint64)
+    for L in range(steps):
+        t0 = 1_000_000 + 50_000 * L          # release of layer L, ns
+        for c in range(n_sms):                # decode CTAs
+            st[L, c] = (t0 - 5000 + 100 * c, t0 + 10 * c, t0 + 40_000 + 500 * c, t0 + 41_000 + 500 * c)
+        for m in range(2):                    # two merge CTAs
+            st[L, n_sms + m] = (t0 + 40_000, t0 + 43_000, 0, t0 + 45_000 + 100 * m)
+    s = bench.stamp_summary(st, n_sms)
+    assert s["steps"] == steps
+    assert abs(s["tiles_us"] - 41.5) < 1e-9          # last tile at +41.5 us
+    assert abs(s["launch_us"] - 45.1) < 1e-9         # last merge CTA at +45.1 us
+    assert abs(s["tail_us"] - 3.6) < 1e-9
+    assert abs(s["period_us"] - 50.0) < 1e-9
+    assert abs(s["early_us"] - 5.0) < 1e-9
