@@ -386,6 +386,44 @@ def test_pinned_host_buffers_short_cache(tg, backend, O, cases):
             assert maxabs(outp[i], ctx) <= F32_TOL, (layer, pos)
 
 
+@pytest.mark.parametrize("splitkv", [False, True])
+def test_staged_positions_change_between_batches(tg, backend, O, cases, splitkv):
+    """The bf16 decode kernel builds its tile schedule from the positions
+    before its grid-dependency wait, while the staging kernel in front of it
+    may still be copying them.  Batches that reuse the same staging slots
+    with different positions (and so different schedules) must each decode
+    with their own: a schedule built from the previous batch's positions
+    gives wrong outputs or a bad-position error."""
+    import torch
+    P = ([9000, 40, 5000, 7], [3, 8100, 64, 6000])
+    layers = 4
+    max_ctx = max(max(p) for p in P) + 1
+    kvs, data = [], []
+    for j, positions in enumerate(P):
+        kv = tg.KVCache(backend, layers, len(positions), max_ctx, dtype=tg.DTYPE_BF16)
+        inputs, refs = _fill_same([kv], cases, positions, True, 71 + j, layers)
+        kvs.append(kv)
+        data.append((torch.from_numpy(np.array(positions, np.int32)).pin_memory(),
+                     inputs, refs))
+    for rnd, j in enumerate([0, 1, 0, 1]):
+        kv, (pos_pin, inputs, refs) = kvs[j], data[j]
+        res = []
+        backend.metal_batch_begin()
+        for layer in range(layers):
+            Qp, Kp, Vp = (torch.from_numpy(x.copy()).pin_memory() for x in inputs[layer])
+            outp = torch.zeros(Qp.shape, dtype=torch.float32).pin_memory()
+            (kv.decode_layer_splitkv if splitkv else kv.decode_layer)(layer, Qp, Kp, Vp,
+                                                                     pos_pin, outp)
+            res.append((Qp, outp))
+        backend.metal_batch_end()
+        for layer in range(layers):
+            Qp, outp = (t.numpy() for t in res[layer])
+            for i, pos in enumerate(P[j]):
+                qr, kr, vr, kc, vc, ctx = refs[layer][i]
+                assert np.array_equal(bits(Qp[i]), bits(qr)), (rnd, layer, pos)
+                assert maxabs(outp[i], ctx) <= BF16_TOL, (rnd, layer, pos)
+
+
 # ------------------------------------------------------ split-KV on one GPU
 
 def test_splitkv_world1_equals_batched(tg, backend, cases):

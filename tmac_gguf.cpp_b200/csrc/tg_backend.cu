@@ -163,6 +163,7 @@ struct tg_context {
   cudaStream_t copy_stream = nullptr;
   cudaEvent_t copy_done = nullptr;
   int* d_err = nullptr;
+  int* h_err = nullptr;  // page-locked copy of d_err, read after a stream wait
 
   float* part = nullptr;     size_t part_cap = 0;    // floats
   int* sched = nullptr;      size_t sched_cap = 0;   // ints
@@ -175,6 +176,15 @@ struct tg_context {
   float* qx = nullptr;        size_t qx_cap = 0;   // decode from x: rotated q
   float* cx = nullptr;        size_t cx_cap = 0;   // attention block: context
   std::vector<PendingCopy> pending;  // device -> host copies of staged outputs
+  // Page-locked host outputs of the current batch: kernels write device
+  // slots, and one store kernel moves them to the host at tg_batch_end.
+  struct DeferredStore {
+    void* host;
+    void* alias;  // device address of `host`
+    const void* dev;
+    size_t bytes;
+  };
+  std::vector<DeferredStore> dstores;
   // Host inputs of the current call, moved to the arena by commit_inputs.
   struct PackEntry {
     char* dev;
@@ -299,10 +309,30 @@ int ensure_buf(tg_context* ctx, T** buf, size_t* cap, size_t need) {
   return TG_OK;
 }
 
-// Reads and clears the device error word (stream must be idle).
-int check_device_error(tg_context* ctx) {
+// Queues the copy of the device error word into its page-locked mirror
+// behind the stream's work, so that the wait that follows also brings the
+// word back (no second, synchronous copy after the wait).  Returns whether
+// it was queued.
+bool queue_error_read(tg_context* ctx) {
+  if (!ctx->h_err || ctx->capturing) return false;
+  if (cudaMemcpyAsync(ctx->h_err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost,
+                      ctx->stream) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return true;
+}
+
+// Reads and clears the device error word (stream must be idle).  queued:
+// queue_error_read ran before the wait, so the mirror holds the word.
+int check_device_error(tg_context* ctx, bool queued = false) {
   int h = 0;
-  TG_CUDA(cudaMemcpy(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (queued) {
+    h = *reinterpret_cast<volatile int*>(ctx->h_err);
+    *ctx->h_err = 0;
+  } else {
+    TG_CUDA(cudaMemcpy(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  }
   if (h != 0) {
     TG_CUDA(cudaMemset(ctx->d_err, 0, sizeof(int)));
     const char* what = h == tg::kDevErrBadPos         ? "position outside the cache / RoPE table"
@@ -603,6 +633,21 @@ int stage_out(tg_context* ctx, void* p, size_t bytes, bool copy_in, void** dev,
   if (ctx->capturing)
     return fail(TG_ERR_STATE, "host pointers cannot be used inside a graph capture");
   ctx->call_staged = true;
+  if (ctx->in_batch && pi.alias) {
+    // Page-locked memory inside a batch: the kernels work on a device slot
+    // (in place when copy_in) and the store kernel at tg_batch_end writes it
+    // to the host, so that no kernel of the batch writes host memory.
+    void* d = nullptr;
+    if (copy_in) {
+      TG_TRY(pack_input(ctx, p, bytes, &d));
+    } else {
+      TG_TRY(arena_alloc(ctx, bytes, &d));
+    }
+    ctx->dstores.push_back({p, pi.alias, d, bytes});
+    *dev = d;
+    if (dev_in) *dev_in = d;
+    return TG_OK;
+  }
   if (dev_in && pi.alias) {
     *dev = pi.alias;
     if (copy_in) {
@@ -626,6 +671,34 @@ int stage_out(tg_context* ctx, void* p, size_t bytes, bool copy_in, void** dev,
   return TG_OK;
 }
 
+// Moves the batch's deferred page-locked outputs to the host: one store
+// kernel over an entry list in page-locked staging, or one copy per output
+// when the staging has no device address.
+int flush_deferred(tg_context* ctx) {
+  if (ctx->dstores.empty()) return TG_OK;
+  const size_t n = ctx->dstores.size();
+  char* h = nullptr;
+  if (n <= (1u << 20)) TG_TRY(hpin_alloc(ctx, n * sizeof(tg::StoreEntry), &h));
+  if (h && ctx->hpin_dev) {
+    tg::StoreEntry* e = reinterpret_cast<tg::StoreEntry*>(h);
+    for (size_t i = 0; i < n; ++i)
+      e[i] = tg::StoreEntry{ctx->dstores[i].alias, ctx->dstores[i].dev,
+                            (unsigned long long)ctx->dstores[i].bytes};
+    const tg::StoreEntry* de =
+        reinterpret_cast<const tg::StoreEntry*>(ctx->hpin_dev + (h - ctx->hpin));
+    ctx->dstores.clear();
+    cudaError_t err = tg::launch_store_out(de, (int)n, ctx->stream);
+    if (err != cudaSuccess)
+      return fail(TG_ERR_CUDA, "output store launch: %s", cudaGetErrorString(err));
+    ctx->launches++;
+    return TG_OK;
+  }
+  for (const auto& d : ctx->dstores)
+    TG_CUDA(cudaMemcpyAsync(d.host, d.dev, d.bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  ctx->dstores.clear();
+  return TG_OK;
+}
+
 // Issues the device->host copies of staged outputs.  A call that moved host
 // data waits for the stream (outside a batch) so that its host outputs are
 // valid on return; a call on device pointers only stays asynchronous, like
@@ -639,11 +712,12 @@ int finish_call(tg_context* ctx) {
     TG_CUDA(cudaMemcpyAsync(c.host, c.dev, c.bytes, cudaMemcpyDeviceToHost, ctx->stream));
   ctx->pending.clear();
   if (ctx->in_batch || !staged) return TG_OK;
+  const bool queued = queue_error_read(ctx);
   TG_TRY(wait_stream(ctx));
   ctx->arena_off = 0;
   ctx->hpin_off = 0;
   free_graveyard(ctx);
-  return check_device_error(ctx);
+  return check_device_error(ctx, queued);
 }
 
 // ------------------------------------------------ host-array mirrors
@@ -775,6 +849,7 @@ int flush_regions(tg_context* ctx) {
       TG_CUDA(cudaMemcpyAsync(r.host + r.dirty_lo, r.dev + r.dirty_lo, r.dirty_hi - r.dirty_lo,
                               cudaMemcpyDeviceToHost, ctx->stream));
   }
+  const bool queued = queue_error_read(ctx);
   TG_TRY(wait_stream(ctx));
   for (auto it = ctx->regions.begin(); it != ctx->regions.end();) {
     if (it->second.transient) {
@@ -789,7 +864,7 @@ int flush_regions(tg_context* ctx) {
   ctx->hpin_off = 0;
   ctx->call_staged = false;
   free_graveyard(ctx);
-  return check_device_error(ctx);
+  return check_device_error(ctx, queued);
 }
 
 // End of a compat op: outside a batch, host arrays are written back and the
@@ -1509,6 +1584,12 @@ int tg_init(int device, tg_context** out) {
     delete c;
     return fail(TG_ERR_CUDA, "context setup failed: %s", cudaGetErrorString(e));
   }
+  if (cudaHostAlloc(&c->h_err, sizeof(int), cudaHostAllocDefault) == cudaSuccess) {
+    *c->h_err = 0;
+  } else {
+    cudaGetLastError();
+    c->h_err = nullptr;  // the error word is then read by a synchronous copy
+  }
   c->own_stream = true;
   *out = c;
   return TG_OK;
@@ -1546,6 +1627,7 @@ int tg_shutdown(tg_context* ctx) {
   cudaFree(ctx->qx);
   cudaFree(ctx->cx);
   cudaFree(ctx->d_err);
+  if (ctx->h_err) cudaFreeHost(ctx->h_err);
   if (ctx->copy_stream) {
     cudaStreamSynchronize(ctx->copy_stream);
     cudaStreamDestroy(ctx->copy_stream);
@@ -1582,6 +1664,7 @@ int tg_batch_begin(tg_context* ctx) {
   if (ctx->in_batch) return fail(TG_ERR_STATE, "batch already open");
   if (ctx->capturing) return fail(TG_ERR_STATE, "graph capture open");
   ctx->in_batch = true;
+  ctx->dstores.clear();
   return TG_OK;
 }
 
@@ -1589,22 +1672,25 @@ int tg_batch_end(tg_context* ctx) {
   TG_TRY(set_device(ctx));
   if (!ctx->in_batch) return fail(TG_ERR_STATE, "tg_batch_end without tg_batch_begin");
   ctx->in_batch = false;
+  const int rc = flush_deferred(ctx);
   for (const PendingCopy& c : ctx->pending)
     TG_CUDA(cudaMemcpyAsync(c.host, c.dev, c.bytes, cudaMemcpyDeviceToHost, ctx->stream));
   ctx->pending.clear();
-  return flush_regions(ctx);
+  const int rf = flush_regions(ctx);
+  return rc != TG_OK ? rc : rf;
 }
 
 int tg_synchronize(tg_context* ctx) {
   TG_TRY(set_device(ctx));
   if (ctx->capturing) return fail(TG_ERR_STATE, "graph capture open");
+  const bool queued = queue_error_read(ctx);
   TG_TRY(wait_stream(ctx));
   if (!ctx->in_batch) {
     ctx->arena_off = 0;
     ctx->hpin_off = 0;
     free_graveyard(ctx);
   }
-  return check_device_error(ctx);
+  return check_device_error(ctx, queued);
 }
 
 int tg_graph_begin(tg_context* ctx) {

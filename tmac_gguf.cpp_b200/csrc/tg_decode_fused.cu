@@ -106,15 +106,17 @@ __device__ __forceinline__ int seq_tiles(const FusedParams& p, int pl) {
 }
 
 // Tile prefix over sequences, as build_tile_prefix in tg_kernels.cu.  Reads
-// only the positions, which no kernel of this library writes, so it may run
-// before the grid-dependency wait.
+// only the positions, so it may run before the grid-dependency wait: the
+// only kernel of this library that writes positions is the staging copy of
+// host inputs, which stores and fences them before it lets the next kernel
+// launch.  The reads go to L2 (no stale L1 line of a reused staging slot).
 __device__ void fused_prefix(const FusedParams& p, int* prefix, int* warp_tot) {
   const int NT = blockDim.x, t = threadIdx.x, lane = t & 31, w = t >> 5;
   const int chunk = (p.B + NT - 1) / NT;
   const int b0 = min(t * chunk, p.B), b1 = min(b0 + chunk, p.B);
   int sum = 0;
   for (int s = b0; s < b1; ++s) {
-    int tiles = seq_tiles(p, p.pos[s]);
+    int tiles = seq_tiles(p, __ldcg(p.pos + s));
     if (tiles < 0) {
       record_error(p.err, kDevErrBadPos);
       tiles = 0;
@@ -209,7 +211,7 @@ __global__ void __launch_bounds__(FusedCfg<NKV, RING_KB>::THREADS, 1)
       while (prefix[ps + 1] <= pt) ++ps;
       const int j = pt - prefix[ps];
       if (guard) {
-        const int local_new = p.pos[ps] - p.shard_start;
+        const int local_new = __ldcg(p.pos + ps) - p.shard_start;
         if (local_new >= j * TILE && local_new < (j + 1) * TILE) break;
       }
       if (!mbar_wait(&empty[pst], pph ^ 1u, p.err, kDevErrWaitEmpty)) {
@@ -564,13 +566,13 @@ __global__ void __launch_bounds__(64 * GROUPS) merge_exchange_kernel(const Fused
   // The RoPE row of this CTA's first item (the table is written only when
   // it is created).
   const int s_first = blockIdx.x / p.n_head;
-  const int pos_first = s_first < p.B ? p.pos[s_first] : -1;
+  const int pos_first = s_first < p.B ? __ldcg(p.pos + s_first) : -1;
   float2 cs_first = make_float2(0.f, 0.f);
   if (p.rope && pos_first >= 0 && pos_first < p.table_len)
     cs_first = reinterpret_cast<const float2*>(p.cs + (size_t)pos_first * 64)[d >> 1];
   if (local_sched) {
     const int lane = tid & 31, w = tid >> 5;
-    const int tiles = tid < p.B ? max(seq_tiles(p, p.pos[tid]), 0) : 0;
+    const int tiles = tid < p.B ? max(seq_tiles(p, __ldcg(p.pos + tid)), 0) : 0;
     int incl = tiles;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {

@@ -1320,11 +1320,12 @@ size_t decode_mma_smem(int nkv, int B) {
 // leave room for single warps only), 4 x 16 bytes in flight per thread.
 // The copies run before the grid-dependency wait: the source is this call's
 // page-locked staging, written by the host before the launch, and the
-// destinations are slots no earlier kernel uses.  The wait comes after them
-// so that the next kernel's wait on this one also covers the previous
-// kernel.
+// destinations are slots no earlier kernel uses.  The next kernel is let
+// launch only after the copies are stored and fenced, because kernels read
+// some inputs (positions, projection weights) before their own
+// grid-dependency wait.  The wait comes last so that the next kernel's wait
+// on this one also covers the previous kernel.
 __global__ void __launch_bounds__(32) stage_copy_kernel(const StageParams p) {
-  griddep_launch_dependents();
   const int stride = gridDim.x * 32;
   for (int r = 0; r < p.n_runs; ++r) {
     const StageRun c = p.run[r];
@@ -1342,7 +1343,47 @@ __global__ void __launch_bounds__(32) stage_copy_kernel(const StageParams p) {
       }
     }
   }
+  __threadfence();
+  griddep_launch_dependents();
   griddep_wait();
+}
+
+// The outputs a batch's kernels left in device slots go to their
+// page-locked host buffers in one launch at the end of the batch, so that
+// no kernel inside the batch writes host memory (a kernel that does ends
+// only once its writes have crossed the host link, and the next kernel's
+// grid-dependency wait waits for that).  The entry list is host-written
+// before the launch, so it is read before the wait; the copies come after
+// it.  16-byte words when both ends and the size allow, else 4-byte words,
+// else bytes.
+__global__ void __launch_bounds__(256) store_out_kernel(const StoreEntry* list, int n) {
+  griddep_launch_dependents();
+  StoreEntry e{};
+  if ((int)blockIdx.x < n) e = list[blockIdx.x];
+  griddep_wait();
+  for (int i0 = blockIdx.x; i0 < n; i0 += gridDim.x) {
+    if (i0 != (int)blockIdx.x) e = list[i0];
+    const uintptr_t a = reinterpret_cast<uintptr_t>(e.dst) | reinterpret_cast<uintptr_t>(e.src);
+    if (((a | e.bytes) & 15) == 0) {
+      const uint4* s = static_cast<const uint4*>(e.src);
+      uint4* d = static_cast<uint4*>(e.dst);
+      for (size_t i = threadIdx.x; i < e.bytes / 16; i += blockDim.x) d[i] = __ldcg(s + i);
+    } else if (((a | e.bytes) & 3) == 0) {
+      const unsigned* s = static_cast<const unsigned*>(e.src);
+      unsigned* d = static_cast<unsigned*>(e.dst);
+      for (size_t i = threadIdx.x; i < e.bytes / 4; i += blockDim.x) d[i] = __ldcg(s + i);
+    } else {
+      const unsigned char* s = static_cast<const unsigned char*>(e.src);
+      unsigned char* d = static_cast<unsigned char*>(e.dst);
+      for (size_t i = threadIdx.x; i < e.bytes; i += blockDim.x) d[i] = s[i];
+    }
+  }
+}
+
+cudaError_t launch_store_out(const StoreEntry* list, int n, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  return launch_pdl(store_out_kernel, dim3((unsigned)(n < 1024 ? n : 1024)), dim3(256), 0, st,
+                    list, n);
 }
 
 cudaError_t launch_stage_copy(const StageParams& p, int total16, cudaStream_t st) {

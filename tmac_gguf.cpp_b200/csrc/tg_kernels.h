@@ -51,6 +51,16 @@ struct StageParams {
   int n_runs;
 };
 cudaError_t launch_stage_copy(const StageParams& p, int total16, cudaStream_t st);
+// Deferred host outputs of a batch: entry e copies `bytes` from device
+// memory `src` to `dst` (the device address of page-locked host memory).
+// The entry list itself lives in page-locked memory (read through its
+// device address before the grid-dependency wait); one CTA per entry.
+struct StoreEntry {
+  void* dst;
+  const void* src;
+  unsigned long long bytes;
+};
+cudaError_t launch_store_out(const StoreEntry* list, int n, cudaStream_t st);
 // Raises the shared-memory limit of the tensor-core decode (n_kv 1, 2, 4) and
 // the CUDA-core decode (fp32, bf16) on the current device to what max_seqs
 // sequences can need, so that later launches change no kernel attribute.
