@@ -26,7 +26,10 @@
  *    host arrays get persistent device mirrors, like the reference's buffer
  *    wrapper cache (metal_backend.hpp:44-65); results in host arrays are
  *    valid after tg_batch_end (or on return when no batch is open), exactly
- *    when Metal results are valid after metal_batch_end.
+ *    when Metal results are valid after metal_batch_end.  Host buffers that
+ *    a call inside a batch writes (outputs, in-place q / k) must stay
+ *    allocated until tg_batch_end: page-locked ones are written there.
+ *    Host inputs are read at the call and may be reused at once.
  *  - Shapes: head_dim even and <= 128, n_head a multiple of n_kv_head,
  *    n_head*head_dim <= 4096.  The tensor-core path serves bf16 caches with
  *    head_dim 64, n_kv_head in {1,2,4} and n_head/n_kv_head <= 8 (Qwen2-0.5B:

@@ -12,7 +12,10 @@ oracle, under the automatic exchange (peer memory for the bf16 cache when
 the GPUs map each other's memory) and the NCCL all-gather.  The layer from
 the normed hidden state (tg_decode_layer_splitkv_x: Q/K/V projection, then
 split-KV attention) is checked against the same layer on one GPU over the
-whole cache.  Exit status 0 on success on every rank.
+whole cache.  Batched calls with page-locked buffers (three layers per batch,
+position sets alternating over the same staging slots) and sequence-partitioned
+decode (each rank its own sequences, no collective) are checked against the
+oracle too.  Exit status 0 on success on every rank.
 """
 from __future__ import annotations
 
@@ -205,6 +208,99 @@ def main() -> int:
             print(f"x path bf16={bf16} exchange {be.exchange} block err {err:.2e}")
         kv.destroy()
         full.destroy()
+    # Inside a batch with page-locked host buffers, as a forward loop calls
+    # the library (and bench.py's end-to-end loop): three layers per batch,
+    # two position sets alternating over the same staging slots, outputs
+    # reaching the host at tg_batch_end; every layer against the oracle.
+    be.set_exchange(tg.EXCHANGE_AUTO)
+    layers = 3
+    sets = ([9000, 777, 12345, 0], [12000, 5, 640, world * 64 + 1])
+    gctx = max(max(s) for s in sets) + 1
+    start, length = tg.shard_range(gctx, world, rank)
+    kvs, data = [], []
+    for j, positions in enumerate(sets):
+        B = len(positions)
+        kvj = tg.KVCache(be, layers, B, max(length, 1), shard_start=start, global_ctx=gctx,
+                         dtype=tg.DTYPE_BF16)
+        ins, refs = [], []
+        for layer in range(layers):
+            Q = np.zeros((B, cases.QD), np.float32)
+            K = np.zeros((B, cases.KD), np.float32)
+            V = np.zeros((B, cases.KD), np.float32)
+            lrefs = []
+            for i, p in enumerate(positions):
+                q, k_new, v_new, kc, vc = cases.decode_inputs(60 + j, p, True, seq=i, layer=layer)
+                hi = min(start + length, p)
+                if hi > start:
+                    kvj.write_rows(layer, i, 0, kc[start:hi], vc[start:hi])
+                Q[i], K[i], V[i] = q, k_new, v_new
+                r = cases.oracle_decode(60 + j, p, True, seq=i, layer=layer)
+                lrefs.append((r[0], r[5]))
+            ins.append((Q, K, V))
+            refs.append(lrefs)
+        kvs.append(kvj)
+        data.append((torch.from_numpy(np.array(positions, np.int32)).pin_memory(), ins, refs))
+    worst = 0.0
+    for rnd, j in enumerate((0, 1, 0, 1)):
+        kvj, (pos_pin, ins, refs) = kvs[j], data[j]
+        # Every buffer of the batch stays allocated until tg_batch_end: the
+        # rotated q / k and the outputs reach the host there (a buffer freed
+        # earlier may already belong to another tensor).
+        res = []
+        be.metal_batch_begin()
+        for layer in range(layers):
+            Qp, Kp, Vp = (torch.from_numpy(x.copy()).pin_memory() for x in ins[layer])
+            outp = torch.zeros(Qp.shape, dtype=torch.float32).pin_memory()
+            kvj.decode_layer_splitkv(layer, Qp, Kp, Vp, pos_pin, outp)
+            res.append((Qp, Kp, Vp, outp))
+        be.metal_batch_end()
+        for layer in range(layers):
+            qo, o = res[layer][0].numpy(), res[layer][3].numpy()
+            for i, p in enumerate(sets[j]):
+                qr, ctx = refs[layer][i]
+                err = float(np.abs(o[i] - ctx).max())
+                worst = max(worst, err)
+                same_q = np.array_equal(qo[i].view(np.uint32), qr.view(np.uint32))
+                if err > 2e-3 or not same_q:
+                    print(f"rank {rank}: batched round {rnd} layer {layer} seq {i} pos {p} "
+                          f"err={err} rope_ok={same_q}")
+                    ok = False
+    if rank == 0:
+        print(f"batched page-locked split-KV x{world}: exchange {be.exchange}, "
+              f"max err {worst:.2e}")
+    for kvj in kvs:
+        kvj.destroy()
+    # Sequence-partitioned decode (BASELINE configs 2-3 over several GPUs):
+    # rank r owns sequences r, r + world, ... of one ragged batch and their
+    # caches, with no collective on the data path; bf16 and fp32 caches
+    # against the oracle.
+    glob = [3, 70, 1025, 4000, 9000, 64, 511, 2049]
+    mine = list(range(rank, len(glob), world))
+    for bf16, tol in ((True, 2e-3), (False, 1e-4)):
+        pr = [glob[s] for s in mine]
+        kvp = tg.KVCache(be, 1, len(pr), max(pr) + 1,
+                         dtype=tg.DTYPE_BF16 if bf16 else tg.DTYPE_F32)
+        Q = np.zeros((len(pr), cases.QD), np.float32)
+        K = np.zeros((len(pr), cases.KD), np.float32)
+        V = np.zeros((len(pr), cases.KD), np.float32)
+        refs = []
+        for i, s in enumerate(mine):
+            p = glob[s]
+            q, k_new, v_new, kc, vc = cases.decode_inputs(66, p, bf16, seq=s)
+            if p > 0:
+                kvp.write_rows(0, i, 0, kc[:p], vc[:p])
+            Q[i], K[i], V[i] = q, k_new, v_new
+            refs.append(cases.oracle_decode(66, p, bf16, seq=s)[5])
+        out = np.zeros((len(pr), cases.QD), np.float32)
+        kvp.decode_layer(0, Q, K, V, np.array(pr, np.int32), out)
+        for i, s in enumerate(mine):
+            err = float(np.abs(out[i] - refs[i]).max())
+            if err > tol:
+                print(f"rank {rank}: sequence-partitioned seq {s} bf16={bf16} err={err}")
+                ok = False
+        kvp.destroy()
+    if rank == 0:
+        print(f"sequence-partitioned x{world}: {len(glob)} sequences checked")
     # Failure detection: with a 1 s wait limit, rank 1 skips one layer's
     # call (it stays alive, its memory stays mapped, nothing of it is in
     # flight).  Every other rank's merge kernel stops waiting for rank 1's

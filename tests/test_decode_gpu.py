@@ -407,6 +407,8 @@ def test_staged_positions_change_between_batches(tg, backend, O, cases, splitkv)
                      inputs, refs))
     for rnd, j in enumerate([0, 1, 0, 1]):
         kv, (pos_pin, inputs, refs) = kvs[j], data[j]
+        # Every buffer of the batch stays allocated until tg_batch_end, where
+        # the rotated q / k and the outputs reach the host.
         res = []
         backend.metal_batch_begin()
         for layer in range(layers):
@@ -414,13 +416,14 @@ def test_staged_positions_change_between_batches(tg, backend, O, cases, splitkv)
             outp = torch.zeros(Qp.shape, dtype=torch.float32).pin_memory()
             (kv.decode_layer_splitkv if splitkv else kv.decode_layer)(layer, Qp, Kp, Vp,
                                                                      pos_pin, outp)
-            res.append((Qp, outp))
+            res.append((Qp, Kp, Vp, outp))
         backend.metal_batch_end()
         for layer in range(layers):
-            Qp, outp = (t.numpy() for t in res[layer])
+            Qp, Kp, _, outp = (t.numpy() for t in res[layer])
             for i, pos in enumerate(P[j]):
                 qr, kr, vr, kc, vc, ctx = refs[layer][i]
                 assert np.array_equal(bits(Qp[i]), bits(qr)), (rnd, layer, pos)
+                assert np.array_equal(bits(Kp[i]), bits(kr)), (rnd, layer, pos)
                 assert maxabs(outp[i], ctx) <= BF16_TOL, (rnd, layer, pos)
 
 
